@@ -1,0 +1,1025 @@
+// C ABI of libpager_b200.so: argument checking, split planning, tensor-map
+// encoding, the combine / mass / finalize kernels, the pinned host pool and
+// the host-link probes.  Declarations and layouts: include/pager_b200.h.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <unordered_map>
+
+#include "pager_b200.h"
+#include "pager_split.cuh"
+
+namespace pager {
+
+__device__ int g_status;
+
+bool lookup_split_mma(int kv_dtype, int head_dim, int mode, SplitKernelInfo* out);
+bool lookup_split_fma_f32(int head_dim, int mode, SplitKernelInfo* out);
+bool lookup_split_fma_f16(int head_dim, int mode, SplitKernelInfo* out);
+bool lookup_split_fma_bf16(int head_dim, int mode, SplitKernelInfo* out);
+
+bool lookup_split_kernel(int kv_dtype, int head_dim, int mode, int backend, SplitKernelInfo* out) {
+  if (backend == BACKEND_MMA) return lookup_split_mma(kv_dtype, head_dim, mode, out);
+  if (kv_dtype == 0) return lookup_split_fma_f32(head_dim, mode, out);
+  if (kv_dtype == 1) return lookup_split_fma_f16(head_dim, mode, out);
+  if (kv_dtype == 2) return lookup_split_fma_bf16(head_dim, mode, out);
+  return false;
+}
+
+namespace {
+
+thread_local std::string t_err;
+
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  t_err = buf;
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  return fail(PAGER_ERR_CUDA, "%s: %s (%s)", what, cudaGetErrorString(e), cudaGetErrorName(e));
+}
+
+#define PAGER_CUDA(call, what)                  \
+  do {                                          \
+    cudaError_t e_ = (call);                    \
+    if (e_ != cudaSuccess) return cuda_fail(e_, what); \
+  } while (0)
+
+constexpr unsigned long long kWaitLimitNs = 4000000000ull;  // 4 s per bounded device wait
+constexpr int kMaxSplits = 1024;
+
+struct DevInfo {
+  bool init = false;
+  int sms = 0;
+  int* status = nullptr;
+};
+std::mutex g_mu;
+DevInfo g_dev[128];
+std::unordered_map<const void*, int> g_occupancy;  // per kernel (one smem config each)
+
+int device_info(DevInfo** out) {
+  int dev = 0;
+  PAGER_CUDA(cudaGetDevice(&dev), "cudaGetDevice");
+  if (dev < 0 || dev >= 128) return fail(PAGER_ERR_CUDA, "device ordinal %d out of range", dev);
+  std::lock_guard<std::mutex> lk(g_mu);
+  DevInfo& d = g_dev[dev];
+  if (!d.init) {
+    PAGER_CUDA(cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev), "sm count");
+    void* p = nullptr;
+    PAGER_CUDA(cudaGetSymbolAddress(&p, g_status), "status symbol");
+    d.status = static_cast<int*>(p);
+    d.init = true;
+  }
+  *out = &d;
+  return PAGER_OK;
+}
+
+// Resident CTAs per SM for a split kernel (sets its dynamic smem limit once per device).
+int ctas_per_sm(const SplitKernelInfo& k, int* out) {
+  int dev = 0;
+  PAGER_CUDA(cudaGetDevice(&dev), "cudaGetDevice");
+  const void* key = reinterpret_cast<const char*>(k.fn) + dev;  // per (kernel, device)
+  {
+    std::lock_guard<std::mutex> lk(g_mu);
+    auto it = g_occupancy.find(key);
+    if (it != g_occupancy.end()) {
+      *out = it->second;
+      return PAGER_OK;
+    }
+  }
+  PAGER_CUDA(cudaFuncSetAttribute(k.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, k.smem_bytes),
+             "cudaFuncSetAttribute(max dynamic smem)");
+  int n = 0;
+  PAGER_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k.fn, kThreads, k.smem_bytes), "occupancy");
+  if (n < 1) n = 1;
+  std::lock_guard<std::mutex> lk(g_mu);
+  g_occupancy[key] = n;
+  *out = n;
+  return PAGER_OK;
+}
+
+struct Plan {
+  int tiles_per_split;
+  int max_splits;
+};
+
+// Split each (row, kv head) unit's tiles so that the grid fills the GPU in a
+// few whole waves, with at least a handful of tiles per CTA.
+Plan plan_splits(long long units, int tiles_per_unit, int sms, int per_sm) {
+  Plan p{1, 1};
+  if (tiles_per_unit <= 0 || units <= 0) return p;
+  const long long capacity = (long long)sms * per_sm;
+  const long long total = units * tiles_per_unit;
+  long long waves = total / (capacity * 16);
+  if (waves < 1) waves = 1;
+  if (waves > 8) waves = 8;
+  long long nsplit = (waves * capacity + units - 1) / units;
+  if (nsplit < 1) nsplit = 1;
+  if (nsplit > tiles_per_unit) nsplit = tiles_per_unit;
+  if (nsplit > kMaxSplits) nsplit = kMaxSplits;
+  int tps = (int)((tiles_per_unit + nsplit - 1) / nsplit);
+  if (tps < 1) tps = 1;
+  p.tiles_per_split = tps;
+  p.max_splits = (tiles_per_unit + tps - 1) / tps;
+  return p;
+}
+
+int dtype_size(int dt) { return dt == PAGER_DTYPE_F32 ? 4 : 2; }
+bool dtype_ok(int dt) { return dt == PAGER_DTYPE_F32 || dt == PAGER_DTYPE_F16 || dt == PAGER_DTYPE_BF16; }
+bool head_dim_ok(int d) { return d == 8 || d == 16 || d == 32 || d == 64 || d == 128 || d == 256; }
+int ilog2(int x) {
+  int r = 0;
+  while ((1 << r) < x) ++r;
+  return r;
+}
+bool is_pow2(int x) { return x > 0 && (x & (x - 1)) == 0; }
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+int get_encoder(EncodeTiledFn* out) {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  static cudaError_t err = cudaSuccess;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    err = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q);
+    if (err == cudaSuccess && q == cudaDriverEntryPointSuccess) fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  if (!fn) return fail(PAGER_ERR_CUDA, "cuTensorMapEncodeTiled entry point unavailable (%s)", cudaGetErrorString(err));
+  *out = fn;
+  return PAGER_OK;
+}
+
+// 3D view [d2][d1][d0] of 16-bit / 32-bit rows, box = one panel x `box_rows` rows x 1.
+int encode_3d(CUtensorMap* map, int kv_dtype, const void* base, uint64_t d0, uint64_t d1, uint64_t d2,
+              uint32_t box0, uint32_t box_rows, int panel_bytes) {
+  EncodeTiledFn enc;
+  int rc = get_encoder(&enc);
+  if (rc) return rc;
+  const uint64_t row_bytes = d0 * dtype_size(kv_dtype);
+  cuuint64_t dims[3] = {d0, d1, d2};
+  cuuint64_t strides[2] = {row_bytes, row_bytes * d1};
+  cuuint32_t box[3] = {box0, box_rows, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUtensorMapDataType dt = kv_dtype == PAGER_DTYPE_F32   ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                           : kv_dtype == PAGER_DTYPE_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                                         : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  CUtensorMapSwizzle sw = panel_bytes == 128  ? CU_TENSOR_MAP_SWIZZLE_128B
+                          : panel_bytes == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
+                          : panel_bytes == 32 ? CU_TENSOR_MAP_SWIZZLE_32B
+                                              : CU_TENSOR_MAP_SWIZZLE_NONE;
+  CUresult r = enc(map, dt, 3, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(PAGER_ERR_INVALID, "cuTensorMapEncodeTiled failed (%d) for dims %llu x %llu x %llu", (int)r,
+                (unsigned long long)d0, (unsigned long long)d1, (unsigned long long)d2);
+  return PAGER_OK;
+}
+
+// ------------------------------------------------------------------ small kernels
+struct CombineParams {
+  int num_q_heads, head_dim;
+  int tile_shift, tiles_per_split, max_splits;
+  GeomArgs geom;
+  const int* active;
+  const float* part_m;
+  const float* part_l;
+  const float* part_acc;
+  int op;  // 0 merge into (m,l,acc); 1 merge into (m,l); 2 acc += sum; 3 paged final -> out
+  float* m;
+  float* l;
+  float* acc;
+  void* out;
+  int out_dtype;
+  float* m_final;
+  float* l_final;
+};
+
+enum { OP_STEP = 0, OP_STATS = 1, OP_FIXED = 2, OP_PAGED = 3 };
+
+__global__ void __launch_bounds__(128) combine_kernel(const CombineParams c) {
+  __shared__ float w_s[kMaxSplits];
+  __shared__ float sh_L;
+  __shared__ float sh_M;
+  __shared__ float sh_win;
+  const int row = blockIdx.x;
+  const int b = row / c.num_q_heads;
+  if (c.active && c.active[b] == 0) return;
+  int t_begin, t_end, nsplit;
+  geom_tiles(row_geom(c.geom, b), c.tile_shift, c.tiles_per_split, t_begin, t_end, nsplit);
+  const int D = c.head_dim;
+  const long long pbase = (long long)row * c.max_splits;
+  if (c.op == OP_FIXED) {
+    for (int d = threadIdx.x; d < D; d += blockDim.x) {
+      float a = c.acc[(long long)row * D + d];
+      for (int s = 0; s < nsplit; ++s) a += c.part_acc[(pbase + s) * D + d];
+      c.acc[(long long)row * D + d] = a;
+    }
+    return;
+  }
+  if (threadIdx.x == 0) {
+    float M = neg_inf();
+    for (int s = 0; s < nsplit; ++s) M = fmaxf(M, c.part_m[pbase + s]);
+    const float m_in = c.op == OP_PAGED ? neg_inf() : c.m[row];
+    const float Mt = fmaxf(M, m_in);
+    // reference guard (streaming_attention.py:171-172): nothing valid yet -> alpha = 0
+    float w_in = 0.f;
+    if (c.op != OP_PAGED && Mt != neg_inf()) w_in = (m_in == Mt) ? 1.f : exp2f((m_in - Mt) * kLog2e);
+    float L = c.op == OP_PAGED ? 0.f : c.l[row] * w_in;
+    for (int s = 0; s < nsplit; ++s) {
+      const float ms = c.part_m[pbase + s];
+      const float ws = ms == neg_inf() ? 0.f : (ms == Mt ? 1.f : exp2f((ms - Mt) * kLog2e));
+      w_s[s] = ws;
+      L += ws * c.part_l[pbase + s];
+    }
+    sh_L = L;
+    sh_M = Mt;
+    sh_win = w_in;
+  }
+  __syncthreads();
+  const float L = sh_L;
+  if (c.op == OP_STEP || c.op == OP_PAGED) {
+    for (int d = threadIdx.x; d < D; d += blockDim.x) {
+      float a = c.op == OP_PAGED ? 0.f : c.acc[(long long)row * D + d] * sh_win;
+      for (int s = 0; s < nsplit; ++s) a += w_s[s] * c.part_acc[(pbase + s) * D + d];
+      if (c.op == OP_STEP)
+        c.acc[(long long)row * D + d] = a;
+      else
+        store_any(c.out, (long long)row * D + d, c.out_dtype, a / L);
+    }
+  }
+  if (threadIdx.x == 0) {
+    if (c.op == OP_PAGED) {
+      c.m_final[row] = sh_M;
+      c.l_final[row] = L;
+    } else {
+      c.m[row] = sh_M;
+      c.l[row] = L;
+    }
+  }
+}
+
+// accumulate_step: block_mass[b, h, off + j] = sum_{groups of local block j} p / l.
+__global__ void chunk_mass_kernel(const float2* mass_part, int gstride, int group_tokens, int tpb, int tokens,
+                                  const float* l, const int* active, int num_q_heads, float* block_mass,
+                                  int max_blocks, int block_id_offset) {
+  const int row = blockIdx.y;
+  const int b = row / num_q_heads;
+  if (active && active[b] == 0) return;
+  const int nloc = (tokens + tpb - 1) / tpb;
+  const int j = blockIdx.x * blockDim.x + threadIdx.x;
+  if (j >= nloc) return;
+  const int gpb = tpb / group_tokens;
+  const int g0 = j * gpb;
+  const int g1 = min(g0 + gpb, gstride);
+  float s = 0.f;
+  for (int gi = g0; gi < g1; ++gi) s += mass_part[(long long)row * gstride + gi].x;
+  const int col = block_id_offset + j;
+  if (col < max_blocks) block_mass[(long long)row * max_blocks + col] = s / l[row];
+}
+
+struct PagedMassParams {
+  const float2* mass_part;
+  int gstride, group_shift, tile_shift, tpb, tiles_per_split;
+  GeomArgs geom;
+  const int* active;
+  const float* m_final;
+  const float* l_final;
+  int batch, num_q_heads, max_blocks;
+  float* block_mass;  // [B, Hq, max_blocks] or null
+  float* mass_accum;
+  int mass_mode;
+};
+
+__device__ float paged_block_head_mass(const PagedMassParams& p, int b, int r, int j, int t_begin, int t_end) {
+  const long long row = (long long)b * p.num_q_heads + r;
+  const float mf = p.m_final[row];
+  const float lf = p.l_final[row];
+  const int gpb = p.tpb >> p.group_shift;
+  float s = 0.f;
+  for (int gi = j * gpb; gi < (j + 1) * gpb; ++gi) {
+    const int tile = (gi << p.group_shift) >> p.tile_shift;
+    if (tile < t_begin || tile >= t_end) continue;  // never loaded: outside the attended range
+    const float2 v = p.mass_part[row * p.gstride + gi];
+    if (v.x != 0.f) s += v.x * exp2f((v.y - mf) * kLog2e);
+  }
+  return s / lf;
+}
+
+__global__ void paged_mass_kernel(const PagedMassParams p) {
+  const int j = blockIdx.x * blockDim.x + threadIdx.x;
+  if (j >= p.max_blocks) return;
+  if (p.mass_mode == PAGER_MASS_BATCH_MEAN) {
+    float tot = 0.f;
+    for (int b = 0; b < p.batch; ++b) {
+      if (p.active && p.active[b] == 0) continue;
+      const RowGeom g = row_geom(p.geom, b);
+      if (j >= g.nb) continue;
+      int tb, te, ns;
+      geom_tiles(g, p.tile_shift, p.tiles_per_split, tb, te, ns);
+      for (int r = 0; r < p.num_q_heads; ++r) {
+        const float v = paged_block_head_mass(p, b, r, j, tb, te);
+        if (p.block_mass) p.block_mass[((long long)b * p.num_q_heads + r) * p.max_blocks + j] = v;
+        tot += v;
+      }
+    }
+    p.mass_accum[j] += tot / (float)(p.batch * p.num_q_heads);
+    return;
+  }
+  const int b = blockIdx.y;
+  if (p.active && p.active[b] == 0) return;
+  const RowGeom g = row_geom(p.geom, b);
+  if (j >= g.nb) return;
+  int tb, te, ns;
+  geom_tiles(g, p.tile_shift, p.tiles_per_split, tb, te, ns);
+  float tot = 0.f;
+  for (int r = 0; r < p.num_q_heads; ++r) {
+    const float v = paged_block_head_mass(p, b, r, j, tb, te);
+    if (p.block_mass) p.block_mass[((long long)b * p.num_q_heads + r) * p.max_blocks + j] = v;
+    tot += v;
+  }
+  if (p.mass_mode == PAGER_MASS_ROW_MEAN) p.mass_accum[(long long)b * p.max_blocks + j] += tot / (float)p.num_q_heads;
+}
+
+__global__ void finalize_kernel(const float* acc, const float* l, void* out, int out_dtype, long long n, int head_dim) {
+  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  store_any(out, i, out_dtype, acc[i] / l[i / head_dim]);
+}
+
+__global__ void state_init_kernel(float* m, float* l, float* acc, long long rows, int head_dim) {
+  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < rows) {
+    m[i] = neg_inf();
+    l[i] = 0.f;
+  }
+  if (i < rows * head_dim) acc[i] = 0.f;
+}
+
+__global__ void zero_copy_probe_kernel(const uint4* __restrict__ src, uint4* __restrict__ dst, long long n16) {
+  const long long stride = (long long)gridDim.x * blockDim.x;
+  long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  for (; i + 3 * stride < n16; i += 4 * stride) {
+    const uint4 a = ld_global_16(src + i);
+    const uint4 b2 = ld_global_16(src + i + stride);
+    const uint4 c = ld_global_16(src + i + 2 * stride);
+    const uint4 d = ld_global_16(src + i + 3 * stride);
+    dst[i] = a;
+    dst[i + stride] = b2;
+    dst[i + 2 * stride] = c;
+    dst[i + 3 * stride] = d;
+  }
+  for (; i < n16; i += stride) dst[i] = ld_global_16(src + i);
+}
+
+// ------------------------------------------------------------------ scratch layout
+struct Scratch {
+  float* part_m;
+  float* part_l;
+  float* part_acc;
+  float2* mass_part;
+  float* m_final;
+  float* l_final;
+  size_t bytes;
+};
+
+size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
+Scratch layout_scratch(char* base, long long rows, int max_splits, int head_dim, long long mass_groups,
+                       bool finals) {
+  Scratch s;
+  size_t off = 0;
+  auto take = [&](size_t n) {
+    char* p = base ? base + off : nullptr;
+    off += align256(n);
+    return p;
+  };
+  s.part_m = reinterpret_cast<float*>(take(sizeof(float) * rows * max_splits));
+  s.part_l = reinterpret_cast<float*>(take(sizeof(float) * rows * max_splits));
+  s.part_acc = reinterpret_cast<float*>(take(sizeof(float) * rows * max_splits * head_dim));
+  s.mass_part = reinterpret_cast<float2*>(take(sizeof(float2) * rows * (mass_groups > 0 ? mass_groups : 0)));
+  s.m_final = reinterpret_cast<float*>(take(finals ? sizeof(float) * rows : 0));
+  s.l_final = reinterpret_cast<float*>(take(finals ? sizeof(float) * rows : 0));
+  s.bytes = off;
+  return s;
+}
+
+int backend_for(int requested, int kv_dtype, int head_dim) {
+  if (requested == PAGER_BACKEND_MMA || requested == PAGER_BACKEND_FMA) return requested;
+  if (kv_dtype != PAGER_DTYPE_F32 && (head_dim == 64 || head_dim == 128)) return PAGER_BACKEND_MMA;
+  return PAGER_BACKEND_FMA;
+}
+
+int check_geometry(int batch, int hq, int hkv, int head_dim, int kv_dtype, int q_dtype) {
+  if (batch < 0 || hq <= 0 || hkv <= 0) return fail(PAGER_ERR_INVALID, "bad shape: batch=%d heads=%d kv_heads=%d", batch, hq, hkv);
+  if (hq % hkv) return fail(PAGER_ERR_INVALID, "num_query_heads (%d) is not a multiple of num_kv_heads (%d)", hq, hkv);
+  const int n_rep = hq / hkv;
+  if (n_rep > kMaxRep)
+    return fail(PAGER_ERR_UNSUPPORTED,
+                "streaming attention's GQA query-head packing supports n_rep up to %d, got %d. This architecture's "
+                "query/KV head ratio is wider than any currently supported model.",
+                kMaxRep, n_rep);
+  if (!head_dim_ok(head_dim)) return fail(PAGER_ERR_UNSUPPORTED, "head_dim %d not supported (8..256, power of two)", head_dim);
+  if (!dtype_ok(kv_dtype) || !dtype_ok(q_dtype)) return fail(PAGER_ERR_INVALID, "unknown dtype code");
+  return PAGER_OK;
+}
+
+struct ChunkArgs {
+  int op;  // 0 step, 1 stats, 2 accumulate, 3 fold_fixed
+  const void* q;
+  int q_dtype;
+  const void* k;
+  const void* v;
+  int kv_dtype;
+  const int32_t* valid;
+  const int32_t* active;
+  float* m;
+  float* l;
+  float* acc;
+  float* block_mass;
+  int max_blocks, block_id_offset, tokens_per_block;
+  int batch, hq, hkv, tokens, head_dim;
+  float scale, softcap;
+  int backend;
+  void* scratch;
+  size_t scratch_bytes;
+  cudaStream_t stream;
+};
+
+int chunk_plan(const ChunkArgs& a, SplitKernelInfo* k, Plan* plan, long long* mass_groups, int* group_tokens) {
+  const int mode = a.op == 0 ? MODE_ONLINE : (a.op == 1 ? MODE_STATS : MODE_FIXED);
+  const int be = backend_for(a.backend, a.kv_dtype, a.head_dim);
+  if (!lookup_split_kernel(a.kv_dtype, a.head_dim, mode, be, k))
+    return fail(PAGER_ERR_UNSUPPORTED, "no split kernel for dtype %d head_dim %d backend %d", a.kv_dtype, a.head_dim, be);
+  DevInfo* di;
+  int rc = device_info(&di);
+  if (rc) return rc;
+  int per_sm = 1;
+  rc = ctas_per_sm(*k, &per_sm);
+  if (rc) return rc;
+  const int tiles = (a.tokens + k->tile - 1) / k->tile;
+  *plan = plan_splits((long long)a.batch * a.hkv, tiles, di->sms, per_sm);
+  *group_tokens = 0;
+  *mass_groups = 0;
+  if (a.op == 2) {
+    *group_tokens = a.tokens_per_block < k->tile ? a.tokens_per_block : k->tile;
+    *mass_groups = (long long)tiles * k->tile / *group_tokens;
+  }
+  return PAGER_OK;
+}
+
+int run_chunk(const ChunkArgs& a) {
+  int rc = check_geometry(a.batch, a.hq, a.hkv, a.head_dim, a.kv_dtype, a.q_dtype);
+  if (rc) return rc;
+  if (a.tokens < 0) return fail(PAGER_ERR_INVALID, "negative token count");
+  if (a.batch == 0 || a.tokens == 0) return PAGER_OK;  // nothing to fold (the reference loop runs zero times)
+  if (!a.q || !a.k || (a.op != 1 && !a.v) || !a.m || !a.l || (a.op != 1 && !a.acc))
+    return fail(PAGER_ERR_INVALID, "null tensor pointer");
+  if (!aligned16(a.k) || (a.op != 1 && !aligned16(a.v)))
+    return fail(PAGER_ERR_INVALID, "k/v must be 16-byte aligned");
+  if (a.op == 2) {
+    if (!a.block_mass) return fail(PAGER_ERR_INVALID, "block_mass is null");
+    if (!is_pow2(a.tokens_per_block) || a.tokens_per_block < 8)
+      return fail(PAGER_ERR_UNSUPPORTED, "tokens_per_block must be a power of two >= 8, got %d", a.tokens_per_block);
+    const int nloc = (a.tokens + a.tokens_per_block - 1) / a.tokens_per_block;
+    if (a.block_id_offset < 0 || a.block_id_offset + nloc > a.max_blocks)
+      return fail(PAGER_ERR_INVALID, "block_mass has %d blocks; offset %d + %d local blocks overflows it", a.max_blocks,
+                  a.block_id_offset, nloc);
+  }
+  SplitKernelInfo k;
+  Plan plan;
+  long long mass_groups;
+  int G;
+  rc = chunk_plan(a, &k, &plan, &mass_groups, &G);
+  if (rc) return rc;
+  const long long rows = (long long)a.batch * a.hq;
+  Scratch sc = layout_scratch(static_cast<char*>(a.scratch), rows, plan.max_splits, a.head_dim, mass_groups, false);
+  if (!a.scratch || a.scratch_bytes < sc.bytes)
+    return fail(PAGER_ERR_SCRATCH, "scratch too small: need %zu bytes, got %zu", sc.bytes, a.scratch_bytes);
+  DevInfo* di;
+  rc = device_info(&di);
+  if (rc) return rc;
+
+  CUtensorMap mk, mv;
+  memset(&mk, 0, sizeof(mk));
+  memset(&mv, 0, sizeof(mv));
+  const uint64_t z = (uint64_t)a.batch * a.hkv;
+  rc = encode_3d(&mk, a.kv_dtype, a.k, a.head_dim, a.tokens, z, k.panel_elts, k.tile, k.panel_bytes);
+  if (rc) return rc;
+  if (a.op != 1) {
+    rc = encode_3d(&mv, a.kv_dtype, a.v, a.head_dim, a.tokens, z, k.panel_elts, k.tile, k.panel_bytes);
+    if (rc) return rc;
+  }
+  SplitParams p;
+  memset(&p, 0, sizeof(p));
+  p.q = a.q;
+  p.q_dtype = a.q_dtype;
+  p.batch = a.batch;
+  p.num_q_heads = a.hq;
+  p.num_kv_heads = a.hkv;
+  p.n_rep = a.hq / a.hkv;
+  p.scale = a.scale;
+  p.softcap = a.softcap > 0.f ? a.softcap : 0.f;
+  p.source = SRC_CONTIG;
+  p.geom.source = SRC_CONTIG;
+  p.geom.tokens = a.tokens;
+  p.geom.max_tokens = a.tokens;
+  p.valid = a.valid;
+  p.valid_stride = a.tokens;
+  p.active = (a.op == 3) ? nullptr : a.active;
+  p.m_fixed = a.m;
+  p.l_fixed = a.l;
+  p.tiles_per_split = plan.tiles_per_split;
+  p.max_splits = plan.max_splits;
+  p.part_m = sc.part_m;
+  p.part_l = sc.part_l;
+  p.part_acc = sc.part_acc;
+  p.mass_part = sc.mass_part;
+  p.mass_gstride = (int)mass_groups;
+  p.group_tokens = G;
+  p.log2_group = G ? ilog2(G) : 0;
+  p.wait_limit_ns = kWaitLimitNs;
+  p.status = di->status;
+
+  dim3 grid(plan.max_splits, a.hkv, a.batch);
+  void* args[] = {&p, &mk, &mv};
+  PAGER_CUDA(cudaLaunchKernel(k.fn, grid, dim3(kThreads), args, k.smem_bytes, a.stream), "split kernel launch");
+
+  CombineParams c;
+  memset(&c, 0, sizeof(c));
+  c.num_q_heads = a.hq;
+  c.head_dim = a.head_dim;
+  c.tile_shift = ilog2(k.tile);
+  c.tiles_per_split = plan.tiles_per_split;
+  c.max_splits = plan.max_splits;
+  c.geom = p.geom;
+  c.active = p.active;
+  c.part_m = sc.part_m;
+  c.part_l = sc.part_l;
+  c.part_acc = sc.part_acc;
+  c.op = a.op == 0 ? OP_STEP : (a.op == 1 ? OP_STATS : OP_FIXED);
+  c.m = a.m;
+  c.l = a.l;
+  c.acc = a.acc;
+  combine_kernel<<<(unsigned)rows, 128, 0, a.stream>>>(c);
+  PAGER_CUDA(cudaGetLastError(), "combine launch");
+  if (a.op == 2) {
+    const int nloc = (a.tokens + a.tokens_per_block - 1) / a.tokens_per_block;
+    dim3 g2((nloc + 127) / 128, (unsigned)rows);
+    chunk_mass_kernel<<<g2, 128, 0, a.stream>>>(sc.mass_part, (int)mass_groups, G, a.tokens_per_block, a.tokens, a.l,
+                                                 a.active, a.hq, a.block_mass, a.max_blocks, a.block_id_offset);
+    PAGER_CUDA(cudaGetLastError(), "mass launch");
+  }
+  return PAGER_OK;
+}
+
+size_t chunk_scratch(const ChunkArgs& a) {
+  if (check_geometry(a.batch, a.hq, a.hkv, a.head_dim, a.kv_dtype, a.q_dtype)) return 0;
+  if (a.batch <= 0 || a.tokens <= 0) return 0;
+  SplitKernelInfo k;
+  Plan plan;
+  long long mass_groups;
+  int G;
+  if (chunk_plan(a, &k, &plan, &mass_groups, &G)) return 0;
+  return layout_scratch(nullptr, (long long)a.batch * a.hq, plan.max_splits, a.head_dim, mass_groups, false).bytes;
+}
+
+struct PagedPlan {
+  SplitKernelInfo k;
+  Plan plan;
+  int G;
+  long long gstride;
+};
+
+int paged_plan(int batch, int hq, int hkv, int head_dim, int kv_dtype, int tpb, int max_row_tokens, int backend,
+               PagedPlan* out) {
+  const int be = backend_for(backend, kv_dtype, head_dim);
+  if (!lookup_split_kernel(kv_dtype, head_dim, MODE_ONLINE, be, &out->k))
+    return fail(PAGER_ERR_UNSUPPORTED, "no split kernel for dtype %d head_dim %d backend %d", kv_dtype, head_dim, be);
+  DevInfo* di;
+  int rc = device_info(&di);
+  if (rc) return rc;
+  int per_sm = 1;
+  rc = ctas_per_sm(out->k, &per_sm);
+  if (rc) return rc;
+  const int tiles = (max_row_tokens + out->k.tile - 1) / out->k.tile;
+  out->plan = plan_splits((long long)batch * hkv, tiles, di->sms, per_sm);
+  out->G = tpb < out->k.tile ? tpb : out->k.tile;
+  out->gstride = (long long)tiles * out->k.tile / out->G;
+  return PAGER_OK;
+}
+
+}  // namespace
+}  // namespace pager
+
+using namespace pager;
+
+extern "C" {
+
+const char* pager_last_error(void) { return t_err.c_str(); }
+
+int pager_version(void) { return 1; }
+
+int pager_device_status(int device, int* status_out) {
+  if (!status_out) return fail(PAGER_ERR_INVALID, "status_out is null");
+  int prev = 0;
+  PAGER_CUDA(cudaGetDevice(&prev), "cudaGetDevice");
+  PAGER_CUDA(cudaSetDevice(device), "cudaSetDevice");
+  int v = 0, zero = 0;
+  cudaError_t e = cudaMemcpyFromSymbol(&v, g_status, sizeof(int));
+  if (e == cudaSuccess) e = cudaMemcpyToSymbol(g_status, &zero, sizeof(int));
+  cudaSetDevice(prev);
+  if (e != cudaSuccess) return cuda_fail(e, "status read");
+  *status_out = v;
+  return PAGER_OK;
+}
+
+int pager_attn_state_init(float* m, float* l, float* acc, int64_t rows, int head_dim, void* stream) {
+  if (rows < 0 || head_dim <= 0) return fail(PAGER_ERR_INVALID, "bad shape");
+  if (rows == 0) return PAGER_OK;
+  const long long n = rows * head_dim;
+  state_init_kernel<<<(unsigned)((n + 255) / 256), 256, 0, (cudaStream_t)stream>>>(m, l, acc, rows, head_dim);
+  PAGER_CUDA(cudaGetLastError(), "state_init launch");
+  return PAGER_OK;
+}
+
+int pager_attn_finalize(const float* acc, const float* l, void* out, int out_dtype, int64_t rows, int head_dim,
+                        void* stream) {
+  if (rows < 0 || head_dim <= 0 || !dtype_ok(out_dtype)) return fail(PAGER_ERR_INVALID, "bad finalize arguments");
+  if (rows == 0) return PAGER_OK;
+  const long long n = rows * head_dim;
+  finalize_kernel<<<(unsigned)((n + 255) / 256), 256, 0, (cudaStream_t)stream>>>(acc, l, out, out_dtype, n, head_dim);
+  PAGER_CUDA(cudaGetLastError(), "finalize launch");
+  return PAGER_OK;
+}
+
+size_t pager_attn_chunk_scratch_bytes(int op, int batch, int num_q_heads, int num_kv_heads, int tokens, int head_dim,
+                                      int kv_dtype, int tokens_per_block) {
+  ChunkArgs a;
+  memset(&a, 0, sizeof(a));
+  a.op = op;
+  a.q_dtype = kv_dtype;
+  a.kv_dtype = kv_dtype;
+  a.batch = batch;
+  a.hq = num_q_heads;
+  a.hkv = num_kv_heads;
+  a.tokens = tokens;
+  a.head_dim = head_dim;
+  a.tokens_per_block = tokens_per_block > 0 ? tokens_per_block : 16;
+  a.backend = PAGER_BACKEND_AUTO;
+  return chunk_scratch(a);
+}
+
+#define CHUNK_COMMON                                                                                     \
+  a.q = q;                                                                                               \
+  a.q_dtype = q_dtype;                                                                                   \
+  a.kv_dtype = kv_dtype;                                                                                 \
+  a.batch = batch;                                                                                       \
+  a.hq = num_q_heads;                                                                                    \
+  a.hkv = num_kv_heads;                                                                                  \
+  a.tokens = tokens;                                                                                     \
+  a.head_dim = head_dim;                                                                                 \
+  a.scale = scale;                                                                                       \
+  a.softcap = softcap;                                                                                   \
+  a.backend = backend;                                                                                   \
+  a.scratch = scratch;                                                                                   \
+  a.scratch_bytes = scratch_bytes;                                                                       \
+  a.stream = (cudaStream_t)stream;
+
+int pager_attn_step(const void* q, int q_dtype, const void* k, const void* v, int kv_dtype, const int32_t* valid,
+                    const int32_t* active, float* m, float* l, float* acc, int batch, int num_q_heads,
+                    int num_kv_heads, int tokens, int head_dim, float scale, float softcap, int backend,
+                    void* scratch, size_t scratch_bytes, void* stream) {
+  ChunkArgs a;
+  memset(&a, 0, sizeof(a));
+  CHUNK_COMMON
+  a.op = 0;
+  a.k = k;
+  a.v = v;
+  a.valid = valid;
+  a.active = active;
+  a.m = m;
+  a.l = l;
+  a.acc = acc;
+  return run_chunk(a);
+}
+
+int pager_attn_stats_step(const void* q, int q_dtype, const void* k, int kv_dtype, const int32_t* valid,
+                          const int32_t* active, float* m, float* l, int batch, int num_q_heads, int num_kv_heads,
+                          int tokens, int head_dim, float scale, float softcap, int backend, void* scratch,
+                          size_t scratch_bytes, void* stream) {
+  ChunkArgs a;
+  memset(&a, 0, sizeof(a));
+  CHUNK_COMMON
+  a.op = 1;
+  a.k = k;
+  a.valid = valid;
+  a.active = active;
+  a.m = m;
+  a.l = l;
+  return run_chunk(a);
+}
+
+int pager_attn_accumulate_step(const void* q, int q_dtype, const void* k, const void* v, int kv_dtype,
+                               const int32_t* valid, const int32_t* active, const float* m, const float* l,
+                               float* acc, float* block_mass, int max_blocks, int block_id_offset,
+                               int tokens_per_block, int batch, int num_q_heads, int num_kv_heads, int tokens,
+                               int head_dim, float scale, float softcap, int backend, void* scratch,
+                               size_t scratch_bytes, void* stream) {
+  ChunkArgs a;
+  memset(&a, 0, sizeof(a));
+  CHUNK_COMMON
+  a.op = 2;
+  a.k = k;
+  a.v = v;
+  a.valid = valid;
+  a.active = active;
+  a.m = const_cast<float*>(m);
+  a.l = const_cast<float*>(l);
+  a.acc = acc;
+  a.block_mass = block_mass;
+  a.max_blocks = max_blocks;
+  a.block_id_offset = block_id_offset;
+  a.tokens_per_block = tokens_per_block;
+  return run_chunk(a);
+}
+
+int pager_attn_fold_fixed_step(const void* q, int q_dtype, const void* k, const void* v, int kv_dtype,
+                               const int32_t* valid, const float* m, const float* l, float* acc, int batch,
+                               int num_q_heads, int num_kv_heads, int tokens, int head_dim, float scale,
+                               float softcap, int backend, void* scratch, size_t scratch_bytes, void* stream) {
+  ChunkArgs a;
+  memset(&a, 0, sizeof(a));
+  CHUNK_COMMON
+  a.op = 3;
+  a.k = k;
+  a.v = v;
+  a.valid = valid;
+  a.m = const_cast<float*>(m);
+  a.l = const_cast<float*>(l);
+  a.acc = acc;
+  return run_chunk(a);
+}
+
+size_t pager_paged_decode_scratch_bytes(int batch, int num_q_heads, int num_kv_heads, int head_dim, int kv_dtype,
+                                        int tokens_per_block, int max_blocks, int max_row_tokens) {
+  (void)max_blocks;
+  if (check_geometry(batch, num_q_heads, num_kv_heads, head_dim, kv_dtype, kv_dtype)) return 0;
+  if (batch <= 0 || max_row_tokens <= 0 || !is_pow2(tokens_per_block) || tokens_per_block < 8) return 0;
+  PagedPlan pp;
+  if (paged_plan(batch, num_q_heads, num_kv_heads, head_dim, kv_dtype, tokens_per_block, max_row_tokens,
+                 PAGER_BACKEND_AUTO, &pp))
+    return 0;
+  PagedPlan pf;  // the FMA backend may plan differently; size for the larger of the two
+  size_t extra = 0;
+  if (!paged_plan(batch, num_q_heads, num_kv_heads, head_dim, kv_dtype, tokens_per_block, max_row_tokens,
+                  PAGER_BACKEND_FMA, &pf))
+    extra = layout_scratch(nullptr, (long long)batch * num_q_heads, pf.plan.max_splits, head_dim, pf.gstride, true).bytes;
+  const size_t base =
+      layout_scratch(nullptr, (long long)batch * num_q_heads, pp.plan.max_splits, head_dim, pp.gstride, true).bytes;
+  return base > extra ? base : extra;
+}
+
+int pager_paged_decode_attention(const void* q, int q_dtype, const void* dev_pool, int dev_slots,
+                                 const void* host_pool, int host_slots, int kv_dtype, int num_layers, int layer,
+                                 int num_kv_heads, int tokens_per_block, int head_dim, const int32_t* block_table,
+                                 int max_blocks, const int32_t* num_blocks, const void* tail_k, const void* tail_v,
+                                 const int32_t* tail_len, int tail_cap, const int32_t* valid_lo,
+                                 const int32_t* valid_hi, const int32_t* active, int batch, int num_q_heads,
+                                 float scale, float softcap, int max_row_tokens, void* out, int out_dtype,
+                                 float* block_mass, float* mass_accum, int mass_mode, int backend, void* scratch,
+                                 size_t scratch_bytes, void* stream) {
+  int rc = check_geometry(batch, num_q_heads, num_kv_heads, head_dim, kv_dtype, q_dtype);
+  if (rc) return rc;
+  if (batch == 0) return PAGER_OK;
+  if (!dtype_ok(out_dtype)) return fail(PAGER_ERR_INVALID, "bad out dtype");
+  if (!is_pow2(tokens_per_block) || tokens_per_block < 8)
+    return fail(PAGER_ERR_UNSUPPORTED, "tokens_per_block must be a power of two >= 8, got %d", tokens_per_block);
+  if (num_layers <= 0 || layer < 0 || layer >= num_layers)
+    return fail(PAGER_ERR_INVALID, "layer %d out of range for %d layers", layer, num_layers);
+  if (!q || !out || !num_blocks || max_blocks < 0 || (max_blocks > 0 && !block_table))
+    return fail(PAGER_ERR_INVALID, "null tensor pointer");
+  if (max_row_tokens <= 0) return fail(PAGER_ERR_INVALID, "max_row_tokens must be positive");
+  if (tail_len && (!tail_k || !tail_v || tail_cap <= 0)) return fail(PAGER_ERR_INVALID, "tail tensors missing");
+  if ((dev_pool && !aligned16(dev_pool)) || (host_pool && !aligned16(host_pool)) || (tail_k && !aligned16(tail_k)) ||
+      (tail_v && !aligned16(tail_v)))
+    return fail(PAGER_ERR_INVALID, "pools and tail tensors must be 16-byte aligned");
+  if (dev_slots < 0 || host_slots < 0) return fail(PAGER_ERR_INVALID, "negative pool capacity");
+  if ((long long)dev_slots * num_layers * 2 * num_kv_heads >= (1LL << 31) ||
+      (long long)host_slots * num_layers * 2 * num_kv_heads >= (1LL << 31))
+    return fail(PAGER_ERR_INVALID, "pool too large: slots * layers * 2 * kv_heads must stay below 2^31");
+  if (mass_mode != PAGER_MASS_NONE && mass_mode != PAGER_MASS_ROW_MEAN && mass_mode != PAGER_MASS_BATCH_MEAN)
+    return fail(PAGER_ERR_INVALID, "unknown mass mode %d", mass_mode);
+  if (mass_mode != PAGER_MASS_NONE && !mass_accum) return fail(PAGER_ERR_INVALID, "mass_accum is null");
+
+  PagedPlan pp;
+  rc = paged_plan(batch, num_q_heads, num_kv_heads, head_dim, kv_dtype, tokens_per_block, max_row_tokens, backend, &pp);
+  if (rc) return rc;
+  const long long rows = (long long)batch * num_q_heads;
+  Scratch sc = layout_scratch(static_cast<char*>(scratch), rows, pp.plan.max_splits, head_dim, pp.gstride, true);
+  if (!scratch || scratch_bytes < sc.bytes)
+    return fail(PAGER_ERR_SCRATCH, "scratch too small: need %zu bytes, got %zu", sc.bytes, scratch_bytes);
+  DevInfo* di;
+  rc = device_info(&di);
+  if (rc) return rc;
+
+  const long long row_bytes = (long long)head_dim * dtype_size(kv_dtype);
+  const long long layer_stride = 2LL * num_kv_heads * tokens_per_block * row_bytes;
+  CUtensorMap mk;
+  memset(&mk, 0, sizeof(mk));
+  if (dev_pool && dev_slots > 0) {
+    const uint64_t z = (uint64_t)dev_slots * num_layers * 2 * num_kv_heads;
+    const int br = tokens_per_block < pp.k.tile ? tokens_per_block : pp.k.tile;
+    rc = encode_3d(&mk, kv_dtype, dev_pool, head_dim, tokens_per_block, z, pp.k.panel_elts, br, pp.k.panel_bytes);
+    if (rc) return rc;
+  }
+  SplitParams p;
+  memset(&p, 0, sizeof(p));
+  p.q = q;
+  p.q_dtype = q_dtype;
+  p.batch = batch;
+  p.num_q_heads = num_q_heads;
+  p.num_kv_heads = num_kv_heads;
+  p.n_rep = num_q_heads / num_kv_heads;
+  p.scale = scale;
+  p.softcap = softcap > 0.f ? softcap : 0.f;
+  p.source = SRC_PAGED;
+  p.dev_pool = (dev_pool && dev_slots > 0) ? static_cast<const char*>(dev_pool) : nullptr;
+  p.host_pool = (host_pool && host_slots > 0) ? static_cast<const char*>(host_pool) : nullptr;
+  p.slot_stride_bytes = layer_stride * num_layers;
+  p.layer_stride_bytes = layer_stride;
+  p.num_layers = num_layers;
+  p.layer = layer;
+  p.tpb = tokens_per_block;
+  p.log2_tpb = ilog2(tokens_per_block);
+  p.dev_slots = dev_slots;
+  p.host_slots = host_slots;
+  p.block_table = block_table;
+  p.max_blocks = max_blocks;
+  p.tail_k = static_cast<const char*>(tail_k);
+  p.tail_v = static_cast<const char*>(tail_v);
+  p.tail_cap = tail_cap;
+  p.geom.source = SRC_PAGED;
+  p.geom.tpb = tokens_per_block;
+  p.geom.num_blocks = num_blocks;
+  p.geom.max_blocks = max_blocks;
+  p.geom.tail_len = tail_len;
+  p.geom.tail_cap = tail_len ? tail_cap : 0;
+  p.geom.max_tokens = max_row_tokens;
+  p.geom.valid_lo = valid_lo;
+  p.geom.valid_hi = valid_hi;
+  p.active = active;
+  p.tiles_per_split = pp.plan.tiles_per_split;
+  p.max_splits = pp.plan.max_splits;
+  p.part_m = sc.part_m;
+  p.part_l = sc.part_l;
+  p.part_acc = sc.part_acc;
+  p.mass_part = sc.mass_part;
+  p.mass_gstride = (int)pp.gstride;
+  p.group_tokens = pp.G;
+  p.log2_group = ilog2(pp.G);
+  p.wait_limit_ns = kWaitLimitNs;
+  p.status = di->status;
+
+  cudaStream_t st = (cudaStream_t)stream;
+  dim3 grid(pp.plan.max_splits, num_kv_heads, batch);
+  void* args[] = {&p, &mk, &mk};
+  PAGER_CUDA(cudaLaunchKernel(pp.k.fn, grid, dim3(kThreads), args, pp.k.smem_bytes, st), "split kernel launch");
+
+  CombineParams c;
+  memset(&c, 0, sizeof(c));
+  c.num_q_heads = num_q_heads;
+  c.head_dim = head_dim;
+  c.tile_shift = ilog2(pp.k.tile);
+  c.tiles_per_split = pp.plan.tiles_per_split;
+  c.max_splits = pp.plan.max_splits;
+  c.geom = p.geom;
+  c.active = active;
+  c.part_m = sc.part_m;
+  c.part_l = sc.part_l;
+  c.part_acc = sc.part_acc;
+  c.op = OP_PAGED;
+  c.out = out;
+  c.out_dtype = out_dtype;
+  c.m_final = sc.m_final;
+  c.l_final = sc.l_final;
+  combine_kernel<<<(unsigned)rows, 128, 0, st>>>(c);
+  PAGER_CUDA(cudaGetLastError(), "combine launch");
+
+  if ((block_mass || mass_mode != PAGER_MASS_NONE) && max_blocks > 0) {
+    PagedMassParams mp;
+    memset(&mp, 0, sizeof(mp));
+    mp.mass_part = sc.mass_part;
+    mp.gstride = (int)pp.gstride;
+    mp.group_shift = ilog2(pp.G);
+    mp.tile_shift = ilog2(pp.k.tile);
+    mp.tpb = tokens_per_block;
+    mp.tiles_per_split = pp.plan.tiles_per_split;
+    mp.geom = p.geom;
+    mp.active = active;
+    mp.m_final = sc.m_final;
+    mp.l_final = sc.l_final;
+    mp.batch = batch;
+    mp.num_q_heads = num_q_heads;
+    mp.max_blocks = max_blocks;
+    mp.block_mass = block_mass;
+    mp.mass_accum = mass_accum;
+    mp.mass_mode = mass_mode;
+    dim3 g2((max_blocks + 127) / 128, mass_mode == PAGER_MASS_BATCH_MEAN ? 1 : batch);
+    paged_mass_kernel<<<g2, 128, 0, st>>>(mp);
+    PAGER_CUDA(cudaGetLastError(), "mass launch");
+  }
+  return PAGER_OK;
+}
+
+int pager_host_pool_alloc(size_t bytes, void** host_ptr) {
+  if (!host_ptr) return fail(PAGER_ERR_INVALID, "host_ptr is null");
+  *host_ptr = nullptr;
+  if (bytes == 0) return PAGER_OK;
+  PAGER_CUDA(cudaHostAlloc(host_ptr, bytes, cudaHostAllocPortable | cudaHostAllocMapped), "cudaHostAlloc");
+  return PAGER_OK;
+}
+
+int pager_host_pool_free(void* host_ptr) {
+  if (!host_ptr) return PAGER_OK;
+  PAGER_CUDA(cudaFreeHost(host_ptr), "cudaFreeHost");
+  return PAGER_OK;
+}
+
+int pager_probe_h2d_copy_gbs(const void* host_src, void* dev_dst, size_t bytes, int iters, void* stream,
+                             double* gbs_out) {
+  if (!host_src || !dev_dst || !gbs_out || bytes == 0 || iters <= 0) return fail(PAGER_ERR_INVALID, "bad probe args");
+  cudaStream_t s = (cudaStream_t)stream;
+  cudaEvent_t e0, e1;
+  PAGER_CUDA(cudaEventCreate(&e0), "event");
+  PAGER_CUDA(cudaEventCreate(&e1), "event");
+  float best = 1e30f;
+  for (int i = 0; i <= iters; ++i) {
+    cudaEventRecord(e0, s);
+    cudaMemcpyAsync(dev_dst, host_src, bytes, cudaMemcpyHostToDevice, s);
+    cudaEventRecord(e1, s);
+    cudaError_t e = cudaEventSynchronize(e1);
+    if (e != cudaSuccess) {
+      cudaEventDestroy(e0);
+      cudaEventDestroy(e1);
+      return cuda_fail(e, "h2d probe");
+    }
+    float ms = 0.f;
+    cudaEventElapsedTime(&ms, e0, e1);
+    if (i > 0 && ms < best) best = ms;  // first copy is a warm-up
+  }
+  cudaEventDestroy(e0);
+  cudaEventDestroy(e1);
+  *gbs_out = (double)bytes / (best * 1e6);
+  return PAGER_OK;
+}
+
+int pager_probe_zero_copy_gbs(const void* host_src, void* dev_dst, size_t bytes, int iters, void* stream,
+                              double* gbs_out) {
+  if (!host_src || !dev_dst || !gbs_out || bytes < 16 || iters <= 0 || !aligned16(host_src) || !aligned16(dev_dst))
+    return fail(PAGER_ERR_INVALID, "bad probe args");
+  DevInfo* di;
+  int rc = device_info(&di);
+  if (rc) return rc;
+  cudaStream_t s = (cudaStream_t)stream;
+  cudaEvent_t e0, e1;
+  PAGER_CUDA(cudaEventCreate(&e0), "event");
+  PAGER_CUDA(cudaEventCreate(&e1), "event");
+  const long long n16 = (long long)(bytes / 16);
+  float best = 1e30f;
+  for (int i = 0; i <= iters; ++i) {
+    cudaEventRecord(e0, s);
+    zero_copy_probe_kernel<<<di->sms * 4, 256, 0, s>>>(static_cast<const uint4*>(host_src), static_cast<uint4*>(dev_dst), n16);
+    cudaEventRecord(e1, s);
+    cudaError_t e = cudaEventSynchronize(e1);
+    if (e != cudaSuccess) {
+      cudaEventDestroy(e0);
+      cudaEventDestroy(e1);
+      return cuda_fail(e, "zero-copy probe");
+    }
+    float ms = 0.f;
+    cudaEventElapsedTime(&ms, e0, e1);
+    if (i > 0 && ms < best) best = ms;
+  }
+  cudaEventDestroy(e0);
+  cudaEventDestroy(e1);
+  *gbs_out = (double)(n16 * 16) / (best * 1e6);
+  return PAGER_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,977 @@
+// Split-KV decode-attention kernel for sm_100a.
+//
+// One CTA = one work unit (batch row b, KV head h, split s): a contiguous run
+// of TILE-token tiles of row b.  Warp 4 is the producer: it streams K/V tiles
+// into a ring of shared-memory stages -- TMA tensor loads (128B-swizzled) for
+// HBM-resident data, 16-byte zero-copy loads for blocks in the pinned host
+// pool and for the tail -- signalling per-stage mbarriers.  Warps 0-3 are
+// consumers: tile i goes to warp i % 4, which folds it into its own online
+// softmax state (m, l, acc) for the n_rep query heads sharing KV head h.  At
+// the end the four warp states are merged and the split's partial state is
+// written to scratch; a combine kernel merges splits.
+//
+// Modes (the reference's four kernels, pager_hf/streaming_attention.py):
+//   ONLINE  one-pass (m, l, acc) fold            (_decode_attention_step_kernel :77-185)
+//   STATS   (m, l) only, K only                  (_decode_attention_stats_kernel :188-261)
+//   FIXED   acc += exp(s - m_final) . V          (_decode_attention_accumulate_kernel :264-352,
+//                                                 _decode_attention_fold_fixed_kernel :355-430)
+// In ONLINE and FIXED modes the kernel also emits per-group attention-mass
+// partials (sum of p over `group_tokens` tokens, with the running max it is
+// relative to), from which the per-block mass is assembled without a second
+// pass over KV.
+#pragma once
+
+#include <type_traits>
+
+#include "pager_device.cuh"
+
+namespace pager {
+
+enum Mode { MODE_ONLINE = 0, MODE_STATS = 1, MODE_FIXED = 2 };
+enum Source { SRC_CONTIG = 0, SRC_PAGED = 1 };
+enum Backend { BACKEND_MMA = 1, BACKEND_FMA = 2 };
+
+constexpr int kConsumerWarps = 4;
+constexpr int kThreads = (kConsumerWarps + 1) * 32;
+constexpr int kMaxRep = 16;
+constexpr int kHostSlotBit = 0x40000000;
+constexpr int kStatusTimeout = 5;
+constexpr int kStatusBadBlock = 6;
+
+struct RowGeom {
+  int nb, ntok, lo, hi;
+};
+
+// Everything that defines a row's token range; shared by the split, combine
+// and mass kernels so that all three agree on the tiles of every row.
+struct GeomArgs {
+  int source;
+  int tokens;  // SRC_CONTIG: tokens per row
+  int tpb;
+  const int* num_blocks;
+  int max_blocks;
+  const int* tail_len;
+  int tail_cap;
+  int max_tokens;  // host-known bound; longer rows are clamped (and flagged)
+  const int* valid_lo;
+  const int* valid_hi;
+};
+
+// Clamps every per-row input to the buffers it indexes, so a bad row length
+// can never send a load or a scratch write out of bounds.
+__device__ __forceinline__ RowGeom row_geom(const GeomArgs& a, int b, bool* clamped = nullptr) {
+  RowGeom g;
+  bool c = false;
+  if (a.source == SRC_CONTIG) {
+    g.nb = 0;
+    g.ntok = a.tokens;
+  } else {
+    int nb = a.num_blocks[b];
+    if (nb < 0 || nb > a.max_blocks) {
+      c = true;
+      nb = nb < 0 ? 0 : a.max_blocks;
+    }
+    int tl = a.tail_len ? a.tail_len[b] : 0;
+    if (tl < 0 || tl > a.tail_cap) {
+      c = true;
+      tl = tl < 0 ? 0 : a.tail_cap;
+    }
+    g.nb = nb;
+    g.ntok = nb * a.tpb + tl;
+    if (g.ntok > a.max_tokens) {
+      c = true;
+      g.ntok = a.max_tokens;
+    }
+  }
+  g.lo = a.valid_lo ? max(0, a.valid_lo[b]) : 0;
+  g.hi = a.valid_hi ? min(g.ntok, a.valid_hi[b]) : g.ntok;
+  if (clamped) *clamped = c;
+  return g;
+}
+
+__device__ __forceinline__ void geom_tiles(const RowGeom& g, int tile_shift, int tps, int& t_begin, int& t_end,
+                                           int& nsplit) {
+  if (g.hi <= g.lo) {
+    t_begin = t_end = nsplit = 0;
+    return;
+  }
+  t_begin = g.lo >> tile_shift;
+  t_end = (g.hi + (1 << tile_shift) - 1) >> tile_shift;
+  nsplit = (t_end - t_begin + tps - 1) / tps;
+}
+
+struct SplitParams {
+  // queries
+  const void* q;
+  int q_dtype;
+  int batch, num_q_heads, num_kv_heads, n_rep;
+  float scale, softcap;  // softcap <= 0: off
+  // source of K/V and row geometry
+  GeomArgs geom;
+  int source;
+  const char* dev_pool;
+  const char* host_pool;
+  long long slot_stride_bytes;   // SRC_PAGED: bytes per pool slot (all layers)
+  long long layer_stride_bytes;  // bytes per (slot, layer) = 2 * Hkv * tpb * row bytes
+  int num_layers, layer, tpb, log2_tpb;
+  int dev_slots, host_slots;  // pool capacities (block-table entries are checked against them)
+  const int* block_table;
+  int max_blocks;
+  const char* tail_k;
+  const char* tail_v;
+  int tail_cap;
+  // validity
+  const int* valid;
+  long long valid_stride;
+  const int* active;
+  // MODE_FIXED: final statistics
+  const float* m_fixed;
+  const float* l_fixed;
+  // decomposition
+  int tiles_per_split, max_splits;
+  // outputs
+  float* part_m;    // [B, Hq, max_splits]
+  float* part_l;    // [B, Hq, max_splits]
+  float* part_acc;  // [B, Hq, max_splits, D]
+  float2* mass_part;  // [B, Hq, mass_gstride]: (sum p, reference max)
+  int mass_gstride;
+  int group_tokens;  // 0: no mass partials
+  int log2_group;
+  unsigned long long wait_limit_ns;
+  int* status;
+};
+
+template <typename T, int D, int MODE>
+struct TileCfg {
+  static constexpr int ELT = sizeof(T);
+  static constexpr int ROW_BYTES = D * ELT;
+  static constexpr int TILE_RAW = 16384 / (2 * ROW_BYTES);
+  static constexpr int TILE = TILE_RAW > 64 ? 64 : (TILE_RAW < 16 ? 16 : TILE_RAW);
+  static constexpr int LOG2_TILE = TILE == 64 ? 6 : (TILE == 32 ? 5 : 4);
+  static constexpr int PANEL_BYTES = ROW_BYTES < 128 ? ROW_BYTES : 128;
+  static constexpr int NPANEL = ROW_BYTES / PANEL_BYTES;
+  static constexpr int PANEL_ELTS = PANEL_BYTES / ELT;
+  static constexpr int CPP = PANEL_BYTES / 16;  // 16-byte chunks per panel row
+  static constexpr int CPR = ROW_BYTES / 16;    // 16-byte chunks per row
+  static constexpr int SWZ_MASK = CPP - 1;
+  static constexpr int PANEL_TILE_BYTES = TILE * PANEL_BYTES;
+  static constexpr int TENSOR_BYTES = TILE * ROW_BYTES;
+  static constexpr int STAGE_BYTES = (MODE == MODE_STATS ? 1 : 2) * TENSOR_BYTES;
+  static constexpr int STAGES_RAW = (96 * 1024) / STAGE_BYTES;
+  static constexpr int STAGES = STAGES_RAW > 8 ? 8 : (STAGES_RAW < 4 ? 4 : STAGES_RAW);
+  static constexpr int STAGE_AREA = STAGES * STAGE_BYTES;
+  static constexpr int MERGE_BYTES = kConsumerWarps * kMaxRep * (2 + (MODE == MODE_STATS ? 0 : D)) * 4;
+  static_assert(MERGE_BYTES <= STAGE_AREA, "merge region must fit in the stage ring");
+  static_assert((TILE & (TILE - 1)) == 0 && TILE >= 16 && TILE <= 64, "tile");
+};
+
+// Physical byte offset of logical offset `off` inside a panel written by TMA
+// with the swizzle mode matching the panel width (128B / 64B / 32B / none).
+template <class Cfg>
+__device__ __forceinline__ uint32_t swz(uint32_t off) {
+  return off ^ (((off >> 7) & Cfg::SWZ_MASK) << 4);
+}
+
+template <class Cfg>
+__device__ __forceinline__ uint32_t chunk_addr(uint32_t tile_base, int row, int chunk) {
+  const int panel = chunk / Cfg::CPP;
+  const int cp = chunk % Cfg::CPP;
+  return tile_base + panel * Cfg::PANEL_TILE_BYTES + swz<Cfg>(row * Cfg::PANEL_BYTES + cp * 16);
+}
+
+// A block-table entry names a slot that exists in a pool that was passed in.
+__device__ __forceinline__ bool entry_usable(const SplitParams& p, int e) {
+  if (e < 0) return false;
+  if (e & kHostSlotBit) return p.host_pool != nullptr && (e & (kHostSlotBit - 1)) < p.host_slots;
+  return p.dev_pool != nullptr && e < p.dev_slots;
+}
+
+__device__ __forceinline__ bool token_valid(const SplitParams& p, int b, int t, const RowGeom& g) {
+  if (t < g.lo || t >= g.hi) return false;
+  if (p.valid && p.valid[(long long)b * p.valid_stride + t] == 0) return false;
+  if (p.source == SRC_PAGED && t < g.nb * p.tpb) {
+    if (!entry_usable(p, p.block_table[(long long)b * p.max_blocks + (t >> p.log2_tpb)])) return false;
+  }
+  return true;
+}
+
+template <int TILE>
+__device__ __forceinline__ void tile_valid_bits(const SplitParams& p, int b, int t0, const RowGeom& g,
+                                                uint32_t& lo_bits, uint32_t& hi_bits) {
+  const int lane = threadIdx.x & 31;
+  const bool v0 = lane < TILE && token_valid(p, b, t0 + lane, g);
+  const bool v1 = TILE > 32 && token_valid(p, b, t0 + 32 + lane, g);
+  lo_bits = __ballot_sync(0xffffffffu, v0);
+  hi_bits = __ballot_sync(0xffffffffu, v1);
+}
+
+__device__ __forceinline__ bool bit_of(uint32_t lo_bits, uint32_t hi_bits, int t) {
+  return ((t < 32 ? (lo_bits >> t) : (hi_bits >> (t - 32))) & 1u) != 0;
+}
+
+// ------------------------------------------------------------------ producer helpers
+
+// Warp-cooperative copy of `nrows` rows (row-contiguous source, any global or
+// mapped-host address) into rows [row0, row0+nrows) of a swizzled tile.
+template <class Cfg>
+__device__ __forceinline__ void sw_copy_rows(uint32_t tile_base, int row0, const char* src, int nrows) {
+  const int lane = threadIdx.x & 31;
+  const int total = nrows * Cfg::CPR;
+  constexpr int U = 8;
+  for (int c0 = 0; c0 < total; c0 += 32 * U) {
+    uint4 v[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int c = c0 + u * 32 + lane;
+      if (c < total) v[u] = ld_global_16(src + (size_t)c * 16);
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int c = c0 + u * 32 + lane;
+      if (c < total) {
+        const int r = c / Cfg::CPR;
+        const int cw = c % Cfg::CPR;
+        st_shared_16(chunk_addr<Cfg>(tile_base, row0 + r, cw), v[u]);
+      }
+    }
+  }
+}
+
+template <class Cfg, int MODE>
+__device__ void run_producer(const SplitParams& p, const CUtensorMap* mapk, const CUtensorMap* mapv,
+                             uint8_t* stages, uint64_t* full, uint64_t* empty, int b, int h, int tile0,
+                             int ntiles, const RowGeom& g, volatile int* abort_flag) {
+  const int lane = threadIdx.x & 31;
+  constexpr bool kNeedV = MODE != MODE_STATS;
+  int issued = 0;
+  for (int i = 0; i < ntiles; ++i) {
+    const int s = i % Cfg::STAGES;
+    const int use = i / Cfg::STAGES;
+    if (use > 0) {
+      int ok = 1;
+      if (lane == 0) ok = mbar_wait_bounded(&empty[s], (use - 1) & 1, p.wait_limit_ns) ? 1 : 0;
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok) {
+        if (lane == 0) {
+          atomicExch(p.status, kStatusTimeout);
+          *abort_flag = 1;
+        }
+        break;
+      }
+    }
+    if (*abort_flag) break;
+    uint8_t* kbuf = stages + s * Cfg::STAGE_BYTES;
+    uint8_t* vbuf = kbuf + Cfg::TENSOR_BYTES;
+    const int t0 = (tile0 + i) * Cfg::TILE;
+    if (p.source == SRC_CONTIG) {
+      if (lane == 0) {
+        mbar_expect_tx(&full[s], (uint32_t)Cfg::STAGE_BYTES);
+        const int z = b * p.num_kv_heads + h;
+#pragma unroll
+        for (int pn = 0; pn < Cfg::NPANEL; ++pn) {
+          tma_load_3d(kbuf + pn * Cfg::PANEL_TILE_BYTES, mapk, pn * Cfg::PANEL_ELTS, t0, z, &full[s]);
+          if (kNeedV) tma_load_3d(vbuf + pn * Cfg::PANEL_TILE_BYTES, mapv, pn * Cfg::PANEL_ELTS, t0, z, &full[s]);
+        }
+        mbar_arrive(&full[s]);
+      }
+    } else {
+      const int br = min(Cfg::TILE, p.tpb);
+      const int nseg = Cfg::TILE / br;
+      const int block_tokens = g.nb * p.tpb;
+      const uint32_t seg_bytes = (uint32_t)br * Cfg::ROW_BYTES * (kNeedV ? 2u : 1u);
+      const long long head_bytes = (long long)p.tpb * Cfg::ROW_BYTES;
+      if (lane == 0) {
+        uint32_t tx = 0;
+        for (int sg = 0; sg < nseg; ++sg) {
+          const int tok = t0 + sg * br;
+          if (tok >= g.hi || tok + br <= g.lo || tok >= block_tokens) continue;
+          const int e = p.block_table[(long long)b * p.max_blocks + (tok >> p.log2_tpb)];
+          if (!entry_usable(p, e)) {
+            if (e >= 0) atomicExch(p.status, kStatusBadBlock);
+            continue;
+          }
+          if (!(e & kHostSlotBit)) tx += seg_bytes;
+        }
+        if (tx) mbar_expect_tx(&full[s], tx);
+        for (int sg = 0; sg < nseg; ++sg) {
+          const int tok = t0 + sg * br;
+          if (tok >= g.hi || tok + br <= g.lo || tok >= block_tokens) continue;
+          const int e = p.block_table[(long long)b * p.max_blocks + (tok >> p.log2_tpb)];
+          if (!entry_usable(p, e) || (e & kHostSlotBit)) continue;
+          const int zk = ((e * p.num_layers + p.layer) * 2) * p.num_kv_heads + h;
+          const int y = tok & (p.tpb - 1);
+#pragma unroll
+          for (int pn = 0; pn < Cfg::NPANEL; ++pn) {
+            const int off = pn * Cfg::PANEL_TILE_BYTES + sg * br * Cfg::PANEL_BYTES;
+            tma_load_3d(kbuf + off, mapk, pn * Cfg::PANEL_ELTS, y, zk, &full[s]);
+            if (kNeedV) tma_load_3d(vbuf + off, mapk, pn * Cfg::PANEL_ELTS, y, zk + p.num_kv_heads, &full[s]);
+          }
+        }
+      }
+      __syncwarp();
+      // zero-copy host blocks and the tail: 16-byte loads into the swizzled layout
+      const uint32_t kaddr = smem_u32(kbuf), vaddr = smem_u32(vbuf);
+      for (int sg = 0; sg < nseg; ++sg) {
+        const int tok = t0 + sg * br;
+        if (tok >= g.hi || tok + br <= g.lo) continue;
+        if (tok < block_tokens) {
+          const int e = p.block_table[(long long)b * p.max_blocks + (tok >> p.log2_tpb)];
+          if (!entry_usable(p, e) || !(e & kHostSlotBit)) continue;
+          const long long slot = e & (kHostSlotBit - 1);
+          const char* kb = p.host_pool + slot * p.slot_stride_bytes + (long long)p.layer * p.layer_stride_bytes +
+                           (long long)h * head_bytes + (long long)(tok & (p.tpb - 1)) * Cfg::ROW_BYTES;
+          sw_copy_rows<Cfg>(kaddr, sg * br, kb, br);
+          if (kNeedV) sw_copy_rows<Cfg>(vaddr, sg * br, kb + (long long)p.num_kv_heads * head_bytes, br);
+        } else {
+          const int tr = tok - block_tokens;
+          const int n = min(br, g.ntok - tok);
+          const long long off = (((long long)b * p.num_kv_heads + h) * p.tail_cap + tr) * Cfg::ROW_BYTES;
+          sw_copy_rows<Cfg>(kaddr, sg * br, p.tail_k + off, n);
+          if (kNeedV) sw_copy_rows<Cfg>(vaddr, sg * br, p.tail_v + off, n);
+        }
+      }
+      __threadfence_block();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&full[s]);
+    }
+    issued = i + 1;
+  }
+  // Drain: never leave the CTA with bulk copies still landing in its shared memory.
+  if (lane == 0) {
+    const int first = issued > Cfg::STAGES ? issued - Cfg::STAGES : 0;
+    for (int i = first; i < issued; ++i) {
+      if (!mbar_wait_bounded(&full[i % Cfg::STAGES], (i / Cfg::STAGES) & 1, p.wait_limit_ns)) {
+        atomicExch(p.status, kStatusTimeout);
+        *abort_flag = 1;
+        break;
+      }
+    }
+  }
+}
+
+// Consumer-side wait: lane 0 does the bounded wait; on success every lane
+// observes the (already completed) phase so the TMA writes are visible to it.
+__device__ __forceinline__ bool consumer_wait(const SplitParams& p, uint64_t* bar, uint32_t parity,
+                                              volatile int* abort_flag) {
+  const int lane = threadIdx.x & 31;
+  int ok = 1;
+  if (lane == 0) ok = mbar_wait_bounded(bar, parity, p.wait_limit_ns) ? 1 : 0;
+  ok = __shfl_sync(0xffffffffu, ok, 0);
+  if (!ok) {
+    if (lane == 0) {
+      atomicExch(p.status, kStatusTimeout);
+      *abort_flag = 1;
+    }
+    return false;
+  }
+  while (!mbar_try_wait(bar, parity)) {
+  }
+  return true;
+}
+
+// Zero the V rows of masked tokens so that 0 * (stale or non-finite) never
+// reaches the P.V product (the reference loads masked rows as 0).
+template <class Cfg>
+__device__ __forceinline__ bool zero_masked_rows(uint8_t* vbuf, uint32_t lo_bits, uint32_t hi_bits) {
+  const uint32_t need_lo = Cfg::TILE >= 32 ? 0xffffffffu : ((1u << Cfg::TILE) - 1u);
+  const uint32_t need_hi = Cfg::TILE == 64 ? 0xffffffffu : 0u;
+  if (lo_bits == need_lo && hi_bits == need_hi) return false;
+  const int lane = threadIdx.x & 31;
+  const uint32_t base = smem_u32(vbuf);
+  const int total = Cfg::TILE * Cfg::CPR;
+  for (int c = lane; c < total; c += 32) {
+    const int r = c / Cfg::CPR;
+    if (!bit_of(lo_bits, hi_bits, r)) st_shared_16(chunk_addr<Cfg>(base, r, c % Cfg::CPR), make_uint4(0, 0, 0, 0));
+  }
+  __syncwarp();
+  return true;
+}
+
+__device__ __forceinline__ void release_stage(uint64_t* bar, bool wrote) {
+  if (wrote) fence_proxy_async_smem();
+  __syncwarp();
+  if ((threadIdx.x & 31) == 0) mbar_arrive(bar);
+}
+
+__device__ __forceinline__ float apply_score(float raw, float scale, float softcap) {
+  float x = raw * scale;
+  if (softcap > 0.f) x = softcap * tanhf(x / softcap);
+  return x;
+}
+
+// Merge the four consumer warps' states (held in the stage area) and write
+// this split's partial state.  `mw`: m_w[4][16], l_w[4][16], acc_w[4][16][D].
+template <int D, int MODE>
+__device__ void merge_and_store(const SplitParams& p, float* mw, int b, int h, int split) {
+  const int tid = threadIdx.x;
+  const float* m_w = mw;
+  const float* l_w = mw + kConsumerWarps * kMaxRep;
+  const float* acc_w = mw + 2 * kConsumerWarps * kMaxRep;
+  const int n_rep = p.n_rep;
+  const int qh0 = h * n_rep;
+  if (MODE != MODE_FIXED) {
+    for (int r = tid; r < n_rep; r += kConsumerWarps * 32) {
+      float M = neg_inf();
+#pragma unroll
+      for (int w = 0; w < kConsumerWarps; ++w) M = fmaxf(M, m_w[w * kMaxRep + r]);
+      float L = 0.f;
+#pragma unroll
+      for (int w = 0; w < kConsumerWarps; ++w) {
+        const float mwr = m_w[w * kMaxRep + r];
+        const float wt = mwr == neg_inf() ? 0.f : fast_exp2((mwr - M) * kLog2e);
+        L += wt * l_w[w * kMaxRep + r];
+      }
+      const long long o = ((long long)b * p.num_q_heads + qh0 + r) * p.max_splits + split;
+      p.part_m[o] = M;
+      p.part_l[o] = L;
+    }
+  }
+  if constexpr (MODE == MODE_STATS) return;
+  for (int idx = tid; idx < n_rep * D; idx += kConsumerWarps * 32) {
+    const int r = idx / D;
+    const int d = idx % D;
+    float A = 0.f;
+    if (MODE == MODE_FIXED) {
+#pragma unroll
+      for (int w = 0; w < kConsumerWarps; ++w) A += acc_w[(w * kMaxRep + r) * D + d];
+    } else {
+      float M = neg_inf();
+#pragma unroll
+      for (int w = 0; w < kConsumerWarps; ++w) M = fmaxf(M, m_w[w * kMaxRep + r]);
+#pragma unroll
+      for (int w = 0; w < kConsumerWarps; ++w) {
+        const float mwr = m_w[w * kMaxRep + r];
+        const float wt = mwr == neg_inf() ? 0.f : fast_exp2((mwr - M) * kLog2e);
+        A += wt * acc_w[(w * kMaxRep + r) * D + d];
+      }
+    }
+    const long long o = ((long long)b * p.num_q_heads + qh0 + r) * p.max_splits + split;
+    p.part_acc[o * D + d] = A;
+  }
+}
+
+// ------------------------------------------------------------------ tensor-core consumer
+template <typename T, int D, int MODE>
+__device__ void run_consumer_mma(const SplitParams& p, uint8_t* stages, uint64_t* full, uint64_t* empty, int b,
+                                 int h, int tile0, int ntiles, const RowGeom& g, volatile int* abort_flag,
+                                 int split) {
+  using Cfg = TileCfg<T, D, MODE>;
+  using Op = MmaOp<T>;
+  constexpr int KSTEPS = D / 16;
+  constexpr int NT_O = D / 8;
+  constexpr int NT_S = Cfg::TILE / 8;
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const int gr = lane >> 2;  // fragment row (query head within the group)
+  const int tq = lane & 3;
+  const int n_rep = p.n_rep;
+  const int qh0 = h * n_rep;
+
+  uint32_t qa[KSTEPS][4];
+  {
+    const long long qbase = ((long long)b * p.num_q_heads + qh0) * D;
+#pragma unroll
+    for (int kk = 0; kk < KSTEPS; ++kk) {
+      const int c = 16 * kk + 2 * tq;
+      float v[2][4];
+#pragma unroll
+      for (int rr = 0; rr < 2; ++rr) {
+        const int row = gr + 8 * rr;
+        const bool ok = row < n_rep;
+        const long long base = qbase + (long long)row * D;
+        v[rr][0] = ok ? load_any(p.q, base + c, p.q_dtype) : 0.f;
+        v[rr][1] = ok ? load_any(p.q, base + c + 1, p.q_dtype) : 0.f;
+        v[rr][2] = ok ? load_any(p.q, base + c + 8, p.q_dtype) : 0.f;
+        v[rr][3] = ok ? load_any(p.q, base + c + 9, p.q_dtype) : 0.f;
+      }
+      qa[kk][0] = Op::pack(v[0][0], v[0][1]);
+      qa[kk][1] = Op::pack(v[1][0], v[1][1]);
+      qa[kk][2] = Op::pack(v[0][2], v[0][3]);
+      qa[kk][3] = Op::pack(v[1][2], v[1][3]);
+    }
+  }
+  float mfix_l2[2] = {0.f, 0.f};
+  if (MODE == MODE_FIXED) {
+#pragma unroll
+    for (int rr = 0; rr < 2; ++rr) {
+      const int row = gr + 8 * rr;
+      const float mf = row < n_rep ? p.m_fixed[(long long)b * p.num_q_heads + qh0 + row] : 0.f;
+      mfix_l2[rr] = mf * kLog2e;
+    }
+  }
+
+  float o[NT_O][4];
+#pragma unroll
+  for (int n = 0; n < NT_O; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+  float m_r[2] = {neg_inf(), neg_inf()};
+  float l_r[2] = {0.f, 0.f};
+  const int G = p.group_tokens;
+
+  for (int i = warp; i < ntiles; i += kConsumerWarps) {
+    const int s = i % Cfg::STAGES;
+    if (*abort_flag) break;
+    if (!consumer_wait(p, &full[s], (i / Cfg::STAGES) & 1, abort_flag)) break;
+    const int t0 = (tile0 + i) * Cfg::TILE;
+    uint32_t vlo, vhi;
+    tile_valid_bits<Cfg::TILE>(p, b, t0, g, vlo, vhi);
+    uint8_t* kbuf = stages + s * Cfg::STAGE_BYTES;
+    uint8_t* vbuf = kbuf + Cfg::TENSOR_BYTES;
+    const uint32_t kaddr = smem_u32(kbuf);
+
+    float sc[NT_S][4];
+#pragma unroll
+    for (int j = 0; j < NT_S; ++j) sc[j][0] = sc[j][1] = sc[j][2] = sc[j][3] = 0.f;
+#pragma unroll
+    for (int j = 0; j < NT_S; ++j) {
+      const int row = 8 * j + (lane & 7);
+#pragma unroll
+      for (int kk = 0; kk < KSTEPS; kk += 2) {
+        uint32_t b0, b1, b2, b3;
+        ldmatrix_x4(chunk_addr<Cfg>(kaddr, row, 2 * kk + (lane >> 3)), b0, b1, b2, b3);
+        Op::run(sc[j], qa[kk], b0, b1);
+        Op::run(sc[j], qa[kk + 1], b2, b3);
+      }
+    }
+    // scale, softcap, token mask (streaming_attention.py:158-161)
+#pragma unroll
+    for (int j = 0; j < NT_S; ++j) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int tok = 8 * j + 2 * tq + (e & 1);
+        const float x = apply_score(sc[j][e], p.scale, p.softcap);
+        sc[j][e] = bit_of(vlo, vhi, tok) ? x : neg_inf();
+      }
+    }
+    float mref[2];
+    if (MODE != MODE_FIXED) {
+      float mx[2] = {neg_inf(), neg_inf()};
+#pragma unroll
+      for (int j = 0; j < NT_S; ++j) {
+        mx[0] = fmaxf(mx[0], fmaxf(sc[j][0], sc[j][1]));
+        mx[1] = fmaxf(mx[1], fmaxf(sc[j][2], sc[j][3]));
+      }
+#pragma unroll
+      for (int rr = 0; rr < 2; ++rr) {
+        mx[rr] = fmaxf(mx[rr], __shfl_xor_sync(0xffffffffu, mx[rr], 1));
+        mx[rr] = fmaxf(mx[rr], __shfl_xor_sync(0xffffffffu, mx[rr], 2));
+        const float m_new = fmaxf(m_r[rr], mx[rr]);
+        const bool empty_row = m_new == neg_inf();  // streaming_attention.py:171-177
+        const float alpha = empty_row ? 0.f : fast_exp2((m_r[rr] - m_new) * kLog2e);
+        l_r[rr] *= alpha;
+        if (MODE == MODE_ONLINE) {
+#pragma unroll
+          for (int n = 0; n < NT_O; ++n) {
+            o[n][2 * rr] *= alpha;
+            o[n][2 * rr + 1] *= alpha;
+          }
+        }
+        m_r[rr] = m_new;
+        mref[rr] = empty_row ? 0.f : m_new * kLog2e;
+      }
+    } else {
+      mref[0] = mfix_l2[0];
+      mref[1] = mfix_l2[1];
+    }
+    // p = exp(s - m)
+#pragma unroll
+    for (int j = 0; j < NT_S; ++j) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) sc[j][e] = fast_exp2(fmaf(sc[j][e], kLog2e, -mref[e >> 1]));
+    }
+    if (MODE != MODE_FIXED) {
+#pragma unroll
+      for (int j = 0; j < NT_S; ++j) {
+        l_r[0] += sc[j][0] + sc[j][1];
+        l_r[1] += sc[j][2] + sc[j][3];
+      }
+    }
+    if (MODE != MODE_STATS && G > 0) {
+      const int ntg = G >> 3;  // S n-tiles per mass group
+      for (int gi = 0; gi < Cfg::TILE / G; ++gi) {
+        float gs[2] = {0.f, 0.f};
+#pragma unroll
+        for (int j = 0; j < NT_S; ++j) {
+          if (j / ntg == gi) {
+            gs[0] += sc[j][0] + sc[j][1];
+            gs[1] += sc[j][2] + sc[j][3];
+          }
+        }
+#pragma unroll
+        for (int rr = 0; rr < 2; ++rr) {
+          gs[rr] += __shfl_xor_sync(0xffffffffu, gs[rr], 1);
+          gs[rr] += __shfl_xor_sync(0xffffffffu, gs[rr], 2);
+        }
+        if (tq == 0) {
+          const long long gidx = (t0 >> p.log2_group) + gi;
+#pragma unroll
+          for (int rr = 0; rr < 2; ++rr) {
+            const int row = gr + 8 * rr;
+            if (row < n_rep)
+              p.mass_part[((long long)b * p.num_q_heads + qh0 + row) * p.mass_gstride + gidx] =
+                  make_float2(gs[rr], MODE == MODE_ONLINE ? m_r[rr] : 0.f);
+          }
+        }
+      }
+    }
+    bool wrote = false;
+    if (MODE != MODE_STATS) {
+      wrote = zero_masked_rows<Cfg>(vbuf, vlo, vhi);
+      const uint32_t vaddr = smem_u32(vbuf);
+#pragma unroll
+      for (int kt = 0; kt < Cfg::TILE / 16; ++kt) {
+        uint32_t pa[4];
+        pa[0] = Op::pack(sc[2 * kt][0], sc[2 * kt][1]);
+        pa[1] = Op::pack(sc[2 * kt][2], sc[2 * kt][3]);
+        pa[2] = Op::pack(sc[2 * kt + 1][0], sc[2 * kt + 1][1]);
+        pa[3] = Op::pack(sc[2 * kt + 1][2], sc[2 * kt + 1][3]);
+        const int mi = lane >> 3;
+        const int vrow = 16 * kt + ((mi & 1) << 3) + (lane & 7);
+#pragma unroll
+        for (int n = 0; n < NT_O; n += 2) {
+          uint32_t b0, b1, b2, b3;
+          ldmatrix_x4_trans(chunk_addr<Cfg>(vaddr, vrow, n + (mi >> 1)), b0, b1, b2, b3);
+          Op::run(o[n], pa, b0, b1);
+          Op::run(o[n + 1], pa, b2, b3);
+        }
+      }
+    }
+    release_stage(&empty[s], wrote);
+  }
+
+  // per-row l from the quad's partial sums
+#pragma unroll
+  for (int rr = 0; rr < 2; ++rr) {
+    l_r[rr] += __shfl_xor_sync(0xffffffffu, l_r[rr], 1);
+    l_r[rr] += __shfl_xor_sync(0xffffffffu, l_r[rr], 2);
+  }
+  named_bar_sync(1, kConsumerWarps * 32);
+  float* mw = reinterpret_cast<float*>(stages);
+  float* m_w = mw;
+  float* l_w = mw + kConsumerWarps * kMaxRep;
+  float* acc_w = mw + 2 * kConsumerWarps * kMaxRep;
+  if (tq == 0) {
+    m_w[warp * kMaxRep + gr] = m_r[0];
+    m_w[warp * kMaxRep + gr + 8] = m_r[1];
+    l_w[warp * kMaxRep + gr] = l_r[0];
+    l_w[warp * kMaxRep + gr + 8] = l_r[1];
+  }
+  if (MODE != MODE_STATS) {
+#pragma unroll
+    for (int n = 0; n < NT_O; ++n) {
+      const int col = 8 * n + 2 * tq;
+      acc_w[(warp * kMaxRep + gr) * D + col] = o[n][0];
+      acc_w[(warp * kMaxRep + gr) * D + col + 1] = o[n][1];
+      acc_w[(warp * kMaxRep + gr + 8) * D + col] = o[n][2];
+      acc_w[(warp * kMaxRep + gr + 8) * D + col + 1] = o[n][3];
+    }
+  }
+  named_bar_sync(1, kConsumerWarps * 32);
+  merge_and_store<D, MODE>(p, mw, b, h, split);
+}
+
+// ------------------------------------------------------------------ CUDA-core consumer
+// Lane <-> token for Q.K (q broadcast from shared memory), lane <-> head_dim
+// column for P.V (p broadcast from shared memory); fp32 throughout.
+template <typename T, int D, int MODE>
+__device__ void run_consumer_fma(const SplitParams& p, uint8_t* stages, uint64_t* full, uint64_t* empty, int b,
+                                 int h, int tile0, int ntiles, const RowGeom& g, volatile int* abort_flag,
+                                 int split, const float* q_sm, float* p_sm_all) {
+  using Cfg = TileCfg<T, D, MODE>;
+  constexpr int TILE = Cfg::TILE;
+  constexpr int TPL = TILE > 32 ? TILE / 32 : 1;   // tokens per lane in Q.K
+  constexpr int EPC = 16 / sizeof(T);              // elements per 16-byte chunk
+  constexpr int DPL = D >= 32 ? D / 32 : 1;        // head_dim columns per lane in P.V
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const int n_rep = p.n_rep;
+  const int qh0 = h * n_rep;
+  float* p_sm = p_sm_all + warp * TILE * kMaxRep;
+
+  float mfix[kMaxRep];
+  if (MODE == MODE_FIXED) {
+#pragma unroll
+    for (int r = 0; r < kMaxRep; ++r)
+      mfix[r] = r < n_rep ? p.m_fixed[(long long)b * p.num_q_heads + qh0 + r] * kLog2e : 0.f;
+  }
+  float acc[kMaxRep][DPL];
+#pragma unroll
+  for (int r = 0; r < kMaxRep; ++r)
+#pragma unroll
+    for (int k = 0; k < DPL; ++k) acc[r][k] = 0.f;
+  float m_r[kMaxRep], l_r[kMaxRep];  // l_r: this lane's partial sum
+#pragma unroll
+  for (int r = 0; r < kMaxRep; ++r) {
+    m_r[r] = neg_inf();
+    l_r[r] = 0.f;
+  }
+  const int G = p.group_tokens;
+
+  for (int i = warp; i < ntiles; i += kConsumerWarps) {
+    const int s = i % Cfg::STAGES;
+    if (*abort_flag) break;
+    if (!consumer_wait(p, &full[s], (i / Cfg::STAGES) & 1, abort_flag)) break;
+    const int t0 = (tile0 + i) * TILE;
+    uint32_t vlo, vhi;
+    tile_valid_bits<TILE>(p, b, t0, g, vlo, vhi);
+    uint8_t* kbuf = stages + s * Cfg::STAGE_BYTES;
+    uint8_t* vbuf = kbuf + Cfg::TENSOR_BYTES;
+    const uint32_t kaddr = smem_u32(kbuf);
+
+    float sc[TPL][kMaxRep];
+#pragma unroll
+    for (int u = 0; u < TPL; ++u) {
+      const int t = lane + 32 * u;
+#pragma unroll
+      for (int r = 0; r < kMaxRep; ++r) sc[u][r] = 0.f;
+      if (t < TILE) {
+#pragma unroll 2
+        for (int c = 0; c < Cfg::CPR; ++c) {
+          float kf[EPC];
+          unpack16(ld_shared_16(chunk_addr<Cfg>(kaddr, t, c)), kf, T());
+#pragma unroll
+          for (int r = 0; r < kMaxRep; ++r) {
+            if (r < n_rep) {
+              const float* qr = q_sm + r * D + c * EPC;
+#pragma unroll
+              for (int e = 0; e < EPC; ++e) sc[u][r] = fmaf(qr[e], kf[e], sc[u][r]);
+            }
+          }
+        }
+      }
+#pragma unroll
+      for (int r = 0; r < kMaxRep; ++r) {
+        const float x = apply_score(sc[u][r], p.scale, p.softcap);
+        sc[u][r] = (t < TILE && bit_of(vlo, vhi, t)) ? x : neg_inf();
+      }
+    }
+    float mref[kMaxRep];
+#pragma unroll
+    for (int r = 0; r < kMaxRep; ++r) {
+      if (MODE != MODE_FIXED) {
+        float mx = sc[0][r];
+#pragma unroll
+        for (int u = 1; u < TPL; ++u) mx = fmaxf(mx, sc[u][r]);
+        mx = warp_max(mx);
+        const float m_new = fmaxf(m_r[r], mx);
+        const bool empty_row = m_new == neg_inf();
+        const float alpha = empty_row ? 0.f : fast_exp2((m_r[r] - m_new) * kLog2e);
+        l_r[r] *= alpha;
+        if (MODE == MODE_ONLINE) {
+#pragma unroll
+          for (int k = 0; k < DPL; ++k) acc[r][k] *= alpha;
+        }
+        m_r[r] = m_new;
+        mref[r] = empty_row ? 0.f : m_new * kLog2e;
+      } else {
+        mref[r] = mfix[r];
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < TPL; ++u) {
+#pragma unroll
+      for (int r = 0; r < kMaxRep; ++r) {
+        sc[u][r] = fast_exp2(fmaf(sc[u][r], kLog2e, -mref[r]));
+        if (MODE != MODE_FIXED) l_r[r] += sc[u][r];
+      }
+    }
+    if (MODE != MODE_STATS && G > 0) {
+      // mass partials per group of G tokens (G >= 16, power of two)
+      const int ngroups = TILE / G;
+      for (int gi = 0; gi < ngroups; ++gi) {
+#pragma unroll
+        for (int r = 0; r < kMaxRep; ++r) {
+          if (r >= n_rep) continue;
+          float v = 0.f;
+#pragma unroll
+          for (int u = 0; u < TPL; ++u) {
+            const int t = lane + 32 * u;
+            if (t < TILE && t / G == gi) v += sc[u][r];
+          }
+          v = warp_sum(v);
+          if (lane == 0) {
+            const long long gidx = (t0 >> p.log2_group) + gi;
+            p.mass_part[((long long)b * p.num_q_heads + qh0 + r) * p.mass_gstride + gidx] =
+                make_float2(v, MODE == MODE_ONLINE ? m_r[r] : 0.f);
+          }
+        }
+      }
+    }
+    bool wrote = false;
+    if (MODE != MODE_STATS) {
+#pragma unroll
+      for (int u = 0; u < TPL; ++u) {
+        const int t = lane + 32 * u;
+        if (t < TILE) {
+#pragma unroll
+          for (int r = 0; r < kMaxRep; ++r) p_sm[t * kMaxRep + r] = sc[u][r];
+        }
+      }
+      wrote = zero_masked_rows<Cfg>(vbuf, vlo, vhi);
+      __syncwarp();
+      const uint32_t vaddr = smem_u32(vbuf);
+      for (int t = 0; t < TILE; ++t) {
+        if (!bit_of(vlo, vhi, t)) continue;
+        float pr[kMaxRep];
+#pragma unroll
+        for (int r4 = 0; r4 < kMaxRep; r4 += 4) {
+          const float4 v4 = *reinterpret_cast<const float4*>(p_sm + t * kMaxRep + r4);
+          pr[r4] = v4.x;
+          pr[r4 + 1] = v4.y;
+          pr[r4 + 2] = v4.z;
+          pr[r4 + 3] = v4.w;
+        }
+#pragma unroll
+        for (int k = 0; k < DPL; ++k) {
+          const int d = lane + 32 * k;
+          if (d < D) {
+            const int byte = d * (int)sizeof(T);
+            const uint32_t a = chunk_addr<Cfg>(vaddr, t, byte >> 4) + (byte & 15);
+            float vv;
+            if (sizeof(T) == 4) {
+              asm volatile("ld.shared.f32 %0, [%1];" : "=f"(vv) : "r"(a));
+            } else {
+              unsigned short raw;
+              asm volatile("ld.shared.u16 %0, [%1];" : "=h"(raw) : "r"(a));
+              if (sizeof(T) == 2 && std::is_same<T, __half>::value)
+                vv = __half2float(__ushort_as_half(raw));
+              else
+                vv = __uint_as_float(((uint32_t)raw) << 16);
+            }
+#pragma unroll
+            for (int r = 0; r < kMaxRep; ++r) acc[r][k] = fmaf(pr[r], vv, acc[r][k]);
+          }
+        }
+      }
+    }
+    release_stage(&empty[s], wrote);
+  }
+
+#pragma unroll
+  for (int r = 0; r < kMaxRep; ++r) l_r[r] = warp_sum(l_r[r]);
+  named_bar_sync(1, kConsumerWarps * 32);
+  float* mw = reinterpret_cast<float*>(stages);
+  float* m_w = mw;
+  float* l_w = mw + kConsumerWarps * kMaxRep;
+  float* acc_w = mw + 2 * kConsumerWarps * kMaxRep;
+  if (lane == 0) {
+#pragma unroll
+    for (int r = 0; r < kMaxRep; ++r) {
+      m_w[warp * kMaxRep + r] = m_r[r];
+      l_w[warp * kMaxRep + r] = l_r[r];
+    }
+  }
+  if (MODE != MODE_STATS) {
+#pragma unroll
+    for (int r = 0; r < kMaxRep; ++r)
+#pragma unroll
+      for (int k = 0; k < DPL; ++k) {
+        const int d = lane + 32 * k;
+        if (d < D) acc_w[(warp * kMaxRep + r) * D + d] = acc[r][k];
+      }
+  }
+  named_bar_sync(1, kConsumerWarps * 32);
+  merge_and_store<D, MODE>(p, mw, b, h, split);
+}
+
+// ------------------------------------------------------------------ kernel
+template <typename T, int D, int MODE, int BACKEND>
+struct SplitSmem {
+  using Cfg = TileCfg<T, D, MODE>;
+  static constexpr int BAR_OFF = Cfg::STAGE_AREA;
+  static constexpr int FLAG_OFF = BAR_OFF + 2 * Cfg::STAGES * 8;
+  static constexpr int Q_OFF = (FLAG_OFF + 16 + 15) / 16 * 16;
+  static constexpr int Q_BYTES = BACKEND == BACKEND_FMA ? kMaxRep * D * 4 : 0;
+  static constexpr int P_OFF = Q_OFF + Q_BYTES;
+  static constexpr int P_BYTES = BACKEND == BACKEND_FMA ? kConsumerWarps * Cfg::TILE * kMaxRep * 4 : 0;
+  static constexpr int TOTAL = P_OFF + P_BYTES + 1024;  // + slack for 1024-byte alignment
+};
+
+template <typename T, int D, int MODE, int BACKEND>
+__global__ void __launch_bounds__(kThreads) split_kernel(const __grid_constant__ SplitParams p,
+                                                         const __grid_constant__ CUtensorMap mapk,
+                                                         const __grid_constant__ CUtensorMap mapv) {
+  using Cfg = TileCfg<T, D, MODE>;
+  using L = SplitSmem<T, D, MODE, BACKEND>;
+  const int split = blockIdx.x;
+  const int h = blockIdx.y;
+  const int b = blockIdx.z;
+  if (p.active && p.active[b] == 0) return;
+  bool clamped = false;
+  const RowGeom g = row_geom(p.geom, b, &clamped);
+  if (clamped && split == 0 && h == 0 && threadIdx.x == 0) atomicExch(p.status, kStatusBadBlock);
+  int t_begin, t_end, nsplit;
+  geom_tiles(g, Cfg::LOG2_TILE, p.tiles_per_split, t_begin, t_end, nsplit);
+  if (split >= nsplit) return;
+  const int tile0 = t_begin + split * p.tiles_per_split;
+  const int ntiles = min(p.tiles_per_split, t_end - tile0);
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* stages = smem;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::BAR_OFF);
+  uint64_t* empty = full + Cfg::STAGES;
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::FLAG_OFF);
+  const int warp = threadIdx.x >> 5;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < Cfg::STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    *abort_flag = 0;
+    mbar_fence_init();
+    if (p.source == SRC_CONTIG || p.dev_pool != nullptr) {
+      tma_prefetch_desc(&mapk);
+      if (p.source == SRC_CONTIG && MODE != MODE_STATS) tma_prefetch_desc(&mapv);
+    }
+  }
+  float* q_sm = reinterpret_cast<float*>(smem + L::Q_OFF);
+  float* p_sm = reinterpret_cast<float*>(smem + L::P_OFF);
+  if (BACKEND == BACKEND_FMA && warp < kConsumerWarps) {
+    const long long qbase = ((long long)b * p.num_q_heads + (long long)h * p.n_rep) * D;
+    for (int idx = threadIdx.x; idx < kMaxRep * D; idx += kConsumerWarps * 32) {
+      const int r = idx / D;
+      q_sm[idx] = r < p.n_rep ? load_any(p.q, qbase + idx, p.q_dtype) : 0.f;
+    }
+  }
+  __syncthreads();
+
+  if (warp == kConsumerWarps) {
+    run_producer<Cfg, MODE>(p, &mapk, &mapv, stages, full, empty, b, h, tile0, ntiles, g, abort_flag);
+  } else {
+    if constexpr (BACKEND == BACKEND_MMA) {
+      run_consumer_mma<T, D, MODE>(p, stages, full, empty, b, h, tile0, ntiles, g, abort_flag, split);
+    } else {
+      run_consumer_fma<T, D, MODE>(p, stages, full, empty, b, h, tile0, ntiles, g, abort_flag, split, q_sm, p_sm);
+    }
+  }
+}
+
+// Host-side description of one instantiation.
+struct SplitKernelInfo {
+  const void* fn;
+  int tile;
+  int smem_bytes;
+  int stages;
+  int panel_elts;
+  int panel_bytes;
+};
+
+template <typename T, int D, int MODE, int BACKEND>
+SplitKernelInfo split_kernel_info() {
+  using Cfg = TileCfg<T, D, MODE>;
+  using L = SplitSmem<T, D, MODE, BACKEND>;
+  SplitKernelInfo k;
+  k.fn = reinterpret_cast<const void*>(&split_kernel<T, D, MODE, BACKEND>);
+  k.tile = Cfg::TILE;
+  k.smem_bytes = L::TOTAL;
+  k.stages = Cfg::STAGES;
+  k.panel_elts = Cfg::PANEL_ELTS;
+  k.panel_bytes = Cfg::PANEL_BYTES;
+  return k;
+}
+
+// Lookup: returns false when the (dtype, D, mode, backend) combination is not built.
+bool lookup_split_kernel(int kv_dtype, int head_dim, int mode, int backend, SplitKernelInfo* out);
+
+}  // namespace pager

@@ -1,0 +1,16 @@
+// CUDA-core (fp32 FMA) split kernels for __half KV, every supported head_dim.
+#include "split_inst.cuh"
+
+namespace pager {
+bool lookup_split_fma_f16(int head_dim, int mode, SplitKernelInfo* out) {
+  switch (head_dim) {
+    PAGER_MODE_CASES(__half, 8, BACKEND_FMA)
+    PAGER_MODE_CASES(__half, 16, BACKEND_FMA)
+    PAGER_MODE_CASES(__half, 32, BACKEND_FMA)
+    PAGER_MODE_CASES(__half, 64, BACKEND_FMA)
+    PAGER_MODE_CASES(__half, 128, BACKEND_FMA)
+    PAGER_MODE_CASES(__half, 256, BACKEND_FMA)
+    default: return false;
+  }
+}
+}  // namespace pager

@@ -1,0 +1,148 @@
+"""Generate the golden parity fixtures from the reference's own kernels.
+
+Run in a container that has the reference checkout (its path is the only
+argument, default ``/root/reference``)::
+
+    python tests/golden/make_golden.py /path/to/rust-llm-pager
+
+It imports the reference's ``pager_hf.streaming_attention`` under Triton's
+CPU interpreter (``TRITON_INTERPRET=1``, set before triton is imported) and
+replays, on the seeded inputs of ``cases.py``, the call sequences the
+reference itself makes (tests/test_streaming_attention.py,
+pager_hf/paged_model.py:993-1039, pager_hf/batched_decode.py:238-277).  Two
+limits of the interpreter are worked around and recorded in each fixture:
+
+* ``softcap > 0`` fails in the interpreter (``tl_libdevice.tanh`` returns
+  None, streaming_attention.py:160), so softcap cases use the reference's
+  own dense test oracle ``_dense_reference``
+  (tests/test_streaming_attention.py:20-40);
+* bf16 tensors come back as garbage (numpy has no bf16), so bf16 cases run
+  the reference on fp32 tensors holding the bf16 values; the P->bf16
+  rounding at streaming_attention.py:178 is therefore not in those vectors.
+
+Outputs go to ``tests/golden/<case>.npz``.  Nothing on the GPU box runs this.
+"""
+
+from __future__ import annotations
+
+import os
+import sys
+
+os.environ["TRITON_INTERPRET"] = "1"
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, HERE)
+from cases import CASES, batched_combined_layout, build_batched, build_contiguous, group_row_active, input_digest  # noqa: E402
+
+
+def _load_reference(ref_root):
+    sys.path.insert(0, ref_root)
+    sys.path.insert(0, os.path.join(ref_root, "tests"))
+    from pager_hf import streaming_attention as sa  # noqa: E402
+    import test_streaming_attention as ref_tests  # noqa: E402
+
+    return sa, ref_tests
+
+
+def _as_ref_dtype(t, c):
+    return t.float() if c["dtype"] == "bf16" else t
+
+
+def run_steps(sa, ref_tests, name, c):
+    q, k, v, valid, active = build_contiguous(c)
+    digest = input_digest([q, k, v, valid, active])
+    B, Hq, D, T = c["B"], c["Hq"], c["D"], c["T"]
+    note = "reference triton kernels (interpreter)"
+    if c.get("softcap"):
+        out, _ = ref_tests._dense_reference(
+            q, k, v, n_rep=Hq // c["Hkv"], tokens_per_block=16, valid=valid, scale=c.get("scale"),
+            softcap=c.get("softcap"),
+        )
+        note = "reference dense test oracle (interpreter cannot run softcap)"
+        return dict(out=out.float().numpy(), digest=digest, note=note)
+    qr, kr, vr = _as_ref_dtype(q, c), _as_ref_dtype(k, c), _as_ref_dtype(v, c)
+    m, l, acc = sa.streaming_attention_state_init(B, Hq, D, "cpu")
+    g = c["group"]
+    for s in range(0, T, g):
+        e = min(s + g, T)
+        sa.streaming_attention_step(qr, kr[:, :, s:e], vr[:, :, s:e], m, l, acc, valid=valid[:, s:e], active=active,
+                                    scale=c.get("scale"), softcap=c.get("softcap"))
+    out = sa.streaming_attention_finalize(acc, l, qr.dtype)
+    return dict(out=out.float().numpy(), m=m.numpy(), l=l.numpy(), acc=acc.numpy(), digest=digest, note=note)
+
+
+def run_two_pass(sa, ref_tests, name, c):
+    q, k, v, valid, active = build_contiguous(c)
+    digest = input_digest([q, k, v, valid, active])
+    q, k, v = _as_ref_dtype(q, c), _as_ref_dtype(k, c), _as_ref_dtype(v, c)
+    B, Hq, D, tpb, nb, tail = c["B"], c["Hq"], c["D"], c["tpb"], c["nb"], c["tail"]
+    full = nb * tpb
+    gt = c["group_blocks"] * tpb
+    act = active if c.get("active") else None
+    m, l, _ = sa.streaming_attention_state_init(B, Hq, D, "cpu")
+    for s in range(0, full, gt):
+        e = min(s + gt, full)
+        sa.streaming_attention_stats_step(q, k[:, :, s:e], m, l, valid=valid[:, s:e], active=act)
+    if tail:
+        sa.streaming_attention_stats_step(q, k[:, :, full:], m, l, valid=valid[:, full:])
+    acc = torch.zeros(B, Hq, D, dtype=torch.float32)
+    block_mass = torch.zeros(B, Hq, max(nb, 1), dtype=torch.float32)
+    for s in range(0, full, gt):
+        e = min(s + gt, full)
+        sa.streaming_attention_accumulate_step(q, k[:, :, s:e], v[:, :, s:e], m, l, acc, block_mass, s // tpb, tpb,
+                                               valid=valid[:, s:e], active=act)
+    if tail:
+        sa.streaming_attention_fold_fixed_step(q, k[:, :, full:], v[:, :, full:], m, l, acc, valid=valid[:, full:])
+    out = sa.streaming_attention_finalize(acc, l, q.dtype)
+    return dict(out=out.float().numpy(), m=m.numpy(), l=l.numpy(), acc=acc.numpy(),
+                block_mass=block_mass[:, :, :nb].numpy(), digest=digest,
+                note="reference triton kernels (interpreter)" + (" on fp32 copies of bf16 data" if c["dtype"] == "bf16" else ""))
+
+
+def run_batched(sa, ref_tests, name, c):
+    q, bk, bv, tk, tv = build_batched(c)
+    digest = input_digest([q] + bk + bv + tk + tv)
+    k, v, valid, pad_blocks, tail_k, tail_v = batched_combined_layout(c, bk, bv, tk, tv)
+    S, Hq, D, tpb = q.shape[0], c["Hq"], c["D"], c["tpb"]
+    max_blocks = max(c["nbs"])
+    group = c["group_blocks"]
+    m, l, acc = sa.streaming_attention_state_init(S, Hq, D, "cpu")
+    tail_valid = torch.ones(S, tail_k.shape[2], dtype=torch.int32)
+    positions = list(range(max_blocks))
+    for i in range(0, max_blocks, group):
+        n = len(positions[i:i + group])
+        sl = slice(i * tpb, (i + n) * tpb)
+        sa.streaming_attention_stats_step(q, k[:, :, sl], m, l, valid=valid[:, sl],
+                                          active=group_row_active(pad_blocks, i, n))
+    sa.streaming_attention_stats_step(q, tail_k, m, l, valid=tail_valid)
+    block_mass = torch.zeros(S, Hq, max(max_blocks, 1), dtype=torch.float32)
+    for i in range(0, max_blocks, group):
+        n = len(positions[i:i + group])
+        sl = slice(i * tpb, (i + n) * tpb)
+        sa.streaming_attention_accumulate_step(q, k[:, :, sl], v[:, :, sl], m, l, acc, block_mass, i, tpb,
+                                               valid=valid[:, sl], active=group_row_active(pad_blocks, i, n))
+    sa.streaming_attention_fold_fixed_step(q, tail_k, tail_v, m, l, acc, valid=tail_valid)
+    out = sa.streaming_attention_finalize(acc, l, q.dtype)
+    per_row = block_mass.mean(dim=1)  # batched_decode.py:273
+    session_mass = np.zeros((S, max(max_blocks, 1)), dtype=np.float32)
+    for row, nb in enumerate(c["nbs"]):
+        session_mass[row, :nb] = per_row[row, pad_blocks[row]:pad_blocks[row] + nb].numpy()
+    return dict(out=out.float().numpy(), m=m.numpy(), l=l.numpy(), acc=acc.numpy(),
+                session_mass=session_mass, digest=digest, note="reference triton kernels (interpreter)")
+
+
+def main():
+    ref_root = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+    sa, ref_tests = _load_reference(ref_root)
+    runners = {"steps": run_steps, "two_pass": run_two_pass, "batched": run_batched}
+    for name, c in CASES.items():
+        res = runners[c["kind"]](sa, ref_tests, name, c)
+        np.savez_compressed(os.path.join(HERE, f"{name}.npz"), **res)
+        print(f"{name}: {sorted(res)}")
+
+
+if __name__ == "__main__":
+    main()

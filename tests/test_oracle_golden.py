@@ -1,0 +1,136 @@
+"""Pin the CPU oracle against vectors produced by the reference's own kernels.
+
+The fixtures under tests/golden/ were produced by tests/golden/make_golden.py,
+which replays the reference's call sequences through its Triton kernels on the
+CPU.  The oracle (numpy restatement) must reproduce them to fp32 rounding.
+"""
+
+import numpy as np
+import pytest
+
+import golden_io as gio
+from cases import CASES, batched_combined_layout, build_batched, build_contiguous, group_row_active, input_digest
+from oracle import streaming_attention_oracle as orc
+
+TOL = dict(rtol=2e-5, atol=2e-6)
+
+
+def _vdt(c):
+    # bf16 fixtures ran the reference on fp32 copies, so P is not rounded to bf16 there
+    return "f32" if c["dtype"] == "bf16" else c["dtype"]
+
+
+def _run_steps(c, q, k, v, valid, active):
+    B, Hq, D, T = c["B"], c["Hq"], c["D"], c["T"]
+    m, l, acc = orc.state_init(B, Hq, D)
+    g = c["group"]
+    for s in range(0, T, g):
+        e = min(s + g, T)
+        orc.step(q, k[:, :, s:e], v[:, :, s:e], m, l, acc, valid=valid[:, s:e], active=active,
+                 scale=c.get("scale"), softcap=c.get("softcap"), v_dtype=_vdt(c))
+    return m, l, acc
+
+
+def _run_two_pass(c, q, k, v, valid, active):
+    B, Hq, D, tpb, nb, tail = c["B"], c["Hq"], c["D"], c["tpb"], c["nb"], c["tail"]
+    full, gt = nb * tpb, c["group_blocks"] * tpb
+    act = active if c.get("active") else None
+    m, l, acc = orc.state_init(B, Hq, D)
+    for s in range(0, full, gt):
+        e = min(s + gt, full)
+        orc.stats_step(q, k[:, :, s:e], m, l, valid=valid[:, s:e], active=act)
+    if tail:
+        orc.stats_step(q, k[:, :, full:], m, l, valid=valid[:, full:])
+    bm = np.zeros((B, Hq, max(nb, 1)), np.float32)
+    for s in range(0, full, gt):
+        e = min(s + gt, full)
+        orc.accumulate_step(q, k[:, :, s:e], v[:, :, s:e], m, l, acc, bm, s // tpb, tpb, valid=valid[:, s:e],
+                            active=act, v_dtype=_vdt(c))
+    if tail:
+        orc.fold_fixed_step(q, k[:, :, full:], v[:, :, full:], m, l, acc, valid=valid[:, full:], v_dtype=_vdt(c))
+    return m, l, acc, bm[:, :, :nb]
+
+
+@pytest.mark.parametrize("name", [n for n, c in CASES.items() if c["kind"] in ("steps", "two_pass")])
+def test_oracle_matches_reference_golden(name):
+    c = CASES[name]
+    g = gio.load(name)
+    q, k, v, valid, active = build_contiguous(c)
+    assert input_digest([q, k, v, valid, active]) == str(g["digest"]), "seeded input generator drifted"
+    qn, kn, vn = gio.np32(q), gio.np32(k), gio.np32(v)
+    validn, activen = valid.numpy(), active.numpy()
+    if c.get("softcap"):
+        out, _ = orc.dense_reference(qn, kn, vn, c["Hq"] // c["Hkv"], 16, valid=validn, scale=c["scale"],
+                                     softcap=c["softcap"])
+        np.testing.assert_allclose(orc.round_to(out, c["dtype"]), g["out"], rtol=1e-3, atol=1e-3)
+        # and the online restatement agrees with the dense one on softcap
+        m, l, acc = _run_steps(c, qn, kn, vn, validn, activen)
+        np.testing.assert_allclose(orc.finalize(acc, l, c["dtype"]), g["out"], rtol=2e-3, atol=2e-3)
+        return
+    if c["kind"] == "steps":
+        m, l, acc = _run_steps(c, qn, kn, vn, validn, activen)
+    else:
+        m, l, acc, bm = _run_two_pass(c, qn, kn, vn, validn, activen)
+        np.testing.assert_allclose(bm, g["block_mass"], **TOL)
+    np.testing.assert_allclose(m, g["m"], **TOL)
+    np.testing.assert_allclose(l, g["l"], **TOL)
+    # acc is unnormalised; single P->f16 rounding flips (one ulp of a 2^-11-relative cast) are expected
+    np.testing.assert_allclose(acc, g["acc"], rtol=1e-4, atol=2e-3)
+    out_dt = "f32" if c["dtype"] == "bf16" else c["dtype"]
+    np.testing.assert_allclose(orc.finalize(acc, l, out_dt), g["out"], rtol=1e-3, atol=2e-4)
+
+
+def test_oracle_matches_batched_sessions_golden():
+    name = "batched_sessions_f16"
+    c = CASES[name]
+    g = gio.load(name)
+    q, bk, bv, tk, tv = build_batched(c)
+    assert input_digest([q] + bk + bv + tk + tv) == str(g["digest"])
+    k, v, valid, pad_blocks, tail_k, tail_v = batched_combined_layout(c, bk, bv, tk, tv)
+    qn, kn, vn, tkn, tvn = map(gio.np32, (q, k, v, tail_k, tail_v))
+    S, Hq, D, tpb, group = qn.shape[0], c["Hq"], c["D"], c["tpb"], c["group_blocks"]
+    max_blocks = max(c["nbs"])
+    m, l, acc = orc.state_init(S, Hq, D)
+    validn = valid.numpy()
+    for i in range(0, max_blocks, group):
+        n = min(group, max_blocks - i)
+        sl = slice(i * tpb, (i + n) * tpb)
+        orc.stats_step(qn, kn[:, :, sl], m, l, valid=validn[:, sl], active=group_row_active(pad_blocks, i, n).numpy())
+    orc.stats_step(qn, tkn, m, l)
+    bm = np.zeros((S, Hq, max_blocks), np.float32)
+    for i in range(0, max_blocks, group):
+        n = min(group, max_blocks - i)
+        sl = slice(i * tpb, (i + n) * tpb)
+        orc.accumulate_step(qn, kn[:, :, sl], vn[:, :, sl], m, l, acc, bm, i, tpb, valid=validn[:, sl],
+                            active=group_row_active(pad_blocks, i, n).numpy(), v_dtype="f16")
+    orc.fold_fixed_step(qn, tkn, tvn, m, l, acc, v_dtype="f16")
+    np.testing.assert_allclose(m, g["m"], **TOL)
+    np.testing.assert_allclose(l, g["l"], **TOL)
+    np.testing.assert_allclose(acc, g["acc"], rtol=1e-4, atol=2e-3)
+    np.testing.assert_allclose(orc.finalize(acc, l, "f16"), g["out"], rtol=1e-3, atol=1e-3)
+    per_row = bm.mean(axis=1)
+    for row, nb in enumerate(c["nbs"]):
+        np.testing.assert_allclose(per_row[row, pad_blocks[row]:pad_blocks[row] + nb], g["session_mass"][row, :nb],
+                                   **TOL)
+
+
+def test_oracle_two_pass_equals_one_pass_and_dense():
+    """Size-independent identities the oracle must satisfy: two-pass == one-pass == dense softmax."""
+    rng = np.random.default_rng(3)
+    q = rng.standard_normal((2, 8, 32)).astype(np.float32)
+    k = rng.standard_normal((2, 2, 300, 32)).astype(np.float32)
+    v = rng.standard_normal((2, 2, 300, 32)).astype(np.float32)
+    m, l, acc = orc.state_init(2, 8, 32)
+    orc.step(q, k, v, m, l, acc)
+    out1 = orc.finalize(acc, l, "f32")
+    out2, mass2, _, _ = orc.two_pass_decode(q, k[:, :, :256], v[:, :, :256], k[:, :, 256:], v[:, :, 256:],
+                                            num_blocks=16, tokens_per_block=16, group_size_blocks=5)
+    dense, dmass = orc.dense_reference(q, k, v, 4, 16)
+    np.testing.assert_allclose(out1, dense, rtol=1e-4, atol=1e-5)
+    np.testing.assert_allclose(out2, dense, rtol=1e-4, atol=1e-5)
+    np.testing.assert_allclose(mass2, dmass[:, :, :16], rtol=1e-4, atol=1e-6)
+
+
+def test_oracle_n_rep_guard():
+    with pytest.raises(NotImplementedError):
+        orc.validate_n_rep(17)

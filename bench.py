@@ -1,0 +1,519 @@
+#!/usr/bin/env python
+"""Decode-attention benchmark: effective KV GB/s against the HBM + host-link roofline.
+
+One *step* is one decode step of attention over every layer of a model for a
+batch of requests at long context: per layer, one fused paged decode-attention
+call (split-KV kernel + combine + mass) walks each request's block table over
+the device KV pool (HBM) and the pinned host pool (read zero-copy over the
+host link), plus its tail, and writes the attention output and the per-block
+attention mass the heavy-hitter policies consume.
+
+Default workload ("cfg5-32k"): the Llama-3-8B attention geometry of the
+reference's serving config (32 layers, 32 query / 8 KV heads, head_dim 128,
+bf16, 64-token blocks) with 12 concurrent requests at a 32,768-token context
+per GPU and a 40 GB per-GPU HBM KV budget; the most recent blocks of each
+request stay in HBM (recent_only placement) and the rest sit in the pinned
+host pool.  KV values are seeded synthetic data (no checkpoints offline).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload NAME] [--impl ours|reference]
+
+N > 1 runs one process per GPU (torchrun); requests are sharded across GPUs
+(weak scaling, no collective on the data path); the timed region is bracketed
+by barriers and its time is the max over ranks.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+for _p in (ROOT, os.path.join(ROOT, "rust-llm-pager_b200")):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+METRIC = "decode-attn effective KV GB/s (HBM + host tiers) at 32k ctx"
+
+WORKLOADS = {
+    # BASELINE config 5 geometry at 32k: 40 GB HBM budget, overflow in the pinned host pool
+    "cfg5-32k": dict(model="Llama-3-8B attention (L32, Hq32, Hkv8, D128)", layers=32, hq=32, hkv=8, d=128,
+                     dtype="bf16", tpb=64, batch=12, context=32768, hbm_budget_gb=40.0, window=None),
+    # same geometry, everything resident in HBM (8 x 4 GiB < 40 GB)
+    "hbm-32k": dict(model="Llama-3-8B attention (L32, Hq32, Hkv8, D128)", layers=32, hq=32, hkv=8, d=128,
+                    dtype="bf16", tpb=64, batch=8, context=32768, hbm_budget_gb=40.0, window=None),
+    # Mistral-7B, B8 x 32k, sliding window 4096, 5% resident (sinks + recent)
+    "cfg4-32k-window": dict(model="Mistral-7B attention (L32, Hq32, Hkv8, D128, window 4096)", layers=32, hq=32,
+                            hkv=8, d=128, dtype="bf16", tpb=64, batch=8, context=32768, resident_frac=0.05,
+                            sinks=4, window=4096),
+}
+
+
+# ----------------------------------------------------------------------------- helpers
+def _dist_env():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled every 200 ms during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device):
+        import torch
+
+        p = torch.cuda.get_device_properties(device)
+        self.gpu = f"{p.pci_domain_id:08X}:{p.pci_bus_id:02X}:{p.pci_device_id:02X}.0"
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        self.lines = []
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [ln for ln in out.splitlines() if ln.strip()]
+
+    def summary(self):
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in getattr(self, "lines", []):
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax = float(parts[2])
+            except ValueError:
+                continue
+            for name, val in zip(names, parts[5:9]):
+                if val.lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def measured_peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured (MEASURED_PEAKS.json)"
+    except (OSError, KeyError, ValueError):
+        return 6650.0, "fallback 6.65 TB/s"
+
+
+# ----------------------------------------------------------------------------- workload
+class Workload:
+    """Device pool, pinned host pool, block tables, tails and queries for one GPU's share."""
+
+    def __init__(self, name: str, device, seed: int):
+        import torch
+
+        from pager_hf import _lib
+        from pager_hf.host_pool import HostPool
+        from pager_hf.streaming_attention import PagedDecodePlan
+
+        w = WORKLOADS[name]
+        self.name, self.w = name, w
+        self.device = device
+        self.L, self.Hq, self.Hkv, self.D, self.tpb = w["layers"], w["hq"], w["hkv"], w["d"], w["tpb"]
+        self.B, self.ctx = w["batch"], w["context"]
+        self.dtype = {"bf16": torch.bfloat16, "f16": torch.float16}[w["dtype"]]
+        elt = 2
+        nb = self.ctx // self.tpb
+        self.nb = nb
+        self.slot_bytes = self.L * 2 * self.Hkv * self.tpb * self.D * elt
+        g = torch.Generator(device="cpu").manual_seed(seed)
+        tails = torch.randint(1, self.tpb + 1, (self.B,), generator=g).tolist()
+        self.tails = tails
+        # residency per row: which block indices live in HBM
+        resident = []
+        if "hbm_budget_gb" in w:
+            per_row = min(nb, int(w["hbm_budget_gb"] * 1e9 // self.slot_bytes) // self.B)
+            for _ in range(self.B):
+                resident.append(set(range(nb - per_row, nb)))  # recent_only: newest blocks
+        else:
+            per_row = max(1, int(math.ceil(w["resident_frac"] * nb)))
+            sinks = min(w.get("sinks", 0), per_row)
+            for _ in range(self.B):
+                resident.append(set(range(sinks)) | set(range(nb - (per_row - sinks), nb)))
+        dev_slots = sum(len(r) for r in resident)
+        host_slots = self.B * nb - dev_slots
+        shape = (self.L, 2, self.Hkv, self.tpb, self.D)
+        self.dev_pool = torch.empty((max(dev_slots, 1),) + shape, dtype=self.dtype, device=device)
+        self.dev_pool.normal_(generator=torch.Generator(device=device).manual_seed(seed + 1))
+        self.host = HostPool((max(host_slots, 1),) + shape, self.dtype) if host_slots else None
+        if self.host is not None:
+            self._fill_host(seed + 2)
+        table = torch.full((self.B, nb), -1, dtype=torch.int32)
+        d_next = h_next = 0
+        self.dev_tokens = self.host_tokens = 0
+        window = w.get("window")
+        lo = []
+        for b in range(self.B):
+            ntok = nb * self.tpb + tails[b]
+            row_lo = max(0, ntok - window) if window else 0
+            lo.append(row_lo)
+            for j in range(nb):
+                if j in resident[b]:
+                    table[b, j] = d_next
+                    d_next += 1
+                    where = "dev"
+                else:
+                    table[b, j] = h_next | _lib.HOST_SLOT_BIT
+                    h_next += 1
+                    where = "host"
+                # tokens of this block that the window keeps (all of them without a window)
+                t0, t1 = j * self.tpb, (j + 1) * self.tpb
+                n_valid = max(0, t1 - max(t0, row_lo))
+                if where == "dev":
+                    self.dev_tokens += n_valid
+                else:
+                    self.host_tokens += n_valid
+        self.tail_tokens = sum(tails)
+        self.table = table.to(device)
+        self.num_blocks = torch.full((self.B,), nb, dtype=torch.int32, device=device)
+        self.tail_len = torch.tensor(tails, dtype=torch.int32, device=device)
+        self.valid_lo = torch.tensor(lo, dtype=torch.int32, device=device) if window else None
+        gd = torch.Generator(device=device).manual_seed(seed + 3)
+        self.tail_k = torch.randn(self.B, self.Hkv, self.tpb, self.D, generator=gd, device=device).to(self.dtype)
+        self.tail_v = torch.randn(self.B, self.Hkv, self.tpb, self.D, generator=gd, device=device).to(self.dtype)
+        self.q = torch.randn(self.L, self.B, self.Hq, self.D, generator=gd, device=device).to(self.dtype)
+        self.out = torch.empty_like(self.q)
+        self.mass = torch.zeros(self.B, nb, dtype=torch.float32, device=device)
+        self.max_row_tokens = nb * self.tpb + self.tpb
+        self.plan = PagedDecodePlan(
+            batch=self.B, num_query_heads=self.Hq, dev_pool=self.dev_pool,
+            host_pool=None if self.host is None else self.host.tensor, num_layers=self.L, tokens_per_block=self.tpb,
+            block_table=self.table, num_blocks=self.num_blocks, max_row_tokens=self.max_row_tokens,
+            tail_k=self.tail_k, tail_v=self.tail_v, tail_len=self.tail_len, valid_lo=self.valid_lo,
+            mass_accum=self.mass, mass_mode="row_mean")
+        # algorithmic bytes per step (only attended tokens are counted)
+        kv_tok = 2 * self.Hkv * self.D * elt
+        qo = 2 * self.B * self.Hq * self.D * elt
+        mass_b = self.B * nb * 4 * 2  # read-modify-write of the mass accumulator
+        self.hbm_bytes = self.L * ((self.dev_tokens + self.tail_tokens) * kv_tok + qo + mass_b)
+        self.host_bytes = self.L * self.host_tokens * kv_tok
+        self.bytes_per_step = self.hbm_bytes + self.host_bytes
+        self.launches_per_step = self.L * 3  # split + combine + mass kernels per layer
+
+    def _fill_host(self, seed):
+        import torch
+
+        flat = self.host.tensor.view(-1)
+        chunk = 1 << 27
+        src = torch.empty(chunk, dtype=self.dtype, device=self.device)
+        src.normal_(generator=torch.Generator(device=self.device).manual_seed(seed))
+        for s in range(0, flat.numel(), chunk):
+            n = min(chunk, flat.numel() - s)
+            flat[s:s + n].copy_(src[:n], non_blocking=False)
+
+    def step(self, events=None):
+        self.mass.zero_()
+        for layer in range(self.L):
+            if events is not None:
+                events[layer][0].record()
+            self.plan.run(self.q[layer], layer, self.out[layer])
+            if events is not None:
+                events[layer][1].record()
+
+    def close(self):
+        if self.host is not None:
+            self.host.close()
+            self.host = None
+
+
+def probe_link(wl, device):
+    """Measured host->device link: best of pinned cudaMemcpyAsync and zero-copy kernel reads (GB/s)."""
+    import ctypes
+
+    import torch
+
+    from pager_hf import _lib
+
+    if wl.host is None:
+        return {"copy_gbs": None, "zero_copy_gbs": None}
+    nbytes = min(1 << 30, wl.host.nbytes) // 16 * 16
+    dst = torch.empty(nbytes, dtype=torch.uint8, device=device)
+    stream = torch.cuda.current_stream(device).cuda_stream
+    c, z = ctypes.c_double(), ctypes.c_double()
+    _lib.check(_lib.lib().pager_probe_h2d_copy_gbs(wl.host.data_ptr, dst.data_ptr(), nbytes, 5, stream, ctypes.byref(c)))
+    _lib.check(_lib.lib().pager_probe_zero_copy_gbs(wl.host.data_ptr, dst.data_ptr(), nbytes, 5, stream,
+                                                    ctypes.byref(z)))
+    del dst
+    return {"copy_gbs": c.value, "zero_copy_gbs": z.value, "probe_bytes": nbytes}
+
+
+# ----------------------------------------------------------------------------- CPU oracle arm
+_CPU_UNIT = None
+
+
+def _cpu_unit_init(args):
+    """Pool initializer: build one (request, layer) unit of the workload in this process (untimed)."""
+    import numpy as np
+
+    global _CPU_UNIT
+    sys.path.insert(0, ROOT)
+    from oracle import streaming_attention_oracle as orc
+
+    hkv, hq, d, tpb, nb, tail, lo, seed = args
+    rng = np.random.default_rng(seed)
+    t = nb * tpb
+    mk = lambda *shape: orc.round_to(rng.standard_normal(shape, dtype=np.float32), "bf16")  # noqa: E731
+    valid = np.ones((1, t), np.int32)
+    valid[:, :lo] = 0
+    _CPU_UNIT = dict(q=mk(1, hq, d), k=mk(1, hkv, t, d), v=mk(1, hkv, t, d), tk=mk(1, hkv, tail, d),
+                     tv=mk(1, hkv, tail, d), valid=valid, tpb=tpb,
+                     bytes=(t - lo + tail) * 2 * hkv * d * 2)
+
+
+def _cpu_unit_run(reps):
+    """Time `reps` decode-attention calls of this process's unit through the CPU oracle."""
+    from oracle import streaming_attention_oracle as orc
+
+    u = _CPU_UNIT
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        orc.dense_decode_gqa(u["q"], u["k"], u["v"], u["tk"], u["tv"], u["tpb"], valid=u["valid"])
+    return u["bytes"] * reps, time.perf_counter() - t0
+
+
+class CpuOracleArm:
+    """The reference's decode attention restated on the CPU (oracle/), one single-threaded process per host core.
+
+    Each process holds one (request, layer) unit of the workload at the full
+    context and times ``reps`` calls; a sample runs every process at once and
+    reports KV bytes over wall time.
+    """
+
+    def __init__(self, wl_name: str, procs: int | None = None, reps: int = 4):
+        import multiprocessing as mp
+
+        w = WORKLOADS[wl_name]
+        self.w = w
+        self.reps = reps
+        self.procs = procs or os.cpu_count() or 1
+        nb = w["context"] // w["tpb"]
+        window = w.get("window")
+        lo = max(0, nb * w["tpb"] + 32 - window) if window else 0
+        for var in ("OMP_NUM_THREADS", "OPENBLAS_NUM_THREADS", "MKL_NUM_THREADS"):
+            os.environ[var] = "1"  # one core per process; the processes provide the parallelism
+        ctx = mp.get_context("spawn")
+        self.pool = ctx.Pool(self.procs, initializer=_cpu_unit_init,
+                             initargs=((w["hkv"], w["hq"], w["d"], w["tpb"], nb, 32, lo, 1000),))
+        self.pool.map(_cpu_unit_run, [1] * self.procs)  # warm-up
+
+    def sample(self):
+        t0 = time.perf_counter()
+        res = self.pool.map(_cpu_unit_run, [self.reps] * self.procs, chunksize=1)
+        wall = time.perf_counter() - t0
+        return sum(r[0] for r in res), wall
+
+    def close(self):
+        self.pool.terminate()
+        self.pool.join()
+
+
+def sample_desc(arm):
+    w = arm.w
+    return (f"{arm.procs} processes x {arm.reps} calls, each one (request, layer) of the workload at "
+            f"{w['context']} tokens; numpy restatement of the reference's dense decode attention with "
+            f"per-block mass, 1 BLAS thread per process")
+
+
+# ----------------------------------------------------------------------------- arms
+def run_reference_arm(args):
+    world, rank, _ = _dist_env()
+    if world > 1 and rank != 0:
+        return 0
+    arm = CpuOracleArm(args.workload)
+    try:
+        for _ in range(args.warmup):
+            arm.sample()
+        tot_b, tot_t = 0, 0.0
+        for _ in range(args.steps):
+            b, t = arm.sample()
+            tot_b += b
+            tot_t += t
+    finally:
+        arm.close()
+    gbs = tot_b / tot_t / 1e9
+    w = WORKLOADS[args.workload]
+    line = {
+        "impl": "reference", "metric": METRIC, "value": gbs, "unit": "GB/s", "n_gpus": args.gpus, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": 1000 * tot_t / args.steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": w["dtype"], "data": "synthetic (seeded random KV)",
+        "config": {"workload": args.workload, "model": w["model"], "context": w["context"]},
+        "cpu_baseline": {"value": gbs, "unit": "GB/s", "cores": arm.procs, "kind": "port", "sample": sample_desc(arm)},
+        "e2e": {"value": gbs, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "reference path = the reference's Triton/torch algorithm restated on the CPU (oracle/); the "
+                "reference ships no compiled CPU implementation",
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    world, rank, local = _dist_env()
+    if world > 1:
+        torch.cuda.set_device(local)
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", init_method="env://", timeout=timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    w = WORKLOADS[args.workload]
+    wl = Workload(args.workload, device, seed=1234 + rank)
+    link = probe_link(wl, device)
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local])
+        torch.cuda.synchronize(device)
+
+    # warm-up (also first-call setup: occupancy queries, smem attributes)
+    for _ in range(max(args.warmup, 1)):
+        wl.step()
+    barrier()
+    events = [[torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)] for _ in range(wl.L)]
+    per_launch = []
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(device) as clk:
+        barrier()
+        start.record()
+        for _ in range(args.steps):
+            wl.step(events)
+            # per-launch durations of this step (events stay on the launching stream)
+            end.record()
+            end.synchronize()
+            per_launch.extend(e0.elapsed_time(e1) for e0, e1 in events)
+        end.record()
+        barrier()
+    # The per-step synchronize above lets the event timings be read; it costs one
+    # host round trip per step (a few microseconds against a ~100 ms step).
+    ms_total = start.elapsed_time(end)
+    t = torch.tensor([ms_total], dtype=torch.float64, device=device)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_total = float(t.item())
+    ms_step = ms_total / args.steps
+    value = world * wl.bytes_per_step / (ms_step / 1000) / 1e9
+    tokens_per_s = world * wl.B / (ms_step / 1000)
+
+    # end-to-end through the public API with host buffers: q from pinned host memory in, output + mass out
+    q_host = wl.q.cpu().pin_memory()
+    out_host = torch.empty(wl.out.shape, dtype=wl.out.dtype).pin_memory()
+    mass_host = torch.empty(wl.mass.shape, dtype=torch.float32).pin_memory()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        wl.q.copy_(q_host, non_blocking=True)
+        wl.step()
+        out_host.copy_(wl.out, non_blocking=True)
+        mass_host.copy_(wl.mass, non_blocking=True)
+    e1.record()
+    barrier()
+    e2e_ms = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=device)
+    if world > 1:
+        dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
+    e2e_step = float(e2e_ms.item()) / args.steps
+    e2e_value = world * wl.bytes_per_step / (e2e_step / 1000) / 1e9
+
+    hbm_peak, peak_src = measured_peaks()
+    h2d = max([x for x in (link.get("copy_gbs"), link.get("zero_copy_gbs")) if x] or [0.0])
+    launch_ms = statistics.mean(per_launch)
+    bytes_per_launch = wl.bytes_per_step / wl.L
+    achieved = bytes_per_launch / (launch_ms / 1000) / 1e9
+    t_roof = wl.hbm_bytes / wl.L / (hbm_peak * 1e9) + (wl.host_bytes / wl.L / (h2d * 1e9) if wl.host_bytes else 0.0)
+    combined_peak = bytes_per_launch / t_roof / 1e9
+    clocks = clk.summary()
+    line = {
+        "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": w["dtype"],
+        "data": "synthetic: seeded random KV in the workload's geometry (no checkpoints offline)",
+        "config": {
+            "workload": args.workload, "model": w["model"], "batch_per_gpu": wl.B, "global_batch": wl.B * world,
+            "context": wl.ctx, "tokens_per_block": wl.tpb, "layers": wl.L,
+            "hbm_kv_gb": round(wl.dev_pool.numel() * 2 / 1e9, 2),
+            "host_pool_gb": round((wl.host.nbytes if wl.host else 0) / 1e9, 2),
+            "hbm_bytes_per_step": wl.hbm_bytes, "host_bytes_per_step": wl.host_bytes,
+            "l2": "inputs larger than L2 (KV per step >> 126 MB), no flush",
+            "parallelism": f"request-sharded x{world}, no collectives on the data path",
+        },
+        "decode_tokens_per_s": tokens_per_s,
+        "roofline": {
+            "bound": "hbm", "achieved": achieved, "peak": combined_peak, "unit": "GB/s",
+            "frac": achieved / combined_peak, "traffic": None,
+            "kernel": "paged decode attention (split-KV + combine + mass) per layer",
+            "peak_kind": f"combined roofline: HBM {hbm_peak:.0f} GB/s ({peak_src}) + host link {h2d:.1f} GB/s "
+                         f"(measured live); peak = bytes / (hbm_bytes/HBM + host_bytes/link)",
+            "launch_ms": launch_ms, "bytes_per_launch": bytes_per_launch,
+        },
+        "host_link": link,
+        "e2e": {"value": e2e_value, "unit": "GB/s", "ms_per_step": e2e_step,
+                "h2d_bytes_per_step": q_host.numel() * q_host.element_size(),
+                "d2h_bytes_per_step": out_host.numel() * out_host.element_size() + mass_host.numel() * 4},
+        "gpu_launches": wl.launches_per_step * args.steps,
+        "clocks": clocks,
+    }
+    wl.close()
+    if world > 1:
+        dist.barrier(device_ids=[local])
+        dist.destroy_process_group()
+    if rank == 0:
+        if world == 1 and not args.no_cpu_baseline:
+            arm = CpuOracleArm(args.workload)
+            try:
+                b, t_cpu = arm.sample()
+            finally:
+                arm.close()
+            line["cpu_baseline"] = {"value": b / t_cpu / 1e9, "unit": "GB/s", "cores": arm.procs, "kind": "port",
+                                    "sample": sample_desc(arm)}
+        print(json.dumps(line), flush=True)
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--workload", default="cfg5-32k", choices=sorted(WORKLOADS))
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        return run_reference_arm(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -317,3 +317,35 @@ def gather_paged_kv(pool_k, pool_v, block_table_row, layer):
         shape = (pool_k.shape[2], 0, pool_k.shape[4])
         return np.zeros(shape, _F32), np.zeros(shape, _F32)
     return np.concatenate(ks, axis=1), np.concatenate(vs, axis=1)
+
+
+def dense_decode_gqa(q, k, v, tail_k, tail_v, tokens_per_block, valid=None, scale=None):
+    """Dense decode attention + per-block mass without materialising the GQA repeat.
+
+    The same mathematics as ``dense_reference`` (the reference's dense test
+    oracle, tests/test_streaming_attention.py:20-40: softmax over all valid
+    tokens, per-``tokens_per_block`` mass) on blocks followed by a tail, with
+    the n_rep query heads of a KV head handled as one matrix product per KV
+    head.  This is the CPU path the benchmark times as the reference arm.
+    q [1, Hq, D]; k/v [1, Hkv, T, D]; tail_k/tail_v [1, Hkv, t, D]; valid [1, T]
+    over the block tokens.  Returns (out [1, Hq, D], block_mass [1, Hq, T/tpb]).
+    """
+    _, hq, d = q.shape
+    hkv = k.shape[1]
+    n_rep = hq // hkv
+    if scale is None:
+        scale = 1.0 / (d**0.5)
+    qg = np.asarray(q, _F32).reshape(hkv, n_rep, d)
+    kk = np.concatenate([k[0], tail_k[0]], axis=1)  # [Hkv, T+t, D]
+    vv = np.concatenate([v[0], tail_v[0]], axis=1)
+    s = np.matmul(qg, np.swapaxes(kk, 1, 2)) * _F32(scale)  # [Hkv, n_rep, T+t]
+    nblk = k.shape[2]
+    if valid is not None:
+        s[:, :, :nblk][:, :, np.asarray(valid)[0] == 0] = -np.inf
+    s -= s.max(axis=-1, keepdims=True)
+    np.exp(s, out=s)
+    s /= s.sum(axis=-1, keepdims=True)
+    out = np.matmul(s, vv).reshape(1, hq, d)
+    nb = nblk // tokens_per_block
+    mass = s[:, :, : nb * tokens_per_block].reshape(hkv, n_rep, nb, tokens_per_block).sum(-1).reshape(1, hq, nb)
+    return out, mass

@@ -390,3 +390,73 @@ def paged_decode_attention(
             L.ptr(block_mass), L.ptr(mass_accum), mode, _BACKEND, scratch.data_ptr(), scratch.numel(),
             L.stream_of(q)))
     return out
+
+
+class PagedDecodePlan:
+    """A validated, reusable call of ``paged_decode_attention`` for one decode step.
+
+    Everything that is fixed across the layers of a step (pools, block table,
+    row lengths, tails, ranges, scratch) is checked and bound once; each
+    ``run(q, layer, out)`` then goes straight to the C ABI.  This keeps the
+    per-layer host cost at one ctypes call, so a step can also be captured in a
+    CUDA graph.
+    """
+
+    def __init__(self, *, batch, num_query_heads, dev_pool, host_pool, num_layers, tokens_per_block, block_table,
+                 num_blocks, max_row_tokens, tail_k=None, tail_v=None, tail_len=None, valid_lo=None, valid_hi=None,
+                 active=None, scale=None, softcap=None, q_dtype=None, block_mass=None, mass_accum=None,
+                 mass_mode="none"):
+        pool = dev_pool if dev_pool is not None else host_pool
+        if pool is None or pool.dim() != 6:
+            raise ValueError("a [slots, layers, 2, kv_heads, tokens_per_block, head_dim] pool is required")
+        self.B, self.Hq = int(batch), int(num_query_heads)
+        self.Hkv, self.D = pool.shape[3], pool.shape[5]
+        if self.Hq % self.Hkv:
+            raise ValueError(f"num_query_heads ({self.Hq}) is not a multiple of num_kv_heads ({self.Hkv})")
+        _validate_n_rep(self.Hq // self.Hkv)
+        device = block_table.device
+        _require_cuda(block_table=block_table, num_blocks=num_blocks, dev_pool=dev_pool, tail_k=tail_k, tail_v=tail_v,
+                      tail_len=tail_len, valid_lo=valid_lo, valid_hi=valid_hi, active=active,
+                      block_mass=block_mass, mass_accum=mass_accum)
+        if block_table.dtype != torch.int32 or tuple(block_table.shape[:1]) != (self.B,):
+            raise ValueError("block_table must be int32 [batch, max_blocks]")
+        self._keep = [block_table.contiguous(), _mask(num_blocks), _mask(tail_len), _mask(valid_lo), _mask(valid_hi),
+                      _mask(active), dev_pool, host_pool]
+        self.block_table, self.num_blocks, self.tail_len, self.valid_lo, self.valid_hi, self.active = self._keep[:6]
+        self.tail_k = None if tail_k is None else _aligned(tail_k)
+        self.tail_v = None if tail_v is None else _aligned(tail_v)
+        self._keep += [self.tail_k, self.tail_v]
+        self.dev_pool, self.host_pool = dev_pool, host_pool
+        self.num_layers, self.tpb = int(num_layers), int(tokens_per_block)
+        self.max_blocks = self.block_table.shape[1]
+        self.max_row_tokens = int(max_row_tokens)
+        self.scale = float(scale if scale is not None else 1.0 / (self.D**0.5))
+        self.softcap = float(softcap or 0.0)
+        self.kv_dtype = _dtype_code(pool, "pool")
+        self.q_dtype = self.kv_dtype if q_dtype is None else L.DTYPE_CODE[q_dtype]
+        self.block_mass, self.mass_accum = block_mass, mass_accum
+        self.mass_mode = _MASS_MODES[mass_mode]
+        lib = L.lib()
+        with torch.cuda.device(device):
+            nbytes = lib.pager_paged_decode_scratch_bytes(self.B, self.Hq, self.Hkv, self.D, self.kv_dtype, self.tpb,
+                                                          self.max_blocks, self.max_row_tokens)
+        self.scratch = _scratch(nbytes, device)
+        self.device = device
+        self._fn = lib.pager_paged_decode_attention
+        self._static = (
+            L.ptr(dev_pool), 0 if dev_pool is None else dev_pool.shape[0], L.ptr(host_pool),
+            0 if host_pool is None else host_pool.shape[0], self.kv_dtype, self.num_layers)
+
+    def run(self, q: torch.Tensor, layer: int, out: torch.Tensor, stream: int | None = None) -> torch.Tensor:
+        dp, ds, hp, hs, kvd, nl = self._static
+        rc = self._fn(
+            q.data_ptr(), self.q_dtype, dp, ds, hp, hs, kvd, nl, layer, self.Hkv, self.tpb, self.D,
+            self.block_table.data_ptr(), self.max_blocks, self.num_blocks.data_ptr(), L.ptr(self.tail_k),
+            L.ptr(self.tail_v), L.ptr(self.tail_len), 0 if self.tail_k is None else self.tail_k.shape[2],
+            L.ptr(self.valid_lo), L.ptr(self.valid_hi), L.ptr(self.active), self.B, self.Hq, self.scale, self.softcap,
+            self.max_row_tokens, out.data_ptr(), L.DTYPE_CODE[out.dtype], L.ptr(self.block_mass),
+            L.ptr(self.mass_accum), self.mass_mode, _BACKEND, self.scratch.data_ptr(), self.scratch.numel(),
+            torch.cuda.current_stream(self.device).cuda_stream if stream is None else stream)
+        if rc:
+            L.check(rc)
+        return out

@@ -134,3 +134,19 @@ def test_oracle_two_pass_equals_one_pass_and_dense():
 def test_oracle_n_rep_guard():
     with pytest.raises(NotImplementedError):
         orc.validate_n_rep(17)
+
+
+def test_dense_gqa_cpu_path_equals_two_pass():
+    """The CPU timing path (dense, GQA-grouped) computes what the two-pass reference sequence computes."""
+    rng = np.random.default_rng(9)
+    q = rng.standard_normal((1, 8, 32)).astype(np.float32)
+    k = rng.standard_normal((1, 2, 128, 32)).astype(np.float32)
+    v = rng.standard_normal((1, 2, 128, 32)).astype(np.float32)
+    tk = rng.standard_normal((1, 2, 5, 32)).astype(np.float32)
+    tv = rng.standard_normal((1, 2, 5, 32)).astype(np.float32)
+    valid = np.ones((1, 128), np.int32)
+    valid[:, :20] = 0
+    out, mass = orc.dense_decode_gqa(q, k, v, tk, tv, 16, valid=valid)
+    out2, mass2, _, _ = orc.two_pass_decode(q, k, v, tk, tv, 8, 16, 8, valid=valid)
+    np.testing.assert_allclose(out, out2, rtol=1e-4, atol=1e-5)
+    np.testing.assert_allclose(mass, mass2, rtol=1e-4, atol=1e-7)

@@ -47,6 +47,9 @@ WORKLOADS = {
     # same geometry, everything resident in HBM (8 x 4 GiB < 40 GB)
     "hbm-32k": dict(model="Llama-3-8B attention (L32, Hq32, Hkv8, D128)", layers=32, hq=32, hkv=8, d=128,
                     dtype="bf16", tpb=64, batch=8, context=32768, hbm_budget_gb=40.0, window=None),
+    # small HBM-only case for ncu captures (two requests, four layers: 1 GB of KV, 268 MB per launch > L2)
+    "prof-hbm": dict(model="Llama-3-8B attention (L4 slice, Hq32, Hkv8, D128)", layers=4, hq=32, hkv=8, d=128,
+                     dtype="bf16", tpb=64, batch=2, context=32768, hbm_budget_gb=40.0, window=None),
     # Mistral-7B, B8 x 32k, sliding window 4096, 5% resident (sinks + recent)
     "cfg4-32k-window": dict(model="Mistral-7B attention (L32, Hq32, Hkv8, D128, window 4096)", layers=32, hq=32,
                             hkv=8, d=128, dtype="bf16", tpb=64, batch=8, context=32768, resident_frac=0.05,

@@ -114,25 +114,37 @@ struct Plan {
   int max_splits;
 };
 
-// Split each (row, kv head) unit's tiles so that the grid fills the GPU in a
-// few whole waves, with at least a handful of tiles per CTA.
-Plan plan_splits(long long units, int tiles_per_unit, int sms, int per_sm) {
-  Plan p{1, 1};
-  if (tiles_per_unit <= 0 || units <= 0) return p;
+// Split each (row, kv head) unit's tiles into CTAs.  Chooses the split count
+// that minimises the modelled time: whole waves of resident CTAs times the
+// tiles each CTA walks plus a fixed per-CTA cost (prologue, pipeline fill,
+// merge) worth a few tiles.  The block-table cache bounds tiles per split.
+Plan plan_splits(long long units, int tiles_per_unit, int sms, int per_sm, int max_tps) {
+  Plan best{1, 1};
+  if (tiles_per_unit <= 0 || units <= 0) return best;
   const long long capacity = (long long)sms * per_sm;
-  const long long total = units * tiles_per_unit;
-  long long waves = total / (capacity * 16);
-  if (waves < 1) waves = 1;
-  if (waves > 8) waves = 8;
-  long long nsplit = (waves * capacity + units - 1) / units;
-  if (nsplit < 1) nsplit = 1;
-  if (nsplit > tiles_per_unit) nsplit = tiles_per_unit;
-  if (nsplit > kMaxSplits) nsplit = kMaxSplits;
-  int tps = (int)((tiles_per_unit + nsplit - 1) / nsplit);
-  if (tps < 1) tps = 1;
-  p.tiles_per_split = tps;
-  p.max_splits = (tiles_per_unit + tps - 1) / tps;
-  return p;
+  const int kFixedTiles = 8;
+  long long best_cost = -1;
+  const int limit = tiles_per_unit < kMaxSplits ? tiles_per_unit : kMaxSplits;
+  for (int ns = 1; ns <= limit; ++ns) {
+    int tps = (tiles_per_unit + ns - 1) / ns;
+    if (tps > max_tps) continue;
+    const int nsplit = (tiles_per_unit + tps - 1) / tps;
+    if (nsplit != ns) continue;  // same plan as a smaller ns
+    const long long ctas = units * nsplit;
+    const long long waves = (ctas + capacity - 1) / capacity;
+    const long long cost = waves * (tps + kFixedTiles);
+    if (best_cost < 0 || cost < best_cost) {
+      best_cost = cost;
+      best.tiles_per_split = tps;
+      best.max_splits = nsplit;
+    }
+  }
+  if (best_cost < 0) {  // every plan exceeds max_tps: use the most splits allowed
+    best.max_splits = limit;
+    best.tiles_per_split = (tiles_per_unit + limit - 1) / limit;
+    best.max_splits = (tiles_per_unit + best.tiles_per_split - 1) / best.tiles_per_split;
+  }
+  return best;
 }
 
 int dtype_size(int dt) { return dt == PAGER_DTYPE_F32 ? 4 : 2; }
@@ -473,7 +485,7 @@ int chunk_plan(const ChunkArgs& a, SplitKernelInfo* k, Plan* plan, long long* ma
   rc = ctas_per_sm(*k, &per_sm);
   if (rc) return rc;
   const int tiles = (a.tokens + k->tile - 1) / k->tile;
-  *plan = plan_splits((long long)a.batch * a.hkv, tiles, di->sms, per_sm);
+  *plan = plan_splits((long long)a.batch * a.hkv, tiles, di->sms, per_sm, 1 << 30);
   *group_tokens = 0;
   *mass_groups = 0;
   if (a.op == 2) {
@@ -618,7 +630,8 @@ int paged_plan(int batch, int hq, int hkv, int head_dim, int kv_dtype, int tpb, 
   rc = ctas_per_sm(out->k, &per_sm);
   if (rc) return rc;
   const int tiles = (max_row_tokens + out->k.tile - 1) / out->k.tile;
-  out->plan = plan_splits((long long)batch * hkv, tiles, di->sms, per_sm);
+  const int max_tps = (int)((long long)(kTableCache - 2) * tpb / out->k.tile);
+  out->plan = plan_splits((long long)batch * hkv, tiles, di->sms, per_sm, max_tps > 0 ? max_tps : 1);
   out->G = tpb < out->k.tile ? tpb : out->k.tile;
   out->gstride = (long long)tiles * out->k.tile / out->G;
   return PAGER_OK;

@@ -55,7 +55,9 @@ __device__ __forceinline__ uint64_t global_timer_ns() {
 // slice) until the phase completes or `limit_ns` of wall time passes.
 // Returns false on timeout; the caller records the error and aborts.
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, uint64_t limit_ns) {
-  if (mbar_try_wait(bar, parity)) return true;
+#pragma unroll 1
+  for (int i = 0; i < 64; ++i)
+    if (mbar_try_wait(bar, parity)) return true;
   const uint64_t start = global_timer_ns();
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;

@@ -31,7 +31,7 @@ enum Mode { MODE_ONLINE = 0, MODE_STATS = 1, MODE_FIXED = 2 };
 enum Source { SRC_CONTIG = 0, SRC_PAGED = 1 };
 enum Backend { BACKEND_MMA = 1, BACKEND_FMA = 2 };
 
-constexpr int kConsumerWarps = 4;
+constexpr int kConsumerWarps = 7;  // + 1 producer warp: 8 warps, 2 per scheduler, up to 255 registers each
 constexpr int kThreads = (kConsumerWarps + 1) * 32;
 constexpr int kMaxRep = 16;
 constexpr int kHostSlotBit = 0x40000000;
@@ -141,7 +141,9 @@ struct SplitParams {
   int* status;
 };
 
-template <typename T, int D, int MODE>
+constexpr int kTableCache = 1024;  // block-table entries cached in shared memory per CTA
+
+template <typename T, int D, int MODE, int BACKEND>
 struct TileCfg {
   static constexpr int ELT = sizeof(T);
   static constexpr int ROW_BYTES = D * ELT;
@@ -157,8 +159,14 @@ struct TileCfg {
   static constexpr int PANEL_TILE_BYTES = TILE * PANEL_BYTES;
   static constexpr int TENSOR_BYTES = TILE * ROW_BYTES;
   static constexpr int STAGE_BYTES = (MODE == MODE_STATS ? 1 : 2) * TENSOR_BYTES;
-  static constexpr int STAGES_RAW = (96 * 1024) / STAGE_BYTES;
-  static constexpr int STAGES = STAGES_RAW > 8 ? 8 : (STAGES_RAW < 4 ? 4 : STAGES_RAW);
+  // Shared memory outside the stage ring: Q (bf16/fp16 for mma, fp32 for fma), the fma
+  // path's P buffer, the block-table cache, barriers.
+  static constexpr int Q_BYTES = BACKEND == BACKEND_FMA ? kMaxRep * D * 4 : kMaxRep * D * ELT;
+  static constexpr int P_BYTES = BACKEND == BACKEND_FMA ? kConsumerWarps * TILE * kMaxRep * 4 : 0;
+  static constexpr int EXTRA = Q_BYTES + P_BYTES + kTableCache * 4 + 1024;
+  // A deep ring: each consumer warp holds a stage while it computes, the rest stay in flight.
+  static constexpr int STAGES_RAW = (200 * 1024 - EXTRA) / STAGE_BYTES;
+  static constexpr int STAGES = STAGES_RAW > 16 ? 16 : (STAGES_RAW < 4 ? 4 : STAGES_RAW);
   static constexpr int STAGE_AREA = STAGES * STAGE_BYTES;
   static constexpr int MERGE_BYTES = kConsumerWarps * kMaxRep * (2 + (MODE == MODE_STATS ? 0 : D)) * 4;
   static_assert(MERGE_BYTES <= STAGE_AREA, "merge region must fit in the stage ring");
@@ -186,27 +194,116 @@ __device__ __forceinline__ bool entry_usable(const SplitParams& p, int e) {
   return p.dev_pool != nullptr && e < p.dev_slots;
 }
 
-__device__ __forceinline__ bool token_valid(const SplitParams& p, int b, int t, const RowGeom& g) {
+// This CTA's block-table entries, copied to shared memory in the prologue so
+// that neither the producer nor the consumers wait on global loads per tile.
+struct TableCache {
+  const int* sm;
+  int blk0, n;
+};
+
+__device__ __forceinline__ int table_entry(const SplitParams& p, const TableCache& tc, int b, int blk) {
+  const int i = blk - tc.blk0;
+  if (i >= 0 && i < tc.n) return tc.sm[i];
+  return p.block_table[(long long)b * p.max_blocks + blk];
+}
+
+__device__ __forceinline__ bool token_valid(const SplitParams& p, const TableCache& tc, int b, int t,
+                                            const RowGeom& g) {
   if (t < g.lo || t >= g.hi) return false;
   if (p.valid && p.valid[(long long)b * p.valid_stride + t] == 0) return false;
   if (p.source == SRC_PAGED && t < g.nb * p.tpb) {
-    if (!entry_usable(p, p.block_table[(long long)b * p.max_blocks + (t >> p.log2_tpb)])) return false;
+    if (!entry_usable(p, table_entry(p, tc, b, t >> p.log2_tpb))) return false;
   }
   return true;
 }
 
 template <int TILE>
-__device__ __forceinline__ void tile_valid_bits(const SplitParams& p, int b, int t0, const RowGeom& g,
-                                                uint32_t& lo_bits, uint32_t& hi_bits) {
+__device__ __forceinline__ void tile_valid_bits(const SplitParams& p, const TableCache& tc, int b, int t0,
+                                                const RowGeom& g, uint32_t& lo_bits, uint32_t& hi_bits) {
   const int lane = threadIdx.x & 31;
-  const bool v0 = lane < TILE && token_valid(p, b, t0 + lane, g);
-  const bool v1 = TILE > 32 && token_valid(p, b, t0 + 32 + lane, g);
+  const bool v0 = lane < TILE && token_valid(p, tc, b, t0 + lane, g);
+  const bool v1 = TILE > 32 && token_valid(p, tc, b, t0 + 32 + lane, g);
   lo_bits = __ballot_sync(0xffffffffu, v0);
   hi_bits = __ballot_sync(0xffffffffu, v1);
 }
 
 __device__ __forceinline__ bool bit_of(uint32_t lo_bits, uint32_t hi_bits, int t) {
   return ((t < 32 ? (lo_bits >> t) : (hi_bits >> (t - 32))) & 1u) != 0;
+}
+
+// Hot fields of SplitParams copied into registers once per warp.  The kernel
+// parameter block lives in parameter space and is reached through a reference;
+// after every volatile shared-memory store (tickets, abort flag) the compiler
+// may not assume it unchanged and re-loads each field, which put several
+// hundred nanoseconds into every tile of the producer's loop.
+struct Hot {
+  const int* block_table;
+  const char* dev_pool;
+  const char* host_pool;
+  const char* tail_k;
+  const char* tail_v;
+  const int* valid;
+  int* status;
+  long long valid_stride, slot_stride, layer_stride;
+  unsigned long long wait_limit;
+  int source, tpb, log2_tpb, max_blocks, num_layers, layer, hkv, dev_slots, host_slots, tail_cap;
+};
+
+__device__ __forceinline__ Hot load_hot(const SplitParams& p) {
+  Hot h;
+  h.block_table = p.block_table;
+  h.dev_pool = p.dev_pool;
+  h.host_pool = p.host_pool;
+  h.tail_k = p.tail_k;
+  h.tail_v = p.tail_v;
+  h.valid = p.valid;
+  h.status = p.status;
+  h.valid_stride = p.valid_stride;
+  h.slot_stride = p.slot_stride_bytes;
+  h.layer_stride = p.layer_stride_bytes;
+  h.wait_limit = p.wait_limit_ns;
+  h.source = p.source;
+  h.tpb = p.tpb;
+  h.log2_tpb = p.log2_tpb;
+  h.max_blocks = p.max_blocks;
+  h.num_layers = p.num_layers;
+  h.layer = p.layer;
+  h.hkv = p.num_kv_heads;
+  h.dev_slots = p.dev_slots;
+  h.host_slots = p.host_slots;
+  h.tail_cap = p.tail_cap;
+  return h;
+}
+
+__device__ __forceinline__ bool entry_ok(const Hot& k, int e) {
+  if (e < 0) return false;
+  if (e & kHostSlotBit) return k.host_pool != nullptr && (e & (kHostSlotBit - 1)) < k.host_slots;
+  return k.dev_pool != nullptr && e < k.dev_slots;
+}
+
+__device__ __forceinline__ int entry_at(const Hot& k, const TableCache& tc, int b, int blk) {
+  const int i = blk - tc.blk0;
+  if (i >= 0 && i < tc.n) return tc.sm[i];
+  return k.block_table[(long long)b * k.max_blocks + blk];
+}
+
+__device__ __forceinline__ bool token_ok(const Hot& k, const TableCache& tc, int b, int t, const RowGeom& g) {
+  if (t < g.lo || t >= g.hi) return false;
+  if (k.valid && k.valid[(long long)b * k.valid_stride + t] == 0) return false;
+  if (k.source == SRC_PAGED && t < g.nb * k.tpb) {
+    if (!entry_ok(k, entry_at(k, tc, b, t >> k.log2_tpb))) return false;
+  }
+  return true;
+}
+
+template <int TILE>
+__device__ __forceinline__ void tile_bits(const Hot& k, const TableCache& tc, int b, int t0, const RowGeom& g,
+                                          uint32_t& lo_bits, uint32_t& hi_bits) {
+  const int lane = threadIdx.x & 31;
+  const bool v0 = lane < TILE && token_ok(k, tc, b, t0 + lane, g);
+  const bool v1 = TILE > 32 && token_ok(k, tc, b, t0 + 32 + lane, g);
+  lo_bits = __ballot_sync(0xffffffffu, v0);
+  hi_bits = __ballot_sync(0xffffffffu, v1);
 }
 
 // ------------------------------------------------------------------ producer helpers
@@ -237,134 +334,165 @@ __device__ __forceinline__ void sw_copy_rows(uint32_t tile_base, int row0, const
   }
 }
 
+// Rows that TMA cannot fetch -- blocks in the pinned host pool (read zero-copy
+// over the host link) and tail rows -- are copied into the stage by the
+// consumer warp that owns the tile, with 16-byte loads.  `mask` has one bit per
+// segment of min(TILE, tokens_per_block) rows.
+template <class Cfg, bool kNeedV>
+__device__ __forceinline__ void copy_sw_segments(const Hot& k, const TableCache& tc, const RowGeom& g, int b, int h,
+                                                 int t0, uint32_t mask, uint8_t* kbuf, uint8_t* vbuf) {
+  const int br = min(Cfg::TILE, k.tpb);
+  const int block_tokens = g.nb * k.tpb;
+  const long long head_bytes = (long long)k.tpb * Cfg::ROW_BYTES;
+  const uint32_t kaddr = smem_u32(kbuf), vaddr = smem_u32(vbuf);
+  for (int sg = 0; mask; ++sg, mask >>= 1) {
+    if (!(mask & 1u)) continue;
+    const int tok = t0 + sg * br;
+    if (tok < block_tokens) {
+      const int e = entry_at(k, tc, b, tok >> k.log2_tpb);
+      const long long slot = e & (kHostSlotBit - 1);
+      const char* kb = k.host_pool + slot * k.slot_stride + (long long)k.layer * k.layer_stride +
+                       (long long)h * head_bytes + (long long)(tok & (k.tpb - 1)) * Cfg::ROW_BYTES;
+      sw_copy_rows<Cfg>(kaddr, sg * br, kb, br);
+      if (kNeedV) sw_copy_rows<Cfg>(vaddr, sg * br, kb + (long long)k.hkv * head_bytes, br);
+    } else {
+      const int tr = tok - block_tokens;
+      const int n = min(br, g.ntok - tok);
+      const long long off = (((long long)b * k.hkv + h) * k.tail_cap + tr) * Cfg::ROW_BYTES;
+      sw_copy_rows<Cfg>(kaddr, sg * br, k.tail_k + off, n);
+      if (kNeedV) sw_copy_rows<Cfg>(vaddr, sg * br, k.tail_v + off, n);
+    }
+  }
+  __syncwarp();
+}
+
+// The producer is one thread: per tile it waits for the stage to be free,
+// issues the TMA boxes of every device-resident segment, arrives on the
+// stage's full barrier and publishes the stage's ticket -- (use) in the low 16
+// bits, the mask of segments left to the consumer in the high bits -- as one
+// 32-bit store.
 template <class Cfg, int MODE>
-__device__ void run_producer(const SplitParams& p, const CUtensorMap* mapk, const CUtensorMap* mapv,
-                             uint8_t* stages, uint64_t* full, uint64_t* empty, int b, int h, int tile0,
-                             int ntiles, const RowGeom& g, volatile int* abort_flag) {
-  const int lane = threadIdx.x & 31;
+__device__ void run_producer(const SplitParams& p, const TableCache& tc, const CUtensorMap* mapk,
+                             const CUtensorMap* mapv, uint8_t* stages, uint64_t* full, uint64_t* empty,
+                             volatile int* tickets, int b, int h, int tile0, int ntiles, const RowGeom& g,
+                             volatile int* abort_flag) {
+  if ((threadIdx.x & 31) != 0) return;
   constexpr bool kNeedV = MODE != MODE_STATS;
+  const Hot k = load_hot(p);
+  const int zc = b * k.hkv + h;  // contiguous source: (row, kv head) plane
+  const int br = min(Cfg::TILE, k.tpb);
+  const int nseg = Cfg::TILE / br;
+  const int block_tokens = g.nb * k.tpb;
+  const uint32_t seg_bytes = (uint32_t)br * Cfg::ROW_BYTES * (kNeedV ? 2u : 1u);
   int issued = 0;
   for (int i = 0; i < ntiles; ++i) {
     const int s = i % Cfg::STAGES;
     const int use = i / Cfg::STAGES;
-    if (use > 0) {
-      int ok = 1;
-      if (lane == 0) ok = mbar_wait_bounded(&empty[s], (use - 1) & 1, p.wait_limit_ns) ? 1 : 0;
-      ok = __shfl_sync(0xffffffffu, ok, 0);
-      if (!ok) {
-        if (lane == 0) {
-          atomicExch(p.status, kStatusTimeout);
-          *abort_flag = 1;
-        }
-        break;
-      }
+    if (use > 0 && !mbar_wait_bounded(&empty[s], (use - 1) & 1, k.wait_limit)) {
+      atomicExch(k.status, kStatusTimeout);
+      *abort_flag = 1;
+      break;
     }
     if (*abort_flag) break;
     uint8_t* kbuf = stages + s * Cfg::STAGE_BYTES;
     uint8_t* vbuf = kbuf + Cfg::TENSOR_BYTES;
     const int t0 = (tile0 + i) * Cfg::TILE;
-    if (p.source == SRC_CONTIG) {
-      if (lane == 0) {
-        mbar_expect_tx(&full[s], (uint32_t)Cfg::STAGE_BYTES);
-        const int z = b * p.num_kv_heads + h;
+    uint32_t sw_mask = 0;
+    if (k.source == SRC_CONTIG) {
+      mbar_expect_tx(&full[s], (uint32_t)Cfg::STAGE_BYTES);
 #pragma unroll
-        for (int pn = 0; pn < Cfg::NPANEL; ++pn) {
-          tma_load_3d(kbuf + pn * Cfg::PANEL_TILE_BYTES, mapk, pn * Cfg::PANEL_ELTS, t0, z, &full[s]);
-          if (kNeedV) tma_load_3d(vbuf + pn * Cfg::PANEL_TILE_BYTES, mapv, pn * Cfg::PANEL_ELTS, t0, z, &full[s]);
-        }
-        mbar_arrive(&full[s]);
+      for (int pn = 0; pn < Cfg::NPANEL; ++pn) {
+        tma_load_3d(kbuf + pn * Cfg::PANEL_TILE_BYTES, mapk, pn * Cfg::PANEL_ELTS, t0, zc, &full[s]);
+        if (kNeedV) tma_load_3d(vbuf + pn * Cfg::PANEL_TILE_BYTES, mapv, pn * Cfg::PANEL_ELTS, t0, zc, &full[s]);
       }
     } else {
-      const int br = min(Cfg::TILE, p.tpb);
-      const int nseg = Cfg::TILE / br;
-      const int block_tokens = g.nb * p.tpb;
-      const uint32_t seg_bytes = (uint32_t)br * Cfg::ROW_BYTES * (kNeedV ? 2u : 1u);
-      const long long head_bytes = (long long)p.tpb * Cfg::ROW_BYTES;
-      if (lane == 0) {
-        uint32_t tx = 0;
-        for (int sg = 0; sg < nseg; ++sg) {
-          const int tok = t0 + sg * br;
-          if (tok >= g.hi || tok + br <= g.lo || tok >= block_tokens) continue;
-          const int e = p.block_table[(long long)b * p.max_blocks + (tok >> p.log2_tpb)];
-          if (!entry_usable(p, e)) {
-            if (e >= 0) atomicExch(p.status, kStatusBadBlock);
-            continue;
-          }
-          if (!(e & kHostSlotBit)) tx += seg_bytes;
-        }
-        if (tx) mbar_expect_tx(&full[s], tx);
-        for (int sg = 0; sg < nseg; ++sg) {
-          const int tok = t0 + sg * br;
-          if (tok >= g.hi || tok + br <= g.lo || tok >= block_tokens) continue;
-          const int e = p.block_table[(long long)b * p.max_blocks + (tok >> p.log2_tpb)];
-          if (!entry_usable(p, e) || (e & kHostSlotBit)) continue;
-          const int zk = ((e * p.num_layers + p.layer) * 2) * p.num_kv_heads + h;
-          const int y = tok & (p.tpb - 1);
-#pragma unroll
-          for (int pn = 0; pn < Cfg::NPANEL; ++pn) {
-            const int off = pn * Cfg::PANEL_TILE_BYTES + sg * br * Cfg::PANEL_BYTES;
-            tma_load_3d(kbuf + off, mapk, pn * Cfg::PANEL_ELTS, y, zk, &full[s]);
-            if (kNeedV) tma_load_3d(vbuf + off, mapk, pn * Cfg::PANEL_ELTS, y, zk + p.num_kv_heads, &full[s]);
-          }
-        }
-      }
-      __syncwarp();
-      // zero-copy host blocks and the tail: 16-byte loads into the swizzled layout
-      const uint32_t kaddr = smem_u32(kbuf), vaddr = smem_u32(vbuf);
       for (int sg = 0; sg < nseg; ++sg) {
         const int tok = t0 + sg * br;
         if (tok >= g.hi || tok + br <= g.lo) continue;
-        if (tok < block_tokens) {
-          const int e = p.block_table[(long long)b * p.max_blocks + (tok >> p.log2_tpb)];
-          if (!entry_usable(p, e) || !(e & kHostSlotBit)) continue;
-          const long long slot = e & (kHostSlotBit - 1);
-          const char* kb = p.host_pool + slot * p.slot_stride_bytes + (long long)p.layer * p.layer_stride_bytes +
-                           (long long)h * head_bytes + (long long)(tok & (p.tpb - 1)) * Cfg::ROW_BYTES;
-          sw_copy_rows<Cfg>(kaddr, sg * br, kb, br);
-          if (kNeedV) sw_copy_rows<Cfg>(vaddr, sg * br, kb + (long long)p.num_kv_heads * head_bytes, br);
-        } else {
-          const int tr = tok - block_tokens;
-          const int n = min(br, g.ntok - tok);
-          const long long off = (((long long)b * p.num_kv_heads + h) * p.tail_cap + tr) * Cfg::ROW_BYTES;
-          sw_copy_rows<Cfg>(kaddr, sg * br, p.tail_k + off, n);
-          if (kNeedV) sw_copy_rows<Cfg>(vaddr, sg * br, p.tail_v + off, n);
+        if (tok >= block_tokens) {
+          sw_mask |= 1u << sg;  // tail rows
+          continue;
+        }
+        const int e = entry_at(k, tc, b, tok >> k.log2_tpb);
+        if (!entry_ok(k, e)) {
+          if (e >= 0) atomicExch(k.status, kStatusBadBlock);
+          continue;
+        }
+        if (e & kHostSlotBit) {
+          sw_mask |= 1u << sg;
+          continue;
+        }
+        mbar_expect_tx(&full[s], seg_bytes);
+        const int zk = ((e * k.num_layers + k.layer) * 2) * k.hkv + h;
+        const int y = tok & (k.tpb - 1);
+#pragma unroll
+        for (int pn = 0; pn < Cfg::NPANEL; ++pn) {
+          const int off = pn * Cfg::PANEL_TILE_BYTES + sg * br * Cfg::PANEL_BYTES;
+          tma_load_3d(kbuf + off, mapk, pn * Cfg::PANEL_ELTS, y, zk, &full[s]);
+          if (kNeedV) tma_load_3d(vbuf + off, mapk, pn * Cfg::PANEL_ELTS, y, zk + k.hkv, &full[s]);
         }
       }
-      __threadfence_block();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&full[s]);
     }
+    mbar_arrive(&full[s]);
+    tickets[s] = (int)((sw_mask << 16) | (uint32_t)use);
     issued = i + 1;
   }
   // Drain: never leave the CTA with bulk copies still landing in its shared memory.
-  if (lane == 0) {
-    const int first = issued > Cfg::STAGES ? issued - Cfg::STAGES : 0;
-    for (int i = first; i < issued; ++i) {
-      if (!mbar_wait_bounded(&full[i % Cfg::STAGES], (i / Cfg::STAGES) & 1, p.wait_limit_ns)) {
-        atomicExch(p.status, kStatusTimeout);
-        *abort_flag = 1;
-        break;
-      }
+  const int first = issued > Cfg::STAGES ? issued - Cfg::STAGES : 0;
+  for (int i = first; i < issued; ++i) {
+    if (!mbar_wait_bounded(&full[i % Cfg::STAGES], (i / Cfg::STAGES) & 1, k.wait_limit)) {
+      atomicExch(k.status, kStatusTimeout);
+      *abort_flag = 1;
+      break;
     }
   }
 }
 
-// Consumer-side wait: lane 0 does the bounded wait; on success every lane
-// observes the (already completed) phase so the TMA writes are visible to it.
-__device__ __forceinline__ bool consumer_wait(const SplitParams& p, uint64_t* bar, uint32_t parity,
-                                              volatile int* abort_flag) {
+// Consumer-side wait for tile i on stage s = i % STAGES (use n = i / STAGES).
+// Tiles of one stage go to different warps, so a warp can reach use n of a
+// stage while use n-1 is still loading; a parity wait posed about a phase that
+// is not yet the current one would alias the phase two back and succeed early.
+// The producer therefore publishes, per stage, the use it is filling (a ticket
+// written after the stage's previous use was released); the consumer first
+// waits for its ticket, which makes phase n the current phase of the full
+// barrier, then waits for that phase.  Lane 0 does the bounded waits; on
+// success every lane observes the completed phase so the TMA writes are
+// visible to it.
+__device__ __forceinline__ bool wait_ticket(volatile int* ticket, int use, uint64_t limit_ns, uint32_t* mask) {
+  int t = *ticket;
+#pragma unroll 1
+  for (int i = 0; i < 256 && (t & 0xffff) != use; ++i) t = *ticket;
+  if ((t & 0xffff) != use) {
+    const uint64_t start = global_timer_ns();
+    while (((t = *ticket) & 0xffff) != use) {
+      if (global_timer_ns() - start > limit_ns) return false;
+    }
+  }
+  *mask = ((uint32_t)t) >> 16;
+  return true;
+}
+
+// Returns false on timeout (abort); *mask = the tile's segments left to the consumer.
+__device__ __forceinline__ bool consumer_wait(const Hot& k, uint64_t* full_bar, volatile int* ticket, int use,
+                                              volatile int* abort_flag, uint32_t* mask) {
   const int lane = threadIdx.x & 31;
+  const uint32_t parity = use & 1;
   int ok = 1;
-  if (lane == 0) ok = mbar_wait_bounded(bar, parity, p.wait_limit_ns) ? 1 : 0;
+  uint32_t m = 0;
+  if (lane == 0) {
+    ok = wait_ticket(ticket, use, k.wait_limit, &m) ? 1 : 0;
+    if (ok) ok = mbar_wait_bounded(full_bar, parity, k.wait_limit) ? 1 : 0;
+  }
   ok = __shfl_sync(0xffffffffu, ok, 0);
+  *mask = __shfl_sync(0xffffffffu, m, 0);
   if (!ok) {
     if (lane == 0) {
-      atomicExch(p.status, kStatusTimeout);
+      atomicExch(k.status, kStatusTimeout);
       *abort_flag = 1;
     }
     return false;
   }
-  while (!mbar_try_wait(bar, parity)) {
+  while (!mbar_try_wait(full_bar, parity)) {
   }
   return true;
 }
@@ -451,12 +579,17 @@ __device__ void merge_and_store(const SplitParams& p, float* mw, int b, int h, i
 }
 
 // ------------------------------------------------------------------ tensor-core consumer
+// One warp folds one tile: S = Q K^T and O += P V with mma.sync m16n8k16
+// (fp32 accumulate), the n_rep query heads in the 16-row M dimension.
+// Per-lane shared-memory addresses are precomputed once: with 128-byte
+// swizzled panels the XOR term only depends on the lane.
 template <typename T, int D, int MODE>
-__device__ void run_consumer_mma(const SplitParams& p, uint8_t* stages, uint64_t* full, uint64_t* empty, int b,
-                                 int h, int tile0, int ntiles, const RowGeom& g, volatile int* abort_flag,
-                                 int split) {
-  using Cfg = TileCfg<T, D, MODE>;
+__device__ void run_consumer_mma(const SplitParams& p, const TableCache& tc, uint8_t* stages, uint64_t* full,
+                                 uint64_t* empty, volatile int* tickets, int b, int h, int tile0, int ntiles,
+                                 const RowGeom& g, volatile int* abort_flag, int split, const T* q_smem) {
+  using Cfg = TileCfg<T, D, MODE, BACKEND_MMA>;
   using Op = MmaOp<T>;
+  static_assert(Cfg::PANEL_BYTES == 128, "mma path expects 128-byte panels");
   constexpr int KSTEPS = D / 16;
   constexpr int NT_O = D / 8;
   constexpr int NT_S = Cfg::TILE / 8;
@@ -466,30 +599,40 @@ __device__ void run_consumer_mma(const SplitParams& p, uint8_t* stages, uint64_t
   const int tq = lane & 3;
   const int n_rep = p.n_rep;
   const int qh0 = h * n_rep;
+  const int l7 = lane & 7;
+  const Hot hk = load_hot(p);
+  const float scale = p.scale;
+  const float softcap = p.softcap;
+  float2* const mass_part = p.mass_part;
+  const int num_q_heads = p.num_q_heads;
+  const int mass_gstride = p.mass_gstride;
+  const int log2_group = p.log2_group;
 
   uint32_t qa[KSTEPS][4];
   {
-    const long long qbase = ((long long)b * p.num_q_heads + qh0) * D;
+    const uint32_t qaddr = smem_u32(q_smem);
+    const int qrow = l7 + ((lane >> 3) & 1) * 8;
 #pragma unroll
     for (int kk = 0; kk < KSTEPS; ++kk) {
-      const int c = 16 * kk + 2 * tq;
-      float v[2][4];
-#pragma unroll
-      for (int rr = 0; rr < 2; ++rr) {
-        const int row = gr + 8 * rr;
-        const bool ok = row < n_rep;
-        const long long base = qbase + (long long)row * D;
-        v[rr][0] = ok ? load_any(p.q, base + c, p.q_dtype) : 0.f;
-        v[rr][1] = ok ? load_any(p.q, base + c + 1, p.q_dtype) : 0.f;
-        v[rr][2] = ok ? load_any(p.q, base + c + 8, p.q_dtype) : 0.f;
-        v[rr][3] = ok ? load_any(p.q, base + c + 9, p.q_dtype) : 0.f;
-      }
-      qa[kk][0] = Op::pack(v[0][0], v[0][1]);
-      qa[kk][1] = Op::pack(v[1][0], v[1][1]);
-      qa[kk][2] = Op::pack(v[0][2], v[0][3]);
-      qa[kk][3] = Op::pack(v[1][2], v[1][3]);
+      const int col = 16 * kk + (lane >> 4) * 8;
+      ldmatrix_x4(qaddr + (qrow * D + col) * (int)sizeof(T), qa[kk][0], qa[kk][1], qa[kk][2], qa[kk][3]);
     }
   }
+  // K fragments: row 8j + l7, 16-byte chunk 2kk + (lane >> 3)
+  uint32_t koff[KSTEPS / 2];
+#pragma unroll
+  for (int kp = 0; kp < KSTEPS / 2; ++kp) {
+    const int c = 4 * kp + (lane >> 3);
+    koff[kp] = (c >> 3) * Cfg::PANEL_TILE_BYTES + l7 * 128 + (((c & 7) ^ l7) << 4);
+  }
+  // V fragments (transposed): row 16kt + ((lane>>3)&1)*8 + l7, chunk n + (lane >> 4)
+  uint32_t voff[NT_O / 2];
+#pragma unroll
+  for (int np = 0; np < NT_O / 2; ++np) {
+    const int c = 2 * np + (lane >> 4);
+    voff[np] = (c >> 3) * Cfg::PANEL_TILE_BYTES + (((lane >> 3) & 1) * 8 + l7) * 128 + (((c & 7) ^ l7) << 4);
+  }
+
   float mfix_l2[2] = {0.f, 0.f};
   if (MODE == MODE_FIXED) {
 #pragma unroll
@@ -506,16 +649,22 @@ __device__ void run_consumer_mma(const SplitParams& p, uint8_t* stages, uint64_t
   float m_r[2] = {neg_inf(), neg_inf()};
   float l_r[2] = {0.f, 0.f};
   const int G = p.group_tokens;
+  const bool softcap_on = softcap > 0.f;
+  const uint64_t full_mask = Cfg::TILE == 64 ? ~0ull : ((1ull << Cfg::TILE) - 1ull);
 
   for (int i = warp; i < ntiles; i += kConsumerWarps) {
     const int s = i % Cfg::STAGES;
     if (*abort_flag) break;
-    if (!consumer_wait(p, &full[s], (i / Cfg::STAGES) & 1, abort_flag)) break;
+    uint32_t swm;
+    if (!consumer_wait(hk, &full[s], &tickets[s], i / Cfg::STAGES, abort_flag, &swm)) break;
     const int t0 = (tile0 + i) * Cfg::TILE;
-    uint32_t vlo, vhi;
-    tile_valid_bits<Cfg::TILE>(p, b, t0, g, vlo, vhi);
     uint8_t* kbuf = stages + s * Cfg::STAGE_BYTES;
     uint8_t* vbuf = kbuf + Cfg::TENSOR_BYTES;
+    if (swm) copy_sw_segments<Cfg, MODE != MODE_STATS>(hk, tc, g, b, h, t0, swm, kbuf, vbuf);
+    uint32_t vlo, vhi;
+    tile_bits<Cfg::TILE>(hk, tc, b, t0, g, vlo, vhi);
+    const uint64_t vmask = ((uint64_t)vhi << 32) | vlo;
+    const bool all_valid = vmask == full_mask;
     const uint32_t kaddr = smem_u32(kbuf);
 
     float sc[NT_S][4];
@@ -523,23 +672,24 @@ __device__ void run_consumer_mma(const SplitParams& p, uint8_t* stages, uint64_t
     for (int j = 0; j < NT_S; ++j) sc[j][0] = sc[j][1] = sc[j][2] = sc[j][3] = 0.f;
 #pragma unroll
     for (int j = 0; j < NT_S; ++j) {
-      const int row = 8 * j + (lane & 7);
 #pragma unroll
-      for (int kk = 0; kk < KSTEPS; kk += 2) {
+      for (int kp = 0; kp < KSTEPS / 2; ++kp) {
         uint32_t b0, b1, b2, b3;
-        ldmatrix_x4(chunk_addr<Cfg>(kaddr, row, 2 * kk + (lane >> 3)), b0, b1, b2, b3);
-        Op::run(sc[j], qa[kk], b0, b1);
-        Op::run(sc[j], qa[kk + 1], b2, b3);
+        ldmatrix_x4(kaddr + koff[kp] + j * 8 * 128, b0, b1, b2, b3);
+        Op::run(sc[j], qa[2 * kp], b0, b1);
+        Op::run(sc[j], qa[2 * kp + 1], b2, b3);
       }
     }
     // scale, softcap, token mask (streaming_attention.py:158-161)
+    const uint64_t tmask = vmask >> (2 * tq);
 #pragma unroll
     for (int j = 0; j < NT_S; ++j) {
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
-        const int tok = 8 * j + 2 * tq + (e & 1);
-        const float x = apply_score(sc[j][e], p.scale, p.softcap);
-        sc[j][e] = bit_of(vlo, vhi, tok) ? x : neg_inf();
+        float x = sc[j][e] * scale;
+        if (softcap_on) x = softcap * tanhf(x / softcap);
+        if (!all_valid && !((tmask >> (8 * j + (e & 1))) & 1ull)) x = neg_inf();
+        sc[j][e] = x;
       }
     }
     float mref[2];
@@ -550,23 +700,31 @@ __device__ void run_consumer_mma(const SplitParams& p, uint8_t* stages, uint64_t
         mx[0] = fmaxf(mx[0], fmaxf(sc[j][0], sc[j][1]));
         mx[1] = fmaxf(mx[1], fmaxf(sc[j][2], sc[j][3]));
       }
+      bool changed = false;
+      float alpha[2];
 #pragma unroll
       for (int rr = 0; rr < 2; ++rr) {
         mx[rr] = fmaxf(mx[rr], __shfl_xor_sync(0xffffffffu, mx[rr], 1));
         mx[rr] = fmaxf(mx[rr], __shfl_xor_sync(0xffffffffu, mx[rr], 2));
         const float m_new = fmaxf(m_r[rr], mx[rr]);
         const bool empty_row = m_new == neg_inf();  // streaming_attention.py:171-177
-        const float alpha = empty_row ? 0.f : fast_exp2((m_r[rr] - m_new) * kLog2e);
-        l_r[rr] *= alpha;
-        if (MODE == MODE_ONLINE) {
-#pragma unroll
-          for (int n = 0; n < NT_O; ++n) {
-            o[n][2 * rr] *= alpha;
-            o[n][2 * rr + 1] *= alpha;
-          }
-        }
+        alpha[rr] = empty_row ? 0.f : (m_new == m_r[rr] ? 1.f : fast_exp2((m_r[rr] - m_new) * kLog2e));
+        changed |= alpha[rr] != 1.f;
         m_r[rr] = m_new;
         mref[rr] = empty_row ? 0.f : m_new * kLog2e;
+      }
+      if (__any_sync(0xffffffffu, changed)) {
+#pragma unroll
+        for (int rr = 0; rr < 2; ++rr) {
+          l_r[rr] *= alpha[rr];
+          if (MODE == MODE_ONLINE) {
+#pragma unroll
+            for (int n = 0; n < NT_O; ++n) {
+              o[n][2 * rr] *= alpha[rr];
+              o[n][2 * rr + 1] *= alpha[rr];
+            }
+          }
+        }
       }
     } else {
       mref[0] = mfix_l2[0];
@@ -602,20 +760,20 @@ __device__ void run_consumer_mma(const SplitParams& p, uint8_t* stages, uint64_t
           gs[rr] += __shfl_xor_sync(0xffffffffu, gs[rr], 2);
         }
         if (tq == 0) {
-          const long long gidx = (t0 >> p.log2_group) + gi;
+          const long long gidx = (t0 >> log2_group) + gi;
 #pragma unroll
           for (int rr = 0; rr < 2; ++rr) {
             const int row = gr + 8 * rr;
             if (row < n_rep)
-              p.mass_part[((long long)b * p.num_q_heads + qh0 + row) * p.mass_gstride + gidx] =
+              mass_part[((long long)b * num_q_heads + qh0 + row) * mass_gstride + gidx] =
                   make_float2(gs[rr], MODE == MODE_ONLINE ? m_r[rr] : 0.f);
           }
         }
       }
     }
-    bool wrote = false;
+    bool wrote = swm != 0;
     if (MODE != MODE_STATS) {
-      wrote = zero_masked_rows<Cfg>(vbuf, vlo, vhi);
+      if (!all_valid) wrote |= zero_masked_rows<Cfg>(vbuf, vlo, vhi);
       const uint32_t vaddr = smem_u32(vbuf);
 #pragma unroll
       for (int kt = 0; kt < Cfg::TILE / 16; ++kt) {
@@ -624,14 +782,12 @@ __device__ void run_consumer_mma(const SplitParams& p, uint8_t* stages, uint64_t
         pa[1] = Op::pack(sc[2 * kt][2], sc[2 * kt][3]);
         pa[2] = Op::pack(sc[2 * kt + 1][0], sc[2 * kt + 1][1]);
         pa[3] = Op::pack(sc[2 * kt + 1][2], sc[2 * kt + 1][3]);
-        const int mi = lane >> 3;
-        const int vrow = 16 * kt + ((mi & 1) << 3) + (lane & 7);
 #pragma unroll
-        for (int n = 0; n < NT_O; n += 2) {
+        for (int np = 0; np < NT_O / 2; ++np) {
           uint32_t b0, b1, b2, b3;
-          ldmatrix_x4_trans(chunk_addr<Cfg>(vaddr, vrow, n + (mi >> 1)), b0, b1, b2, b3);
-          Op::run(o[n], pa, b0, b1);
-          Op::run(o[n + 1], pa, b2, b3);
+          ldmatrix_x4_trans(vaddr + voff[np] + kt * 16 * 128, b0, b1, b2, b3);
+          Op::run(o[2 * np], pa, b0, b1);
+          Op::run(o[2 * np + 1], pa, b2, b3);
         }
       }
     }
@@ -673,10 +829,11 @@ __device__ void run_consumer_mma(const SplitParams& p, uint8_t* stages, uint64_t
 // Lane <-> token for Q.K (q broadcast from shared memory), lane <-> head_dim
 // column for P.V (p broadcast from shared memory); fp32 throughout.
 template <typename T, int D, int MODE>
-__device__ void run_consumer_fma(const SplitParams& p, uint8_t* stages, uint64_t* full, uint64_t* empty, int b,
-                                 int h, int tile0, int ntiles, const RowGeom& g, volatile int* abort_flag,
-                                 int split, const float* q_sm, float* p_sm_all) {
-  using Cfg = TileCfg<T, D, MODE>;
+__device__ void run_consumer_fma(const SplitParams& p, const TableCache& tc, uint8_t* stages, uint64_t* full,
+                                 uint64_t* empty, volatile int* tickets, int b, int h, int tile0, int ntiles,
+                                 const RowGeom& g, volatile int* abort_flag, int split, const float* q_sm,
+                                 float* p_sm_all) {
+  using Cfg = TileCfg<T, D, MODE, BACKEND_FMA>;
   constexpr int TILE = Cfg::TILE;
   constexpr int TPL = TILE > 32 ? TILE / 32 : 1;   // tokens per lane in Q.K
   constexpr int EPC = 16 / sizeof(T);              // elements per 16-byte chunk
@@ -686,6 +843,13 @@ __device__ void run_consumer_fma(const SplitParams& p, uint8_t* stages, uint64_t
   const int n_rep = p.n_rep;
   const int qh0 = h * n_rep;
   float* p_sm = p_sm_all + warp * TILE * kMaxRep;
+  const Hot hk = load_hot(p);
+  const float scale = p.scale;
+  const float softcap = p.softcap;
+  float2* const mass_part = p.mass_part;
+  const int num_q_heads = p.num_q_heads;
+  const int mass_gstride = p.mass_gstride;
+  const int log2_group = p.log2_group;
 
   float mfix[kMaxRep];
   if (MODE == MODE_FIXED) {
@@ -709,12 +873,14 @@ __device__ void run_consumer_fma(const SplitParams& p, uint8_t* stages, uint64_t
   for (int i = warp; i < ntiles; i += kConsumerWarps) {
     const int s = i % Cfg::STAGES;
     if (*abort_flag) break;
-    if (!consumer_wait(p, &full[s], (i / Cfg::STAGES) & 1, abort_flag)) break;
+    uint32_t swm;
+    if (!consumer_wait(hk, &full[s], &tickets[s], i / Cfg::STAGES, abort_flag, &swm)) break;
     const int t0 = (tile0 + i) * TILE;
-    uint32_t vlo, vhi;
-    tile_valid_bits<TILE>(p, b, t0, g, vlo, vhi);
     uint8_t* kbuf = stages + s * Cfg::STAGE_BYTES;
     uint8_t* vbuf = kbuf + Cfg::TENSOR_BYTES;
+    if (swm) copy_sw_segments<Cfg, MODE != MODE_STATS>(hk, tc, g, b, h, t0, swm, kbuf, vbuf);
+    uint32_t vlo, vhi;
+    tile_bits<TILE>(hk, tc, b, t0, g, vlo, vhi);
     const uint32_t kaddr = smem_u32(kbuf);
 
     float sc[TPL][kMaxRep];
@@ -740,7 +906,7 @@ __device__ void run_consumer_fma(const SplitParams& p, uint8_t* stages, uint64_t
       }
 #pragma unroll
       for (int r = 0; r < kMaxRep; ++r) {
-        const float x = apply_score(sc[u][r], p.scale, p.softcap);
+        const float x = apply_score(sc[u][r], scale, softcap);
         sc[u][r] = (t < TILE && bit_of(vlo, vhi, t)) ? x : neg_inf();
       }
     }
@@ -789,14 +955,14 @@ __device__ void run_consumer_fma(const SplitParams& p, uint8_t* stages, uint64_t
           }
           v = warp_sum(v);
           if (lane == 0) {
-            const long long gidx = (t0 >> p.log2_group) + gi;
-            p.mass_part[((long long)b * p.num_q_heads + qh0 + r) * p.mass_gstride + gidx] =
+            const long long gidx = (t0 >> log2_group) + gi;
+            mass_part[((long long)b * num_q_heads + qh0 + r) * mass_gstride + gidx] =
                 make_float2(v, MODE == MODE_ONLINE ? m_r[r] : 0.f);
           }
         }
       }
     }
-    bool wrote = false;
+    bool wrote = swm != 0;
     if (MODE != MODE_STATS) {
 #pragma unroll
       for (int u = 0; u < TPL; ++u) {
@@ -806,7 +972,7 @@ __device__ void run_consumer_fma(const SplitParams& p, uint8_t* stages, uint64_t
           for (int r = 0; r < kMaxRep; ++r) p_sm[t * kMaxRep + r] = sc[u][r];
         }
       }
-      wrote = zero_masked_rows<Cfg>(vbuf, vlo, vhi);
+      wrote |= zero_masked_rows<Cfg>(vbuf, vlo, vhi);
       __syncwarp();
       const uint32_t vaddr = smem_u32(vbuf);
       for (int t = 0; t < TILE; ++t) {
@@ -876,21 +1042,22 @@ __device__ void run_consumer_fma(const SplitParams& p, uint8_t* stages, uint64_t
 // ------------------------------------------------------------------ kernel
 template <typename T, int D, int MODE, int BACKEND>
 struct SplitSmem {
-  using Cfg = TileCfg<T, D, MODE>;
+  using Cfg = TileCfg<T, D, MODE, BACKEND>;
   static constexpr int BAR_OFF = Cfg::STAGE_AREA;
   static constexpr int FLAG_OFF = BAR_OFF + 2 * Cfg::STAGES * 8;
-  static constexpr int Q_OFF = (FLAG_OFF + 16 + 15) / 16 * 16;
-  static constexpr int Q_BYTES = BACKEND == BACKEND_FMA ? kMaxRep * D * 4 : 0;
-  static constexpr int P_OFF = Q_OFF + Q_BYTES;
-  static constexpr int P_BYTES = BACKEND == BACKEND_FMA ? kConsumerWarps * Cfg::TILE * kMaxRep * 4 : 0;
-  static constexpr int TOTAL = P_OFF + P_BYTES + 1024;  // + slack for 1024-byte alignment
+  static constexpr int TICKET_OFF = FLAG_OFF + 16;
+  static constexpr int TBL_OFF = (TICKET_OFF + 4 * Cfg::STAGES + 15) / 16 * 16;
+  static constexpr int Q_OFF = TBL_OFF + kTableCache * 4;
+  static constexpr int P_OFF = Q_OFF + Cfg::Q_BYTES;
+  static constexpr int TOTAL = P_OFF + Cfg::P_BYTES + 1024;  // + slack for 1024-byte alignment
+  static_assert(TOTAL <= 227 * 1024, "shared memory budget");
 };
 
 template <typename T, int D, int MODE, int BACKEND>
-__global__ void __launch_bounds__(kThreads) split_kernel(const __grid_constant__ SplitParams p,
+__global__ void __launch_bounds__(kThreads, 1) split_kernel(const __grid_constant__ SplitParams p,
                                                          const __grid_constant__ CUtensorMap mapk,
                                                          const __grid_constant__ CUtensorMap mapv) {
-  using Cfg = TileCfg<T, D, MODE>;
+  using Cfg = TileCfg<T, D, MODE, BACKEND>;
   using L = SplitSmem<T, D, MODE, BACKEND>;
   const int split = blockIdx.x;
   const int h = blockIdx.y;
@@ -911,12 +1078,14 @@ __global__ void __launch_bounds__(kThreads) split_kernel(const __grid_constant__
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::BAR_OFF);
   uint64_t* empty = full + Cfg::STAGES;
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::FLAG_OFF);
+  volatile int* tickets = reinterpret_cast<volatile int*>(smem + L::TICKET_OFF);
   const int warp = threadIdx.x >> 5;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < Cfg::STAGES; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
+      tickets[s] = -1;  // low 16 bits 0xffff: no use published yet
     }
     *abort_flag = 0;
     mbar_fence_init();
@@ -926,23 +1095,42 @@ __global__ void __launch_bounds__(kThreads) split_kernel(const __grid_constant__
     }
   }
   float* q_sm = reinterpret_cast<float*>(smem + L::Q_OFF);
+  T* q_smem_t = reinterpret_cast<T*>(smem + L::Q_OFF);
   float* p_sm = reinterpret_cast<float*>(smem + L::P_OFF);
-  if (BACKEND == BACKEND_FMA && warp < kConsumerWarps) {
+  int* tbl = reinterpret_cast<int*>(smem + L::TBL_OFF);
+  TableCache tc{tbl, 0, 0};
+  if (p.source == SRC_PAGED) {
+    const int blk0 = (tile0 * Cfg::TILE) >> p.log2_tpb;
+    int blk1 = ((tile0 + ntiles) * Cfg::TILE + p.tpb - 1) >> p.log2_tpb;
+    blk1 = min(blk1, g.nb);
+    tc.blk0 = blk0;
+    tc.n = max(0, min(blk1 - blk0, kTableCache));
+    for (int i = threadIdx.x; i < tc.n; i += kThreads) tbl[i] = p.block_table[(long long)b * p.max_blocks + blk0 + i];
+  }
+  if (warp < kConsumerWarps) {
     const long long qbase = ((long long)b * p.num_q_heads + (long long)h * p.n_rep) * D;
     for (int idx = threadIdx.x; idx < kMaxRep * D; idx += kConsumerWarps * 32) {
       const int r = idx / D;
-      q_sm[idx] = r < p.n_rep ? load_any(p.q, qbase + idx, p.q_dtype) : 0.f;
+      const float v = r < p.n_rep ? load_any(p.q, qbase + idx, p.q_dtype) : 0.f;
+      if constexpr (BACKEND == BACKEND_FMA) {
+        q_sm[idx] = v;
+      } else {
+        q_smem_t[idx] = T(v);
+      }
     }
   }
   __syncthreads();
 
   if (warp == kConsumerWarps) {
-    run_producer<Cfg, MODE>(p, &mapk, &mapv, stages, full, empty, b, h, tile0, ntiles, g, abort_flag);
+    run_producer<Cfg, MODE>(p, tc, &mapk, &mapv, stages, full, empty, tickets, b, h, tile0, ntiles, g,
+                            abort_flag);
   } else {
     if constexpr (BACKEND == BACKEND_MMA) {
-      run_consumer_mma<T, D, MODE>(p, stages, full, empty, b, h, tile0, ntiles, g, abort_flag, split);
+      run_consumer_mma<T, D, MODE>(p, tc, stages, full, empty, tickets, b, h, tile0, ntiles, g, abort_flag, split,
+                                   q_smem_t);
     } else {
-      run_consumer_fma<T, D, MODE>(p, stages, full, empty, b, h, tile0, ntiles, g, abort_flag, split, q_sm, p_sm);
+      run_consumer_fma<T, D, MODE>(p, tc, stages, full, empty, tickets, b, h, tile0, ntiles, g, abort_flag, split,
+                                   q_sm, p_sm);
     }
   }
 }
@@ -959,7 +1147,7 @@ struct SplitKernelInfo {
 
 template <typename T, int D, int MODE, int BACKEND>
 SplitKernelInfo split_kernel_info() {
-  using Cfg = TileCfg<T, D, MODE>;
+  using Cfg = TileCfg<T, D, MODE, BACKEND>;
   using L = SplitSmem<T, D, MODE, BACKEND>;
   SplitKernelInfo k;
   k.fn = reinterpret_cast<const void*>(&split_kernel<T, D, MODE, BACKEND>);

@@ -31,8 +31,11 @@ enum Mode { MODE_ONLINE = 0, MODE_STATS = 1, MODE_FIXED = 2 };
 enum Source { SRC_CONTIG = 0, SRC_PAGED = 1 };
 enum Backend { BACKEND_MMA = 1, BACKEND_FMA = 2 };
 
-constexpr int kConsumerWarps = 7;  // + 1 producer warp: 8 warps, 2 per scheduler, up to 255 registers each
-constexpr int kThreads = (kConsumerWarps + 1) * 32;
+// 6 consumer warps + 2 producer warps: 8 warps, 2 per scheduler, up to 255 registers each.
+// The consumer count must be even and at most the stage count (see consumer_wait).
+constexpr int kConsumerWarps = 6;
+constexpr int kProducerWarps = 2;
+constexpr int kThreads = (kConsumerWarps + kProducerWarps) * 32;
 constexpr int kMaxRep = 16;
 constexpr int kHostSlotBit = 0x40000000;
 constexpr int kStatusTimeout = 5;
@@ -163,10 +166,12 @@ struct TileCfg {
   // path's P buffer, the block-table cache, barriers.
   static constexpr int Q_BYTES = BACKEND == BACKEND_FMA ? kMaxRep * D * 4 : kMaxRep * D * ELT;
   static constexpr int P_BYTES = BACKEND == BACKEND_FMA ? kConsumerWarps * TILE * kMaxRep * 4 : 0;
-  static constexpr int EXTRA = Q_BYTES + P_BYTES + kTableCache * 4 + 1024;
+  static constexpr int EXTRA = Q_BYTES + P_BYTES + kTableCache * 4 + 1536;
   // A deep ring: each consumer warp holds a stage while it computes, the rest stay in flight.
-  static constexpr int STAGES_RAW = (200 * 1024 - EXTRA) / STAGE_BYTES;
-  static constexpr int STAGES = STAGES_RAW > 16 ? 16 : (STAGES_RAW < 4 ? 4 : STAGES_RAW);
+  // Even, so that each stage is always filled by the same one of the two producer warps.
+  static constexpr int STAGES_RAW = ((225 * 1024 - EXTRA) / STAGE_BYTES) & ~1;
+  static constexpr int STAGES = STAGES_RAW > 16 ? 16 : STAGES_RAW;
+  static_assert(STAGES >= kConsumerWarps && STAGES % 2 == 0, "stage ring too shallow for the consumer warps");
   static constexpr int STAGE_AREA = STAGES * STAGE_BYTES;
   static constexpr int MERGE_BYTES = kConsumerWarps * kMaxRep * (2 + (MODE == MODE_STATS ? 0 : D)) * 4;
   static_assert(MERGE_BYTES <= STAGE_AREA, "merge region must fit in the stage ring");
@@ -366,16 +371,17 @@ __device__ __forceinline__ void copy_sw_segments(const Hot& k, const TableCache&
   __syncwarp();
 }
 
-// The producer is one thread: per tile it waits for the stage to be free,
-// issues the TMA boxes of every device-resident segment, arrives on the
-// stage's full barrier and publishes the stage's ticket -- (use) in the low 16
-// bits, the mask of segments left to the consumer in the high bits -- as one
-// 32-bit store.
+// The producers are one thread each of two warps, taking alternate tiles (the
+// stage ring has an even length, so a stage is always filled by the same
+// producer).  Per tile: wait for the stage to be free, issue the TMA boxes of
+// every device-resident segment, record the stage's segment masks in shared
+// memory (bits 0-7: segments the consumer copies itself, bits 8-15: segments
+// holding data) and arrive on the stage's full barrier (release).
 template <class Cfg, int MODE>
 __device__ void run_producer(const SplitParams& p, const TableCache& tc, const CUtensorMap* mapk,
                              const CUtensorMap* mapv, uint8_t* stages, uint64_t* full, uint64_t* empty,
-                             volatile int* tickets, int b, int h, int tile0, int ntiles, const RowGeom& g,
-                             volatile int* abort_flag) {
+                             volatile int* infos, int b, int h, int tile0, int ntiles, const RowGeom& g,
+                             volatile int* abort_flag, int producer) {
   if ((threadIdx.x & 31) != 0) return;
   constexpr bool kNeedV = MODE != MODE_STATS;
   const Hot k = load_hot(p);
@@ -384,8 +390,8 @@ __device__ void run_producer(const SplitParams& p, const TableCache& tc, const C
   const int nseg = Cfg::TILE / br;
   const int block_tokens = g.nb * k.tpb;
   const uint32_t seg_bytes = (uint32_t)br * Cfg::ROW_BYTES * (kNeedV ? 2u : 1u);
-  int issued = 0;
-  for (int i = 0; i < ntiles; ++i) {
+  int last = -1;
+  for (int i = producer; i < ntiles; i += kProducerWarps) {
     const int s = i % Cfg::STAGES;
     const int use = i / Cfg::STAGES;
     if (use > 0 && !mbar_wait_bounded(&empty[s], (use - 1) & 1, k.wait_limit)) {
@@ -393,12 +399,13 @@ __device__ void run_producer(const SplitParams& p, const TableCache& tc, const C
       *abort_flag = 1;
       break;
     }
-    if (*abort_flag) break;
     uint8_t* kbuf = stages + s * Cfg::STAGE_BYTES;
     uint8_t* vbuf = kbuf + Cfg::TENSOR_BYTES;
     const int t0 = (tile0 + i) * Cfg::TILE;
     uint32_t sw_mask = 0;
+    uint32_t present = 0;  // segments whose rows hold data (device, host or tail)
     if (k.source == SRC_CONTIG) {
+      present = 1u;  // one segment: the whole tile
       mbar_expect_tx(&full[s], (uint32_t)Cfg::STAGE_BYTES);
 #pragma unroll
       for (int pn = 0; pn < Cfg::NPANEL; ++pn) {
@@ -411,6 +418,7 @@ __device__ void run_producer(const SplitParams& p, const TableCache& tc, const C
         if (tok >= g.hi || tok + br <= g.lo) continue;
         if (tok >= block_tokens) {
           sw_mask |= 1u << sg;  // tail rows
+          present |= 1u << sg;
           continue;
         }
         const int e = entry_at(k, tc, b, tok >> k.log2_tpb);
@@ -418,6 +426,7 @@ __device__ void run_producer(const SplitParams& p, const TableCache& tc, const C
           if (e >= 0) atomicExch(k.status, kStatusBadBlock);
           continue;
         }
+        present |= 1u << sg;
         if (e & kHostSlotBit) {
           sw_mask |= 1u << sg;
           continue;
@@ -433,13 +442,12 @@ __device__ void run_producer(const SplitParams& p, const TableCache& tc, const C
         }
       }
     }
-    mbar_arrive(&full[s]);
-    tickets[s] = (int)((sw_mask << 16) | (uint32_t)use);
-    issued = i + 1;
+    infos[s] = (int)((present << 8) | sw_mask);
+    mbar_arrive(&full[s]);  // release: the consumer that acquires the phase sees infos[s]
+    last = i;
   }
   // Drain: never leave the CTA with bulk copies still landing in its shared memory.
-  const int first = issued > Cfg::STAGES ? issued - Cfg::STAGES : 0;
-  for (int i = first; i < issued; ++i) {
+  for (int i = last; i >= 0 && i > last - Cfg::STAGES; i -= kProducerWarps) {
     if (!mbar_wait_bounded(&full[i % Cfg::STAGES], (i / Cfg::STAGES) & 1, k.wait_limit)) {
       atomicExch(k.status, kStatusTimeout);
       *abort_flag = 1;
@@ -450,38 +458,27 @@ __device__ void run_producer(const SplitParams& p, const TableCache& tc, const C
 
 // Consumer-side wait for tile i on stage s = i % STAGES (use n = i / STAGES).
 // Tiles of one stage go to different warps, so a warp can reach use n of a
-// stage while use n-1 is still loading; a parity wait posed about a phase that
-// is not yet the current one would alias the phase two back and succeed early.
-// The producer therefore publishes, per stage, the use it is filling (a ticket
-// written after the stage's previous use was released); the consumer first
-// waits for its ticket, which makes phase n the current phase of the full
-// barrier, then waits for that phase.  Lane 0 does the bounded waits; on
-// success every lane observes the completed phase so the TMA writes are
-// visible to it.
-__device__ __forceinline__ bool wait_ticket(volatile int* ticket, int use, uint64_t limit_ns, uint32_t* mask) {
-  int t = *ticket;
-#pragma unroll 1
-  for (int i = 0; i < 256 && (t & 0xffff) != use; ++i) t = *ticket;
-  if ((t & 0xffff) != use) {
-    const uint64_t start = global_timer_ns();
-    while (((t = *ticket) & 0xffff) != use) {
-      if (global_timer_ns() - start > limit_ns) return false;
-    }
-  }
-  *mask = ((uint32_t)t) >> 16;
-  return true;
-}
-
-// Returns false on timeout (abort); *mask = the tile's segments left to the consumer.
-__device__ __forceinline__ bool consumer_wait(const Hot& k, uint64_t* full_bar, volatile int* ticket, int use,
-                                              volatile int* abort_flag, uint32_t* mask) {
+// stage while use n-1 is still loading or being consumed; a parity wait posed
+// about a phase that is not yet the current one would alias the phase two back
+// and succeed early.  The warp therefore first waits for use n-1 to be
+// released (empty barrier, phase n-1) and then for use n to land (full
+// barrier, phase n).  The empty wait itself cannot alias: this warp's previous
+// tile, i - kConsumerWarps, was issued, and with STAGES >= kConsumerWarps (and
+// both counts even, so tiles i - STAGES and i - kConsumerWarps share a
+// producer) tile i - STAGES was issued before it -- after use n-2 of the stage
+// had been released.  Both waits suspend in hardware (mbarrier.try_wait) and
+// are bounded; lane 0 waits, then every lane observes the completed full phase
+// so the TMA writes are visible to it.  *info = the stage's segment masks.
+__device__ __forceinline__ bool consumer_wait(const Hot& k, uint64_t* full_bar, uint64_t* empty_bar,
+                                              volatile int* info, int use, volatile int* abort_flag, uint32_t* mask) {
   const int lane = threadIdx.x & 31;
   const uint32_t parity = use & 1;
   int ok = 1;
   uint32_t m = 0;
   if (lane == 0) {
-    ok = wait_ticket(ticket, use, k.wait_limit, &m) ? 1 : 0;
+    if (use > 0) ok = mbar_wait_bounded(empty_bar, (use - 1) & 1, k.wait_limit) ? 1 : 0;
     if (ok) ok = mbar_wait_bounded(full_bar, parity, k.wait_limit) ? 1 : 0;
+    if (ok) m = (uint32_t)*info;
   }
   ok = __shfl_sync(0xffffffffu, ok, 0);
   *mask = __shfl_sync(0xffffffffu, m, 0);
@@ -495,6 +492,38 @@ __device__ __forceinline__ bool consumer_wait(const Hot& k, uint64_t* full_bar, 
   while (!mbar_try_wait(full_bar, parity)) {
   }
   return true;
+}
+
+// Valid-token bits of a tile from its token range, the segments the producer
+// found present, and (chunk ops only) the caller's per-token 0/1 mask.
+template <int TILE>
+__device__ __forceinline__ void tile_bits_fast(const Hot& k, int b, int t0, const RowGeom& g, uint32_t present,
+                                               int seg_rows, uint32_t& lo_bits, uint32_t& hi_bits) {
+  const int lower = max(g.lo - t0, 0);
+  const int upper = min(g.hi - t0, TILE);
+  uint64_t m = 0;
+  if (upper > lower) {
+    const uint64_t hi_part = upper >= 64 ? ~0ull : ((1ull << upper) - 1ull);
+    m = hi_part & ~((1ull << lower) - 1ull);
+  }
+  if (present != 1u || seg_rows < TILE) {
+    uint64_t pm = 0;
+    const uint64_t seg = seg_rows >= 64 ? ~0ull : ((1ull << seg_rows) - 1ull);
+    for (int sg = 0; sg * seg_rows < TILE; ++sg)
+      if ((present >> sg) & 1u) pm |= seg << (sg * seg_rows);
+    m &= pm;
+  }
+  if (k.valid) {
+    const int lane = threadIdx.x & 31;
+    const bool v0 = lane < TILE && ((m >> lane) & 1ull) && k.valid[(long long)b * k.valid_stride + t0 + lane] != 0;
+    const bool v1 = TILE > 32 && ((m >> (32 + lane)) & 1ull) &&
+                    k.valid[(long long)b * k.valid_stride + t0 + 32 + lane] != 0;
+    lo_bits = __ballot_sync(0xffffffffu, v0);
+    hi_bits = __ballot_sync(0xffffffffu, v1);
+    return;
+  }
+  lo_bits = (uint32_t)m;
+  hi_bits = (uint32_t)(m >> 32);
 }
 
 // Zero the V rows of masked tokens so that 0 * (stale or non-finite) never
@@ -585,7 +614,7 @@ __device__ void merge_and_store(const SplitParams& p, float* mw, int b, int h, i
 // swizzled panels the XOR term only depends on the lane.
 template <typename T, int D, int MODE>
 __device__ void run_consumer_mma(const SplitParams& p, const TableCache& tc, uint8_t* stages, uint64_t* full,
-                                 uint64_t* empty, volatile int* tickets, int b, int h, int tile0, int ntiles,
+                                 uint64_t* empty, volatile int* infos, int b, int h, int tile0, int ntiles,
                                  const RowGeom& g, volatile int* abort_flag, int split, const T* q_smem) {
   using Cfg = TileCfg<T, D, MODE, BACKEND_MMA>;
   using Op = MmaOp<T>;
@@ -601,6 +630,7 @@ __device__ void run_consumer_mma(const SplitParams& p, const TableCache& tc, uin
   const int qh0 = h * n_rep;
   const int l7 = lane & 7;
   const Hot hk = load_hot(p);
+  const int seg_rows = hk.source == SRC_CONTIG ? Cfg::TILE : min(Cfg::TILE, hk.tpb);
   const float scale = p.scale;
   const float softcap = p.softcap;
   float2* const mass_part = p.mass_part;
@@ -656,13 +686,13 @@ __device__ void run_consumer_mma(const SplitParams& p, const TableCache& tc, uin
     const int s = i % Cfg::STAGES;
     if (*abort_flag) break;
     uint32_t swm;
-    if (!consumer_wait(hk, &full[s], &tickets[s], i / Cfg::STAGES, abort_flag, &swm)) break;
+    if (!consumer_wait(hk, &full[s], &empty[s], &infos[s], i / Cfg::STAGES, abort_flag, &swm)) break;
     const int t0 = (tile0 + i) * Cfg::TILE;
     uint8_t* kbuf = stages + s * Cfg::STAGE_BYTES;
     uint8_t* vbuf = kbuf + Cfg::TENSOR_BYTES;
-    if (swm) copy_sw_segments<Cfg, MODE != MODE_STATS>(hk, tc, g, b, h, t0, swm, kbuf, vbuf);
+    if (swm & 0xffu) copy_sw_segments<Cfg, MODE != MODE_STATS>(hk, tc, g, b, h, t0, swm & 0xffu, kbuf, vbuf);
     uint32_t vlo, vhi;
-    tile_bits<Cfg::TILE>(hk, tc, b, t0, g, vlo, vhi);
+    tile_bits_fast<Cfg::TILE>(hk, b, t0, g, swm >> 8, seg_rows, vlo, vhi);
     const uint64_t vmask = ((uint64_t)vhi << 32) | vlo;
     const bool all_valid = vmask == full_mask;
     const uint32_t kaddr = smem_u32(kbuf);
@@ -771,7 +801,7 @@ __device__ void run_consumer_mma(const SplitParams& p, const TableCache& tc, uin
         }
       }
     }
-    bool wrote = swm != 0;
+    bool wrote = (swm & 0xffu) != 0;
     if (MODE != MODE_STATS) {
       if (!all_valid) wrote |= zero_masked_rows<Cfg>(vbuf, vlo, vhi);
       const uint32_t vaddr = smem_u32(vbuf);
@@ -830,7 +860,7 @@ __device__ void run_consumer_mma(const SplitParams& p, const TableCache& tc, uin
 // column for P.V (p broadcast from shared memory); fp32 throughout.
 template <typename T, int D, int MODE>
 __device__ void run_consumer_fma(const SplitParams& p, const TableCache& tc, uint8_t* stages, uint64_t* full,
-                                 uint64_t* empty, volatile int* tickets, int b, int h, int tile0, int ntiles,
+                                 uint64_t* empty, volatile int* infos, int b, int h, int tile0, int ntiles,
                                  const RowGeom& g, volatile int* abort_flag, int split, const float* q_sm,
                                  float* p_sm_all) {
   using Cfg = TileCfg<T, D, MODE, BACKEND_FMA>;
@@ -844,6 +874,7 @@ __device__ void run_consumer_fma(const SplitParams& p, const TableCache& tc, uin
   const int qh0 = h * n_rep;
   float* p_sm = p_sm_all + warp * TILE * kMaxRep;
   const Hot hk = load_hot(p);
+  const int seg_rows = hk.source == SRC_CONTIG ? Cfg::TILE : min(Cfg::TILE, hk.tpb);
   const float scale = p.scale;
   const float softcap = p.softcap;
   float2* const mass_part = p.mass_part;
@@ -874,13 +905,13 @@ __device__ void run_consumer_fma(const SplitParams& p, const TableCache& tc, uin
     const int s = i % Cfg::STAGES;
     if (*abort_flag) break;
     uint32_t swm;
-    if (!consumer_wait(hk, &full[s], &tickets[s], i / Cfg::STAGES, abort_flag, &swm)) break;
+    if (!consumer_wait(hk, &full[s], &empty[s], &infos[s], i / Cfg::STAGES, abort_flag, &swm)) break;
     const int t0 = (tile0 + i) * TILE;
     uint8_t* kbuf = stages + s * Cfg::STAGE_BYTES;
     uint8_t* vbuf = kbuf + Cfg::TENSOR_BYTES;
-    if (swm) copy_sw_segments<Cfg, MODE != MODE_STATS>(hk, tc, g, b, h, t0, swm, kbuf, vbuf);
+    if (swm & 0xffu) copy_sw_segments<Cfg, MODE != MODE_STATS>(hk, tc, g, b, h, t0, swm & 0xffu, kbuf, vbuf);
     uint32_t vlo, vhi;
-    tile_bits<TILE>(hk, tc, b, t0, g, vlo, vhi);
+    tile_bits_fast<TILE>(hk, b, t0, g, swm >> 8, seg_rows, vlo, vhi);
     const uint32_t kaddr = smem_u32(kbuf);
 
     float sc[TPL][kMaxRep];
@@ -962,7 +993,7 @@ __device__ void run_consumer_fma(const SplitParams& p, const TableCache& tc, uin
         }
       }
     }
-    bool wrote = swm != 0;
+    bool wrote = (swm & 0xffu) != 0;
     if (MODE != MODE_STATS) {
 #pragma unroll
       for (int u = 0; u < TPL; ++u) {
@@ -1045,8 +1076,8 @@ struct SplitSmem {
   using Cfg = TileCfg<T, D, MODE, BACKEND>;
   static constexpr int BAR_OFF = Cfg::STAGE_AREA;
   static constexpr int FLAG_OFF = BAR_OFF + 2 * Cfg::STAGES * 8;
-  static constexpr int TICKET_OFF = FLAG_OFF + 16;
-  static constexpr int TBL_OFF = (TICKET_OFF + 4 * Cfg::STAGES + 15) / 16 * 16;
+  static constexpr int INFO_OFF = FLAG_OFF + 16;
+  static constexpr int TBL_OFF = (INFO_OFF + 4 * Cfg::STAGES + 15) / 16 * 16;
   static constexpr int Q_OFF = TBL_OFF + kTableCache * 4;
   static constexpr int P_OFF = Q_OFF + Cfg::Q_BYTES;
   static constexpr int TOTAL = P_OFF + Cfg::P_BYTES + 1024;  // + slack for 1024-byte alignment
@@ -1078,14 +1109,14 @@ __global__ void __launch_bounds__(kThreads, 1) split_kernel(const __grid_constan
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::BAR_OFF);
   uint64_t* empty = full + Cfg::STAGES;
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::FLAG_OFF);
-  volatile int* tickets = reinterpret_cast<volatile int*>(smem + L::TICKET_OFF);
+  volatile int* infos = reinterpret_cast<volatile int*>(smem + L::INFO_OFF);
   const int warp = threadIdx.x >> 5;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < Cfg::STAGES; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
-      tickets[s] = -1;  // low 16 bits 0xffff: no use published yet
+      infos[s] = 0;
     }
     *abort_flag = 0;
     mbar_fence_init();
@@ -1121,15 +1152,15 @@ __global__ void __launch_bounds__(kThreads, 1) split_kernel(const __grid_constan
   }
   __syncthreads();
 
-  if (warp == kConsumerWarps) {
-    run_producer<Cfg, MODE>(p, tc, &mapk, &mapv, stages, full, empty, tickets, b, h, tile0, ntiles, g,
-                            abort_flag);
+  if (warp >= kConsumerWarps) {
+    run_producer<Cfg, MODE>(p, tc, &mapk, &mapv, stages, full, empty, infos, b, h, tile0, ntiles, g, abort_flag,
+                            warp - kConsumerWarps);
   } else {
     if constexpr (BACKEND == BACKEND_MMA) {
-      run_consumer_mma<T, D, MODE>(p, tc, stages, full, empty, tickets, b, h, tile0, ntiles, g, abort_flag, split,
+      run_consumer_mma<T, D, MODE>(p, tc, stages, full, empty, infos, b, h, tile0, ntiles, g, abort_flag, split,
                                    q_smem_t);
     } else {
-      run_consumer_fma<T, D, MODE>(p, tc, stages, full, empty, tickets, b, h, tile0, ntiles, g, abort_flag, split,
+      run_consumer_fma<T, D, MODE>(p, tc, stages, full, empty, infos, b, h, tile0, ntiles, g, abort_flag, split,
                                    q_sm, p_sm);
     }
   }

@@ -18,7 +18,9 @@ import threading
 import torch
 
 PKG_ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-LIB_PATH = os.path.join(PKG_ROOT, "libpager_b200.so")
+# The in-tree build, unless PAGER_B200_LIB points elsewhere (e.g. when these modules are dropped
+# into the reference's own pager_hf package).
+LIB_PATH = os.environ.get("PAGER_B200_LIB") or os.path.join(PKG_ROOT, "libpager_b200.so")
 HEADER_PATH = os.path.join(os.path.dirname(PKG_ROOT), "include", "pager_b200.h")
 
 PAGER_OK = 0

@@ -139,6 +139,30 @@ int pager_paged_decode_attention(const void* q, int q_dtype, const void* dev_poo
                                  float* block_mass, float* mass_accum, int mass_mode, int backend, void* scratch,
                                  size_t scratch_bytes, void* stream);
 
+/* ---- The same fused paged decode attention for callers that cannot allocate device
+ *      memory (a client binding this C ABI from a host language without a CUDA allocator,
+ *      or a serving loop that forbids device allocation after start-up).  No counterpart in
+ *      the reference: it takes every argument of pager_paged_decode_attention except the
+ *      scratch buffer, and uses instead a fixed array of PAGER_NOALLOC_SCRATCH_BYTES of device
+ *      memory built into the library -- reserved on every GPU that loads the library until
+ *      the process exits.  Calls needing more scratch than that
+ *      (pager_paged_decode_scratch_bytes) fail with PAGER_ERR_SCRATCH.  All calls on a device
+ *      share the array and leave their contents in it (nothing needs to start at zero); calls
+ *      that overlap on the GPU race on it.  The first call on a device looks up the array's
+ *      address with that device current; make it before any stream capture.  Calls no
+ *      cudaMalloc / cudaFree. */
+#define PAGER_NOALLOC_SCRATCH_BYTES ((size_t)32 << 20)
+int pager_paged_decode_attention_noalloc(const void* q, int q_dtype, const void* dev_pool, int dev_slots,
+                                         const void* host_pool, int host_slots, int kv_dtype, int num_layers,
+                                         int layer, int num_kv_heads, int tokens_per_block, int head_dim,
+                                         const int32_t* block_table, int max_blocks, const int32_t* num_blocks,
+                                         const void* tail_k, const void* tail_v, const int32_t* tail_len,
+                                         int tail_cap, const int32_t* valid_lo, const int32_t* valid_hi,
+                                         const int32_t* active, int batch, int num_q_heads, float scale,
+                                         float softcap, int max_row_tokens, void* out, int out_dtype,
+                                         float* block_mass, float* mass_accum, int mass_mode, int backend,
+                                         void* stream);
+
 /* ---- Pinned host pool (the host tier of KVBlockStore, pager_hf/kv_block_store.py:45-46).
  *      cudaHostAlloc(Portable | Mapped): the returned pointer is readable by kernels
  *      on every device (zero-copy) and is the host address as well. */

@@ -638,6 +638,9 @@ int paged_plan(int batch, int hq, int hkv, int head_dim, int kv_dtype, int tpb, 
 }
 
 }  // namespace
+
+void set_last_error(const char* msg) { t_err = msg; }
+
 }  // namespace pager
 
 using namespace pager;

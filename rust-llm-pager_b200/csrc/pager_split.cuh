@@ -319,7 +319,7 @@ template <class Cfg>
 __device__ __forceinline__ void sw_copy_rows(uint32_t tile_base, int row0, const char* src, int nrows) {
   const int lane = threadIdx.x & 31;
   const int total = nrows * Cfg::CPR;
-  constexpr int U = 8;
+  constexpr int U = 4;  // 4 x 16 B in flight per lane: ample for the host link, few registers
   for (int c0 = 0; c0 < total; c0 += 32 * U) {
     uint4 v[U];
 #pragma unroll
@@ -344,29 +344,39 @@ __device__ __forceinline__ void sw_copy_rows(uint32_t tile_base, int row0, const
 // consumer warp that owns the tile, with 16-byte loads.  `mask` has one bit per
 // segment of min(TILE, tokens_per_block) rows.
 template <class Cfg, bool kNeedV>
-__device__ __forceinline__ void copy_sw_segments(const Hot& k, const TableCache& tc, const RowGeom& g, int b, int h,
-                                                 int t0, uint32_t mask, uint8_t* kbuf, uint8_t* vbuf) {
-  const int br = min(Cfg::TILE, k.tpb);
-  const int block_tokens = g.nb * k.tpb;
-  const long long head_bytes = (long long)k.tpb * Cfg::ROW_BYTES;
+__device__ __forceinline__ void copy_sw_segments(const SplitParams& p, const TableCache& tc, const RowGeom& g, int b,
+                                                 int h, int t0, uint32_t mask, uint8_t* kbuf, uint8_t* vbuf) {
+  // Slow path (host-pool blocks, tail rows): fields are read from the parameter block here
+  // rather than kept live across the tile loop.
+  const int tpb = p.tpb;
+  const int br = min(Cfg::TILE, tpb);
+  const int block_tokens = g.nb * tpb;
+  const long long head_bytes = (long long)tpb * Cfg::ROW_BYTES;
   const uint32_t kaddr = smem_u32(kbuf), vaddr = smem_u32(vbuf);
   for (int sg = 0; mask; ++sg, mask >>= 1) {
     if (!(mask & 1u)) continue;
     const int tok = t0 + sg * br;
+    const char* ksrc;
+    long long vdelta;
+    int n;
     if (tok < block_tokens) {
-      const int e = entry_at(k, tc, b, tok >> k.log2_tpb);
+      const int blk = tok >> p.log2_tpb;
+      const int i = blk - tc.blk0;
+      const int e = (i >= 0 && i < tc.n) ? tc.sm[i] : p.block_table[(long long)b * p.max_blocks + blk];
       const long long slot = e & (kHostSlotBit - 1);
-      const char* kb = k.host_pool + slot * k.slot_stride + (long long)k.layer * k.layer_stride +
-                       (long long)h * head_bytes + (long long)(tok & (k.tpb - 1)) * Cfg::ROW_BYTES;
-      sw_copy_rows<Cfg>(kaddr, sg * br, kb, br);
-      if (kNeedV) sw_copy_rows<Cfg>(vaddr, sg * br, kb + (long long)k.hkv * head_bytes, br);
+      ksrc = p.host_pool + slot * p.slot_stride_bytes + (long long)p.layer * p.layer_stride_bytes +
+             (long long)h * head_bytes + (long long)(tok & (tpb - 1)) * Cfg::ROW_BYTES;
+      vdelta = (long long)p.num_kv_heads * head_bytes;
+      n = br;
     } else {
-      const int tr = tok - block_tokens;
-      const int n = min(br, g.ntok - tok);
-      const long long off = (((long long)b * k.hkv + h) * k.tail_cap + tr) * Cfg::ROW_BYTES;
-      sw_copy_rows<Cfg>(kaddr, sg * br, k.tail_k + off, n);
-      if (kNeedV) sw_copy_rows<Cfg>(vaddr, sg * br, k.tail_v + off, n);
+      const long long off =
+          (((long long)b * p.num_kv_heads + h) * p.tail_cap + (tok - block_tokens)) * Cfg::ROW_BYTES;
+      ksrc = p.tail_k + off;
+      vdelta = p.tail_v - p.tail_k;
+      n = min(br, g.ntok - tok);
     }
+    sw_copy_rows<Cfg>(kaddr, sg * br, ksrc, n);
+    if (kNeedV) sw_copy_rows<Cfg>(vaddr, sg * br, ksrc + vdelta, n);
   }
   __syncwarp();
 }
@@ -469,22 +479,23 @@ __device__ void run_producer(const SplitParams& p, const TableCache& tc, const C
 // had been released.  Both waits suspend in hardware (mbarrier.try_wait) and
 // are bounded; lane 0 waits, then every lane observes the completed full phase
 // so the TMA writes are visible to it.  *info = the stage's segment masks.
-__device__ __forceinline__ bool consumer_wait(const Hot& k, uint64_t* full_bar, uint64_t* empty_bar,
-                                              volatile int* info, int use, volatile int* abort_flag, uint32_t* mask) {
+__device__ __forceinline__ bool consumer_wait(uint64_t wait_limit, int* status, uint64_t* full_bar,
+                                              uint64_t* empty_bar, volatile int* info, int use,
+                                              volatile int* abort_flag, uint32_t* mask) {
   const int lane = threadIdx.x & 31;
   const uint32_t parity = use & 1;
   int ok = 1;
   uint32_t m = 0;
   if (lane == 0) {
-    if (use > 0) ok = mbar_wait_bounded(empty_bar, (use - 1) & 1, k.wait_limit) ? 1 : 0;
-    if (ok) ok = mbar_wait_bounded(full_bar, parity, k.wait_limit) ? 1 : 0;
+    if (use > 0) ok = mbar_wait_bounded(empty_bar, (use - 1) & 1, wait_limit) ? 1 : 0;
+    if (ok) ok = mbar_wait_bounded(full_bar, parity, wait_limit) ? 1 : 0;
     if (ok) m = (uint32_t)*info;
   }
   ok = __shfl_sync(0xffffffffu, ok, 0);
   *mask = __shfl_sync(0xffffffffu, m, 0);
   if (!ok) {
     if (lane == 0) {
-      atomicExch(k.status, kStatusTimeout);
+      atomicExch(status, kStatusTimeout);
       *abort_flag = 1;
     }
     return false;
@@ -497,8 +508,9 @@ __device__ __forceinline__ bool consumer_wait(const Hot& k, uint64_t* full_bar, 
 // Valid-token bits of a tile from its token range, the segments the producer
 // found present, and (chunk ops only) the caller's per-token 0/1 mask.
 template <int TILE>
-__device__ __forceinline__ void tile_bits_fast(const Hot& k, int b, int t0, const RowGeom& g, uint32_t present,
-                                               int seg_rows, uint32_t& lo_bits, uint32_t& hi_bits) {
+__device__ __forceinline__ void tile_bits_fast(const int* valid, long long valid_stride, int b, int t0,
+                                               const RowGeom& g, uint32_t present, int seg_rows, uint32_t& lo_bits,
+                                               uint32_t& hi_bits) {
   const int lower = max(g.lo - t0, 0);
   const int upper = min(g.hi - t0, TILE);
   uint64_t m = 0;
@@ -513,11 +525,11 @@ __device__ __forceinline__ void tile_bits_fast(const Hot& k, int b, int t0, cons
       if ((present >> sg) & 1u) pm |= seg << (sg * seg_rows);
     m &= pm;
   }
-  if (k.valid) {
+  if (valid) {
     const int lane = threadIdx.x & 31;
-    const bool v0 = lane < TILE && ((m >> lane) & 1ull) && k.valid[(long long)b * k.valid_stride + t0 + lane] != 0;
+    const bool v0 = lane < TILE && ((m >> lane) & 1ull) && valid[(long long)b * valid_stride + t0 + lane] != 0;
     const bool v1 = TILE > 32 && ((m >> (32 + lane)) & 1ull) &&
-                    k.valid[(long long)b * k.valid_stride + t0 + 32 + lane] != 0;
+                    valid[(long long)b * valid_stride + t0 + 32 + lane] != 0;
     lo_bits = __ballot_sync(0xffffffffu, v0);
     hi_bits = __ballot_sync(0xffffffffu, v1);
     return;
@@ -629,8 +641,11 @@ __device__ void run_consumer_mma(const SplitParams& p, const TableCache& tc, uin
   const int n_rep = p.n_rep;
   const int qh0 = h * n_rep;
   const int l7 = lane & 7;
-  const Hot hk = load_hot(p);
-  const int seg_rows = hk.source == SRC_CONTIG ? Cfg::TILE : min(Cfg::TILE, hk.tpb);
+  const int seg_rows = p.source == SRC_CONTIG ? Cfg::TILE : min(Cfg::TILE, p.tpb);
+  const int* const valid = p.valid;
+  const long long valid_stride = p.valid_stride;
+  const uint64_t wait_limit = p.wait_limit_ns;
+  int* const status = p.status;
   const float scale = p.scale;
   const float softcap = p.softcap;
   float2* const mass_part = p.mass_part;
@@ -638,31 +653,10 @@ __device__ void run_consumer_mma(const SplitParams& p, const TableCache& tc, uin
   const int mass_gstride = p.mass_gstride;
   const int log2_group = p.log2_group;
 
-  uint32_t qa[KSTEPS][4];
-  {
-    const uint32_t qaddr = smem_u32(q_smem);
-    const int qrow = l7 + ((lane >> 3) & 1) * 8;
-#pragma unroll
-    for (int kk = 0; kk < KSTEPS; ++kk) {
-      const int col = 16 * kk + (lane >> 4) * 8;
-      ldmatrix_x4(qaddr + (qrow * D + col) * (int)sizeof(T), qa[kk][0], qa[kk][1], qa[kk][2], qa[kk][3]);
-    }
-  }
-  // K fragments: row 8j + l7, 16-byte chunk 2kk + (lane >> 3)
-  uint32_t koff[KSTEPS / 2];
-#pragma unroll
-  for (int kp = 0; kp < KSTEPS / 2; ++kp) {
-    const int c = 4 * kp + (lane >> 3);
-    koff[kp] = (c >> 3) * Cfg::PANEL_TILE_BYTES + l7 * 128 + (((c & 7) ^ l7) << 4);
-  }
-  // V fragments (transposed): row 16kt + ((lane>>3)&1)*8 + l7, chunk n + (lane >> 4)
-  uint32_t voff[NT_O / 2];
-#pragma unroll
-  for (int np = 0; np < NT_O / 2; ++np) {
-    const int c = 2 * np + (lane >> 4);
-    voff[np] = (c >> 3) * Cfg::PANEL_TILE_BYTES + (((lane >> 3) & 1) * 8 + l7) * 128 + (((c & 7) ^ l7) << 4);
-  }
-
+  // Q is kept in shared memory in the tiles' 128-byte swizzled layout (16 rows) and its
+  // fragments are re-read per tile: holding them in registers across the loop spilled.
+  const uint32_t qaddr = smem_u32(q_smem);
+  const int qrow = l7 + ((lane >> 3) & 1) * 8;
   float mfix_l2[2] = {0.f, 0.f};
   if (MODE == MODE_FIXED) {
 #pragma unroll
@@ -686,13 +680,13 @@ __device__ void run_consumer_mma(const SplitParams& p, const TableCache& tc, uin
     const int s = i % Cfg::STAGES;
     if (*abort_flag) break;
     uint32_t swm;
-    if (!consumer_wait(hk, &full[s], &empty[s], &infos[s], i / Cfg::STAGES, abort_flag, &swm)) break;
+    if (!consumer_wait(wait_limit, status, &full[s], &empty[s], &infos[s], i / Cfg::STAGES, abort_flag, &swm)) break;
     const int t0 = (tile0 + i) * Cfg::TILE;
     uint8_t* kbuf = stages + s * Cfg::STAGE_BYTES;
     uint8_t* vbuf = kbuf + Cfg::TENSOR_BYTES;
-    if (swm & 0xffu) copy_sw_segments<Cfg, MODE != MODE_STATS>(hk, tc, g, b, h, t0, swm & 0xffu, kbuf, vbuf);
+    if (swm & 0xffu) copy_sw_segments<Cfg, MODE != MODE_STATS>(p, tc, g, b, h, t0, swm & 0xffu, kbuf, vbuf);
     uint32_t vlo, vhi;
-    tile_bits_fast<Cfg::TILE>(hk, b, t0, g, swm >> 8, seg_rows, vlo, vhi);
+    tile_bits_fast<Cfg::TILE>(valid, valid_stride, b, t0, g, swm >> 8, seg_rows, vlo, vhi);
     const uint64_t vmask = ((uint64_t)vhi << 32) | vlo;
     const bool all_valid = vmask == full_mask;
     const uint32_t kaddr = smem_u32(kbuf);
@@ -701,13 +695,22 @@ __device__ void run_consumer_mma(const SplitParams& p, const TableCache& tc, uin
 #pragma unroll
     for (int j = 0; j < NT_S; ++j) sc[j][0] = sc[j][1] = sc[j][2] = sc[j][3] = 0.f;
 #pragma unroll
-    for (int j = 0; j < NT_S; ++j) {
+    for (int kp = 0; kp < KSTEPS / 2; ++kp) {
+      uint32_t qa0[4], qa1[4];
+      {
+        const int c0 = 4 * kp + (lane >> 4);  // A fragment chunk of k-step 2kp; +2 for 2kp+1
+        const int c1 = c0 + 2;
+        ldmatrix_x4(qaddr + (c0 >> 3) * 2048 + qrow * 128 + (((c0 & 7) ^ l7) << 4), qa0[0], qa0[1], qa0[2], qa0[3]);
+        ldmatrix_x4(qaddr + (c1 >> 3) * 2048 + qrow * 128 + (((c1 & 7) ^ l7) << 4), qa1[0], qa1[1], qa1[2], qa1[3]);
+      }
+      const int c = 4 * kp + (lane >> 3);
+      const uint32_t koff = (c >> 3) * Cfg::PANEL_TILE_BYTES + l7 * 128 + (((c & 7) ^ l7) << 4);
 #pragma unroll
-      for (int kp = 0; kp < KSTEPS / 2; ++kp) {
+      for (int j = 0; j < NT_S; ++j) {
         uint32_t b0, b1, b2, b3;
-        ldmatrix_x4(kaddr + koff[kp] + j * 8 * 128, b0, b1, b2, b3);
-        Op::run(sc[j], qa[2 * kp], b0, b1);
-        Op::run(sc[j], qa[2 * kp + 1], b2, b3);
+        ldmatrix_x4(kaddr + koff + j * 8 * 128, b0, b1, b2, b3);
+        Op::run(sc[j], qa0, b0, b1);
+        Op::run(sc[j], qa1, b2, b3);
       }
     }
     // scale, softcap, token mask (streaming_attention.py:158-161)
@@ -815,7 +818,10 @@ __device__ void run_consumer_mma(const SplitParams& p, const TableCache& tc, uin
 #pragma unroll
         for (int np = 0; np < NT_O / 2; ++np) {
           uint32_t b0, b1, b2, b3;
-          ldmatrix_x4_trans(vaddr + voff[np] + kt * 16 * 128, b0, b1, b2, b3);
+          const int c = 2 * np + (lane >> 4);
+          const uint32_t voff =
+              (c >> 3) * Cfg::PANEL_TILE_BYTES + (((lane >> 3) & 1) * 8 + l7) * 128 + (((c & 7) ^ l7) << 4);
+          ldmatrix_x4_trans(vaddr + voff + kt * 16 * 128, b0, b1, b2, b3);
           Op::run(o[2 * np], pa, b0, b1);
           Op::run(o[2 * np + 1], pa, b2, b3);
         }
@@ -873,8 +879,11 @@ __device__ void run_consumer_fma(const SplitParams& p, const TableCache& tc, uin
   const int n_rep = p.n_rep;
   const int qh0 = h * n_rep;
   float* p_sm = p_sm_all + warp * TILE * kMaxRep;
-  const Hot hk = load_hot(p);
-  const int seg_rows = hk.source == SRC_CONTIG ? Cfg::TILE : min(Cfg::TILE, hk.tpb);
+  const int seg_rows = p.source == SRC_CONTIG ? Cfg::TILE : min(Cfg::TILE, p.tpb);
+  const int* const valid = p.valid;
+  const long long valid_stride = p.valid_stride;
+  const uint64_t wait_limit = p.wait_limit_ns;
+  int* const status = p.status;
   const float scale = p.scale;
   const float softcap = p.softcap;
   float2* const mass_part = p.mass_part;
@@ -905,13 +914,13 @@ __device__ void run_consumer_fma(const SplitParams& p, const TableCache& tc, uin
     const int s = i % Cfg::STAGES;
     if (*abort_flag) break;
     uint32_t swm;
-    if (!consumer_wait(hk, &full[s], &empty[s], &infos[s], i / Cfg::STAGES, abort_flag, &swm)) break;
+    if (!consumer_wait(wait_limit, status, &full[s], &empty[s], &infos[s], i / Cfg::STAGES, abort_flag, &swm)) break;
     const int t0 = (tile0 + i) * TILE;
     uint8_t* kbuf = stages + s * Cfg::STAGE_BYTES;
     uint8_t* vbuf = kbuf + Cfg::TENSOR_BYTES;
-    if (swm & 0xffu) copy_sw_segments<Cfg, MODE != MODE_STATS>(hk, tc, g, b, h, t0, swm & 0xffu, kbuf, vbuf);
+    if (swm & 0xffu) copy_sw_segments<Cfg, MODE != MODE_STATS>(p, tc, g, b, h, t0, swm & 0xffu, kbuf, vbuf);
     uint32_t vlo, vhi;
-    tile_bits_fast<TILE>(hk, b, t0, g, swm >> 8, seg_rows, vlo, vhi);
+    tile_bits_fast<TILE>(valid, valid_stride, b, t0, g, swm >> 8, seg_rows, vlo, vhi);
     const uint32_t kaddr = smem_u32(kbuf);
 
     float sc[TPL][kMaxRep];
@@ -1146,7 +1155,12 @@ __global__ void __launch_bounds__(kThreads, 1) split_kernel(const __grid_constan
       if constexpr (BACKEND == BACKEND_FMA) {
         q_sm[idx] = v;
       } else {
-        q_smem_t[idx] = T(v);
+        // 128-byte swizzled, 16 rows per 128-byte panel (the consumers' ldmatrix layout)
+        const int col = idx % D;
+        const int byte = col * (int)sizeof(T);
+        const int chunk = byte >> 4;
+        const int off = (chunk >> 3) * 2048 + r * 128 + ((((chunk & 7) ^ (r & 7)) << 4) | (byte & 15));
+        *reinterpret_cast<T*>(reinterpret_cast<uint8_t*>(q_smem_t) + off) = T(v);
       }
     }
   }

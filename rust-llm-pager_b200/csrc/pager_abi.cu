@@ -333,39 +333,45 @@ __device__ float paged_block_head_mass(const PagedMassParams& p, int b, int r, i
   return s / lf;
 }
 
-__global__ void paged_mass_kernel(const PagedMassParams p) {
-  const int j = blockIdx.x * blockDim.x + threadIdx.x;
-  if (j >= p.max_blocks) return;
-  if (p.mass_mode == PAGER_MASS_BATCH_MEAN) {
-    float tot = 0.f;
-    for (int b = 0; b < p.batch; ++b) {
-      if (p.active && p.active[b] == 0) continue;
-      const RowGeom g = row_geom(p.geom, b);
-      if (j >= g.nb) continue;
-      int tb, te, ns;
-      geom_tiles(g, p.tile_shift, p.tiles_per_split, tb, te, ns);
-      for (int r = 0; r < p.num_q_heads; ++r) {
-        const float v = paged_block_head_mass(p, b, r, j, tb, te);
-        if (p.block_mass) p.block_mass[((long long)b * p.num_q_heads + r) * p.max_blocks + j] = v;
-        tot += v;
-      }
-    }
-    p.mass_accum[j] += tot / (float)(p.batch * p.num_q_heads);
-    return;
-  }
-  const int b = blockIdx.y;
-  if (p.active && p.active[b] == 0) return;
-  const RowGeom g = row_geom(p.geom, b);
-  if (j >= g.nb) return;
-  int tb, te, ns;
-  geom_tiles(g, p.tile_shift, p.tiles_per_split, tb, te, ns);
+// One CTA per (32 blocks, row): lane <-> block, warp <-> a subset of the query heads,
+// heads summed through shared memory.  In batch-mean mode one CTA walks all rows.
+constexpr int kMassWarps = 8;
+
+__global__ void __launch_bounds__(kMassWarps * 32) paged_mass_kernel(const PagedMassParams p) {
+  __shared__ float red[kMassWarps][32];
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const int j = blockIdx.x * 32 + lane;
+  const bool batch_mean = p.mass_mode == PAGER_MASS_BATCH_MEAN;
+  const int b_first = batch_mean ? 0 : blockIdx.y;
+  const int b_last = batch_mean ? p.batch : blockIdx.y + 1;
   float tot = 0.f;
-  for (int r = 0; r < p.num_q_heads; ++r) {
-    const float v = paged_block_head_mass(p, b, r, j, tb, te);
-    if (p.block_mass) p.block_mass[((long long)b * p.num_q_heads + r) * p.max_blocks + j] = v;
-    tot += v;
+  for (int b = b_first; b < b_last; ++b) {
+    if (p.active && p.active[b] == 0) continue;
+    const RowGeom g = row_geom(p.geom, b);
+    if (j >= g.nb || j >= p.max_blocks) continue;
+    int tb, te, ns;
+    geom_tiles(g, p.tile_shift, p.tiles_per_split, tb, te, ns);
+    for (int r = warp; r < p.num_q_heads; r += kMassWarps) {
+      const float v = paged_block_head_mass(p, b, r, j, tb, te);
+      if (p.block_mass) p.block_mass[((long long)b * p.num_q_heads + r) * p.max_blocks + j] = v;
+      tot += v;
+    }
   }
-  if (p.mass_mode == PAGER_MASS_ROW_MEAN) p.mass_accum[(long long)b * p.max_blocks + j] += tot / (float)p.num_q_heads;
+  red[warp][lane] = tot;
+  __syncthreads();
+  if (warp != 0 || j >= p.max_blocks || p.mass_mode == PAGER_MASS_NONE) return;
+  float sum = 0.f;
+#pragma unroll
+  for (int w = 0; w < kMassWarps; ++w) sum += red[w][lane];
+  if (batch_mean) {
+    p.mass_accum[j] += sum / (float)(p.batch * p.num_q_heads);
+  } else {
+    const int b = blockIdx.y;
+    if (p.active && p.active[b] == 0) return;
+    if (j >= row_geom(p.geom, b).nb) return;
+    p.mass_accum[(long long)b * p.max_blocks + j] += sum / (float)p.num_q_heads;
+  }
 }
 
 __global__ void finalize_kernel(const float* acc, const float* l, void* out, int out_dtype, long long n, int head_dim) {
@@ -956,8 +962,8 @@ int pager_paged_decode_attention(const void* q, int q_dtype, const void* dev_poo
     mp.block_mass = block_mass;
     mp.mass_accum = mass_accum;
     mp.mass_mode = mass_mode;
-    dim3 g2((max_blocks + 127) / 128, mass_mode == PAGER_MASS_BATCH_MEAN ? 1 : batch);
-    paged_mass_kernel<<<g2, 128, 0, st>>>(mp);
+    dim3 g2((max_blocks + 31) / 32, mass_mode == PAGER_MASS_BATCH_MEAN ? 1 : batch);
+    paged_mass_kernel<<<g2, kMassWarps * 32, 0, st>>>(mp);
     PAGER_CUDA(cudaGetLastError(), "mass launch");
   }
   return PAGER_OK;

@@ -39,6 +39,9 @@ for _p in (ROOT, os.path.join(ROOT, "rust-llm-pager_b200")):
         sys.path.insert(0, _p)
 
 METRIC = "decode-attn effective KV GB/s (HBM + host tiers) at 32k ctx"
+# (268.82 MB read + 4.33 MB written) / 268.75 MB of K/V per launch, from one ncu capture of the
+# split kernel on the prof-hbm workload (profiles/split_kernel_paged_hbm_prof-hbm.md).
+NCU_DRAM_PER_HBM_BYTE = (268.82 + 4.33) / 268.75
 
 WORKLOADS = {
     # BASELINE config 5 geometry at 32k: 40 GB HBM budget, overflow in the pinned host pool
@@ -456,6 +459,10 @@ def run_ours(args):
     achieved = bytes_per_launch / (launch_ms / 1000) / 1e9
     t_roof = wl.hbm_bytes / wl.L / (hbm_peak * 1e9) + (wl.host_bytes / wl.L / (h2d * 1e9) if wl.host_bytes else 0.0)
     combined_peak = bytes_per_launch / t_roof / 1e9
+    # DRAM traffic per launch: the ncu capture of the split kernel on the small HBM-resident case read
+    # and wrote NCU_DRAM_PER_HBM_BYTE bytes per algorithmic HBM byte; scaled here to this launch's HBM
+    # bytes (host-tier blocks cross the host link, not DRAM).
+    traffic = wl.hbm_bytes / wl.L * NCU_DRAM_PER_HBM_BYTE
     clocks = clk.summary()
     line = {
         "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
@@ -474,7 +481,9 @@ def run_ours(args):
         "decode_tokens_per_s": tokens_per_s,
         "roofline": {
             "bound": "hbm", "achieved": achieved, "peak": combined_peak, "unit": "GB/s",
-            "frac": achieved / combined_peak, "traffic": None,
+            "frac": achieved / combined_peak, "traffic": traffic,
+            "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of split_kernel on prof-hbm "
+                              f"({NCU_DRAM_PER_HBM_BYTE:.4f} B per algorithmic HBM byte), scaled to this launch",
             "kernel": "paged decode attention (split-KV + combine + mass) per layer",
             "peak_kind": f"combined roofline: HBM {hbm_peak:.0f} GB/s ({peak_src}) + host link {h2d:.1f} GB/s "
                          f"(measured live); peak = bytes / (hbm_bytes/HBM + host_bytes/link)",

@@ -387,6 +387,8 @@ def run_ours(args):
 
     world, rank, local = _dist_env()
     if world > 1:
+        # NCCL's banner and debug lines go to stderr: stdout carries exactly one JSON line
+        os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
         torch.cuda.set_device(local)
         from datetime import timedelta
 
@@ -394,14 +396,23 @@ def run_ours(args):
                                 device_id=torch.device("cuda", local))
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
+    from pager_hf.request_shard import local_requests, max_over_ranks, shard_requests
+
     w = WORKLOADS[args.workload]
-    wl = Workload(args.workload, device, seed=1234 + rank)
-    link = probe_link(wl, device)
+    # world x batch requests of equal length, routed by least load: each rank owns `batch` of them
+    owners = shard_requests(world * w["batch"], world)
+    mine = local_requests(owners, rank)
+    assert len(mine) == w["batch"], (len(mine), w["batch"])
+    wl = Workload(args.workload, device, seed=1234 + 7919 * mine[0])
 
     def barrier():
         if world > 1:
             dist.barrier(device_ids=[local])
         torch.cuda.synchronize(device)
+
+    # all ranks probe the host link at once: with N GPUs the pinned pools share host DRAM bandwidth
+    barrier()
+    link = probe_link(wl, device)
 
     # warm-up (also first-call setup: occupancy queries, smem attributes)
     for _ in range(max(args.warmup, 1)):
@@ -423,11 +434,7 @@ def run_ours(args):
         barrier()
     # The per-step synchronize above lets the event timings be read; it costs one
     # host round trip per step (a few microseconds against a ~100 ms step).
-    ms_total = start.elapsed_time(end)
-    t = torch.tensor([ms_total], dtype=torch.float64, device=device)
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms_total = float(t.item())
+    ms_total = max_over_ranks(start.elapsed_time(end), device)
     ms_step = ms_total / args.steps
     value = world * wl.bytes_per_step / (ms_step / 1000) / 1e9
     tokens_per_s = world * wl.B / (ms_step / 1000)
@@ -446,10 +453,7 @@ def run_ours(args):
         mass_host.copy_(wl.mass, non_blocking=True)
     e1.record()
     barrier()
-    e2e_ms = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=device)
-    if world > 1:
-        dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
-    e2e_step = float(e2e_ms.item()) / args.steps
+    e2e_step = max_over_ranks(e0.elapsed_time(e1), device) / args.steps
     e2e_value = world * wl.bytes_per_step / (e2e_step / 1000) / 1e9
 
     hbm_peak, peak_src = measured_peaks()

@@ -1,0 +1,545 @@
+"""KV block store over a device pool and a pinned host pool.
+
+Same API as the reference's ``pager_hf/kv_block_store.py:36-274``
+(``KVBlockStore``: ``put_gpu``, ``offload_to_cpu``, ``load_to_gpu``,
+``ensure_gpu/cpu``, ``apply_tiers``, ``reorder_batch_rows``, ``get_gpu``,
+``get_any``, ``summary``, resident-byte accounting, the RAM budget with its
+80 % warning and ``RuntimeError``), with the block storage the decode kernel
+reads directly:
+
+* a block of ``B`` batch rows occupies ``B`` consecutive *slots* (a slot
+  group) of a pool ``[slots, layers, 2 (K,V), kv_heads, tokens_per_block,
+  head_dim]``: the device pool in HBM (torch-allocated) or the pinned,
+  device-mapped host pool (``HostPool``);
+* a tier move is one contiguous ``cudaMemcpyAsync`` of the group on a copy
+  stream (pinned memory, so it runs at link speed and overlaps the compute
+  stream), instead of per-tensor synchronous ``.to()`` copies from pageable
+  memory (``kv_block_store.py:114-156``);
+* ``block_table()`` turns the store's residency into the int32 block table of
+  ``paged_decode_attention`` (slot, or slot | host bit), so no gather runs.
+
+``key``/``value`` tensors handed in and out keep the reference's layout
+``[layers, batch, block_len, kv_heads, head_dim]``; what ``get_gpu`` /
+``get_any`` return are views into the pools (same values, not contiguous).
+
+Differences, all deliberate:
+* every block has the geometry and dtype of the first one, and at most
+  ``tokens_per_block`` tokens (a shorter block is stored padded and counted at
+  its real size; ``block_table`` refuses short blocks, the kernel reads whole
+  blocks); the reference stores arbitrary tensors;
+* moves are stream-ordered: with ``sync=True`` (the default, the reference's
+  behaviour) calls return after the copies finish; ``apply_tiers(...,
+  sync=False)`` only orders the current stream after them;
+* the pools grow by doubling when full (device groups are copied on the GPU,
+  host groups into a new pinned pool), which changes their base pointers:
+  ``version`` increments, and a ``PagedDecodePlan`` built before must be
+  rebuilt.
+"""
+
+from __future__ import annotations
+
+import logging
+from collections.abc import Mapping
+from dataclasses import dataclass
+
+import torch
+
+from .host_pool import HostPool
+
+logger = logging.getLogger(__name__)
+
+# kv_block_store.py:10-13: warn once CPU-resident bytes pass this fraction of ram_budget_bytes
+_RAM_BUDGET_WARNING_THRESHOLD = 0.8
+HOST_SLOT_BIT = 0x40000000
+
+
+@dataclass
+class KVBlockStoreStats:
+    gpu_to_cpu_bytes: int = 0
+    cpu_to_gpu_bytes: int = 0
+    gpu_to_cpu_copies: int = 0
+    cpu_to_gpu_copies: int = 0
+    gpu_to_cpu_sec: float = 0.0
+    cpu_to_gpu_sec: float = 0.0
+
+
+def tensor_nbytes(tensor: torch.Tensor) -> int:
+    """Return how many bytes a tensor occupies."""
+    return tensor.numel() * tensor.element_size()
+
+
+def kv_nbytes(key: torch.Tensor, value: torch.Tensor) -> int:
+    """Return the combined byte size of a key/value tensor pair."""
+    return tensor_nbytes(key) + tensor_nbytes(value)
+
+
+class SlotGroups:
+    """Free list of slot groups in one pool (group g = slots [g*batch, (g+1)*batch))."""
+
+    def __init__(self, capacity: int = 0):
+        self.capacity = 0
+        self._free: list[int] = []
+        self.grow(capacity)
+
+    def grow(self, capacity: int) -> None:
+        if capacity < self.capacity:
+            raise ValueError("slot groups cannot shrink")
+        # lowest group first: keep the free list sorted descending so pop() returns the lowest
+        self._free = sorted(set(self._free) | set(range(self.capacity, capacity)), reverse=True)
+        self.capacity = capacity
+
+    def take(self) -> int | None:
+        return self._free.pop() if self._free else None
+
+    def give(self, group: int) -> None:
+        if not 0 <= group < self.capacity or group in self._free:
+            raise ValueError(f"slot group {group} is not in use")
+        self._free.append(group)
+        self._free.sort(reverse=True)
+
+    @property
+    def used(self) -> int:
+        return self.capacity - len(self._free)
+
+
+class _TierView(Mapping):
+    """Read-only ``block_id -> (key, value)`` mapping of one tier, the reference's
+    ``gpu_blocks`` / ``cpu_blocks`` dicts."""
+
+    def __init__(self, store: "KVBlockStore", on_gpu: bool):
+        self._s, self._gpu = store, on_gpu
+
+    def _ids(self):
+        return self._s._dev_group if self._gpu else self._s._host_group
+
+    def __getitem__(self, block_id):
+        ids = self._ids()
+        if block_id not in ids:
+            raise KeyError(block_id)
+        return self._s._kv_view(block_id, self._gpu)
+
+    def __iter__(self):
+        return iter(list(self._ids()))
+
+    def __len__(self):
+        return len(self._ids())
+
+    def __contains__(self, block_id):
+        return block_id in self._ids()
+
+
+class KVBlockStore:
+    """Blocks of KV cache in a device pool and a pinned host pool, indexed by block id."""
+
+    def __init__(self, tokens_per_block: int, ram_budget_bytes: int | None = None, *,
+                 gpu_capacity_blocks: int = 8, cpu_capacity_blocks: int = 8):
+        self.tokens_per_block = tokens_per_block
+        self.ram_budget_bytes = ram_budget_bytes
+        self._cap0 = (max(1, gpu_capacity_blocks), max(1, cpu_capacity_blocks))
+        self.stats = KVBlockStoreStats()
+        self.version = 0
+        # geometry, fixed by the first block
+        self.num_layers = self.batch = self.kv_heads = self.head_dim = None
+        self.dtype = self.device = None
+        self.dev_pool: torch.Tensor | None = None
+        self.host_pool: HostPool | None = None
+        self._dev_groups = SlotGroups()
+        self._host_groups = SlotGroups()
+        self._dev_group: dict[int, int] = {}  # block id -> group in the device pool
+        self._host_group: dict[int, int] = {}  # block id -> group in the host pool
+        self._tokens: dict[int, int] = {}  # block id -> tokens stored (<= tokens_per_block)
+        self._resident_gpu_bytes = 0
+        self._resident_cpu_bytes = 0
+        self._copy_stream = None
+        self._pending: list[tuple[str, torch.cuda.Event, torch.cuda.Event]] = []
+        self.gpu_blocks = _TierView(self, True)
+        self.cpu_blocks = _TierView(self, False)
+
+    # ------------------------------------------------------------------ geometry and pools
+    def _block_bytes(self, tokens: int) -> int:
+        return 2 * self.num_layers * self.batch * tokens * self.kv_heads * self.head_dim * self._elt
+
+    def _init_geometry(self, key: torch.Tensor) -> None:
+        L, B, t, H, D = key.shape
+        self.num_layers, self.batch, self.kv_heads, self.head_dim = L, B, H, D
+        self.dtype, self.device = key.dtype, key.device
+        self._elt = key.element_size()
+        self._copy_stream = torch.cuda.Stream(device=self.device)
+        self._alloc_pools(self._cap0[0], self._cap0[1], B)
+
+    def _slot_shape(self):
+        return (self.num_layers, 2, self.kv_heads, self.tokens_per_block, self.head_dim)
+
+    def _alloc_pools(self, dev_groups: int, host_groups: int, batch: int) -> None:
+        self.dev_pool = torch.empty((dev_groups * batch,) + self._slot_shape(), dtype=self.dtype, device=self.device)
+        self.host_pool = HostPool((host_groups * batch,) + self._slot_shape(), self.dtype)
+        self._dev_groups = SlotGroups(dev_groups)
+        self._host_groups = SlotGroups(host_groups)
+        self.version += 1
+
+    def _check_block(self, key: torch.Tensor, value: torch.Tensor) -> int:
+        if key.dim() != 5 or key.shape != value.shape:
+            raise ValueError(f"expected key/value of shape [layers, batch, block_len, kv_heads, head_dim], got "
+                             f"{tuple(key.shape)} and {tuple(value.shape)}")
+        if key.dtype != value.dtype:
+            raise ValueError("key and value must share a dtype")
+        if self.num_layers is None:
+            self._init_geometry(key)
+        L, B, t, H, D = key.shape
+        if (L, B, H, D) != (self.num_layers, self.batch, self.kv_heads, self.head_dim) or key.dtype != self.dtype:
+            raise ValueError(f"block geometry {(L, B, H, D)} {key.dtype} differs from the store's "
+                             f"{(self.num_layers, self.batch, self.kv_heads, self.head_dim)} {self.dtype}")
+        if key.device != self.device:
+            raise ValueError(f"block on {key.device}, store on {self.device}")
+        if not 0 < t <= self.tokens_per_block:
+            raise ValueError(f"block of {t} tokens; this store holds blocks of 1..{self.tokens_per_block} tokens")
+        return t
+
+    def _group_slots(self, group: int) -> slice:
+        return slice(group * self.batch, (group + 1) * self.batch)
+
+    def _take_dev_group(self) -> int:
+        g = self._dev_groups.take()
+        if g is None:
+            self._grow_dev(2 * self._dev_groups.capacity)
+            g = self._dev_groups.take()
+        return g
+
+    def _take_host_group(self) -> int:
+        g = self._host_groups.take()
+        if g is None:
+            self._grow_host(2 * self._host_groups.capacity)
+            g = self._host_groups.take()
+        return g
+
+    def _grow_dev(self, groups: int) -> None:
+        self._drain()
+        new = torch.empty((groups * self.batch,) + self._slot_shape(), dtype=self.dtype, device=self.device)
+        new[: self.dev_pool.shape[0]].copy_(self.dev_pool)
+        self.dev_pool = new
+        self._dev_groups.grow(groups)
+        self.version += 1
+
+    def _grow_host(self, groups: int) -> None:
+        self._drain()
+        new = HostPool((groups * self.batch,) + self._slot_shape(), self.dtype)
+        new.tensor[: self.host_pool.shape[0]].copy_(self.host_pool.tensor)
+        self.host_pool.close()
+        self.host_pool = new
+        self._host_groups.grow(groups)
+        self.version += 1
+
+    def _kv_view(self, block_id: int, on_gpu: bool):
+        pool = self.dev_pool if on_gpu else self.host_pool.tensor
+        g = (self._dev_group if on_gpu else self._host_group)[block_id]
+        t = self._tokens[block_id]
+        grp = pool[self._group_slots(g)]  # [B, L, 2, H, T, D]
+        key = grp[:, :, 0, :, :t].permute(1, 0, 3, 2, 4)
+        value = grp[:, :, 1, :, :t].permute(1, 0, 3, 2, 4)
+        return key, value
+
+    # ------------------------------------------------------------------ copy stream
+    def _copy(self, dst: torch.Tensor, src: torch.Tensor, kind: str) -> None:
+        s = self._copy_stream
+        s.wait_stream(torch.cuda.current_stream(self.device))
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(s):
+            e0.record(s)
+            dst.copy_(src, non_blocking=True)
+            e1.record(s)
+        self._pending.append((kind, e0, e1))
+
+    def _drain(self) -> None:
+        """Wait for pending tier copies and add their device time to the stats."""
+        if self._copy_stream is None:
+            return
+        self._copy_stream.synchronize()
+        for kind, e0, e1 in self._pending:
+            sec = e0.elapsed_time(e1) / 1000.0
+            if kind == "d2h":
+                self.stats.gpu_to_cpu_sec += sec
+            else:
+                self.stats.cpu_to_gpu_sec += sec
+        self._pending.clear()
+
+    def synchronize(self) -> None:
+        """Block until every tier move issued so far has landed."""
+        self._drain()
+
+    def _order_after_copies(self) -> None:
+        if self._copy_stream is not None:
+            torch.cuda.current_stream(self.device).wait_stream(self._copy_stream)
+
+    # ------------------------------------------------------------------ the reference API
+    def put_gpu(self, block_id: int, key: torch.Tensor, value: torch.Tensor) -> None:
+        """Register a block that already lives on the GPU (copied into a device slot group).
+
+        Registering an id that is already on the GPU replaces that block (the
+        reference replaces it too but counts its bytes twice)."""
+        if not key.is_cuda or not value.is_cuda:
+            raise ValueError("put_gpu expects CUDA tensors.")
+        if block_id in self._host_group:
+            raise ValueError(f"Block {block_id} already exists on CPU.")
+        t = self._check_block(key, value)
+        if block_id in self._dev_group:  # re-registering replaces the block in place
+            self._resident_gpu_bytes -= self._block_bytes(self._tokens[block_id])
+            g = self._dev_group[block_id]
+        else:
+            g = self._take_dev_group()
+        dst = self.dev_pool[self._group_slots(g)]
+        dst[:, :, 0, :, :t].copy_(key.detach().permute(1, 0, 3, 2, 4))
+        dst[:, :, 1, :, :t].copy_(value.detach().permute(1, 0, 3, 2, 4))
+        self._dev_group[block_id] = g
+        self._tokens[block_id] = t
+        self._resident_gpu_bytes += kv_nbytes(key, value)
+
+    def put_gpu_layers(self, block_id: int, keys, values) -> None:
+        """Register a block from per-layer HF tensors ``[batch, kv_heads, block_len, head_dim]``.
+
+        The layout of a slot holds exactly those tensors, so each layer is one
+        contiguous copy; no ``torch.stack`` of the layers (``kv_utils.py:37-53``).
+        """
+        if len(keys) != len(values) or not keys:
+            raise ValueError("need one key and one value tensor per layer")
+        k0 = keys[0]
+        B, H, t, D = k0.shape
+        probe = k0.new_empty((len(keys), B, t, H, D)) if self.num_layers is None else None
+        if probe is not None:
+            self._check_block(probe, probe)
+        if (len(keys), B, H, D) != (self.num_layers, self.batch, self.kv_heads, self.head_dim):
+            raise ValueError("layer tensors do not match the store's geometry")
+        if block_id in self._host_group:
+            raise ValueError(f"Block {block_id} already exists on CPU.")
+        if not 0 < t <= self.tokens_per_block:
+            raise ValueError(f"block of {t} tokens; this store holds blocks of 1..{self.tokens_per_block} tokens")
+        if block_id in self._dev_group:
+            self._resident_gpu_bytes -= self._block_bytes(self._tokens[block_id])
+            g = self._dev_group[block_id]
+        else:
+            g = self._take_dev_group()
+        dst = self.dev_pool[self._group_slots(g)]
+        for layer, (k, v) in enumerate(zip(keys, values)):
+            if k.device != self.device or k.dtype != self.dtype or tuple(k.shape) != (B, H, t, D):
+                raise ValueError(f"layer {layer}: tensor does not match the store")
+            dst[:, layer, 0, :, :t].copy_(k)
+            dst[:, layer, 1, :, :t].copy_(v)
+        self._dev_group[block_id] = g
+        self._tokens[block_id] = t
+        self._resident_gpu_bytes += self._block_bytes(t)
+
+    def has_gpu(self, block_id: int) -> bool:
+        return block_id in self._dev_group
+
+    def has_cpu(self, block_id: int) -> bool:
+        return block_id in self._host_group
+
+    def _offload(self, block_id: int) -> None:
+        if block_id not in self._dev_group:
+            raise KeyError(f"Block {block_id} is not on GPU.")
+        incoming = self._block_bytes(self._tokens[block_id])
+        if self.ram_budget_bytes is not None:
+            projected = self._resident_cpu_bytes + incoming
+            if projected > self.ram_budget_bytes:
+                logger.error("ram_budget exceeded: block %d would need %.2f MB, budget is %.2f MB.", block_id,
+                             projected / 1_000_000, self.ram_budget_bytes / 1_000_000)
+                raise RuntimeError(
+                    f"ram_budget exceeded: moving block {block_id} to CPU would need {projected / 1_000_000:.2f} MB, "
+                    f"budget is {self.ram_budget_bytes / 1_000_000:.2f} MB. There is no SSD tier yet, so overflow "
+                    "can't be absorbed further; use a shorter context, a larger ram_budget, or a bigger "
+                    "tokens_per_block.")
+            if projected > _RAM_BUDGET_WARNING_THRESHOLD * self.ram_budget_bytes:
+                logger.warning("ram_budget usage at %.0f%% after offloading block %d (%.2f MB of %.2f MB budget).",
+                               100.0 * projected / self.ram_budget_bytes, block_id, projected / 1_000_000,
+                               self.ram_budget_bytes / 1_000_000)
+        hg = self._take_host_group()
+        dg = self._dev_group.pop(block_id)
+        self._copy(self.host_pool.tensor[self._group_slots(hg)], self.dev_pool[self._group_slots(dg)], "d2h")
+        self._dev_groups.give(dg)
+        self._host_group[block_id] = hg
+        self._resident_gpu_bytes -= incoming
+        self._resident_cpu_bytes += incoming
+        self.stats.gpu_to_cpu_bytes += incoming
+        self.stats.gpu_to_cpu_copies += 1
+
+    def _load(self, block_id: int, device) -> None:
+        if block_id not in self._host_group:
+            raise KeyError(f"Block {block_id} is not on CPU.")
+        device = torch.device(device)
+        if device.type != "cuda":
+            raise ValueError("load_to_gpu expects a CUDA device.")
+        index = device.index if device.index is not None else torch.cuda.current_device()
+        if index != self.device.index:
+            raise ValueError(f"this store's device pool is on {self.device}, not {device}")
+        incoming = self._block_bytes(self._tokens[block_id])
+        dg = self._take_dev_group()
+        hg = self._host_group.pop(block_id)
+        self._copy(self.dev_pool[self._group_slots(dg)], self.host_pool.tensor[self._group_slots(hg)], "h2d")
+        self._host_groups.give(hg)
+        self._dev_group[block_id] = dg
+        self._resident_cpu_bytes -= incoming
+        self._resident_gpu_bytes += incoming
+        self.stats.cpu_to_gpu_bytes += incoming
+        self.stats.cpu_to_gpu_copies += 1
+
+    def offload_to_cpu(self, block_id: int) -> None:
+        """Move a block from GPU to CPU and record how long the copy took."""
+        self._offload(block_id)
+        self._drain()
+
+    def load_to_gpu(self, block_id: int, device: torch.device | str) -> None:
+        """Move a block from CPU to GPU and record how long the copy took."""
+        self._load(block_id, device)
+        self._drain()
+
+    def ensure_gpu(self, block_id: int, device: torch.device | str) -> None:
+        if self.has_gpu(block_id):
+            return
+        self.load_to_gpu(block_id, device)
+
+    def ensure_cpu(self, block_id: int) -> None:
+        if self.has_cpu(block_id):
+            return
+        self.offload_to_cpu(block_id)
+
+    def resident_gpu_bytes(self) -> int:
+        return self._resident_gpu_bytes
+
+    def resident_cpu_bytes(self) -> int:
+        return self._resident_cpu_bytes
+
+    def gpu_block_ids(self) -> list[int]:
+        return sorted(self._dev_group)
+
+    def cpu_block_ids(self) -> list[int]:
+        return sorted(self._host_group)
+
+    def summary(self) -> dict:
+        """Resident bytes and cumulative transfer stats as a plain dict (``kv_block_store.py:183-196``)."""
+        self._drain()
+        return {
+            "gpu_blocks": len(self._dev_group),
+            "cpu_blocks": len(self._host_group),
+            "resident_gpu_bytes": self.resident_gpu_bytes(),
+            "resident_cpu_bytes": self.resident_cpu_bytes(),
+            "gpu_to_cpu_bytes": self.stats.gpu_to_cpu_bytes,
+            "cpu_to_gpu_bytes": self.stats.cpu_to_gpu_bytes,
+            "gpu_to_cpu_copies": self.stats.gpu_to_cpu_copies,
+            "cpu_to_gpu_copies": self.stats.cpu_to_gpu_copies,
+            "gpu_to_cpu_sec": self.stats.gpu_to_cpu_sec,
+            "cpu_to_gpu_sec": self.stats.cpu_to_gpu_sec,
+        }
+
+    def apply_tiers(self, tiers: list[int], device: torch.device | str, sync: bool = True) -> dict[str, list[int]]:
+        """Move each block to the tier the pager assigned it (0 GPU, anything else CPU;
+        ids past the end of ``tiers`` go to CPU), in ascending block order like
+        ``kv_block_store.py:198-227``.  All copies are queued on the copy stream;
+        ``sync=True`` waits for them, ``sync=False`` orders the current stream after them.
+        A RAM-budget error leaves the moves before it done (as in the reference).
+        """
+        device = torch.device(device)
+        to_gpu: list[int] = []
+        to_cpu: list[int] = []
+        try:
+            for block_id in sorted(set(self._dev_group) | set(self._host_group)):
+                desired = tiers[block_id] if block_id < len(tiers) else 2
+                if desired == 0:
+                    if not self.has_gpu(block_id):
+                        self._load(block_id, device)
+                        to_gpu.append(block_id)
+                elif not self.has_cpu(block_id):
+                    self._offload(block_id)
+                    to_cpu.append(block_id)
+        except BaseException:
+            self._drain()
+            raise
+        if sync:
+            self._drain()
+        else:
+            self._order_after_copies()
+        return {"to_gpu": to_gpu, "to_cpu": to_cpu}
+
+    def reorder_batch_rows(self, new_row_indices: list[int]) -> None:
+        """Reindex every block's batch rows on whichever tier it lives (``kv_block_store.py:229-254``):
+        new row i takes old row ``new_row_indices[i]``; repeats duplicate, omissions drop.
+        A new row count re-lays both pools for the new batch size."""
+        idx = [int(i) for i in new_row_indices]
+        if self.batch is None:
+            return
+        if any(not -self.batch <= i < self.batch for i in idx):
+            raise IndexError(f"row index out of range for batch {self.batch}: {new_row_indices}")
+        idx = [i % self.batch for i in idx]
+        self._drain()
+        torch.cuda.current_stream(self.device).synchronize()
+        n = len(idx)
+        old_dev, old_host = self.dev_pool, self.host_pool
+        if n == self.batch:
+            new_dev, new_host = old_dev, old_host
+        else:
+            new_dev = torch.empty((self._dev_groups.capacity * n,) + self._slot_shape(), dtype=self.dtype,
+                                  device=self.device)
+            new_host = HostPool((self._host_groups.capacity * n,) + self._slot_shape(), self.dtype)
+        for groups, old, new, dev in ((self._dev_group, old_dev, new_dev, True),
+                                      (self._host_group, old_host.tensor, new_host.tensor, False)):
+            if not groups:
+                continue
+            src = [g * self.batch + i for g in groups.values() for i in idx]
+            dst = [g * n + r for g in groups.values() for r in range(n)]
+            where = self.device if dev else "cpu"
+            src_t = torch.tensor(src, dtype=torch.long, device=where)
+            dst_t = torch.tensor(dst, dtype=torch.long, device=where)
+            rows = old.index_select(0, src_t)
+            new.index_copy_(0, dst_t, rows)
+        torch.cuda.current_stream(self.device).synchronize()
+        if n != self.batch:
+            old_host.close()
+            self.dev_pool, self.host_pool = new_dev, new_host
+            self._resident_gpu_bytes = self._resident_gpu_bytes // self.batch * n
+            self._resident_cpu_bytes = self._resident_cpu_bytes // self.batch * n
+            self.batch = n
+            self.version += 1
+
+    def get_gpu(self, block_id: int) -> tuple[torch.Tensor, torch.Tensor]:
+        if block_id not in self._dev_group:
+            raise KeyError(f"Block {block_id} is not on GPU.")
+        return self._kv_view(block_id, True)
+
+    def get_any(self, block_id: int) -> tuple[torch.Tensor, torch.Tensor]:
+        """A block's (key, value) from whichever tier holds it, residency unchanged (``:256-274``)."""
+        if block_id in self._dev_group:
+            return self._kv_view(block_id, True)
+        if block_id in self._host_group:
+            self._drain()
+            return self._kv_view(block_id, False)
+        raise KeyError(f"Block {block_id} is not on GPU or CPU.")
+
+    # ------------------------------------------------------------------ fused-op bridge
+    def block_table(self, block_ids=None, device=None) -> torch.Tensor:
+        """int32 ``[batch, len(block_ids)]`` table for ``paged_decode_attention``: row r of block j
+        is ``slot`` (device pool) or ``slot | 0x40000000`` (host pool); absent blocks are -1.
+        ``block_ids`` defaults to ``0 .. max id``."""
+        if self.batch is None:
+            raise ValueError("the store holds no blocks yet")
+        if block_ids is None:
+            known = set(self._dev_group) | set(self._host_group)
+            block_ids = range(max(known) + 1) if known else range(0)
+        block_ids = list(block_ids)
+        table = torch.full((self.batch, len(block_ids)), -1, dtype=torch.int32)
+        for j, bid in enumerate(block_ids):
+            if bid in self._dev_group or bid in self._host_group:
+                if self._tokens[bid] != self.tokens_per_block:
+                    raise ValueError(f"block {bid} holds {self._tokens[bid]} of {self.tokens_per_block} tokens; "
+                                     "the decode op reads whole blocks")
+            if bid in self._dev_group:
+                base = self._dev_group[bid] * self.batch
+                table[:, j] = torch.arange(base, base + self.batch, dtype=torch.int32)
+            elif bid in self._host_group:
+                base = self._host_group[bid] * self.batch
+                table[:, j] = torch.arange(base, base + self.batch, dtype=torch.int32) | HOST_SLOT_BIT
+        return table.to(device if device is not None else self.device)
+
+    def close(self) -> None:
+        """Free the pinned host pool now (it is also freed when the store is collected)."""
+        self._drain()
+        if self.host_pool is not None:
+            self.host_pool.close()
+            self.host_pool = None

@@ -163,6 +163,17 @@ int pager_paged_decode_attention_noalloc(const void* q, int q_dtype, const void*
                                          float* block_mass, float* mass_accum, int mass_mode, int backend,
                                          void* stream);
 
+/* ---- Writing one decode step's new token into pool slots.
+ *      Replaces the tail concatenation of a decode step (pager_hf/batched_decode.py:170-171,
+ *      the DynamicCache update of paged_model.py's patched forward): row b's new K and V
+ *      (k_new / v_new [batch, kv_heads, head_dim], the pool's dtype) are written at token
+ *      positions[b] of pool slot slots[b], layer `layer`.  A row with slots[b] < 0 is
+ *      skipped; a slot outside [0, pool_slots) or a position outside [0, tokens_per_block)
+ *      is not written and sets the device status word to 6. */
+int pager_append_tokens(void* pool, int dtype, int pool_slots, int num_layers, int layer, int num_kv_heads,
+                        int tokens_per_block, int head_dim, const int32_t* slots, const int32_t* positions,
+                        const void* k_new, const void* v_new, int batch, void* stream);
+
 /* ---- Pinned host pool (the host tier of KVBlockStore, pager_hf/kv_block_store.py:45-46).
  *      cudaHostAlloc(Portable | Mapped): the returned pointer is readable by kernels
  *      on every device (zero-copy) and is the host address as well. */

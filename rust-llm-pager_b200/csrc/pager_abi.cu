@@ -647,6 +647,15 @@ int paged_plan(int batch, int hq, int hkv, int head_dim, int kv_dtype, int tpb, 
 
 void set_last_error(const char* msg) { t_err = msg; }
 
+// Device status word of the current device, for kernels compiled in other files.
+int current_status_word(int** out) {
+  DevInfo* d = nullptr;
+  const int rc = device_info(&d);
+  if (rc) return rc;
+  *out = d->status;
+  return PAGER_OK;
+}
+
 }  // namespace pager
 
 using namespace pager;

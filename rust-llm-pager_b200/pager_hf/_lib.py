@@ -65,6 +65,7 @@ _SIGNATURES = {
     "pager_paged_decode_attention_noalloc": (_i, [_vp, _i, _vp, _i, _vp, _i, _i, _i, _i, _i, _i, _i, _vp, _i, _vp,
                                                   _vp, _vp, _vp, _i, _vp, _vp, _vp, _i, _i, _f, _f, _i, _vp, _i,
                                                   _vp, _vp, _i, _i, _vp]),
+    "pager_append_tokens": (_i, [_vp, _i, _i, _i, _i, _i, _i, _i, _vp, _vp, _vp, _vp, _i, _vp]),
     "pager_host_pool_alloc": (_i, [_sz, ctypes.POINTER(_vp)]),
     "pager_host_pool_free": (_i, [_vp]),
     "pager_probe_h2d_copy_gbs": (_i, [_vp, _vp, _sz, _i, _vp, ctypes.POINTER(ctypes.c_double)]),

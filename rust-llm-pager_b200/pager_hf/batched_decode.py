@@ -1,0 +1,213 @@
+"""Cross-session batched decode attention: one launch per layer for many sessions.
+
+The attention half of the reference's ``batched_decode_step``
+(``pager_hf/batched_decode.py:32-348``): several single-row decode sessions,
+each with its own block store and pager, advance by one token with one fused
+``paged_decode_attention`` launch per layer instead of a per-row, per-block
+Python gather (``:143-219``) and a group loop.  The model half (projections,
+RoPE, MLP, the logits) belongs to the caller: ``layer()`` takes the layer's
+query and new key/value rows and returns the attention output.
+
+B200 layout: the sessions share one ``KVPools`` (device pool + pinned host
+pool), so a single int32 block table names every session's blocks on either
+tier.  A session's tail (tokens after its last full block) lives in a device
+pool slot; each step's new K/V is written into it (``pager_append_tokens``)
+and the decode op reads it as the row's last block with ``valid_hi`` marking
+its real tokens.  When the tail reaches ``tokens_per_block`` tokens it already
+is a full block in the pool: it is registered with the store without a copy
+(the reference stacks and copies it, ``paged_model.py:1210-1233``).
+
+Lifted restrictions of the reference (``batched_decode.py:80-108``): tails
+need not have equal lengths, sessions may use sliding windows (per-row
+``valid_lo``), and attention-scoring and uniform policies may share a launch.
+After ``finish()``, each session's pager sees exactly what the reference's
+post-step sequence gives it (``:320-338``): ``on_step(query_block, 0,
+block_attention)``, ``force_rebalance`` when a block was added, then
+``apply_tiers``.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from . import _lib as L
+from .kv_block_store import KVBlockStore, KVPools
+from .streaming_attention import PagedDecodePlan
+
+_SCORING_POLICIES = frozenset({"heavy_hitter", "sinks_heavy_hitter"})
+
+
+class DecodeSession:
+    """One single-row decode session over shared pools: blocks, tail slot, pager."""
+
+    def __init__(self, pools: KVPools, *, pager_kwargs: dict | None = None, ram_budget_bytes: int | None = None,
+                 sliding_window: int | None = None, needs_attention: bool | None = None):
+        if pools.rows_per_group != 1:
+            raise ValueError("decode sessions are single-row: the shared pools must have rows_per_group=1")
+        self.pools = pools
+        self.store = KVBlockStore(pools.tokens_per_block, ram_budget_bytes, pools=pools)
+        self.pager = None
+        if pager_kwargs is not None:
+            import pager as _pager
+
+            self.pager = _pager.PyPager(**pager_kwargs)
+        policy = (pager_kwargs or {}).get("policy", "heavy_hitter")
+        self.needs_attention = (policy in _SCORING_POLICIES) if needs_attention is None else bool(needs_attention)
+        self.sliding_window = sliding_window
+        self.num_blocks = 0
+        self.tail_len = 0
+        self.tail_group = pools.take_dev_group()
+        self.mass_accum: torch.Tensor | None = None
+
+    @property
+    def tail_slot(self) -> int:
+        return self.tail_group
+
+    @property
+    def num_tokens(self) -> int:
+        return self.num_blocks * self.pools.tokens_per_block + self.tail_len
+
+    def prefill(self, keys, values) -> None:
+        """Load a prompt's KV: per layer ``[1, kv_heads, T, head_dim]`` (the HF cache layout).
+        Full blocks go to the device pool as blocks 0.., the rest into the tail slot."""
+        p = self.pools
+        if len(keys) != p.num_layers or len(values) != p.num_layers:
+            raise ValueError(f"need {p.num_layers} key and value tensors")
+        T = keys[0].shape[2]
+        tpb = p.tokens_per_block
+        full = T // tpb
+        for j in range(full):
+            self.store.put_gpu_layers(self.num_blocks, [k[:, :, j * tpb:(j + 1) * tpb] for k in keys],
+                                      [v[:, :, j * tpb:(j + 1) * tpb] for v in values])
+            self.num_blocks += 1
+        rem = T - full * tpb
+        for layer, (k, v) in enumerate(zip(keys, values)):
+            p.dev_pool[self.tail_slot, layer, 0, :, :rem].copy_(k[0, :, full * tpb:])
+            p.dev_pool[self.tail_slot, layer, 1, :, :rem].copy_(v[0, :, full * tpb:])
+        self.tail_len = rem
+
+    def block_attention(self, num_layers: int) -> list[float]:
+        """``PagedModel._finalize_streaming_block_attention`` (``paged_model.py:865-876``)."""
+        n = self.num_blocks
+        if n == 0 or self.mass_accum is None:
+            return [1.0 / n] * n if n else []
+        averaged = (self.mass_accum / num_layers).tolist()
+        total = sum(averaged)
+        if total <= 0:
+            return [1.0 / n] * n
+        return [x / total for x in averaged]
+
+    def close(self) -> None:
+        self.store.close()
+        self.pools.dev_groups.give(self.tail_group)
+
+
+class BatchedDecodeAttention:
+    """One decode step of attention for ``sessions``: ``layer()`` per layer, then ``finish()``."""
+
+    def __init__(self, sessions: list[DecodeSession], num_query_heads: int, *, scale: float | None = None,
+                 softcap: float | None = None):
+        if not sessions:
+            raise ValueError("batched decode needs at least one session")
+        pools = sessions[0].pools
+        for s in sessions:
+            if s.pools is not pools:
+                raise ValueError("batched decode requires every session to share the same KVPools")
+        self.sessions, self.pools = list(sessions), pools
+        S, tpb = len(sessions), pools.tokens_per_block
+        self.device = pools.device
+        width = max(s.num_blocks for s in sessions) + 1  # + the tail slot
+        table = torch.full((S, width), -1, dtype=torch.int32)
+        nblk, lo, hi, slots, pos = [], [], [], [], []
+        any_window = False
+        for r, s in enumerate(sessions):
+            if s.num_blocks:
+                table[r, :s.num_blocks] = s.store.block_table(range(s.num_blocks), device="cpu")[0]
+            table[r, s.num_blocks] = s.tail_slot
+            nblk.append(s.num_blocks + 1)
+            total = s.num_tokens + 1  # with this step's token
+            hi.append(total)
+            if s.sliding_window is not None:
+                any_window = True
+                lo.append(max(0, total - int(s.sliding_window)))  # keeps positions > pos - window
+            else:
+                lo.append(0)
+            slots.append(s.tail_slot)
+            pos.append(s.tail_len)
+        i32 = dict(dtype=torch.int32, device=self.device)
+        self.table = table.to(self.device)
+        self.num_blocks = torch.tensor(nblk, **i32)
+        self.valid_hi = torch.tensor(hi, **i32)
+        self.valid_lo = torch.tensor(lo, **i32) if any_window else None
+        self.slots = torch.tensor(slots, **i32)
+        self.positions = torch.tensor(pos, **i32)
+        self.needs_attention = any(s.needs_attention for s in sessions)
+        self.mass = torch.zeros(S, width, dtype=torch.float32, device=self.device) if self.needs_attention else None
+        self.plan = PagedDecodePlan(
+            batch=S, num_query_heads=num_query_heads, dev_pool=pools.dev_pool, host_pool=pools.host_pool.tensor,
+            num_layers=pools.num_layers, tokens_per_block=tpb, block_table=self.table, num_blocks=self.num_blocks,
+            max_row_tokens=width * tpb, valid_lo=self.valid_lo, valid_hi=self.valid_hi, scale=scale,
+            softcap=softcap, mass_accum=self.mass, mass_mode="row_mean" if self.needs_attention else "none")
+        self._layers_done = 0
+        self._lib = L.lib()
+
+    def layer(self, layer: int, q: torch.Tensor, k_new: torch.Tensor, v_new: torch.Tensor,
+              out: torch.Tensor | None = None) -> torch.Tensor:
+        """Attention of one layer: q ``[S, Hq, D]``; k_new / v_new ``[S, Hkv, D]`` (or ``[S, Hkv, 1, D]``)
+        in the pools' dtype.  Writes the new token into each tail slot, then runs the fused op."""
+        p = self.pools
+        S = len(self.sessions)
+        k_new = k_new.reshape(S, p.kv_heads, p.head_dim).contiguous()
+        v_new = v_new.reshape(S, p.kv_heads, p.head_dim).contiguous()
+        if k_new.dtype != p.dtype or v_new.dtype != p.dtype or k_new.device != self.device:
+            raise ValueError("k_new / v_new must be on the pools' device in the pools' dtype")
+        if p.dev_pool.data_ptr() != self.plan.dev_pool.data_ptr():
+            raise RuntimeError("the shared pools grew after this step was planned; plan the step again")
+        stream = torch.cuda.current_stream(self.device).cuda_stream
+        L.check(self._lib.pager_append_tokens(
+            p.dev_pool.data_ptr(), L.DTYPE_CODE[p.dtype], p.dev_pool.shape[0], p.num_layers, layer, p.kv_heads,
+            p.tokens_per_block, p.head_dim, self.slots.data_ptr(), self.positions.data_ptr(), k_new.data_ptr(),
+            v_new.data_ptr(), S, stream))
+        if out is None:
+            out = torch.empty(q.shape, dtype=q.dtype, device=self.device)
+        self.plan.run(q.contiguous(), layer, out)
+        self._layers_done += 1
+        return out
+
+    def finish(self, apply_tiers: bool = True) -> list[list[float]]:
+        """Advance every session by the decoded token (``batched_decode.py:320-338``): roll a full
+        tail into a block, hand the step's block attention to the pager, move blocks to the tiers
+        it picks.  Returns each session's block attention list."""
+        p = self.pools
+        tpb = p.tokens_per_block
+        mass = self.mass.cpu() if self.mass is not None else None
+        result = []
+        for r, s in enumerate(self.sessions):
+            old_nb = s.num_blocks
+            s.mass_accum = mass[r, :old_nb].clone() if (mass is not None and s.needs_attention) else None
+            s.tail_len += 1
+            added = []
+            if s.tail_len == tpb:  # the tail slot now holds a full block: adopt it, take a fresh slot
+                s.store.adopt_gpu_group(s.num_blocks, s.tail_group)
+                added.append(s.num_blocks)
+                s.num_blocks += 1
+                s.tail_group = p.take_dev_group()
+                s.tail_len = 0
+            if s.num_blocks == 0:
+                result.append([])
+                continue
+            if s.needs_attention:
+                attention = s.block_attention(p.num_layers)
+            else:
+                attention = [1.0 / s.num_blocks] * s.num_blocks
+            result.append(attention)
+            if s.pager is not None:
+                query_block = s.num_blocks - 1
+                s.pager.on_step(query_block, 0, attention)
+                if added:
+                    s.pager.force_rebalance(query_block)
+                if apply_tiers:
+                    s.store.apply_tiers(s.pager.tiers(), self.device, sync=False)
+        return result
+
+

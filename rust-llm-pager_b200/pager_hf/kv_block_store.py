@@ -128,54 +128,122 @@ class _TierView(Mapping):
         return block_id in self._ids()
 
 
+class KVPools:
+    """A device pool and a pinned host pool of KV slots, with their slot-group allocators.
+
+    One store owns a private ``KVPools`` by default; decode sessions that are
+    batched into one launch share one (``KVBlockStore(..., pools=shared)``), so
+    that a single block table can name every session's blocks.  A slot group is
+    ``rows_per_group`` consecutive slots (one per batch row of a block).
+    Growing a pool (doubling) changes its base pointer and bumps ``version``.
+    """
+
+    def __init__(self, *, num_layers: int, kv_heads: int, head_dim: int, tokens_per_block: int,
+                 dtype: torch.dtype, device, rows_per_group: int = 1, gpu_groups: int = 8, cpu_groups: int = 8):
+        self.num_layers, self.kv_heads, self.head_dim = num_layers, kv_heads, head_dim
+        self.tokens_per_block, self.dtype = tokens_per_block, dtype
+        self.elt = torch.tensor([], dtype=dtype).element_size()
+        self.device = torch.device(device)
+        if self.device.type != "cuda":
+            raise ValueError("KVPools needs a CUDA device for its device pool.")
+        if self.device.index is None:
+            self.device = torch.device("cuda", torch.cuda.current_device())
+        self.rows_per_group = rows_per_group
+        self.copy_stream = torch.cuda.Stream(device=self.device)
+        self.version = 0
+        self._alloc(max(1, gpu_groups), max(1, cpu_groups), rows_per_group)
+
+    def slot_shape(self):
+        return (self.num_layers, 2, self.kv_heads, self.tokens_per_block, self.head_dim)
+
+    def _alloc(self, gpu_groups: int, cpu_groups: int, rows: int) -> None:
+        self.dev_pool = torch.empty((gpu_groups * rows,) + self.slot_shape(), dtype=self.dtype, device=self.device)
+        self.host_pool = HostPool((cpu_groups * rows,) + self.slot_shape(), self.dtype)
+        self.dev_groups = SlotGroups(gpu_groups)
+        self.host_groups = SlotGroups(cpu_groups)
+        self.rows_per_group = rows
+        self.version += 1
+
+    def group_slots(self, group: int) -> slice:
+        return slice(group * self.rows_per_group, (group + 1) * self.rows_per_group)
+
+    def take_dev_group(self) -> int:
+        g = self.dev_groups.take()
+        if g is None:
+            self.grow_dev(2 * self.dev_groups.capacity)
+            g = self.dev_groups.take()
+        return g
+
+    def take_host_group(self) -> int:
+        g = self.host_groups.take()
+        if g is None:
+            self.grow_host(2 * self.host_groups.capacity)
+            g = self.host_groups.take()
+        return g
+
+    def grow_dev(self, groups: int) -> None:
+        self.copy_stream.synchronize()
+        new = torch.empty((groups * self.rows_per_group,) + self.slot_shape(), dtype=self.dtype, device=self.device)
+        new[: self.dev_pool.shape[0]].copy_(self.dev_pool)
+        self.dev_pool = new
+        self.dev_groups.grow(groups)
+        self.version += 1
+
+    def grow_host(self, groups: int) -> None:
+        self.copy_stream.synchronize()
+        new = HostPool((groups * self.rows_per_group,) + self.slot_shape(), self.dtype)
+        new.tensor[: self.host_pool.shape[0]].copy_(self.host_pool.tensor)
+        self.host_pool.close()
+        self.host_pool = new
+        self.host_groups.grow(groups)
+        self.version += 1
+
+    def close(self) -> None:
+        self.copy_stream.synchronize()
+        if self.host_pool is not None:
+            self.host_pool.close()
+            self.host_pool = None
+
+
 class KVBlockStore:
     """Blocks of KV cache in a device pool and a pinned host pool, indexed by block id."""
 
     def __init__(self, tokens_per_block: int, ram_budget_bytes: int | None = None, *,
-                 gpu_capacity_blocks: int = 8, cpu_capacity_blocks: int = 8):
+                 gpu_capacity_blocks: int = 8, cpu_capacity_blocks: int = 8, pools: KVPools | None = None):
         self.tokens_per_block = tokens_per_block
         self.ram_budget_bytes = ram_budget_bytes
         self._cap0 = (max(1, gpu_capacity_blocks), max(1, cpu_capacity_blocks))
         self.stats = KVBlockStoreStats()
-        self.version = 0
-        # geometry, fixed by the first block
-        self.num_layers = self.batch = self.kv_heads = self.head_dim = None
-        self.dtype = self.device = None
-        self.dev_pool: torch.Tensor | None = None
-        self.host_pool: HostPool | None = None
-        self._dev_groups = SlotGroups()
-        self._host_groups = SlotGroups()
+        if pools is not None and pools.tokens_per_block != tokens_per_block:
+            raise ValueError(f"shared pools hold {pools.tokens_per_block}-token blocks, not {tokens_per_block}")
+        self.pools = pools
+        self._owns_pools = pools is None
         self._dev_group: dict[int, int] = {}  # block id -> group in the device pool
         self._host_group: dict[int, int] = {}  # block id -> group in the host pool
         self._tokens: dict[int, int] = {}  # block id -> tokens stored (<= tokens_per_block)
         self._resident_gpu_bytes = 0
         self._resident_cpu_bytes = 0
-        self._copy_stream = None
         self._pending: list[tuple[str, torch.cuda.Event, torch.cuda.Event]] = []
         self.gpu_blocks = _TierView(self, True)
         self.cpu_blocks = _TierView(self, False)
 
     # ------------------------------------------------------------------ geometry and pools
+    def _geo(self, name):
+        return None if self.pools is None else getattr(self.pools, name)
+
+    num_layers = property(lambda self: self._geo("num_layers"))
+    kv_heads = property(lambda self: self._geo("kv_heads"))
+    head_dim = property(lambda self: self._geo("head_dim"))
+    dtype = property(lambda self: self._geo("dtype"))
+    device = property(lambda self: self._geo("device"))
+    batch = property(lambda self: self._geo("rows_per_group"))
+    version = property(lambda self: 0 if self.pools is None else self.pools.version)
+    dev_pool = property(lambda self: self._geo("dev_pool"))
+    host_pool = property(lambda self: self._geo("host_pool"))
+
     def _block_bytes(self, tokens: int) -> int:
-        return 2 * self.num_layers * self.batch * tokens * self.kv_heads * self.head_dim * self._elt
-
-    def _init_geometry(self, key: torch.Tensor) -> None:
-        L, B, t, H, D = key.shape
-        self.num_layers, self.batch, self.kv_heads, self.head_dim = L, B, H, D
-        self.dtype, self.device = key.dtype, key.device
-        self._elt = key.element_size()
-        self._copy_stream = torch.cuda.Stream(device=self.device)
-        self._alloc_pools(self._cap0[0], self._cap0[1], B)
-
-    def _slot_shape(self):
-        return (self.num_layers, 2, self.kv_heads, self.tokens_per_block, self.head_dim)
-
-    def _alloc_pools(self, dev_groups: int, host_groups: int, batch: int) -> None:
-        self.dev_pool = torch.empty((dev_groups * batch,) + self._slot_shape(), dtype=self.dtype, device=self.device)
-        self.host_pool = HostPool((host_groups * batch,) + self._slot_shape(), self.dtype)
-        self._dev_groups = SlotGroups(dev_groups)
-        self._host_groups = SlotGroups(host_groups)
-        self.version += 1
+        p = self.pools
+        return 2 * p.num_layers * p.rows_per_group * tokens * p.kv_heads * p.head_dim * p.elt
 
     def _check_block(self, key: torch.Tensor, value: torch.Tensor) -> int:
         if key.dim() != 5 or key.shape != value.shape:
@@ -183,9 +251,11 @@ class KVBlockStore:
                              f"{tuple(key.shape)} and {tuple(value.shape)}")
         if key.dtype != value.dtype:
             raise ValueError("key and value must share a dtype")
-        if self.num_layers is None:
-            self._init_geometry(key)
         L, B, t, H, D = key.shape
+        if self.pools is None:
+            self.pools = KVPools(num_layers=L, kv_heads=H, head_dim=D, tokens_per_block=self.tokens_per_block,
+                                 dtype=key.dtype, device=key.device, rows_per_group=B, gpu_groups=self._cap0[0],
+                                 cpu_groups=self._cap0[1])
         if (L, B, H, D) != (self.num_layers, self.batch, self.kv_heads, self.head_dim) or key.dtype != self.dtype:
             raise ValueError(f"block geometry {(L, B, H, D)} {key.dtype} differs from the store's "
                              f"{(self.num_layers, self.batch, self.kv_heads, self.head_dim)} {self.dtype}")
@@ -196,38 +266,7 @@ class KVBlockStore:
         return t
 
     def _group_slots(self, group: int) -> slice:
-        return slice(group * self.batch, (group + 1) * self.batch)
-
-    def _take_dev_group(self) -> int:
-        g = self._dev_groups.take()
-        if g is None:
-            self._grow_dev(2 * self._dev_groups.capacity)
-            g = self._dev_groups.take()
-        return g
-
-    def _take_host_group(self) -> int:
-        g = self._host_groups.take()
-        if g is None:
-            self._grow_host(2 * self._host_groups.capacity)
-            g = self._host_groups.take()
-        return g
-
-    def _grow_dev(self, groups: int) -> None:
-        self._drain()
-        new = torch.empty((groups * self.batch,) + self._slot_shape(), dtype=self.dtype, device=self.device)
-        new[: self.dev_pool.shape[0]].copy_(self.dev_pool)
-        self.dev_pool = new
-        self._dev_groups.grow(groups)
-        self.version += 1
-
-    def _grow_host(self, groups: int) -> None:
-        self._drain()
-        new = HostPool((groups * self.batch,) + self._slot_shape(), self.dtype)
-        new.tensor[: self.host_pool.shape[0]].copy_(self.host_pool.tensor)
-        self.host_pool.close()
-        self.host_pool = new
-        self._host_groups.grow(groups)
-        self.version += 1
+        return self.pools.group_slots(group)
 
     def _kv_view(self, block_id: int, on_gpu: bool):
         pool = self.dev_pool if on_gpu else self.host_pool.tensor
@@ -240,7 +279,7 @@ class KVBlockStore:
 
     # ------------------------------------------------------------------ copy stream
     def _copy(self, dst: torch.Tensor, src: torch.Tensor, kind: str) -> None:
-        s = self._copy_stream
+        s = self.pools.copy_stream
         s.wait_stream(torch.cuda.current_stream(self.device))
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         with torch.cuda.stream(s):
@@ -251,9 +290,9 @@ class KVBlockStore:
 
     def _drain(self) -> None:
         """Wait for pending tier copies and add their device time to the stats."""
-        if self._copy_stream is None:
+        if self.pools is None:
             return
-        self._copy_stream.synchronize()
+        self.pools.copy_stream.synchronize()
         for kind, e0, e1 in self._pending:
             sec = e0.elapsed_time(e1) / 1000.0
             if kind == "d2h":
@@ -267,8 +306,8 @@ class KVBlockStore:
         self._drain()
 
     def _order_after_copies(self) -> None:
-        if self._copy_stream is not None:
-            torch.cuda.current_stream(self.device).wait_stream(self._copy_stream)
+        if self.pools is not None:
+            torch.cuda.current_stream(self.device).wait_stream(self.pools.copy_stream)
 
     # ------------------------------------------------------------------ the reference API
     def put_gpu(self, block_id: int, key: torch.Tensor, value: torch.Tensor) -> None:
@@ -285,7 +324,7 @@ class KVBlockStore:
             self._resident_gpu_bytes -= self._block_bytes(self._tokens[block_id])
             g = self._dev_group[block_id]
         else:
-            g = self._take_dev_group()
+            g = self.pools.take_dev_group()
         dst = self.dev_pool[self._group_slots(g)]
         dst[:, :, 0, :, :t].copy_(key.detach().permute(1, 0, 3, 2, 4))
         dst[:, :, 1, :, :t].copy_(value.detach().permute(1, 0, 3, 2, 4))
@@ -303,7 +342,7 @@ class KVBlockStore:
             raise ValueError("need one key and one value tensor per layer")
         k0 = keys[0]
         B, H, t, D = k0.shape
-        probe = k0.new_empty((len(keys), B, t, H, D)) if self.num_layers is None else None
+        probe = k0.new_empty((len(keys), B, t, H, D)) if self.pools is None else None
         if probe is not None:
             self._check_block(probe, probe)
         if (len(keys), B, H, D) != (self.num_layers, self.batch, self.kv_heads, self.head_dim):
@@ -316,7 +355,7 @@ class KVBlockStore:
             self._resident_gpu_bytes -= self._block_bytes(self._tokens[block_id])
             g = self._dev_group[block_id]
         else:
-            g = self._take_dev_group()
+            g = self.pools.take_dev_group()
         dst = self.dev_pool[self._group_slots(g)]
         for layer, (k, v) in enumerate(zip(keys, values)):
             if k.device != self.device or k.dtype != self.dtype or tuple(k.shape) != (B, H, t, D):
@@ -326,6 +365,17 @@ class KVBlockStore:
         self._dev_group[block_id] = g
         self._tokens[block_id] = t
         self._resident_gpu_bytes += self._block_bytes(t)
+
+    def adopt_gpu_group(self, block_id: int, group: int) -> None:
+        """Register a full block that already sits in device slot group ``group`` of the pools
+        (a decode session's tail slot once it holds ``tokens_per_block`` tokens): no copy."""
+        if self.pools is None:
+            raise ValueError("adopt_gpu_group needs pools")
+        if block_id in self._dev_group or block_id in self._host_group:
+            raise ValueError(f"Block {block_id} already exists.")
+        self._dev_group[block_id] = group
+        self._tokens[block_id] = self.tokens_per_block
+        self._resident_gpu_bytes += self._block_bytes(self.tokens_per_block)
 
     def has_gpu(self, block_id: int) -> bool:
         return block_id in self._dev_group
@@ -351,10 +401,10 @@ class KVBlockStore:
                 logger.warning("ram_budget usage at %.0f%% after offloading block %d (%.2f MB of %.2f MB budget).",
                                100.0 * projected / self.ram_budget_bytes, block_id, projected / 1_000_000,
                                self.ram_budget_bytes / 1_000_000)
-        hg = self._take_host_group()
+        hg = self.pools.take_host_group()
         dg = self._dev_group.pop(block_id)
         self._copy(self.host_pool.tensor[self._group_slots(hg)], self.dev_pool[self._group_slots(dg)], "d2h")
-        self._dev_groups.give(dg)
+        self.pools.dev_groups.give(dg)
         self._host_group[block_id] = hg
         self._resident_gpu_bytes -= incoming
         self._resident_cpu_bytes += incoming
@@ -371,10 +421,10 @@ class KVBlockStore:
         if index != self.device.index:
             raise ValueError(f"this store's device pool is on {self.device}, not {device}")
         incoming = self._block_bytes(self._tokens[block_id])
-        dg = self._take_dev_group()
+        dg = self.pools.take_dev_group()
         hg = self._host_group.pop(block_id)
         self._copy(self.dev_pool[self._group_slots(dg)], self.host_pool.tensor[self._group_slots(hg)], "h2d")
-        self._host_groups.give(hg)
+        self.pools.host_groups.give(hg)
         self._dev_group[block_id] = dg
         self._resident_cpu_bytes -= incoming
         self._resident_gpu_bytes += incoming
@@ -461,42 +511,42 @@ class KVBlockStore:
     def reorder_batch_rows(self, new_row_indices: list[int]) -> None:
         """Reindex every block's batch rows on whichever tier it lives (``kv_block_store.py:229-254``):
         new row i takes old row ``new_row_indices[i]``; repeats duplicate, omissions drop.
-        A new row count re-lays both pools for the new batch size."""
+        A new row count re-lays both pools for the new batch size (private pools only)."""
         idx = [int(i) for i in new_row_indices]
-        if self.batch is None:
+        if self.pools is None:
             return
-        if any(not -self.batch <= i < self.batch for i in idx):
-            raise IndexError(f"row index out of range for batch {self.batch}: {new_row_indices}")
-        idx = [i % self.batch for i in idx]
+        B = self.batch
+        if any(not -B <= i < B for i in idx):
+            raise IndexError(f"row index out of range for batch {B}: {new_row_indices}")
+        idx = [i % B for i in idx]
+        n = len(idx)
+        p = self.pools
+        if n != B and not self._owns_pools:
+            raise ValueError("cannot change the row count of blocks that live in shared pools")
         self._drain()
         torch.cuda.current_stream(self.device).synchronize()
-        n = len(idx)
-        old_dev, old_host = self.dev_pool, self.host_pool
-        if n == self.batch:
+        old_dev, old_host = p.dev_pool, p.host_pool
+        if n == B:
             new_dev, new_host = old_dev, old_host
         else:
-            new_dev = torch.empty((self._dev_groups.capacity * n,) + self._slot_shape(), dtype=self.dtype,
-                                  device=self.device)
-            new_host = HostPool((self._host_groups.capacity * n,) + self._slot_shape(), self.dtype)
+            new_dev = torch.empty((p.dev_groups.capacity * n,) + p.slot_shape(), dtype=p.dtype, device=p.device)
+            new_host = HostPool((p.host_groups.capacity * n,) + p.slot_shape(), p.dtype)
         for groups, old, new, dev in ((self._dev_group, old_dev, new_dev, True),
                                       (self._host_group, old_host.tensor, new_host.tensor, False)):
             if not groups:
                 continue
-            src = [g * self.batch + i for g in groups.values() for i in idx]
+            src = [g * B + i for g in groups.values() for i in idx]
             dst = [g * n + r for g in groups.values() for r in range(n)]
             where = self.device if dev else "cpu"
-            src_t = torch.tensor(src, dtype=torch.long, device=where)
-            dst_t = torch.tensor(dst, dtype=torch.long, device=where)
-            rows = old.index_select(0, src_t)
-            new.index_copy_(0, dst_t, rows)
+            rows = old.index_select(0, torch.tensor(src, dtype=torch.long, device=where))
+            new.index_copy_(0, torch.tensor(dst, dtype=torch.long, device=where), rows)
         torch.cuda.current_stream(self.device).synchronize()
-        if n != self.batch:
+        if n != B:
             old_host.close()
-            self.dev_pool, self.host_pool = new_dev, new_host
-            self._resident_gpu_bytes = self._resident_gpu_bytes // self.batch * n
-            self._resident_cpu_bytes = self._resident_cpu_bytes // self.batch * n
-            self.batch = n
-            self.version += 1
+            p.dev_pool, p.host_pool, p.rows_per_group = new_dev, new_host, n
+            p.version += 1
+            self._resident_gpu_bytes = self._resident_gpu_bytes // B * n
+            self._resident_cpu_bytes = self._resident_cpu_bytes // B * n
 
     def get_gpu(self, block_id: int) -> tuple[torch.Tensor, torch.Tensor]:
         if block_id not in self._dev_group:
@@ -538,8 +588,18 @@ class KVBlockStore:
         return table.to(device if device is not None else self.device)
 
     def close(self) -> None:
-        """Free the pinned host pool now (it is also freed when the store is collected)."""
+        """Free this store's blocks; a store with private pools also frees its pinned host pool."""
         self._drain()
-        if self.host_pool is not None:
-            self.host_pool.close()
-            self.host_pool = None
+        if self.pools is None:
+            return
+        if self._owns_pools:
+            self.pools.close()
+        else:
+            for g in self._dev_group.values():
+                self.pools.dev_groups.give(g)
+            for g in self._host_group.values():
+                self.pools.host_groups.give(g)
+        self._dev_group.clear()
+        self._host_group.clear()
+        self._tokens.clear()
+        self._resident_gpu_bytes = self._resident_cpu_bytes = 0

@@ -134,7 +134,7 @@ def measured_peaks():
 class Workload:
     """Device pool, pinned host pool, block tables, tails and queries for one GPU's share."""
 
-    def __init__(self, name: str, device, seed: int):
+    def __init__(self, name: str, device, seed: int, host_read: str = "auto"):
         import torch
 
         from pager_hf import _lib
@@ -215,7 +215,7 @@ class Workload:
             host_pool=None if self.host is None else self.host.tensor, num_layers=self.L, tokens_per_block=self.tpb,
             block_table=self.table, num_blocks=self.num_blocks, max_row_tokens=self.max_row_tokens,
             tail_k=self.tail_k, tail_v=self.tail_v, tail_len=self.tail_len, valid_lo=self.valid_lo,
-            mass_accum=self.mass, mass_mode="row_mean")
+            mass_accum=self.mass, mass_mode="row_mean", host_read=host_read, prefetch_next_step=True)
         # algorithmic bytes per step (only attended tokens are counted)
         kv_tok = 2 * self.Hkv * self.D * elt
         qo = 2 * self.B * self.Hq * self.D * elt
@@ -403,7 +403,7 @@ def run_ours(args):
     owners = shard_requests(world * w["batch"], world)
     mine = local_requests(owners, rank)
     assert len(mine) == w["batch"], (len(mine), w["batch"])
-    wl = Workload(args.workload, device, seed=1234 + 7919 * mine[0])
+    wl = Workload(args.workload, device, seed=1234 + 7919 * mine[0], host_read=args.host_read)
 
     def barrier():
         if world > 1:
@@ -481,6 +481,7 @@ def run_ours(args):
             "hbm_bytes_per_step": wl.hbm_bytes, "host_bytes_per_step": wl.host_bytes,
             "l2": "inputs larger than L2 (KV per step >> 126 MB), no flush",
             "parallelism": f"request-sharded x{world}, no collectives on the data path",
+            "host_read": wl.plan.host_read,
         },
         "decode_tokens_per_s": tokens_per_s,
         "roofline": {
@@ -525,6 +526,8 @@ def main():
     ap.add_argument("--workload", default="cfg5-32k", choices=sorted(WORKLOADS))
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--host-read", default="auto", choices=["auto", "zero_copy", "staged"],
+                    help="host tier: zero-copy kernel reads, copy-engine staging, or pick from the measured link")
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference_arm(args)

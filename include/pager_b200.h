@@ -163,6 +163,35 @@ int pager_paged_decode_attention_noalloc(const void* q, int q_dtype, const void*
                                          float* block_mass, float* mass_accum, int mass_mode, int backend,
                                          void* stream);
 
+/* ---- Staged host tier.
+ *      Block-table entries may also be `slot | PAGER_STAGE_SLOT_BIT`: slot of a device staging
+ *      buffer [stage_slots, 2, kv_heads, tokens_per_block, head_dim] holding THIS layer's copy of
+ *      a host block (filled by pager_stage_host_blocks on a copy stream).  The kernel reads staged
+ *      blocks with TMA like device-pool blocks; host entries (PAGER_HOST_SLOT_BIT) are still read
+ *      zero-copy.  Same arguments as pager_paged_decode_attention plus the staging buffer; every
+ *      pool holds fewer than 2^29 slots.  The reference reads host blocks with synchronous
+ *      pageable copies per layer and group (pager_hf/paged_model.py:878-924). */
+#define PAGER_STAGE_SLOT_BIT 0x20000000
+int pager_paged_decode_attention_staged(const void* q, int q_dtype, const void* dev_pool, int dev_slots,
+                                        const void* host_pool, int host_slots, const void* stage_pool,
+                                        int stage_slots, int kv_dtype, int num_layers, int layer, int num_kv_heads,
+                                        int tokens_per_block, int head_dim, const int32_t* block_table,
+                                        int max_blocks, const int32_t* num_blocks, const void* tail_k,
+                                        const void* tail_v, const int32_t* tail_len, int tail_cap,
+                                        const int32_t* valid_lo, const int32_t* valid_hi, const int32_t* active,
+                                        int batch, int num_q_heads, float scale, float softcap, int max_row_tokens,
+                                        void* out, int out_dtype, float* block_mass, float* mass_accum,
+                                        int mass_mode, int backend, void* scratch, size_t scratch_bytes,
+                                        void* stream);
+
+/* Copy one layer of host-pool blocks into a staging buffer, one cudaMemcpy2DAsync per run:
+ * run r copies run_len[r] consecutive host slots starting at run_src[r] into consecutive staging
+ * slots starting at run_dst[r]; from each host slot it takes chunk_bytes at layer_offset_bytes
+ * (slot_bytes apart).  run_* are HOST arrays.  Stream-ordered on `stream`. */
+int pager_stage_host_blocks(void* stage, const void* host_pool, int64_t slot_bytes, int64_t layer_offset_bytes,
+                            int64_t chunk_bytes, const int32_t* run_src, const int32_t* run_dst,
+                            const int32_t* run_len, int nruns, void* stream);
+
 /* ---- Writing one decode step's new token into pool slots.
  *      Replaces the tail concatenation of a decode step (pager_hf/batched_decode.py:170-171,
  *      the DynamicCache update of paged_model.py's patched forward): row b's new K and V

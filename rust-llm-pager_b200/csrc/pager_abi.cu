@@ -835,6 +835,25 @@ int pager_paged_decode_attention(const void* q, int q_dtype, const void* dev_poo
                                  float scale, float softcap, int max_row_tokens, void* out, int out_dtype,
                                  float* block_mass, float* mass_accum, int mass_mode, int backend, void* scratch,
                                  size_t scratch_bytes, void* stream) {
+  return pager_paged_decode_attention_staged(q, q_dtype, dev_pool, dev_slots, host_pool, host_slots, nullptr, 0,
+                                             kv_dtype, num_layers, layer, num_kv_heads, tokens_per_block, head_dim,
+                                             block_table, max_blocks, num_blocks, tail_k, tail_v, tail_len, tail_cap,
+                                             valid_lo, valid_hi, active, batch, num_q_heads, scale, softcap,
+                                             max_row_tokens, out, out_dtype, block_mass, mass_accum, mass_mode,
+                                             backend, scratch, scratch_bytes, stream);
+}
+
+int pager_paged_decode_attention_staged(const void* q, int q_dtype, const void* dev_pool, int dev_slots,
+                                        const void* host_pool, int host_slots, const void* stage_pool,
+                                        int stage_slots, int kv_dtype, int num_layers, int layer, int num_kv_heads,
+                                        int tokens_per_block, int head_dim, const int32_t* block_table,
+                                        int max_blocks, const int32_t* num_blocks, const void* tail_k,
+                                        const void* tail_v, const int32_t* tail_len, int tail_cap,
+                                        const int32_t* valid_lo, const int32_t* valid_hi, const int32_t* active,
+                                        int batch, int num_q_heads, float scale, float softcap, int max_row_tokens,
+                                        void* out, int out_dtype, float* block_mass, float* mass_accum,
+                                        int mass_mode, int backend, void* scratch, size_t scratch_bytes,
+                                        void* stream) {
   int rc = check_geometry(batch, num_q_heads, num_kv_heads, head_dim, kv_dtype, q_dtype);
   if (rc) return rc;
   if (batch == 0) return PAGER_OK;
@@ -850,10 +869,14 @@ int pager_paged_decode_attention(const void* q, int q_dtype, const void* dev_poo
   if ((dev_pool && !aligned16(dev_pool)) || (host_pool && !aligned16(host_pool)) || (tail_k && !aligned16(tail_k)) ||
       (tail_v && !aligned16(tail_v)))
     return fail(PAGER_ERR_INVALID, "pools and tail tensors must be 16-byte aligned");
-  if (dev_slots < 0 || host_slots < 0) return fail(PAGER_ERR_INVALID, "negative pool capacity");
+  if (dev_slots < 0 || host_slots < 0 || stage_slots < 0) return fail(PAGER_ERR_INVALID, "negative pool capacity");
+  if (dev_slots >= (1 << 29) || host_slots >= (1 << 29) || stage_slots >= (1 << 29))
+    return fail(PAGER_ERR_INVALID, "pool capacity must stay below 2^29 slots (block-table tag bits)");
   if ((long long)dev_slots * num_layers * 2 * num_kv_heads >= (1LL << 31) ||
-      (long long)host_slots * num_layers * 2 * num_kv_heads >= (1LL << 31))
+      (long long)host_slots * num_layers * 2 * num_kv_heads >= (1LL << 31) ||
+      (long long)stage_slots * 2 * num_kv_heads >= (1LL << 31))
     return fail(PAGER_ERR_INVALID, "pool too large: slots * layers * 2 * kv_heads must stay below 2^31");
+  if (stage_pool && !aligned16(stage_pool)) return fail(PAGER_ERR_INVALID, "staging buffer must be 16-byte aligned");
   if (mass_mode != PAGER_MASS_NONE && mass_mode != PAGER_MASS_ROW_MEAN && mass_mode != PAGER_MASS_BATCH_MEAN)
     return fail(PAGER_ERR_INVALID, "unknown mass mode %d", mass_mode);
   if (mass_mode != PAGER_MASS_NONE && !mass_accum) return fail(PAGER_ERR_INVALID, "mass_accum is null");
@@ -879,6 +902,15 @@ int pager_paged_decode_attention(const void* q, int q_dtype, const void* dev_poo
     rc = encode_3d(&mk, kv_dtype, dev_pool, head_dim, tokens_per_block, z, pp.k.panel_elts, br, pp.k.panel_bytes);
     if (rc) return rc;
   }
+  CUtensorMap ms;  // staging buffer [stage_slots, 2, Hkv, tpb, D]: one layer of copied host blocks
+  memset(&ms, 0, sizeof(ms));
+  const bool staged = stage_pool && stage_slots > 0;
+  if (staged) {
+    const uint64_t z = (uint64_t)stage_slots * 2 * num_kv_heads;
+    const int br = tokens_per_block < pp.k.tile ? tokens_per_block : pp.k.tile;
+    rc = encode_3d(&ms, kv_dtype, stage_pool, head_dim, tokens_per_block, z, pp.k.panel_elts, br, pp.k.panel_bytes);
+    if (rc) return rc;
+  }
   SplitParams p;
   memset(&p, 0, sizeof(p));
   p.q = q;
@@ -892,6 +924,8 @@ int pager_paged_decode_attention(const void* q, int q_dtype, const void* dev_poo
   p.source = SRC_PAGED;
   p.dev_pool = (dev_pool && dev_slots > 0) ? static_cast<const char*>(dev_pool) : nullptr;
   p.host_pool = (host_pool && host_slots > 0) ? static_cast<const char*>(host_pool) : nullptr;
+  p.stage_pool = staged ? static_cast<const char*>(stage_pool) : nullptr;
+  p.stage_slots = staged ? stage_slots : 0;
   p.slot_stride_bytes = layer_stride * num_layers;
   p.layer_stride_bytes = layer_stride;
   p.num_layers = num_layers;
@@ -929,7 +963,7 @@ int pager_paged_decode_attention(const void* q, int q_dtype, const void* dev_poo
 
   cudaStream_t st = (cudaStream_t)stream;
   dim3 grid(pp.plan.max_splits, num_kv_heads, batch);
-  void* args[] = {&p, &mk, &mk};
+  void* args[] = {&p, &mk, staged ? &ms : &mk};
   PAGER_CUDA(cudaLaunchKernel(pp.k.fn, grid, dim3(kThreads), args, pp.k.smem_bytes, st), "split kernel launch");
 
   CombineParams c;

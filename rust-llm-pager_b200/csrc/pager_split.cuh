@@ -37,7 +37,8 @@ constexpr int kConsumerWarps = 6;
 constexpr int kProducerWarps = 2;
 constexpr int kThreads = (kConsumerWarps + kProducerWarps) * 32;
 constexpr int kMaxRep = 16;
-constexpr int kHostSlotBit = 0x40000000;
+constexpr int kHostSlotBit = 0x40000000;   // block-table entry: slot of the pinned host pool
+constexpr int kStageSlotBit = 0x20000000;  // block-table entry: slot of the device staging buffer
 constexpr int kStatusTimeout = 5;
 constexpr int kStatusBadBlock = 6;
 
@@ -114,10 +115,11 @@ struct SplitParams {
   int source;
   const char* dev_pool;
   const char* host_pool;
+  const char* stage_pool;        // one layer's host blocks copied to the device: [slots, 2, Hkv, tpb, D]
   long long slot_stride_bytes;   // SRC_PAGED: bytes per pool slot (all layers)
   long long layer_stride_bytes;  // bytes per (slot, layer) = 2 * Hkv * tpb * row bytes
   int num_layers, layer, tpb, log2_tpb;
-  int dev_slots, host_slots;  // pool capacities (block-table entries are checked against them)
+  int dev_slots, host_slots, stage_slots;  // capacities (block-table entries are checked against them)
   const int* block_table;
   int max_blocks;
   const char* tail_k;
@@ -192,45 +194,12 @@ __device__ __forceinline__ uint32_t chunk_addr(uint32_t tile_base, int row, int 
   return tile_base + panel * Cfg::PANEL_TILE_BYTES + swz<Cfg>(row * Cfg::PANEL_BYTES + cp * 16);
 }
 
-// A block-table entry names a slot that exists in a pool that was passed in.
-__device__ __forceinline__ bool entry_usable(const SplitParams& p, int e) {
-  if (e < 0) return false;
-  if (e & kHostSlotBit) return p.host_pool != nullptr && (e & (kHostSlotBit - 1)) < p.host_slots;
-  return p.dev_pool != nullptr && e < p.dev_slots;
-}
-
 // This CTA's block-table entries, copied to shared memory in the prologue so
 // that neither the producer nor the consumers wait on global loads per tile.
 struct TableCache {
   const int* sm;
   int blk0, n;
 };
-
-__device__ __forceinline__ int table_entry(const SplitParams& p, const TableCache& tc, int b, int blk) {
-  const int i = blk - tc.blk0;
-  if (i >= 0 && i < tc.n) return tc.sm[i];
-  return p.block_table[(long long)b * p.max_blocks + blk];
-}
-
-__device__ __forceinline__ bool token_valid(const SplitParams& p, const TableCache& tc, int b, int t,
-                                            const RowGeom& g) {
-  if (t < g.lo || t >= g.hi) return false;
-  if (p.valid && p.valid[(long long)b * p.valid_stride + t] == 0) return false;
-  if (p.source == SRC_PAGED && t < g.nb * p.tpb) {
-    if (!entry_usable(p, table_entry(p, tc, b, t >> p.log2_tpb))) return false;
-  }
-  return true;
-}
-
-template <int TILE>
-__device__ __forceinline__ void tile_valid_bits(const SplitParams& p, const TableCache& tc, int b, int t0,
-                                                const RowGeom& g, uint32_t& lo_bits, uint32_t& hi_bits) {
-  const int lane = threadIdx.x & 31;
-  const bool v0 = lane < TILE && token_valid(p, tc, b, t0 + lane, g);
-  const bool v1 = TILE > 32 && token_valid(p, tc, b, t0 + 32 + lane, g);
-  lo_bits = __ballot_sync(0xffffffffu, v0);
-  hi_bits = __ballot_sync(0xffffffffu, v1);
-}
 
 __device__ __forceinline__ bool bit_of(uint32_t lo_bits, uint32_t hi_bits, int t) {
   return ((t < 32 ? (lo_bits >> t) : (hi_bits >> (t - 32))) & 1u) != 0;
@@ -251,7 +220,7 @@ struct Hot {
   int* status;
   long long valid_stride, slot_stride, layer_stride;
   unsigned long long wait_limit;
-  int source, tpb, log2_tpb, max_blocks, num_layers, layer, hkv, dev_slots, host_slots, tail_cap;
+  int source, tpb, log2_tpb, max_blocks, num_layers, layer, hkv, dev_slots, host_slots, stage_slots, tail_cap;
 };
 
 __device__ __forceinline__ Hot load_hot(const SplitParams& p) {
@@ -276,13 +245,19 @@ __device__ __forceinline__ Hot load_hot(const SplitParams& p) {
   h.hkv = p.num_kv_heads;
   h.dev_slots = p.dev_slots;
   h.host_slots = p.host_slots;
+  h.stage_slots = p.stage_pool != nullptr ? p.stage_slots : 0;
   h.tail_cap = p.tail_cap;
   return h;
 }
 
+// A block-table entry names a slot that exists in a pool that was passed in:
+// slot (device pool), slot | kHostSlotBit (host pool, read zero-copy) or
+// slot | kStageSlotBit (this layer's copy of a host block in the staging buffer).
 __device__ __forceinline__ bool entry_ok(const Hot& k, int e) {
   if (e < 0) return false;
-  if (e & kHostSlotBit) return k.host_pool != nullptr && (e & (kHostSlotBit - 1)) < k.host_slots;
+  if (e & kHostSlotBit)
+    return !(e & kStageSlotBit) && k.host_pool != nullptr && (e & (kStageSlotBit - 1)) < k.host_slots;
+  if (e & kStageSlotBit) return (e & (kStageSlotBit - 1)) < k.stage_slots;
   return k.dev_pool != nullptr && e < k.dev_slots;
 }
 
@@ -290,25 +265,6 @@ __device__ __forceinline__ int entry_at(const Hot& k, const TableCache& tc, int 
   const int i = blk - tc.blk0;
   if (i >= 0 && i < tc.n) return tc.sm[i];
   return k.block_table[(long long)b * k.max_blocks + blk];
-}
-
-__device__ __forceinline__ bool token_ok(const Hot& k, const TableCache& tc, int b, int t, const RowGeom& g) {
-  if (t < g.lo || t >= g.hi) return false;
-  if (k.valid && k.valid[(long long)b * k.valid_stride + t] == 0) return false;
-  if (k.source == SRC_PAGED && t < g.nb * k.tpb) {
-    if (!entry_ok(k, entry_at(k, tc, b, t >> k.log2_tpb))) return false;
-  }
-  return true;
-}
-
-template <int TILE>
-__device__ __forceinline__ void tile_bits(const Hot& k, const TableCache& tc, int b, int t0, const RowGeom& g,
-                                          uint32_t& lo_bits, uint32_t& hi_bits) {
-  const int lane = threadIdx.x & 31;
-  const bool v0 = lane < TILE && token_ok(k, tc, b, t0 + lane, g);
-  const bool v1 = TILE > 32 && token_ok(k, tc, b, t0 + 32 + lane, g);
-  lo_bits = __ballot_sync(0xffffffffu, v0);
-  hi_bits = __ballot_sync(0xffffffffu, v1);
 }
 
 // ------------------------------------------------------------------ producer helpers
@@ -442,13 +398,17 @@ __device__ void run_producer(const SplitParams& p, const TableCache& tc, const C
           continue;
         }
         mbar_expect_tx(&full[s], seg_bytes);
-        const int zk = ((e * k.num_layers + k.layer) * 2) * k.hkv + h;
+        // device pool: plane ((slot * L + layer) * 2 + kv) * Hkv + h; staging buffer (one layer,
+        // described by the second tensor map): plane (slot * 2 + kv) * Hkv + h
+        const bool staged = (e & kStageSlotBit) != 0;
+        const int zk = staged ? ((e & (kStageSlotBit - 1)) * 2) * k.hkv + h : ((e * k.num_layers + k.layer) * 2) * k.hkv + h;
+        const CUtensorMap* map = staged ? mapv : mapk;
         const int y = tok & (k.tpb - 1);
 #pragma unroll
         for (int pn = 0; pn < Cfg::NPANEL; ++pn) {
           const int off = pn * Cfg::PANEL_TILE_BYTES + sg * br * Cfg::PANEL_BYTES;
-          tma_load_3d(kbuf + off, mapk, pn * Cfg::PANEL_ELTS, y, zk, &full[s]);
-          if (kNeedV) tma_load_3d(vbuf + off, mapk, pn * Cfg::PANEL_ELTS, y, zk + k.hkv, &full[s]);
+          tma_load_3d(kbuf + off, map, pn * Cfg::PANEL_ELTS, y, zk, &full[s]);
+          if (kNeedV) tma_load_3d(vbuf + off, map, pn * Cfg::PANEL_ELTS, y, zk + k.hkv, &full[s]);
         }
       }
     }
@@ -1129,10 +1089,9 @@ __global__ void __launch_bounds__(kThreads, 1) split_kernel(const __grid_constan
     }
     *abort_flag = 0;
     mbar_fence_init();
-    if (p.source == SRC_CONTIG || p.dev_pool != nullptr) {
-      tma_prefetch_desc(&mapk);
-      if (p.source == SRC_CONTIG && MODE != MODE_STATS) tma_prefetch_desc(&mapv);
-    }
+    if (p.source == SRC_CONTIG || p.dev_pool != nullptr) tma_prefetch_desc(&mapk);
+    if ((p.source == SRC_CONTIG && MODE != MODE_STATS) || (p.source == SRC_PAGED && p.stage_pool != nullptr))
+      tma_prefetch_desc(&mapv);
   }
   float* q_sm = reinterpret_cast<float*>(smem + L::Q_OFF);
   T* q_smem_t = reinterpret_cast<T*>(smem + L::Q_OFF);

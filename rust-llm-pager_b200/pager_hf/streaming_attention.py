@@ -405,7 +405,7 @@ class PagedDecodePlan:
     def __init__(self, *, batch, num_query_heads, dev_pool, host_pool, num_layers, tokens_per_block, block_table,
                  num_blocks, max_row_tokens, tail_k=None, tail_v=None, tail_len=None, valid_lo=None, valid_hi=None,
                  active=None, scale=None, softcap=None, q_dtype=None, block_mass=None, mass_accum=None,
-                 mass_mode="none"):
+                 mass_mode="none", host_read="auto", prefetch_next_step=False):
         pool = dev_pool if dev_pool is not None else host_pool
         if pool is None or pool.dim() != 6:
             raise ValueError("a [slots, layers, 2, kv_heads, tokens_per_block, head_dim] pool is required")
@@ -442,21 +442,47 @@ class PagedDecodePlan:
                                                           self.max_blocks, self.max_row_tokens)
         self.scratch = _scratch(nbytes, device)
         self.device = device
-        self._fn = lib.pager_paged_decode_attention
+        self._fn = lib.pager_paged_decode_attention_staged
         self._static = (
             L.ptr(dev_pool), 0 if dev_pool is None else dev_pool.shape[0], L.ptr(host_pool),
             0 if host_pool is None else host_pool.shape[0], self.kv_dtype, self.num_layers)
+        # host tier: zero-copy reads, or staged per layer by the copy engines (host_staging.py)
+        self.staging = None
+        if host_read not in ("auto", "zero_copy", "staged"):
+            raise ValueError(f"host_read must be 'auto', 'zero_copy' or 'staged', got {host_read!r}")
+        if host_pool is not None and host_read != "zero_copy":
+            tbl = self.block_table
+            has_host = bool(((tbl >= 0) & ((tbl & L.HOST_SLOT_BIT) != 0)).any())
+            if has_host:
+                from .host_staging import HostStaging, choose_host_read
+
+                mode = choose_host_read(device) if host_read == "auto" else "staged"
+                if mode == "staged":
+                    self.staging = HostStaging(tbl, host_pool, self.num_layers, device, prefetch_next_step,
+                                               self.tpb, self.num_blocks, self.valid_lo, self.valid_hi, self.active)
+                    if self.staging.num_slots == 0:  # no host block is read: nothing to stage
+                        self.staging = None
+        self.host_read = "staged" if self.staging is not None else "zero_copy"
 
     def run(self, q: torch.Tensor, layer: int, out: torch.Tensor, stream: int | None = None) -> torch.Tensor:
         dp, ds, hp, hs, kvd, nl = self._static
+        stg = self.staging
+        if stg is None:
+            sp, ss, table = None, 0, self.block_table
+            sh = torch.cuda.current_stream(self.device).cuda_stream if stream is None else stream
+        else:
+            st = (torch.cuda.current_stream(self.device) if stream is None
+                  else torch.cuda.ExternalStream(stream, device=self.device))
+            sp, ss, table, sh = stg.before_kernel(layer, st).data_ptr(), stg.num_slots, stg.table, st.cuda_stream
         rc = self._fn(
-            q.data_ptr(), self.q_dtype, dp, ds, hp, hs, kvd, nl, layer, self.Hkv, self.tpb, self.D,
-            self.block_table.data_ptr(), self.max_blocks, self.num_blocks.data_ptr(), L.ptr(self.tail_k),
+            q.data_ptr(), self.q_dtype, dp, ds, hp, hs, sp, ss, kvd, nl, layer, self.Hkv, self.tpb, self.D,
+            table.data_ptr(), self.max_blocks, self.num_blocks.data_ptr(), L.ptr(self.tail_k),
             L.ptr(self.tail_v), L.ptr(self.tail_len), 0 if self.tail_k is None else self.tail_k.shape[2],
             L.ptr(self.valid_lo), L.ptr(self.valid_hi), L.ptr(self.active), self.B, self.Hq, self.scale, self.softcap,
             self.max_row_tokens, out.data_ptr(), L.DTYPE_CODE[out.dtype], L.ptr(self.block_mass),
-            L.ptr(self.mass_accum), self.mass_mode, _BACKEND, self.scratch.data_ptr(), self.scratch.numel(),
-            torch.cuda.current_stream(self.device).cuda_stream if stream is None else stream)
+            L.ptr(self.mass_accum), self.mass_mode, _BACKEND, self.scratch.data_ptr(), self.scratch.numel(), sh)
+        if stg is not None:
+            stg.after_kernel(layer, st)
         if rc:
             L.check(rc)
         return out

@@ -1,0 +1,48 @@
+"""Run planning of the staged host tier (``pager_hf/host_staging.plan_host_runs``)."""
+
+import numpy as np
+import torch
+
+from pager_hf.host_staging import HOST_SLOT_BIT, STAGE_SLOT_BIT, plan_host_runs
+
+
+def test_runs_cover_distinct_host_slots_in_order():
+    H = HOST_SLOT_BIT
+    table = torch.tensor([[0, 5 | H, 6 | H, -1, 9 | H],
+                          [1, 7 | H, 5 | H, 2, 12 | H]], dtype=torch.int32)
+    staged, slots, (src, dst, ln) = plan_host_runs(table)
+    assert slots.tolist() == [5, 6, 7, 9, 12]
+    # runs of consecutive host slots -> consecutive staging slots
+    assert src.tolist() == [5, 9, 12] and dst.tolist() == [0, 3, 4] and ln.tolist() == [3, 1, 1]
+    # device entries and absent entries unchanged; host entries renamed to their staging slot
+    assert staged[0, 0] == 0 and staged[1, 3] == 2 and staged[0, 3] == -1
+    expect = {5: 0, 6: 1, 7: 2, 9: 3, 12: 4}
+    for (r, c) in [(0, 1), (0, 2), (0, 4), (1, 1), (1, 2), (1, 4)]:
+        e = int(table[r, c])
+        assert int(staged[r, c]) == (expect[e & (H - 1)] | STAGE_SLOT_BIT)
+    assert int(np.sum(ln)) == len(slots)
+
+
+def test_table_without_host_blocks_has_no_runs():
+    table = torch.tensor([[0, 1, -1], [2, 3, 4]], dtype=torch.int32)
+    staged, slots, runs = plan_host_runs(table)
+    assert torch.equal(staged, table) and slots.numel() == 0 and all(len(r) == 0 for r in runs)
+
+
+def test_only_blocks_the_kernel_reads_are_staged():
+    """Blocks beyond num_blocks, outside [valid_lo, valid_hi) or in inactive rows keep their host tag."""
+    H = HOST_SLOT_BIT
+    tpb = 16
+    table = torch.tensor([[0 | H, 1 | H, 2 | H, 3 | H],
+                          [4 | H, 5 | H, 6 | H, 7 | H],
+                          [8 | H, 9 | H, 10 | H, 11 | H]], dtype=torch.int32)
+    nb = torch.tensor([4, 3, 4], dtype=torch.int32)
+    lo = torch.tensor([20, 0, 0], dtype=torch.int32)   # row 0: block 0 (tokens 0..15) is before the window
+    hi = torch.tensor([64, 33, 64], dtype=torch.int32)  # row 1: tokens 33.. excluded -> block 2 starts at 32: kept
+    active = torch.tensor([1, 1, 0], dtype=torch.int32)
+    staged, slots, _ = plan_host_runs(table, tpb, nb, lo, hi, active)
+    assert slots.tolist() == [1, 2, 3, 4, 5, 6]
+    assert int(staged[0, 0]) == 0 | H                  # outside the window: still a host entry
+    assert int(staged[1, 3]) == 7 | H                  # beyond num_blocks
+    assert all(int(staged[2, j]) == table[2, j] for j in range(4))  # inactive row
+    assert int(staged[1, 2]) & STAGE_SLOT_BIT

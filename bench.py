@@ -464,9 +464,11 @@ def run_ours(args):
     t_roof = wl.hbm_bytes / wl.L / (hbm_peak * 1e9) + (wl.host_bytes / wl.L / (h2d * 1e9) if wl.host_bytes else 0.0)
     combined_peak = bytes_per_launch / t_roof / 1e9
     # DRAM traffic per launch: the ncu capture of the split kernel on the small HBM-resident case read
-    # and wrote NCU_DRAM_PER_HBM_BYTE bytes per algorithmic HBM byte; scaled here to this launch's HBM
-    # bytes (host-tier blocks cross the host link, not DRAM).
-    traffic = wl.hbm_bytes / wl.L * NCU_DRAM_PER_HBM_BYTE
+    # and wrote NCU_DRAM_PER_HBM_BYTE bytes per algorithmic HBM byte; scaled here to the bytes this
+    # launch's kernel reads from DRAM: the HBM tier, plus the staged copies of host blocks when the
+    # host tier is staged (zero-copy host reads cross the link, not DRAM).
+    kernel_dram_bytes = wl.hbm_bytes + (wl.host_bytes if wl.plan.host_read == "staged" else 0)
+    traffic = kernel_dram_bytes / wl.L * NCU_DRAM_PER_HBM_BYTE
     clocks = clk.summary()
     line = {
         "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,

@@ -1,0 +1,394 @@
+"""``PagedModel``: greedy / sampled generation with the KV cache paged by the pager.
+
+Same surface as the reference's ``pager_hf/paged_model.py:192-420``
+(``PagedModel(model, *, vram_budget, ram_budget, recent_window,
+rebalance_interval, promote_margin, ram_promote_margin, policy,
+tokens_per_block, ...)``, ``generate(input_ids, attention_mask,
+max_new_tokens, *, do_sample, temperature, top_k, top_p, generator)``,
+``reset()``, one session per instance that later ``generate`` calls extend,
+``last_run_stats``), for the decoder families whose layers are
+``input_layernorm -> self_attn(q/k/v/o_proj, RoPE) -> post_attention_layernorm
+-> mlp`` (Qwen2, Llama, Mistral) in the installed transformers.
+
+The reference patches each attention module's ``forward`` for the
+transformers 4.44 API and gathers every block group per layer.  Here:
+
+* prefill is the model's own forward (the prompt minus its last token, like
+  ``_start_session``, ``:671-690``), whose cache is moved into a device slot
+  pool as blocks of ``tokens_per_block`` tokens (all batch rows of a block in
+  one slot group) plus a tail slot group;
+* every decode step drives the decoder modules directly: norms, projections,
+  RoPE and MLP from the model, and per layer one ``pager_append_tokens``
+  (the new K/V into the tail slots) and one fused ``paged_decode_attention``
+  launch over the block table (device, staged/zero-copy host blocks, tail),
+  which also accumulates the batch-and-head mean block mass the heavy-hitter
+  policies score (``paged_model.py:1048``);
+* after each token, the pager gets exactly the reference's calls
+  (``_forward_step_streaming`` / ``_append_new_full_blocks_from_grown_tail``):
+  ``on_step(query_block, 0, block_attention)``, ``force_rebalance`` when the
+  tail became a block (adopted in place, no copy), then ``apply_tiers``.
+"""
+
+from __future__ import annotations
+
+import logging
+import threading
+from dataclasses import dataclass
+
+import torch
+
+from . import _lib as L
+from .kv_block_store import KVBlockStore, KVPools
+from .streaming_attention import PagedDecodePlan
+
+logger = logging.getLogger(__name__)
+
+_POLICIES_WITHOUT_ATTENTION_SIGNAL = frozenset({"recent_only", "sinks_recent"})
+_SUPPORTED_MODEL_TYPES = frozenset({"qwen2", "llama", "mistral"})
+
+
+@dataclass
+class GenerationStats:
+    total_new_blocks: int = 0
+    final_num_blocks: int = 0
+    total_gpu_to_cpu_mb: float = 0.0
+    total_cpu_to_gpu_mb: float = 0.0
+    total_gpu_to_cpu_copies: int = 0
+    total_cpu_to_gpu_copies: int = 0
+    mean_attention_in_gpu: float = 0.0
+    min_attention_in_gpu: float = 0.0
+    max_attention_in_gpu: float = 0.0
+
+
+def _rope_fn(model):
+    import importlib
+
+    mod = importlib.import_module(type(model).__module__)
+    return mod.apply_rotary_pos_emb
+
+
+class PagedModel:
+    """A HuggingFace causal LM whose KV cache lives in paged device / host pools."""
+
+    def __init__(self, model, *, vram_budget: int, ram_budget: int, recent_window: int = 64,
+                 rebalance_interval: int = 4, promote_margin: float = 0.05, ram_promote_margin: float = 0.20,
+                 policy: str = "sinks_heavy_hitter", tokens_per_block: int = 16, prefill_chunk_tokens: int = 512,
+                 use_streaming_attention: bool = True, streaming_group_size_blocks: int = 64,
+                 host_read: str = "auto"):
+        if not use_streaming_attention:
+            raise NotImplementedError("only the streaming (fused paged) attention path is implemented")
+        self.model = model
+        self.tokens_per_block = tokens_per_block
+        self.prefill_chunk_tokens = prefill_chunk_tokens
+        self.use_streaming_attention = True
+        self.streaming_group_size_blocks = streaming_group_size_blocks  # kept for API parity; one launch per layer
+        self.host_read = host_read
+        self._needs_attention = policy not in _POLICIES_WITHOUT_ATTENTION_SIGNAL
+        self._ram_budget = ram_budget
+        self._pager_kwargs = dict(vram=vram_budget, ram=ram_budget, recent=recent_window,
+                                  rebalance_interval=rebalance_interval, promote_margin=promote_margin,
+                                  ram_promote_margin=ram_promote_margin, policy=policy)
+        self.last_run_stats: GenerationStats | None = None
+        self._lock = threading.Lock()
+        self._clear_session()
+
+    # ------------------------------------------------------------------ session state
+    def _clear_session(self):
+        self._pools = None
+        self._store = None
+        self._rust_pager = None
+        self._num_layers = None
+        self._num_blocks = None
+        self._tail_group = None
+        self._tail_len = 0
+        self._pad = None  # per row: left-padding columns
+        self._total = 0  # columns in the sequence so far (padding included)
+        self._mass_accum = None
+        self._primed_tokens = 0
+        self._primed_prefix = None
+
+    def _acquire_or_raise(self) -> None:
+        if not self._lock.acquire(blocking=False):
+            raise RuntimeError(
+                "Another generate() or reset() call is already running on this PagedModel instance. It holds one "
+                "mutable session, so concurrent calls from another thread would corrupt its state rather than run "
+                "as independent requests. Use a separate PagedModel per concurrent session, or synchronize calls "
+                "to this one yourself.")
+
+    def reset(self) -> None:
+        """Drop the current session; the next generate() call starts fresh."""
+        self._acquire_or_raise()
+        try:
+            self._release_pools()
+            self._clear_session()
+        finally:
+            self._lock.release()
+
+    def _release_pools(self):
+        if self._store is not None:
+            self._store.close()
+        if self._pools is not None:
+            self._pools.close()
+
+    # ------------------------------------------------------------------ helpers
+    @staticmethod
+    def _validate_left_padded(attention_mask: torch.Tensor) -> None:
+        mask = attention_mask.bool()
+        if not mask.any(dim=1).all():
+            raise NotImplementedError("attention_mask has a row with no real (non-padding) tokens.")
+        if not torch.all(mask[:, :-1] <= mask[:, 1:]):
+            raise NotImplementedError(
+                "PagedModel only supports left-padding (zero or more leading zeros, then all ones, per row); "
+                "right-padding or interleaved masking is not supported.")
+
+    @staticmethod
+    def _position_ids_from_mask(attention_mask: torch.Tensor) -> torch.Tensor:
+        position_ids = attention_mask.long().cumsum(-1) - 1
+        return position_ids.masked_fill(attention_mask == 0, 0)
+
+    @staticmethod
+    def _sample_next_token(logits, *, temperature, top_k, top_p, generator):
+        """``paged_model.py:643-670``: temperature, top-k, top-p (nucleus), then a multinomial draw."""
+        logits = logits / temperature
+        if top_k is not None:
+            kth_value = torch.topk(logits, min(top_k, logits.shape[-1]), dim=-1).values[:, -1, None]
+            logits = logits.masked_fill(logits < kth_value, float("-inf"))
+        if top_p is not None:
+            sorted_logits, sorted_indices = torch.sort(logits, descending=True, dim=-1)
+            sorted_probs = torch.softmax(sorted_logits, dim=-1)
+            cumulative_probs = torch.cumsum(sorted_probs, dim=-1)
+            sorted_logits = sorted_logits.masked_fill(cumulative_probs - sorted_probs > top_p, float("-inf"))
+            logits = torch.full_like(logits, float("-inf")).scatter(-1, sorted_indices, sorted_logits)
+        probs = torch.softmax(logits, dim=-1)
+        return torch.multinomial(probs, num_samples=1, generator=generator)
+
+    def _arch(self):
+        cfg = self.model.config
+        model_type = getattr(cfg, "model_type", None)
+        if model_type not in _SUPPORTED_MODEL_TYPES:
+            raise NotImplementedError(f"PagedModel doesn't recognize model_type={model_type!r}.")
+        attn = self.model.model.layers[0].self_attn
+        head_dim = getattr(attn, "head_dim", cfg.hidden_size // cfg.num_attention_heads)
+        window = getattr(cfg, "sliding_window", None) if model_type == "mistral" else getattr(attn, "sliding_window",
+                                                                                              None)
+        return dict(layers=len(self.model.model.layers), hq=cfg.num_attention_heads,
+                    hkv=cfg.num_key_value_heads, d=head_dim, scale=attn.scaling, window=window)
+
+    # ------------------------------------------------------------------ session start
+    def _start_session(self, input_ids, attention_mask):
+        """Prefill all but the last token with the model's own forward, then move its cache into the pools."""
+        from transformers import DynamicCache
+
+        a = self._arch()
+        B, T = input_ids.shape
+        dev = input_ids.device
+        dtype = self.model.dtype
+        tpb = self.tokens_per_block
+        cache = DynamicCache()
+        prefix = input_ids[:, :-1]
+        pmask = attention_mask[:, :-1]
+        pos_all = self._position_ids_from_mask(attention_mask)
+        for s in range(0, prefix.shape[1], self.prefill_chunk_tokens):
+            e = min(s + self.prefill_chunk_tokens, prefix.shape[1])
+            self.model(input_ids=prefix[:, s:e], attention_mask=pmask[:, :e], position_ids=pos_all[:, s:e],
+                       past_key_values=cache, use_cache=True)
+        n = prefix.shape[1]
+        nfull = n // tpb
+        budget_blocks = max(1, self._pager_kwargs["vram"] // (16 * 1024 * 1024))
+        self._pools = KVPools(num_layers=a["layers"], kv_heads=a["hkv"], head_dim=a["d"], tokens_per_block=tpb,
+                              dtype=dtype, device=dev, rows_per_group=B, gpu_groups=max(nfull + 2, 2),
+                              cpu_groups=max(4, nfull - min(nfull, budget_blocks) + 2))
+        self._store = KVBlockStore(tpb, self._ram_budget, pools=self._pools)
+        keys = [layer.keys for layer in cache.layers]
+        values = [layer.values for layer in cache.layers]
+        for j in range(nfull):
+            self._store.put_gpu_layers(j, [k[:, :, j * tpb:(j + 1) * tpb] for k in keys],
+                                       [v[:, :, j * tpb:(j + 1) * tpb] for v in values])
+        self._tail_group = self._pools.take_dev_group()
+        rem = n - nfull * tpb
+        tail = self._pools.dev_pool[self._pools.group_slots(self._tail_group)]
+        for layer in range(a["layers"]):
+            tail[:, layer, 0, :, :rem].copy_(keys[layer][:, :, nfull * tpb:])
+            tail[:, layer, 1, :, :rem].copy_(values[layer][:, :, nfull * tpb:])
+        del cache, keys, values
+        self._num_layers = a["layers"]
+        self._num_blocks = nfull
+        self._tail_len = rem
+        self._total = n
+        self._pad = (attention_mask == 0).sum(dim=1).to(torch.int32)  # left padding per row
+        import pager as _pager
+
+        self._rust_pager = _pager.PyPager(**self._pager_kwargs)
+        logger.info("Started PagedModel session: batch_size=%d prompt_tokens=%d layers=%d blocks=%d policy=%r",
+                    B, T, a["layers"], nfull, self._pager_kwargs["policy"])
+
+    # ------------------------------------------------------------------ one decode step
+    def _block_attention(self) -> list[float]:
+        n = self._num_blocks
+        if n == 0 or self._mass_accum is None:
+            return [1.0 / n] * n if n else []
+        averaged = (self._mass_accum / self._num_layers).tolist()
+        total = sum(averaged)
+        if total <= 0:
+            return [1.0 / n] * n
+        return [x / total for x in averaged]
+
+    def _forward_step(self, input_ids: torch.Tensor, attention_mask: torch.Tensor):
+        """One token per row through the model with paged attention; then blocks, pager, tiers."""
+        a = self._arch()
+        m = self.model
+        B = input_ids.shape[0]
+        dev = input_ids.device
+        p = self._pools
+        tpb = self.tokens_per_block
+        nb = self._num_blocks
+        total = self._total + 1  # columns including this step's token
+        # block table: row b reads slot (group * B + b) of each block's group, then its tail slot
+        table = torch.full((B, nb + 1), -1, dtype=torch.int32)
+        if nb:
+            table[:, :nb] = self._store.block_table(range(nb), device="cpu")
+        table[:, nb] = torch.arange(self._tail_group * B, self._tail_group * B + B, dtype=torch.int32)
+        lo = self._pad.clone()
+        if a["window"] is not None:
+            lo = torch.clamp(lo, min=max(0, total - int(a["window"])))
+        i32 = dict(dtype=torch.int32, device=dev)
+        mass = torch.zeros(nb + 1, dtype=torch.float32, device=dev) if self._needs_attention else None
+        plan = PagedDecodePlan(
+            batch=B, num_query_heads=a["hq"], dev_pool=p.dev_pool, host_pool=p.host_pool.tensor,
+            num_layers=a["layers"], tokens_per_block=tpb, block_table=table.to(dev),
+            num_blocks=torch.full((B,), nb + 1, **i32), max_row_tokens=(nb + 1) * tpb,
+            valid_lo=lo.to(dev) if bool((lo > 0).any()) else None, valid_hi=torch.full((B,), total, **i32),
+            scale=a["scale"], mass_accum=mass, mass_mode="batch_mean" if mass is not None else "none",
+            host_read=self.host_read)
+        slots = torch.arange(self._tail_group * B, self._tail_group * B + B, **i32)
+        positions = torch.full((B,), self._tail_len, **i32)
+        position_ids = self._position_ids_from_mask(attention_mask)[:, -1:]
+        rope = _rope_fn(m)
+        hidden = m.model.embed_tokens(input_ids)
+        cos, sin = m.model.rotary_emb(hidden, position_ids)
+        lib = L.lib()
+        stream = torch.cuda.current_stream(dev).cuda_stream
+        out = torch.empty(B, a["hq"], a["d"], dtype=hidden.dtype, device=dev)
+        for li, layer in enumerate(m.model.layers):
+            residual = hidden
+            h = layer.input_layernorm(hidden)
+            attn = layer.self_attn
+            q = attn.q_proj(h).view(B, 1, -1, a["d"]).transpose(1, 2)
+            k = attn.k_proj(h).view(B, 1, -1, a["d"]).transpose(1, 2)
+            v = attn.v_proj(h).view(B, 1, -1, a["d"]).transpose(1, 2)
+            q, k = rope(q, k, cos, sin)
+            kn = k[:, :, 0].contiguous()
+            vn = v[:, :, 0].contiguous()
+            L.check(lib.pager_append_tokens(p.dev_pool.data_ptr(), L.DTYPE_CODE[p.dtype], p.dev_pool.shape[0],
+                                            a["layers"], li, a["hkv"], tpb, a["d"], slots.data_ptr(),
+                                            positions.data_ptr(), kn.data_ptr(), vn.data_ptr(), B, stream))
+            plan.run(q[:, :, 0].contiguous(), li, out)
+            hidden = residual + attn.o_proj(out.reshape(B, 1, -1))
+            residual = hidden
+            hidden = residual + layer.mlp(layer.post_attention_layernorm(hidden))
+        logits = m.lm_head(m.model.norm(hidden))
+        # --- bookkeeping (paged_model.py:1210-1233, :785-798)
+        self._total = total
+        self._tail_len += 1
+        added = []
+        if self._tail_len == tpb:
+            self._store.adopt_gpu_group(nb, self._tail_group)
+            added.append(nb)
+            self._num_blocks = nb + 1
+            self._tail_group = p.take_dev_group()
+            self._tail_len = 0
+        self._mass_accum = mass[:nb].cpu() if mass is not None else None
+        step = {"new_blocks": len(added), "gpu_to_cpu_mb": 0.0, "cpu_to_gpu_mb": 0.0, "gpu_to_cpu_copies": 0,
+                "cpu_to_gpu_copies": 0, "attention_in_gpu": 0.0}
+        if self._num_blocks == 0:
+            return logits, step
+        block_attention = (self._block_attention() if self._needs_attention
+                           else [1.0 / self._num_blocks] * self._num_blocks)
+        before = self._store.summary()
+        query_block = self._num_blocks - 1
+        self._rust_pager.on_step(query_block, 0, block_attention)
+        if added:
+            self._rust_pager.force_rebalance(query_block)
+        self._store.apply_tiers(self._rust_pager.tiers(), dev)
+        after = self._store.summary()
+        step.update(gpu_to_cpu_mb=(after["gpu_to_cpu_bytes"] - before["gpu_to_cpu_bytes"]) / 1e6,
+                    cpu_to_gpu_mb=(after["cpu_to_gpu_bytes"] - before["cpu_to_gpu_bytes"]) / 1e6,
+                    gpu_to_cpu_copies=after["gpu_to_cpu_copies"] - before["gpu_to_cpu_copies"],
+                    cpu_to_gpu_copies=after["cpu_to_gpu_copies"] - before["cpu_to_gpu_copies"],
+                    attention_in_gpu=sum(block_attention[i] for i in self._store.gpu_block_ids()
+                                         if i < len(block_attention)))
+        return logits, step
+
+    def _extend_session(self, input_ids, attention_mask):
+        total_len = input_ids.shape[-1]
+        if total_len - 1 < self._primed_tokens:
+            raise ValueError(
+                "input_ids is shorter than the already-primed session "
+                f"({total_len - 1} < {self._primed_tokens} tokens). "
+                "Call reset() to start a new session instead of rewinding one.")
+        if not torch.equal(input_ids[:, :self._primed_tokens].cpu(), self._primed_prefix.cpu()):
+            raise ValueError(
+                "input_ids diverges from the already-primed session prefix. generate() expects each call to extend "
+                "the same growing sequence (previous input + previously generated tokens + any new tokens). Call "
+                "reset() to start a different session.")
+        pending = input_ids[:, self._primed_tokens:total_len - 1]
+        for i in range(pending.shape[-1]):
+            self._forward_step(pending[:, i:i + 1], attention_mask[:, :self._primed_tokens + i + 1])
+
+    # ------------------------------------------------------------------ public API
+    @torch.inference_mode()
+    def generate(self, input_ids: torch.Tensor, attention_mask: torch.Tensor, max_new_tokens: int, *,
+                 do_sample: bool = False, temperature: float = 1.0, top_k: int | None = None,
+                 top_p: float | None = None, generator: torch.Generator | None = None):
+        """Generate up to max_new_tokens tokens, continuing any previous session on this model."""
+        self._acquire_or_raise()
+        try:
+            batch_size = input_ids.shape[0]
+            self._validate_left_padded(attention_mask)
+            if do_sample:
+                if temperature <= 0:
+                    raise ValueError(f"temperature must be > 0 for sampling, got {temperature}.")
+                if top_k is not None and top_k < 1:
+                    raise ValueError(f"top_k must be >= 1, got {top_k}.")
+                if top_p is not None and not (0.0 < top_p <= 1.0):
+                    raise ValueError(f"top_p must be in (0, 1], got {top_p}.")
+            fresh = self._store is None
+            if fresh:
+                self._start_session(input_ids, attention_mask)
+            else:
+                self._extend_session(input_ids, attention_mask)
+            next_input_id = input_ids[:, -1:]
+            mask = attention_mask
+            generated: list[list[int]] = [[] for _ in range(batch_size)]
+            stats = GenerationStats()
+            in_gpu = []
+            for _ in range(max_new_tokens):
+                logits, step = self._forward_step(next_input_id, mask)
+                if do_sample:
+                    nxt = self._sample_next_token(logits[:, -1, :], temperature=temperature, top_k=top_k,
+                                                  top_p=top_p, generator=generator)
+                else:
+                    nxt = torch.argmax(logits[:, -1, :], dim=-1, keepdim=True)
+                for row, tok in zip(generated, nxt[:, 0].tolist()):
+                    row.append(tok)
+                stats.total_new_blocks += step["new_blocks"]
+                stats.total_gpu_to_cpu_mb += step["gpu_to_cpu_mb"]
+                stats.total_cpu_to_gpu_mb += step["cpu_to_gpu_mb"]
+                stats.total_gpu_to_cpu_copies += step["gpu_to_cpu_copies"]
+                stats.total_cpu_to_gpu_copies += step["cpu_to_gpu_copies"]
+                in_gpu.append(step["attention_in_gpu"])
+                next_input_id = nxt
+                mask = torch.cat([mask, torch.ones((mask.shape[0], 1), dtype=mask.dtype, device=mask.device)], dim=1)
+            full = torch.cat([input_ids, torch.tensor(generated, dtype=input_ids.dtype, device=input_ids.device)],
+                             dim=1)
+            self._primed_prefix = full[:, :-1].detach().clone()
+            self._primed_tokens = full.shape[-1] - 1
+            stats.final_num_blocks = self._num_blocks
+            if in_gpu:
+                stats.mean_attention_in_gpu = sum(in_gpu) / len(in_gpu)
+                stats.min_attention_in_gpu = min(in_gpu)
+                stats.max_attention_in_gpu = max(in_gpu)
+            self.last_run_stats = stats
+            return generated[0] if batch_size == 1 else generated
+        finally:
+            self._lock.release()

@@ -1,0 +1,167 @@
+"""Greedy generation through ``pager_hf.paged_model.PagedModel`` matches unpaged HF greedy decoding.
+
+The north star's end-to-end criterion: greedy token IDs from
+``PagedModel.generate`` on random-init weights match exactly.  The unpaged
+reference is the model's own forward with a ``DynamicCache`` (transformers'
+stock attention), one token at a time with argmax -- the reference project's
+own correctness bar (greedy parity with plain HF generation).  Token IDs
+must match exactly; the only tolerated difference is a tie at the model's
+fp16 output precision in the unpaged run's own logits (two tokens within 2
+fp16 ulps: either choice is within rounding of the fp32 result, and the two
+runs then follow different continuations).  The paged run
+keeps most blocks in the pinned host tier (small VRAM budget), scores blocks
+with the heavy-hitter mass the kernel emits, and rolls tails into blocks many
+times.
+"""
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+BLOCK = 16 * 1024 * 1024
+
+
+@torch.inference_mode()
+def _hf_greedy(model, input_ids, attention_mask, n):
+    """Unpaged greedy decoding; returns (token lists per row, logits per step [rows, vocab])."""
+    from transformers import DynamicCache
+
+    cache = DynamicCache()
+    mask = attention_mask
+    pos = (mask.long().cumsum(-1) - 1).clamp(min=0)
+    out = model(input_ids=input_ids, attention_mask=mask, position_ids=pos, past_key_values=cache, use_cache=True)
+    toks, logits = [], []
+    for _ in range(n):
+        logits.append(out.logits[:, -1].float())
+        nxt = out.logits[:, -1].argmax(-1, keepdim=True)
+        toks.append(nxt)
+        mask = torch.cat([mask, torch.ones_like(mask[:, :1])], dim=1)
+        pos = (mask.long().cumsum(-1) - 1)[:, -1:]
+        out = model(input_ids=nxt, attention_mask=mask, position_ids=pos, past_key_values=cache, use_cache=True)
+    return torch.cat(toks, dim=1).tolist(), logits
+
+
+def _assert_greedy_match(got, want, logits, row=0):
+    """Token IDs must match exactly.  The one allowed exception: at the first differing step the
+    unpaged run's own fp16 logits of the two tokens are a tie at output precision (within 2 fp16
+    ulps); the continuations then differ and are not compared further."""
+    for i, (a, b) in enumerate(zip(got, want)):
+        if a == b:
+            continue
+        lg = logits[i][row]
+        gap = abs(float(lg[a]) - float(lg[b]))
+        ulp = float(torch.finfo(torch.float16).eps) * max(abs(float(lg[b])), 1e-3)
+        assert gap <= 2 * ulp, f"step {i}: paged picked {a}, unpaged {b}; logit gap {gap:.5f} > 2 fp16 ulp {ulp:.5f}"
+        return i
+    assert len(got) == len(want)
+    return None
+
+
+def _model(kind, **over):
+    from transformers import MistralConfig, MistralForCausalLM, Qwen2Config, Qwen2ForCausalLM
+
+    torch.manual_seed(0)
+    common = dict(hidden_size=256, intermediate_size=512, num_hidden_layers=4, num_attention_heads=4,
+                  num_key_value_heads=2, head_dim=64, vocab_size=2000, max_position_embeddings=4096,
+                  initializer_range=0.02)
+    common.update(over)
+    if kind == "qwen2":
+        cfg = Qwen2Config(rope_theta=1e6, **common)
+        m = Qwen2ForCausalLM(cfg)
+    else:
+        cfg = MistralConfig(sliding_window=64, **common)
+        m = MistralForCausalLM(cfg)
+    return m.to(device="cuda", dtype=torch.float16).eval()
+
+
+@pytest.mark.parametrize("policy", ["sinks_heavy_hitter", "recent_only", "heavy_hitter"])
+def test_greedy_tokens_match_unpaged_qwen2(policy):
+    from pager_hf.paged_model import PagedModel
+
+    model = _model("qwen2")
+    g = torch.Generator().manual_seed(1)
+    ids = torch.randint(0, 2000, (1, 230), generator=g).cuda()
+    mask = torch.ones_like(ids)
+    want, logits = _hf_greedy(model, ids, mask, 40)
+    pm = PagedModel(model, vram_budget=3 * BLOCK, ram_budget=1000 * BLOCK, recent_window=2, rebalance_interval=2,
+                    policy=policy, tokens_per_block=16)
+    got = pm.generate(ids, mask, 40)
+    _assert_greedy_match(got, want[0], logits)
+    assert pm._store.cpu_block_ids(), "no block reached the host tier"
+    assert pm.last_run_stats.total_new_blocks >= 2
+
+
+def test_greedy_tokens_match_with_sliding_window_mistral():
+    from pager_hf.paged_model import PagedModel
+
+    model = _model("mistral")
+    g = torch.Generator().manual_seed(2)
+    ids = torch.randint(0, 2000, (1, 150), generator=g).cuda()
+    mask = torch.ones_like(ids)
+    want, logits = _hf_greedy(model, ids, mask, 30)
+    pm = PagedModel(model, vram_budget=2 * BLOCK, ram_budget=1000 * BLOCK, recent_window=1, policy="sinks_recent",
+                    tokens_per_block=16)
+    _assert_greedy_match(pm.generate(ids, mask, 30), want[0], logits)
+
+
+def test_left_padded_batch_rows_match_single_row_runs():
+    from pager_hf.paged_model import PagedModel
+
+    model = _model("qwen2")
+    g = torch.Generator().manual_seed(3)
+    lens = [180, 131]
+    rows = [torch.randint(0, 2000, (1, n), generator=g).cuda() for n in lens]
+    T = max(lens)
+    ids = torch.zeros(2, T, dtype=torch.long, device="cuda")
+    mask = torch.zeros(2, T, dtype=torch.long, device="cuda")
+    for b, r in enumerate(rows):
+        ids[b, T - r.shape[1]:] = r[0]
+        mask[b, T - r.shape[1]:] = 1
+    refs = [_hf_greedy(model, r, torch.ones_like(r), 24) for r in rows]
+    pm = PagedModel(model, vram_budget=3 * BLOCK, ram_budget=1000 * BLOCK, recent_window=2, policy="heavy_hitter",
+                    tokens_per_block=16)
+    got = pm.generate(ids, mask, 24)
+    for b, (want, logits) in enumerate(refs):
+        _assert_greedy_match(got[b], want[0], logits)
+
+
+def test_session_continues_across_generate_calls():
+    from pager_hf.paged_model import PagedModel
+
+    model = _model("qwen2")
+    g = torch.Generator().manual_seed(4)
+    ids = torch.randint(0, 2000, (1, 100), generator=g).cuda()
+    pm = PagedModel(model, vram_budget=2 * BLOCK, ram_budget=1000 * BLOCK, recent_window=1,
+                    policy="sinks_heavy_hitter", tokens_per_block=16)
+    first = pm.generate(ids, torch.ones_like(ids), 12)
+    want1, logits1 = _hf_greedy(model, ids, torch.ones_like(ids), 12)
+    _assert_greedy_match(first, want1[0], logits1)
+    # the second call extends the session with the tokens it returned: compare with unpaged greedy
+    # decoding from that same extended prompt
+    ids2 = torch.cat([ids, torch.tensor([first], device="cuda")], dim=1)
+    second = pm.generate(ids2, torch.ones_like(ids2), 18)
+    want2, logits2 = _hf_greedy(model, ids2, torch.ones_like(ids2), 18)
+    _assert_greedy_match(second, want2[0], logits2)
+    with pytest.raises(ValueError):
+        pm.generate(ids[:, :50], torch.ones_like(ids[:, :50]), 1)  # shorter than the primed session
+    pm.reset()
+    _assert_greedy_match(pm.generate(ids, torch.ones_like(ids), 5), want1[0][:5], logits1)
+
+
+def test_baseline_config2_geometry_greedy_parity():
+    """BASELINE config 2's architecture (random-init Qwen2.5-0.5B: 24 layers, hidden 896, 14/2 heads, D 64,
+    fp16), 8192-token prompt, 10% of blocks resident, recent_only; 32 new tokens (128 in the benchmark config)."""
+    from pager_hf.paged_model import PagedModel
+
+    model = _model("qwen2", hidden_size=896, intermediate_size=4864, num_hidden_layers=24, num_attention_heads=14,
+                   num_key_value_heads=2, head_dim=64, vocab_size=151936, max_position_embeddings=32768)
+    g = torch.Generator().manual_seed(1)
+    ids = torch.randint(0, 151936, (1, 8192), generator=g).cuda()
+    mask = torch.ones_like(ids)
+    want, logits = _hf_greedy(model, ids, mask, 32)
+    nblocks = 8192 // 64
+    pm = PagedModel(model, vram_budget=-(-nblocks // 10) * BLOCK, ram_budget=10 * nblocks * BLOCK,
+                    recent_window=-(-nblocks // 10) - 1, policy="recent_only", tokens_per_block=64)
+    _assert_greedy_match(pm.generate(ids, mask, 32), want[0], logits)
+    assert len(pm._store.gpu_block_ids()) <= -(-nblocks // 10) + 1

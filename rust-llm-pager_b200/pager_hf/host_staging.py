@@ -190,3 +190,9 @@ class HostStaging:
 
     def synchronize(self) -> None:
         self.copy_stream.synchronize()
+
+    def invalidate(self) -> None:
+        """Wait for pending copies and forget what the buffer halves hold: the next ``run`` of each
+        layer copies it again (e.g. before a timed region, so that no copy done earlier counts)."""
+        self.copy_stream.synchronize()
+        self.content = [None, None]

@@ -65,6 +65,18 @@ WORKLOADS = {
 
 
 # ----------------------------------------------------------------------------- helpers
+def _json_stdout(world: int):
+    """Where the one JSON line goes.  Under torchrun, native libraries (NCCL's version banner) write to
+    file descriptor 1 too; that descriptor is pointed at stderr and the JSON line goes to a saved copy
+    of the original stdout, so stdout carries exactly one line."""
+    if world <= 1:
+        return sys.stdout
+    sys.stdout.flush()
+    saved = os.dup(1)
+    os.dup2(2, 1)
+    return os.fdopen(saved, "w", buffering=1)
+
+
 def _dist_env():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -138,12 +150,11 @@ def measured_peaks():
 class Workload:
     """Device pool, pinned host pool, block tables, tails and queries for one GPU's share."""
 
-    def __init__(self, name: str, device, seed: int, host_read: str = "auto"):
+    def __init__(self, name: str, device, seed: int):
         import torch
 
         from pager_hf import _lib
         from pager_hf.host_pool import HostPool
-        from pager_hf.streaming_attention import PagedDecodePlan
 
         w = WORKLOADS[name]
         self.name, self.w = name, w
@@ -214,12 +225,7 @@ class Workload:
         self.out = torch.empty_like(self.q)
         self.mass = torch.zeros(self.B, nb, dtype=torch.float32, device=device)
         self.max_row_tokens = nb * self.tpb + self.tpb
-        self.plan = PagedDecodePlan(
-            batch=self.B, num_query_heads=self.Hq, dev_pool=self.dev_pool,
-            host_pool=None if self.host is None else self.host.tensor, num_layers=self.L, tokens_per_block=self.tpb,
-            block_table=self.table, num_blocks=self.num_blocks, max_row_tokens=self.max_row_tokens,
-            tail_k=self.tail_k, tail_v=self.tail_v, tail_len=self.tail_len, valid_lo=self.valid_lo,
-            mass_accum=self.mass, mass_mode="row_mean", host_read=host_read, prefetch_next_step=True)
+        self.plan = None
         # algorithmic bytes per step (only attended tokens are counted)
         kv_tok = 2 * self.Hkv * self.D * elt
         qo = 2 * self.B * self.Hq * self.D * elt
@@ -239,6 +245,16 @@ class Workload:
         for s in range(0, flat.numel(), chunk):
             n = min(chunk, flat.numel() - s)
             flat[s:s + n].copy_(src[:n], non_blocking=False)
+
+    def build_plan(self, host_read: str):
+        from pager_hf.streaming_attention import PagedDecodePlan
+
+        self.plan = PagedDecodePlan(
+            batch=self.B, num_query_heads=self.Hq, dev_pool=self.dev_pool,
+            host_pool=None if self.host is None else self.host.tensor, num_layers=self.L, tokens_per_block=self.tpb,
+            block_table=self.table, num_blocks=self.num_blocks, max_row_tokens=self.max_row_tokens,
+            tail_k=self.tail_k, tail_v=self.tail_v, tail_len=self.tail_len, valid_lo=self.valid_lo,
+            mass_accum=self.mass, mass_mode="row_mean", host_read=host_read, prefetch_next_step=True)
 
     def invalidate_staging(self):
         if self.plan.staging is not None:
@@ -394,9 +410,8 @@ def run_ours(args):
     import torch.distributed as dist
 
     world, rank, local = _dist_env()
+    out = _json_stdout(world)
     if world > 1:
-        # NCCL's banner and debug lines go to stderr: stdout carries exactly one JSON line
-        os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
         torch.cuda.set_device(local)
         from datetime import timedelta
 
@@ -411,16 +426,22 @@ def run_ours(args):
     owners = shard_requests(world * w["batch"], world)
     mine = local_requests(owners, rank)
     assert len(mine) == w["batch"], (len(mine), w["batch"])
-    wl = Workload(args.workload, device, seed=1234 + 7919 * mine[0], host_read=args.host_read)
+    wl = Workload(args.workload, device, seed=1234 + 7919 * mine[0])
 
     def barrier():
         if world > 1:
             dist.barrier(device_ids=[local])
         torch.cuda.synchronize(device)
 
-    # all ranks probe the host link at once: with N GPUs the pinned pools share host DRAM bandwidth
+    # all ranks probe the host link at once: with N GPUs the pinned pools share host DRAM bandwidth;
+    # the host tier's read mode ("auto") is then chosen from this concurrent measurement
     barrier()
     link = probe_link(wl, device)
+    if link.get("copy_gbs"):
+        from pager_hf.host_staging import record_link_bandwidth
+
+        record_link_bandwidth(device, link["copy_gbs"], link["zero_copy_gbs"])
+    wl.build_plan(args.host_read)
 
     # warm-up (also first-call setup: occupancy queries, smem attributes)
     for _ in range(max(args.warmup, 1)):
@@ -526,7 +547,7 @@ def run_ours(args):
                 arm.close()
             line["cpu_baseline"] = {"value": b / t_cpu / 1e9, "unit": "GB/s", "cores": arm.procs, "kind": "port",
                                     "sample": sample_desc(arm)}
-        print(json.dumps(line), flush=True)
+        print(json.dumps(line), file=out, flush=True)
     return 0
 
 

@@ -102,6 +102,15 @@ def link_bandwidth(device) -> dict:
         return _LINK[idx]
 
 
+def record_link_bandwidth(device, copy_gbs: float, zero_copy_gbs: float) -> None:
+    """Use an outside measurement of this device's link (e.g. taken with every GPU of the box copying
+    at once) for later ``auto`` choices instead of probing it alone."""
+    device = torch.device(device)
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    with _LINK_LOCK:
+        _LINK[idx] = {"copy_gbs": float(copy_gbs), "zero_copy_gbs": float(zero_copy_gbs)}
+
+
 def choose_host_read(device) -> str:
     """``"staged"`` when the copy engines beat zero-copy reads on this device's link, else ``"zero_copy"``."""
     bw = link_bandwidth(device)

@@ -42,6 +42,7 @@ import logging
 from collections.abc import Mapping
 from dataclasses import dataclass
 
+import numpy as np
 import torch
 
 from .host_pool import HostPool
@@ -377,6 +378,21 @@ class KVBlockStore:
         self._tokens[block_id] = self.tokens_per_block
         self._resident_gpu_bytes += self._block_bytes(self.tokens_per_block)
 
+    def adopt_host_group(self, block_id: int, group: int) -> None:
+        """Register a full block whose data the caller already wrote into host slot group ``group``."""
+        if self.pools is None:
+            raise ValueError("adopt_host_group needs pools")
+        if block_id in self._dev_group or block_id in self._host_group:
+            raise ValueError(f"Block {block_id} already exists.")
+        incoming = self._block_bytes(self.tokens_per_block)
+        if self.ram_budget_bytes is not None and self._resident_cpu_bytes + incoming > self.ram_budget_bytes:
+            raise RuntimeError(f"ram_budget exceeded: block {block_id} would need "
+                               f"{(self._resident_cpu_bytes + incoming) / 1_000_000:.2f} MB, budget is "
+                               f"{self.ram_budget_bytes / 1_000_000:.2f} MB.")
+        self._host_group[block_id] = group
+        self._tokens[block_id] = self.tokens_per_block
+        self._resident_cpu_bytes += incoming
+
     def has_gpu(self, block_id: int) -> bool:
         return block_id in self._dev_group
 
@@ -572,20 +588,22 @@ class KVBlockStore:
         if block_ids is None:
             known = set(self._dev_group) | set(self._host_group)
             block_ids = range(max(known) + 1) if known else range(0)
-        block_ids = list(block_ids)
-        table = torch.full((self.batch, len(block_ids)), -1, dtype=torch.int32)
-        for j, bid in enumerate(block_ids):
-            if bid in self._dev_group or bid in self._host_group:
-                if self._tokens[bid] != self.tokens_per_block:
-                    raise ValueError(f"block {bid} holds {self._tokens[bid]} of {self.tokens_per_block} tokens; "
-                                     "the decode op reads whole blocks")
-            if bid in self._dev_group:
-                base = self._dev_group[bid] * self.batch
-                table[:, j] = torch.arange(base, base + self.batch, dtype=torch.int32)
-            elif bid in self._host_group:
-                base = self._host_group[bid] * self.batch
-                table[:, j] = torch.arange(base, base + self.batch, dtype=torch.int32) | HOST_SLOT_BIT
-        return table.to(device if device is not None else self.device)
+        ids = list(block_ids)
+        dev = np.fromiter((self._dev_group.get(b, -1) for b in ids), dtype=np.int64, count=len(ids))
+        host = np.fromiter((self._host_group.get(b, -1) for b in ids), dtype=np.int64, count=len(ids))
+        short = [b for b in ids if b in self._tokens and self._tokens[b] != self.tokens_per_block]
+        if short:
+            b = short[0]
+            raise ValueError(f"block {b} holds {self._tokens[b]} of {self.tokens_per_block} tokens; "
+                             "the decode op reads whole blocks")
+        B = self.batch
+        rows = np.arange(B, dtype=np.int64)[:, None]
+        table = np.full((B, len(ids)), -1, dtype=np.int64)
+        on_dev = dev >= 0
+        on_host = host >= 0
+        table[:, on_dev] = dev[on_dev][None, :] * B + rows
+        table[:, on_host] = (host[on_host][None, :] * B + rows) | HOST_SLOT_BIT
+        return torch.from_numpy(table.astype(np.int32)).to(device if device is not None else self.device)
 
     def close(self) -> None:
         """Free this store's blocks; a store with private pools also frees its pinned host pool."""

@@ -330,7 +330,7 @@ __device__ float paged_block_head_mass(const PagedMassParams& p, int b, int r, i
     const float2 v = p.mass_part[row * p.gstride + gi];
     if (v.x != 0.f) s += v.x * exp2f((v.y - mf) * kLog2e);
   }
-  return s / lf;
+  return lf > 0.f ? s / lf : 0.f;  // nothing valid in the row: no mass (streaming_attention.py:317 defaults l_final to 1)
 }
 
 // One CTA per (32 blocks, row): lane <-> block, warp <-> a subset of the query heads,

@@ -161,3 +161,19 @@ def test_out_of_range_slot_is_flagged_not_read(mods):
     ref_out, ref_mass = oracle_row(s, 0, 0, "f16")
     np.testing.assert_allclose(out[0].numpy(), ref_out, rtol=0, atol=2e-3)
     np.testing.assert_allclose(bm[0].numpy(), ref_mass, rtol=1e-4, atol=1e-6)
+
+
+def test_row_with_nothing_to_read_next_to_full_rows(mods):
+    """A row with no block and no tail token (no tile at all) gets the reference's 0/0 output and zero
+    mass; the other rows of the same launch are unaffected."""
+    sa, HostPool, lib = mods
+    s = build(9, 3, 8, 2, 64, 16, 1, [5, 0, 3], [4, 0, 2], torch.float16)
+    out, bm, accum = run_gpu(sa, HostPool, s, 0)
+    assert torch.isnan(out[1]).all()
+    assert float(bm[1].abs().sum()) == 0 and float(accum[1].abs().sum()) == 0
+    for b in (0, 2):
+        ref_out, ref_mass = oracle_row(s, b, 0, "f16")
+        np.testing.assert_allclose(out[b].numpy(), ref_out, rtol=0, atol=2e-3)
+        nb = s["nbs"][b]
+        np.testing.assert_allclose(accum[b, :nb].numpy(), ref_mass[:, :nb].mean(0), rtol=1e-4, atol=1e-6)
+    assert lib.device_status(0) == 0

@@ -226,6 +226,7 @@ enum { OP_STEP = 0, OP_STATS = 1, OP_FIXED = 2, OP_PAGED = 3 };
 
 __global__ void __launch_bounds__(128) combine_kernel(const CombineParams c) {
   __shared__ float w_s[kMaxSplits];
+  __shared__ float l_s[kMaxSplits];
   __shared__ float sh_L;
   __shared__ float sh_M;
   __shared__ float sh_win;
@@ -239,14 +240,21 @@ __global__ void __launch_bounds__(128) combine_kernel(const CombineParams c) {
   if (c.op == OP_FIXED) {
     for (int d = threadIdx.x; d < D; d += blockDim.x) {
       float a = c.acc[(long long)row * D + d];
+#pragma unroll 8
       for (int s = 0; s < nsplit; ++s) a += c.part_acc[(pbase + s) * D + d];
       c.acc[(long long)row * D + d] = a;
     }
     return;
   }
+  // the splits' statistics are loaded by all threads at once, then reduced by one in split order
+  for (int s = threadIdx.x; s < nsplit; s += blockDim.x) {
+    w_s[s] = c.part_m[pbase + s];
+    l_s[s] = c.part_l[pbase + s];
+  }
+  __syncthreads();
   if (threadIdx.x == 0) {
     float M = neg_inf();
-    for (int s = 0; s < nsplit; ++s) M = fmaxf(M, c.part_m[pbase + s]);
+    for (int s = 0; s < nsplit; ++s) M = fmaxf(M, w_s[s]);
     const float m_in = c.op == OP_PAGED ? neg_inf() : c.m[row];
     const float Mt = fmaxf(M, m_in);
     // reference guard (streaming_attention.py:171-172): nothing valid yet -> alpha = 0
@@ -254,10 +262,10 @@ __global__ void __launch_bounds__(128) combine_kernel(const CombineParams c) {
     if (c.op != OP_PAGED && Mt != neg_inf()) w_in = (m_in == Mt) ? 1.f : exp2f((m_in - Mt) * kLog2e);
     float L = c.op == OP_PAGED ? 0.f : c.l[row] * w_in;
     for (int s = 0; s < nsplit; ++s) {
-      const float ms = c.part_m[pbase + s];
+      const float ms = w_s[s];
       const float ws = ms == neg_inf() ? 0.f : (ms == Mt ? 1.f : exp2f((ms - Mt) * kLog2e));
       w_s[s] = ws;
-      L += ws * c.part_l[pbase + s];
+      L += ws * l_s[s];
     }
     sh_L = L;
     sh_M = Mt;
@@ -268,6 +276,7 @@ __global__ void __launch_bounds__(128) combine_kernel(const CombineParams c) {
   if (c.op == OP_STEP || c.op == OP_PAGED) {
     for (int d = threadIdx.x; d < D; d += blockDim.x) {
       float a = c.op == OP_PAGED ? 0.f : c.acc[(long long)row * D + d] * sh_win;
+#pragma unroll 8
       for (int s = 0; s < nsplit; ++s) a += w_s[s] * c.part_acc[(pbase + s) * D + d];
       if (c.op == OP_STEP)
         c.acc[(long long)row * D + d] = a;
@@ -324,6 +333,7 @@ __device__ float paged_block_head_mass(const PagedMassParams& p, int b, int r, i
   const float lf = p.l_final[row];
   const int gpb = p.tpb >> p.group_shift;
   float s = 0.f;
+#pragma unroll 4
   for (int gi = j * gpb; gi < (j + 1) * gpb; ++gi) {
     const int tile = (gi << p.group_shift) >> p.tile_shift;
     if (tile < t_begin || tile >= t_end) continue;  // never loaded: outside the attended range
@@ -352,6 +362,7 @@ __global__ void __launch_bounds__(kMassWarps * 32) paged_mass_kernel(const Paged
     if (j >= g.nb || j >= p.max_blocks) continue;
     int tb, te, ns;
     geom_tiles(g, p.tile_shift, p.tiles_per_split, tb, te, ns);
+#pragma unroll 4
     for (int r = warp; r < p.num_q_heads; r += kMassWarps) {
       const float v = paged_block_head_mass(p, b, r, j, tb, te);
       if (p.block_mass) p.block_mass[((long long)b * p.num_q_heads + r) * p.max_blocks + j] = v;

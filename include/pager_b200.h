@@ -203,6 +203,14 @@ int pager_append_tokens(void* pool, int dtype, int pool_slots, int num_layers, i
                         int tokens_per_block, int head_dim, const int32_t* slots, const int32_t* positions,
                         const void* k_new, const void* v_new, int batch, void* stream);
 
+/* ---- Self-test of the kernels' bounded waits (no counterpart in the reference).
+ *      Every wait in the decode kernels (on a TMA stage, on a producer) gives up after a time
+ *      limit, sets the device status word to PAGER_ERR_TIMEOUT and lets the kernel finish, so a
+ *      stuck copy never hangs the GPU.  This launches one thread that waits on an mbarrier nothing
+ *      arrives on, with a limit of limit_ns (at most 100 ms); afterwards pager_device_status
+ *      reports 5 and *waited_ns holds the time the wait took.  Synchronises `stream`. */
+int pager_selftest_bounded_wait(unsigned long long limit_ns, unsigned long long* waited_ns, void* stream);
+
 /* ---- Pinned host pool (the host tier of KVBlockStore, pager_hf/kv_block_store.py:45-46).
  *      cudaHostAlloc(Portable | Mapped): the returned pointer is readable by kernels
  *      on every device (zero-copy) and is the host address as well. */

@@ -400,6 +400,21 @@ __global__ void state_init_kernel(float* m, float* l, float* acc, long long rows
   if (i < rows * head_dim) acc[i] = 0.f;
 }
 
+// Self-test of the bounded waits every kernel uses: one thread waits on an mbarrier that nothing
+// ever arrives on; the wait gives up after limit_ns and the device status word reports a timeout.
+__device__ unsigned long long g_selftest_waited_ns;
+
+__global__ void bounded_wait_selftest_kernel(unsigned long long limit_ns, int* status) {
+  __shared__ __align__(8) uint64_t bar;
+  if (threadIdx.x != 0) return;
+  mbar_init(&bar, 1);
+  mbar_fence_init();
+  const unsigned long long t0 = global_timer_ns();
+  const bool arrived = mbar_wait_bounded(&bar, 0, limit_ns);
+  g_selftest_waited_ns = global_timer_ns() - t0;
+  if (!arrived) atomicExch(status, kStatusTimeout);
+}
+
 __global__ void zero_copy_probe_kernel(const uint4* __restrict__ src, uint4* __restrict__ dst, long long n16) {
   const long long stride = (long long)gridDim.x * blockDim.x;
   long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
@@ -1020,6 +1035,23 @@ int pager_paged_decode_attention_staged(const void* q, int q_dtype, const void* 
     paged_mass_kernel<<<g2, kMassWarps * 32, 0, st>>>(mp);
     PAGER_CUDA(cudaGetLastError(), "mass launch");
   }
+  return PAGER_OK;
+}
+
+int pager_selftest_bounded_wait(unsigned long long limit_ns, unsigned long long* waited_ns, void* stream) {
+  if (limit_ns == 0 || limit_ns > 100000000ull)
+    return fail(PAGER_ERR_INVALID, "limit_ns must be in (0, 100 ms], got %llu", limit_ns);
+  DevInfo* di;
+  const int rc = device_info(&di);
+  if (rc) return rc;
+  cudaStream_t st = (cudaStream_t)stream;
+  bounded_wait_selftest_kernel<<<1, 32, 0, st>>>(limit_ns, di->status);
+  PAGER_CUDA(cudaGetLastError(), "self-test launch");
+  unsigned long long w = 0;
+  PAGER_CUDA(cudaMemcpyFromSymbolAsync(&w, g_selftest_waited_ns, sizeof(w), 0, cudaMemcpyDeviceToHost, st),
+             "self-test readback");
+  PAGER_CUDA(cudaStreamSynchronize(st), "self-test sync");
+  if (waited_ns) *waited_ns = w;
   return PAGER_OK;
 }
 

@@ -70,6 +70,7 @@ _SIGNATURES = {
                                                  _i, _vp, _vp, _vp, _vp, _i, _vp, _vp, _vp, _i, _i, _f, _f, _i,
                                                  _vp, _i, _vp, _vp, _i, _i, _vp, _sz, _vp]),
     "pager_stage_host_blocks": (_i, [_vp, _vp, _i64, _i64, _i64, _vp, _vp, _vp, _i, _vp]),
+    "pager_selftest_bounded_wait": (_i, [ctypes.c_ulonglong, ctypes.POINTER(ctypes.c_ulonglong), _vp]),
     "pager_host_pool_alloc": (_i, [_sz, ctypes.POINTER(_vp)]),
     "pager_host_pool_free": (_i, [_vp]),
     "pager_probe_h2d_copy_gbs": (_i, [_vp, _vp, _sz, _i, _vp, ctypes.POINTER(ctypes.c_double)]),

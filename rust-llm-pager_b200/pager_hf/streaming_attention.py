@@ -314,7 +314,7 @@ def paged_decode_attention(
 
     q [B, Hq, D]; dev_pool [dev_slots, L, 2, Hkv, tpb, D] (CUDA) and host_pool
     [host_slots, L, 2, Hkv, tpb, D] (pinned, device-mapped host memory; see
-    ``kv_block_store.HostPool``); block_table [B, max_blocks] int32 with
+    ``host_pool.HostPool``); block_table [B, max_blocks] int32 with
     entries slot (device), slot | HOST_SLOT_BIT (host) or -1 (absent);
     num_blocks [B]; tail_k/tail_v [B, Hkv, tail_cap, D] with tail_len [B];
     valid_lo/valid_hi [B] bound the attended tokens (left padding, sliding

@@ -177,3 +177,66 @@ def test_row_with_nothing_to_read_next_to_full_rows(mods):
         nb = s["nbs"][b]
         np.testing.assert_allclose(accum[b, :nb].numpy(), ref_mass[:, :nb].mean(0), rtol=1e-4, atol=1e-6)
     assert lib.device_status(0) == 0
+
+
+EXTRA = [
+    # (name, seed, B, Hq, Hkv, D, tpb, L, nbs, tails, dtype, kw) -- kw: scale / softcap / backend
+    ("softcap_mma_d128", 11, 2, 16, 8, 128, 64, 2, [6, 3], [9, 2], torch.bfloat16, dict(scale=0.0625, softcap=50.0)),
+    ("softcap_fma_d256", 12, 2, 8, 4, 256, 32, 1, [5, 2], [4, 31], torch.bfloat16, dict(scale=1 / 16, softcap=30.0)),
+    ("blocks_of_256", 13, 2, 8, 2, 64, 256, 1, [3, 2], [200, 17], torch.float16, {}),
+    ("blocks_of_8", 14, 2, 8, 2, 64, 8, 1, [40, 7], [5, 8], torch.float16, {}),
+    ("n_rep_16", 15, 2, 32, 2, 128, 64, 1, [4, 5], [3, 60], torch.float16, {}),
+    ("n_rep_1_mha", 16, 2, 4, 4, 64, 32, 2, [6, 2], [1, 30], torch.float16, {}),
+    ("fp32_d8", 17, 3, 4, 2, 8, 16, 1, [5, 1, 3], [2, 16, 1], torch.float32, {}),
+    ("fp16_d32", 18, 2, 6, 3, 32, 16, 1, [9, 4], [15, 1], torch.float16, {}),
+]
+
+
+@pytest.mark.parametrize("case", EXTRA, ids=[c[0] for c in EXTRA])
+def test_paged_op_options_match_the_reference(mods, case):
+    """Softcap and custom scale (MMA and FMA), blocks larger than a tile and the smallest blocks,
+    GQA fan-out 16 and plain MHA, fp32 and small head dims."""
+    sa, HostPool, lib = mods
+    name, seed, B, Hq, Hkv, D, tpb, L, nbs, tails, dtype, kw = case
+    s = build(seed, B, Hq, Hkv, D, tpb, L, nbs, tails, dtype)
+    dt = {torch.float16: "f16", torch.bfloat16: "bf16", torch.float32: "f32"}[dtype]
+    layer = L - 1
+    out, bm, accum = run_gpu(sa, HostPool, s, layer, **kw)
+    atol = 5e-3 if dtype == torch.bfloat16 else 2e-3
+    for b in range(B):
+        ref_out, ref_mass = oracle_row(s, b, layer, dt, scale=kw.get("scale"), softcap=kw.get("softcap"))
+        np.testing.assert_allclose(out[b].numpy(), ref_out, rtol=0, atol=atol, err_msg=f"{name} row {b}")
+        nb = nbs[b]
+        np.testing.assert_allclose(bm[b, :, :nb].numpy(), ref_mass[:, :nb], rtol=1e-4, atol=1e-6)
+    assert lib.device_status(0) == 0
+
+
+def test_host_pool_only_and_batch_mean_with_inactive_rows(mods):
+    """No device pool at all (every block in the pinned host pool), one inactive row: the inactive row's
+    output is untouched and the batch mean divides by all rows and heads, as the separate mass kernel does."""
+    sa, HostPool, lib = mods
+    s = build(19, 3, 8, 2, 64, 16, 1, [6, 4, 5], [3, 9, 2], torch.float16, host_every=1)
+    s["table"] = torch.where(s["table"] >= 0, s["table"] | HOST, s["table"])  # every entry in the host pool
+    hp = HostPool(s["host"].shape, s["host"].dtype)
+    hp.tensor.copy_(s["host"])
+    B, Hq, D = 3, 8, 64
+    cu = lambda x: torch.tensor(x, dtype=torch.int32, device="cuda")
+    out = torch.full((B, Hq, D), 7.0, dtype=torch.float16, device="cuda")
+    accum = torch.zeros(s["table"].shape[1], device="cuda")
+    bm = torch.zeros(B, Hq, s["table"].shape[1], device="cuda")
+    sa.paged_decode_attention(
+        s["q"].cuda(), s["table"].cuda(), cu(s["nbs"]), dev_pool=None, host_pool=hp.tensor, num_layers=1, layer=0,
+        tokens_per_block=16, max_row_tokens=max(nb * 16 + t for nb, t in zip(s["nbs"], s["tails"])),
+        tail_k=s["tk"].cuda(), tail_v=s["tv"].cuda(), tail_len=cu(s["tails"]), active=cu([1, 0, 1]),
+        out=out, block_mass=bm, mass_accum=accum, mass_mode="batch_mean")
+    torch.cuda.synchronize()
+    hp.close()
+    assert torch.all(out[1] == 7.0)  # inactive row untouched
+    refs = {b: oracle_row(s, b, 0, "f16") for b in (0, 2)}
+    for b, (ref_out, _) in refs.items():
+        np.testing.assert_allclose(out[b].float().cpu().numpy(), ref_out, rtol=0, atol=2e-3)
+    want = np.zeros(s["table"].shape[1], np.float32)
+    for b, (_, ref_mass) in refs.items():
+        want[:s["nbs"][b]] += ref_mass[:, :s["nbs"][b]].sum(0)
+    np.testing.assert_allclose(accum.cpu().numpy(), want / (B * Hq), rtol=1e-4, atol=1e-7)
+    assert lib.device_status(0) == 0

@@ -101,7 +101,7 @@ int ctas_per_sm(const SplitKernelInfo& k, int* out) {
   PAGER_CUDA(cudaFuncSetAttribute(k.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, k.smem_bytes),
              "cudaFuncSetAttribute(max dynamic smem)");
   int n = 0;
-  PAGER_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k.fn, kThreads, k.smem_bytes), "occupancy");
+  PAGER_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k.fn, k.threads, k.smem_bytes), "occupancy");
   if (n < 1) n = 1;
   std::lock_guard<std::mutex> lk(g_mu);
   g_occupancy[key] = n;
@@ -602,7 +602,7 @@ int run_chunk(const ChunkArgs& a) {
 
   dim3 grid(plan.max_splits, a.hkv, a.batch);
   void* args[] = {&p, &mk, &mv};
-  PAGER_CUDA(cudaLaunchKernel(k.fn, grid, dim3(kThreads), args, k.smem_bytes, a.stream), "split kernel launch");
+  PAGER_CUDA(cudaLaunchKernel(k.fn, grid, dim3(k.threads), args, k.smem_bytes, a.stream), "split kernel launch");
 
   CombineParams c;
   memset(&c, 0, sizeof(c));
@@ -990,7 +990,7 @@ int pager_paged_decode_attention_staged(const void* q, int q_dtype, const void* 
   cudaStream_t st = (cudaStream_t)stream;
   dim3 grid(pp.plan.max_splits, num_kv_heads, batch);
   void* args[] = {&p, &mk, staged ? &ms : &mk};
-  PAGER_CUDA(cudaLaunchKernel(pp.k.fn, grid, dim3(kThreads), args, pp.k.smem_bytes, st), "split kernel launch");
+  PAGER_CUDA(cudaLaunchKernel(pp.k.fn, grid, dim3(pp.k.threads), args, pp.k.smem_bytes, st), "split kernel launch");
 
   CombineParams c;
   memset(&c, 0, sizeof(c));

@@ -33,9 +33,6 @@ enum Backend { BACKEND_MMA = 1, BACKEND_FMA = 2 };
 
 // 6 consumer warps + 2 producer warps: 8 warps, 2 per scheduler, up to 255 registers each.
 // The consumer count must be even and at most the stage count (see consumer_wait).
-constexpr int kConsumerWarps = 6;
-constexpr int kProducerWarps = 2;
-constexpr int kThreads = (kConsumerWarps + kProducerWarps) * 32;
 constexpr int kMaxRep = 16;
 constexpr int kHostSlotBit = 0x40000000;   // block-table entry: slot of the pinned host pool
 constexpr int kStageSlotBit = 0x20000000;  // block-table entry: slot of the device staging buffer
@@ -166,16 +163,25 @@ struct TileCfg {
   static constexpr int STAGE_BYTES = (MODE == MODE_STATS ? 1 : 2) * TENSOR_BYTES;
   // Shared memory outside the stage ring: Q (bf16/fp16 for mma, fp32 for fma), the fma
   // path's P buffer, the block-table cache, barriers.
+  // CTA shape.  Tensor-core configs: 3 consumer warps + 1 producer warp in 128 threads, two CTAs
+  // per SM (half the shared memory each), so that one CTA's prologue, pipeline fill and merge
+  // overlap the other's streaming and the grid has twice the slots to balance splits over.
+  // CUDA-core configs (compute-bound): 6 consumer + 2 producer warps, one CTA per SM.
+  static constexpr int NCW = BACKEND == BACKEND_MMA ? 3 : 6;  // consumer warps
+  static constexpr int NPW = BACKEND == BACKEND_MMA ? 1 : 2;  // producer warps (one thread each)
+  static constexpr int THREADS = (NCW + NPW) * 32;
+  static constexpr int MIN_BLOCKS = BACKEND == BACKEND_MMA ? 2 : 1;
+  static constexpr int SMEM_BUDGET = BACKEND == BACKEND_MMA ? 110 * 1024 : 225 * 1024;
   static constexpr int Q_BYTES = BACKEND == BACKEND_FMA ? kMaxRep * D * 4 : kMaxRep * D * ELT;
-  static constexpr int P_BYTES = BACKEND == BACKEND_FMA ? kConsumerWarps * TILE * kMaxRep * 4 : 0;
+  static constexpr int P_BYTES = BACKEND == BACKEND_FMA ? NCW * TILE * kMaxRep * 4 : 0;
   static constexpr int EXTRA = Q_BYTES + P_BYTES + kTableCache * 4 + 1536;
   // A deep ring: each consumer warp holds a stage while it computes, the rest stay in flight.
-  // Even, so that each stage is always filled by the same one of the two producer warps.
-  static constexpr int STAGES_RAW = ((225 * 1024 - EXTRA) / STAGE_BYTES) & ~1;
+  // Even, so that with two producer warps each stage is always filled by the same one.
+  static constexpr int STAGES_RAW = ((SMEM_BUDGET - EXTRA) / STAGE_BYTES) & ~1;
   static constexpr int STAGES = STAGES_RAW > 16 ? 16 : STAGES_RAW;
-  static_assert(STAGES >= kConsumerWarps && STAGES % 2 == 0, "stage ring too shallow for the consumer warps");
+  static_assert(STAGES >= NCW && STAGES % 2 == 0, "stage ring too shallow for the consumer warps");
   static constexpr int STAGE_AREA = STAGES * STAGE_BYTES;
-  static constexpr int MERGE_BYTES = kConsumerWarps * kMaxRep * (2 + (MODE == MODE_STATS ? 0 : D)) * 4;
+  static constexpr int MERGE_BYTES = NCW * kMaxRep * (2 + (MODE == MODE_STATS ? 0 : D)) * 4;
   static_assert(MERGE_BYTES <= STAGE_AREA, "merge region must fit in the stage ring");
   static_assert((TILE & (TILE - 1)) == 0 && TILE >= 16 && TILE <= 64, "tile");
 };
@@ -357,7 +363,7 @@ __device__ void run_producer(const SplitParams& p, const TableCache& tc, const C
   const int block_tokens = g.nb * k.tpb;
   const uint32_t seg_bytes = (uint32_t)br * Cfg::ROW_BYTES * (kNeedV ? 2u : 1u);
   int last = -1;
-  for (int i = producer; i < ntiles; i += kProducerWarps) {
+  for (int i = producer; i < ntiles; i += Cfg::NPW) {
     const int s = i % Cfg::STAGES;
     const int use = i / Cfg::STAGES;
     if (use > 0 && !mbar_wait_bounded(&empty[s], (use - 1) & 1, k.wait_limit)) {
@@ -417,7 +423,7 @@ __device__ void run_producer(const SplitParams& p, const TableCache& tc, const C
     last = i;
   }
   // Drain: never leave the CTA with bulk copies still landing in its shared memory.
-  for (int i = last; i >= 0 && i > last - Cfg::STAGES; i -= kProducerWarps) {
+  for (int i = last; i >= 0 && i > last - Cfg::STAGES; i -= Cfg::NPW) {
     if (!mbar_wait_bounded(&full[i % Cfg::STAGES], (i / Cfg::STAGES) & 1, k.wait_limit)) {
       atomicExch(k.status, kStatusTimeout);
       *abort_flag = 1;
@@ -433,10 +439,11 @@ __device__ void run_producer(const SplitParams& p, const TableCache& tc, const C
 // and succeed early.  The warp therefore first waits for use n-1 to be
 // released (empty barrier, phase n-1) and then for use n to land (full
 // barrier, phase n).  The empty wait itself cannot alias: this warp's previous
-// tile, i - kConsumerWarps, was issued, and with STAGES >= kConsumerWarps (and
-// both counts even, so tiles i - STAGES and i - kConsumerWarps share a
-// producer) tile i - STAGES was issued before it -- after use n-2 of the stage
-// had been released.  Both waits suspend in hardware (mbarrier.try_wait) and
+// tile, i - NCW, was issued, and with STAGES >= NCW tile i - STAGES was issued
+// before it by the same producer (with one producer warp trivially; with two,
+// because both counts are even, so tiles i - STAGES and i - NCW have the same
+// producer, which issues in order) -- after use n-2 of the stage had been
+// released.  Both waits suspend in hardware (mbarrier.try_wait) and
 // are bounded; lane 0 waits, then every lane observes the completed full phase
 // so the TMA writes are visible to it.  *info = the stage's segment masks.
 __device__ __forceinline__ bool consumer_wait(uint64_t wait_limit, int* status, uint64_t* full_bar,
@@ -530,22 +537,22 @@ __device__ __forceinline__ float apply_score(float raw, float scale, float softc
 
 // Merge the four consumer warps' states (held in the stage area) and write
 // this split's partial state.  `mw`: m_w[4][16], l_w[4][16], acc_w[4][16][D].
-template <int D, int MODE>
+template <int D, int MODE, int NCW>
 __device__ void merge_and_store(const SplitParams& p, float* mw, int b, int h, int split) {
   const int tid = threadIdx.x;
   const float* m_w = mw;
-  const float* l_w = mw + kConsumerWarps * kMaxRep;
-  const float* acc_w = mw + 2 * kConsumerWarps * kMaxRep;
+  const float* l_w = mw + NCW * kMaxRep;
+  const float* acc_w = mw + 2 * NCW * kMaxRep;
   const int n_rep = p.n_rep;
   const int qh0 = h * n_rep;
   if (MODE != MODE_FIXED) {
-    for (int r = tid; r < n_rep; r += kConsumerWarps * 32) {
+    for (int r = tid; r < n_rep; r += NCW * 32) {
       float M = neg_inf();
 #pragma unroll
-      for (int w = 0; w < kConsumerWarps; ++w) M = fmaxf(M, m_w[w * kMaxRep + r]);
+      for (int w = 0; w < NCW; ++w) M = fmaxf(M, m_w[w * kMaxRep + r]);
       float L = 0.f;
 #pragma unroll
-      for (int w = 0; w < kConsumerWarps; ++w) {
+      for (int w = 0; w < NCW; ++w) {
         const float mwr = m_w[w * kMaxRep + r];
         const float wt = mwr == neg_inf() ? 0.f : fast_exp2((mwr - M) * kLog2e);
         L += wt * l_w[w * kMaxRep + r];
@@ -556,19 +563,19 @@ __device__ void merge_and_store(const SplitParams& p, float* mw, int b, int h, i
     }
   }
   if constexpr (MODE == MODE_STATS) return;
-  for (int idx = tid; idx < n_rep * D; idx += kConsumerWarps * 32) {
+  for (int idx = tid; idx < n_rep * D; idx += NCW * 32) {
     const int r = idx / D;
     const int d = idx % D;
     float A = 0.f;
     if (MODE == MODE_FIXED) {
 #pragma unroll
-      for (int w = 0; w < kConsumerWarps; ++w) A += acc_w[(w * kMaxRep + r) * D + d];
+      for (int w = 0; w < NCW; ++w) A += acc_w[(w * kMaxRep + r) * D + d];
     } else {
       float M = neg_inf();
 #pragma unroll
-      for (int w = 0; w < kConsumerWarps; ++w) M = fmaxf(M, m_w[w * kMaxRep + r]);
+      for (int w = 0; w < NCW; ++w) M = fmaxf(M, m_w[w * kMaxRep + r]);
 #pragma unroll
-      for (int w = 0; w < kConsumerWarps; ++w) {
+      for (int w = 0; w < NCW; ++w) {
         const float mwr = m_w[w * kMaxRep + r];
         const float wt = mwr == neg_inf() ? 0.f : fast_exp2((mwr - M) * kLog2e);
         A += wt * acc_w[(w * kMaxRep + r) * D + d];
@@ -636,7 +643,7 @@ __device__ void run_consumer_mma(const SplitParams& p, const TableCache& tc, uin
   const bool softcap_on = softcap > 0.f;
   const uint64_t full_mask = Cfg::TILE == 64 ? ~0ull : ((1ull << Cfg::TILE) - 1ull);
 
-  for (int i = warp; i < ntiles; i += kConsumerWarps) {
+  for (int i = warp; i < ntiles; i += Cfg::NCW) {
     const int s = i % Cfg::STAGES;
     if (*abort_flag) break;
     uint32_t swm;
@@ -796,11 +803,11 @@ __device__ void run_consumer_mma(const SplitParams& p, const TableCache& tc, uin
     l_r[rr] += __shfl_xor_sync(0xffffffffu, l_r[rr], 1);
     l_r[rr] += __shfl_xor_sync(0xffffffffu, l_r[rr], 2);
   }
-  named_bar_sync(1, kConsumerWarps * 32);
+  named_bar_sync(1, Cfg::NCW * 32);
   float* mw = reinterpret_cast<float*>(stages);
   float* m_w = mw;
-  float* l_w = mw + kConsumerWarps * kMaxRep;
-  float* acc_w = mw + 2 * kConsumerWarps * kMaxRep;
+  float* l_w = mw + Cfg::NCW * kMaxRep;
+  float* acc_w = mw + 2 * Cfg::NCW * kMaxRep;
   if (tq == 0) {
     m_w[warp * kMaxRep + gr] = m_r[0];
     m_w[warp * kMaxRep + gr + 8] = m_r[1];
@@ -817,8 +824,8 @@ __device__ void run_consumer_mma(const SplitParams& p, const TableCache& tc, uin
       acc_w[(warp * kMaxRep + gr + 8) * D + col + 1] = o[n][3];
     }
   }
-  named_bar_sync(1, kConsumerWarps * 32);
-  merge_and_store<D, MODE>(p, mw, b, h, split);
+  named_bar_sync(1, Cfg::NCW * 32);
+  merge_and_store<D, MODE, Cfg::NCW>(p, mw, b, h, split);
 }
 
 // ------------------------------------------------------------------ CUDA-core consumer
@@ -870,7 +877,7 @@ __device__ void run_consumer_fma(const SplitParams& p, const TableCache& tc, uin
   }
   const int G = p.group_tokens;
 
-  for (int i = warp; i < ntiles; i += kConsumerWarps) {
+  for (int i = warp; i < ntiles; i += Cfg::NCW) {
     const int s = i % Cfg::STAGES;
     if (*abort_flag) break;
     uint32_t swm;
@@ -1014,11 +1021,11 @@ __device__ void run_consumer_fma(const SplitParams& p, const TableCache& tc, uin
 
 #pragma unroll
   for (int r = 0; r < kMaxRep; ++r) l_r[r] = warp_sum(l_r[r]);
-  named_bar_sync(1, kConsumerWarps * 32);
+  named_bar_sync(1, Cfg::NCW * 32);
   float* mw = reinterpret_cast<float*>(stages);
   float* m_w = mw;
-  float* l_w = mw + kConsumerWarps * kMaxRep;
-  float* acc_w = mw + 2 * kConsumerWarps * kMaxRep;
+  float* l_w = mw + Cfg::NCW * kMaxRep;
+  float* acc_w = mw + 2 * Cfg::NCW * kMaxRep;
   if (lane == 0) {
 #pragma unroll
     for (int r = 0; r < kMaxRep; ++r) {
@@ -1035,8 +1042,8 @@ __device__ void run_consumer_fma(const SplitParams& p, const TableCache& tc, uin
         if (d < D) acc_w[(warp * kMaxRep + r) * D + d] = acc[r][k];
       }
   }
-  named_bar_sync(1, kConsumerWarps * 32);
-  merge_and_store<D, MODE>(p, mw, b, h, split);
+  named_bar_sync(1, Cfg::NCW * 32);
+  merge_and_store<D, MODE, Cfg::NCW>(p, mw, b, h, split);
 }
 
 // ------------------------------------------------------------------ kernel
@@ -1054,7 +1061,8 @@ struct SplitSmem {
 };
 
 template <typename T, int D, int MODE, int BACKEND>
-__global__ void __launch_bounds__(kThreads, 1) split_kernel(const __grid_constant__ SplitParams p,
+__global__ void __launch_bounds__(TileCfg<T, D, MODE, BACKEND>::THREADS, TileCfg<T, D, MODE, BACKEND>::MIN_BLOCKS)
+    split_kernel(const __grid_constant__ SplitParams p,
                                                          const __grid_constant__ CUtensorMap mapk,
                                                          const __grid_constant__ CUtensorMap mapv) {
   using Cfg = TileCfg<T, D, MODE, BACKEND>;
@@ -1104,11 +1112,11 @@ __global__ void __launch_bounds__(kThreads, 1) split_kernel(const __grid_constan
     blk1 = min(blk1, g.nb);
     tc.blk0 = blk0;
     tc.n = max(0, min(blk1 - blk0, kTableCache));
-    for (int i = threadIdx.x; i < tc.n; i += kThreads) tbl[i] = p.block_table[(long long)b * p.max_blocks + blk0 + i];
+    for (int i = threadIdx.x; i < tc.n; i += Cfg::THREADS) tbl[i] = p.block_table[(long long)b * p.max_blocks + blk0 + i];
   }
-  if (warp < kConsumerWarps) {
+  if (warp < Cfg::NCW) {
     const long long qbase = ((long long)b * p.num_q_heads + (long long)h * p.n_rep) * D;
-    for (int idx = threadIdx.x; idx < kMaxRep * D; idx += kConsumerWarps * 32) {
+    for (int idx = threadIdx.x; idx < kMaxRep * D; idx += Cfg::NCW * 32) {
       const int r = idx / D;
       const float v = r < p.n_rep ? load_any(p.q, qbase + idx, p.q_dtype) : 0.f;
       if constexpr (BACKEND == BACKEND_FMA) {
@@ -1125,9 +1133,9 @@ __global__ void __launch_bounds__(kThreads, 1) split_kernel(const __grid_constan
   }
   __syncthreads();
 
-  if (warp >= kConsumerWarps) {
+  if (warp >= Cfg::NCW) {
     run_producer<Cfg, MODE>(p, tc, &mapk, &mapv, stages, full, empty, infos, b, h, tile0, ntiles, g, abort_flag,
-                            warp - kConsumerWarps);
+                            warp - Cfg::NCW);
   } else {
     if constexpr (BACKEND == BACKEND_MMA) {
       run_consumer_mma<T, D, MODE>(p, tc, stages, full, empty, infos, b, h, tile0, ntiles, g, abort_flag, split,
@@ -1142,6 +1150,7 @@ __global__ void __launch_bounds__(kThreads, 1) split_kernel(const __grid_constan
 // Host-side description of one instantiation.
 struct SplitKernelInfo {
   const void* fn;
+  int threads;
   int tile;
   int smem_bytes;
   int stages;
@@ -1155,6 +1164,7 @@ SplitKernelInfo split_kernel_info() {
   using L = SplitSmem<T, D, MODE, BACKEND>;
   SplitKernelInfo k;
   k.fn = reinterpret_cast<const void*>(&split_kernel<T, D, MODE, BACKEND>);
+  k.threads = Cfg::THREADS;
   k.tile = Cfg::TILE;
   k.smem_bytes = L::TOTAL;
   k.stages = Cfg::STAGES;

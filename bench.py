@@ -147,30 +147,25 @@ def measured_peaks():
 
 
 # ----------------------------------------------------------------------------- workload
-class Workload:
-    """Device pool, pinned host pool, block tables, tails and queries for one GPU's share."""
+class WorkloadLayout:
+    """Placement and byte accounting of one GPU's share (CPU only): tails, which blocks of each row
+    live in HBM or in the host pool, the block table, the attended range, the bytes per step.
+    Shared by the GPU workload and by the reference arm, which reports the same configuration."""
 
-    def __init__(self, name: str, device, seed: int):
+    def __init__(self, name: str, seed: int):
         import torch
-
-        from pager_hf import _lib
-        from pager_hf.host_pool import HostPool
 
         w = WORKLOADS[name]
         self.name, self.w = name, w
-        self.device = device
         self.L, self.Hq, self.Hkv, self.D, self.tpb = w["layers"], w["hq"], w["hkv"], w["d"], w["tpb"]
         self.B, self.ctx = w["batch"], w["context"]
-        self.dtype = {"bf16": torch.bfloat16, "f16": torch.float16}[w["dtype"]]
         elt = 2
         nb = self.ctx // self.tpb
         self.nb = nb
         self.slot_bytes = self.L * 2 * self.Hkv * self.tpb * self.D * elt
         g = torch.Generator(device="cpu").manual_seed(seed)
-        tails = torch.randint(1, self.tpb + 1, (self.B,), generator=g).tolist()
-        self.tails = tails
-        # residency per row: which block indices live in HBM
-        resident = []
+        self.tails = torch.randint(1, self.tpb + 1, (self.B,), generator=g).tolist()
+        resident = []  # per row: block indices that live in HBM
         if "hbm_budget_gb" in w:
             per_row = min(nb, int(w["hbm_budget_gb"] * 1e9 // self.slot_bytes) // self.B)
             for _ in range(self.B):
@@ -180,52 +175,36 @@ class Workload:
             sinks = min(w.get("sinks", 0), per_row)
             for _ in range(self.B):
                 resident.append(set(range(sinks)) | set(range(nb - (per_row - sinks), nb)))
-        dev_slots = sum(len(r) for r in resident)
-        host_slots = self.B * nb - dev_slots
-        shape = (self.L, 2, self.Hkv, self.tpb, self.D)
-        self.dev_pool = torch.empty((max(dev_slots, 1),) + shape, dtype=self.dtype, device=device)
-        self.dev_pool.normal_(generator=torch.Generator(device=device).manual_seed(seed + 1))
-        self.host = HostPool((max(host_slots, 1),) + shape, self.dtype) if host_slots else None
-        if self.host is not None:
-            self._fill_host(seed + 2)
+        self.dev_slots = sum(len(r) for r in resident)
+        self.host_slots = self.B * nb - self.dev_slots
+        host_bit = 0x40000000
         table = torch.full((self.B, nb), -1, dtype=torch.int32)
         d_next = h_next = 0
         self.dev_tokens = self.host_tokens = 0
         window = w.get("window")
-        lo = []
+        self.window = window
+        self.lo = []
         for b in range(self.B):
-            ntok = nb * self.tpb + tails[b]
+            ntok = nb * self.tpb + self.tails[b]
             row_lo = max(0, ntok - window) if window else 0
-            lo.append(row_lo)
+            self.lo.append(row_lo)
             for j in range(nb):
-                if j in resident[b]:
+                on_dev = j in resident[b]
+                if on_dev:
                     table[b, j] = d_next
                     d_next += 1
-                    where = "dev"
                 else:
-                    table[b, j] = h_next | _lib.HOST_SLOT_BIT
+                    table[b, j] = h_next | host_bit
                     h_next += 1
-                    where = "host"
                 # tokens of this block that the window keeps (all of them without a window)
                 t0, t1 = j * self.tpb, (j + 1) * self.tpb
                 n_valid = max(0, t1 - max(t0, row_lo))
-                if where == "dev":
+                if on_dev:
                     self.dev_tokens += n_valid
                 else:
                     self.host_tokens += n_valid
-        self.tail_tokens = sum(tails)
-        self.table = table.to(device)
-        self.num_blocks = torch.full((self.B,), nb, dtype=torch.int32, device=device)
-        self.tail_len = torch.tensor(tails, dtype=torch.int32, device=device)
-        self.valid_lo = torch.tensor(lo, dtype=torch.int32, device=device) if window else None
-        gd = torch.Generator(device=device).manual_seed(seed + 3)
-        self.tail_k = torch.randn(self.B, self.Hkv, self.tpb, self.D, generator=gd, device=device).to(self.dtype)
-        self.tail_v = torch.randn(self.B, self.Hkv, self.tpb, self.D, generator=gd, device=device).to(self.dtype)
-        self.q = torch.randn(self.L, self.B, self.Hq, self.D, generator=gd, device=device).to(self.dtype)
-        self.out = torch.empty_like(self.q)
-        self.mass = torch.zeros(self.B, nb, dtype=torch.float32, device=device)
-        self.max_row_tokens = nb * self.tpb + self.tpb
-        self.plan = None
+        self.table = table
+        self.tail_tokens = sum(self.tails)
         # algorithmic bytes per step (only attended tokens are counted)
         kv_tok = 2 * self.Hkv * self.D * elt
         qo = 2 * self.B * self.Hq * self.D * elt
@@ -234,6 +213,51 @@ class Workload:
         self.host_bytes = self.L * self.host_tokens * kv_tok
         self.bytes_per_step = self.hbm_bytes + self.host_bytes
         self.launches_per_step = self.L * 3  # split + combine + mass kernels per layer
+
+    def config(self, world: int, host_read: str) -> dict:
+        w = self.w
+        return {
+            "workload": self.name, "model": w["model"], "batch_per_gpu": self.B, "global_batch": self.B * world,
+            "context": self.ctx, "tokens_per_block": self.tpb, "layers": self.L,
+            "hbm_kv_gb": round(max(self.dev_slots, 1) * self.slot_bytes / 1e9, 2),
+            "host_pool_gb": round(self.host_slots * self.slot_bytes / 1e9, 2),
+            "hbm_bytes_per_step": self.hbm_bytes, "host_bytes_per_step": self.host_bytes,
+            "l2": "inputs larger than L2 (KV per step >> 126 MB), no flush",
+            "parallelism": f"request-sharded x{world}, no collectives on the data path",
+            "host_read": host_read,
+        }
+
+
+class Workload(WorkloadLayout):
+    """Device pool, pinned host pool, block tables, tails and queries for one GPU's share."""
+
+    def __init__(self, name: str, device, seed: int):
+        import torch
+
+        from pager_hf.host_pool import HostPool
+
+        super().__init__(name, seed)
+        self.device = device
+        self.dtype = {"bf16": torch.bfloat16, "f16": torch.float16}[self.w["dtype"]]
+        shape = (self.L, 2, self.Hkv, self.tpb, self.D)
+        self.dev_pool = torch.empty((max(self.dev_slots, 1),) + shape, dtype=self.dtype, device=device)
+        self.dev_pool.normal_(generator=torch.Generator(device=device).manual_seed(seed + 1))
+        self.host = HostPool((max(self.host_slots, 1),) + shape, self.dtype) if self.host_slots else None
+        if self.host is not None:
+            self._fill_host(seed + 2)
+        self.table = self.table.to(device)
+        nb = self.nb
+        self.num_blocks = torch.full((self.B,), nb, dtype=torch.int32, device=device)
+        self.tail_len = torch.tensor(self.tails, dtype=torch.int32, device=device)
+        self.valid_lo = torch.tensor(self.lo, dtype=torch.int32, device=device) if self.window else None
+        gd = torch.Generator(device=device).manual_seed(seed + 3)
+        self.tail_k = torch.randn(self.B, self.Hkv, self.tpb, self.D, generator=gd, device=device).to(self.dtype)
+        self.tail_v = torch.randn(self.B, self.Hkv, self.tpb, self.D, generator=gd, device=device).to(self.dtype)
+        self.q = torch.randn(self.L, self.B, self.Hq, self.D, generator=gd, device=device).to(self.dtype)
+        self.out = torch.empty_like(self.q)
+        self.mass = torch.zeros(self.B, nb, dtype=torch.float32, device=device)
+        self.max_row_tokens = nb * self.tpb + self.tpb
+        self.plan = None
 
     def _fill_host(self, seed):
         import torch
@@ -395,7 +419,7 @@ def run_reference_arm(args):
         "impl": "reference", "metric": METRIC, "value": gbs, "unit": "GB/s", "n_gpus": args.gpus, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": 1000 * tot_t / args.steps, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": w["dtype"], "data": "synthetic (seeded random KV)",
-        "config": {"workload": args.workload, "model": w["model"], "context": w["context"]},
+        "config": WorkloadLayout(args.workload, seed=1234).config(args.gpus, "n/a (CPU)"),
         "cpu_baseline": {"value": gbs, "unit": "GB/s", "cores": arm.procs, "kind": "port", "sample": sample_desc(arm)},
         "e2e": {"value": gbs, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "note": "reference path = the reference's Triton/torch algorithm restated on the CPU (oracle/); the "
@@ -506,16 +530,7 @@ def run_ours(args):
         "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": w["dtype"],
         "data": "synthetic: seeded random KV in the workload's geometry (no checkpoints offline)",
-        "config": {
-            "workload": args.workload, "model": w["model"], "batch_per_gpu": wl.B, "global_batch": wl.B * world,
-            "context": wl.ctx, "tokens_per_block": wl.tpb, "layers": wl.L,
-            "hbm_kv_gb": round(wl.dev_pool.numel() * 2 / 1e9, 2),
-            "host_pool_gb": round((wl.host.nbytes if wl.host else 0) / 1e9, 2),
-            "hbm_bytes_per_step": wl.hbm_bytes, "host_bytes_per_step": wl.host_bytes,
-            "l2": "inputs larger than L2 (KV per step >> 126 MB), no flush",
-            "parallelism": f"request-sharded x{world}, no collectives on the data path",
-            "host_read": wl.plan.host_read,
-        },
+        "config": wl.config(world, wl.plan.host_read),
         "decode_tokens_per_s": tokens_per_s,
         "roofline": {
             "bound": "hbm", "achieved": achieved, "peak": combined_peak, "unit": "GB/s",

@@ -44,7 +44,7 @@ METRIC = "decode-attn effective KV GB/s (HBM + host tiers) at 32k ctx"
 NCU_DRAM_PER_HBM_BYTE = (268.82 + 6.80) / 268.75
 
 WORKLOADS = {
-    # BASELINE config 5 geometry at 32k: 40 GB HBM budget, overflow in the pinned host pool
+    # the serving config's Llama-3-8B geometry at 32k: 40 GB HBM budget, overflow in the pinned host pool
     "cfg5-32k": dict(model="Llama-3-8B attention (L32, Hq32, Hkv8, D128)", layers=32, hq=32, hkv=8, d=128,
                      dtype="bf16", tpb=64, batch=12, context=32768, hbm_budget_gb=40.0, window=None),
     # same geometry, everything resident in HBM (8 x 4 GiB < 40 GB)
@@ -57,7 +57,7 @@ WORKLOADS = {
     # rest in the host pool (staged per layer by the copy engines when the link favours it)
     "prof-tiered": dict(model="Llama-3-8B attention (L4 slice, Hq32, Hkv8, D128)", layers=4, hq=32, hkv=8, d=128,
                         dtype="bf16", tpb=64, batch=2, context=32768, resident_frac=0.2, sinks=0, window=None),
-    # Mistral-7B, B8 x 32k, sliding window 4096, 5% resident (sinks + recent)
+    # the sliding-window config: Mistral-7B, B8 x 32k, window 4096, 5% resident (sinks + recent)
     "cfg4-32k-window": dict(model="Mistral-7B attention (L32, Hq32, Hkv8, D128, window 4096)", layers=32, hq=32,
                             hkv=8, d=128, dtype="bf16", tpb=64, batch=8, context=32768, resident_frac=0.05,
                             sinks=4, window=4096),

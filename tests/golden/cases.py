@@ -67,7 +67,7 @@ CASES = {
                         scale=224.0**-0.5, softcap=50.0),
     # tests/test_streaming_attention.py:275-293
     "ref_default_scale": dict(kind="steps", seed=7, B=1, Hq=14, Hkv=2, D=64, T=64, group=64, dtype="f16"),
-    # Qwen2.5-0.5B geometry, fp32, 4096 tokens in 64 blocks of 64, seed 0 (q, k, v)
+    # the CPU benchmark config: Qwen2.5-0.5B geometry, fp32, 4096 tokens in 64 blocks of 64, seed 0 (q, k, v)
     "cfg1_qwen05b_f32": dict(kind="two_pass", seed=0, B=1, Hq=14, Hkv=2, D=64, tpb=64, nb=64, tail=0,
                              group_blocks=64, dtype="f32", randn_order="qkv"),
     "cfg1_qwen05b_f32_onepass": dict(kind="steps", seed=0, B=1, Hq=14, Hkv=2, D=64, T=4096, group=4096,

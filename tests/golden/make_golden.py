@@ -1,7 +1,7 @@
 """Generate the golden parity fixtures from the reference's own kernels.
 
-Run in a container that has the reference checkout (its path is the only
-argument, default ``/root/reference``)::
+Run where the reference checkout is available (its root is the only,
+required, argument)::
 
     python tests/golden/make_golden.py /path/to/rust-llm-pager
 
@@ -135,7 +135,9 @@ def run_batched(sa, ref_tests, name, c):
 
 
 def main():
-    ref_root = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+    if len(sys.argv) != 2:
+        sys.exit("usage: python tests/golden/make_golden.py /path/to/rust-llm-pager")
+    ref_root = sys.argv[1]
     sa, ref_tests = _load_reference(ref_root)
     runners = {"steps": run_steps, "two_pass": run_two_pass, "batched": run_batched}
     for name, c in CASES.items():

@@ -150,7 +150,7 @@ def test_session_continues_across_generate_calls():
 
 
 def test_baseline_config2_geometry_greedy_parity():
-    """BASELINE config 2's architecture (random-init Qwen2.5-0.5B: 24 layers, hidden 896, 14/2 heads, D 64,
+    """The greedy-generation benchmark config's architecture (random-init Qwen2.5-0.5B: 24 layers, hidden 896, 14/2 heads, D 64,
     fp16), 8192-token prompt, 10% of blocks resident, recent_only; 32 new tokens (128 in the benchmark config)."""
     from pager_hf.paged_model import PagedModel
 

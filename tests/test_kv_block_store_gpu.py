@@ -224,3 +224,23 @@ def test_block_table_drives_the_decode_op_to_the_oracle(kvs, policy):
         np.testing.assert_allclose(out[b].float().cpu().numpy(), ref_out[0], rtol=0, atol=2e-3)
         np.testing.assert_allclose(mass[b].cpu().numpy(), ref_mass[0].mean(0), rtol=1e-4, atol=1e-6)
     store.close()
+
+
+def test_reference_kv_utils_round_trip_through_the_pool_store(kvs):
+    """kv_utils.real_past_to_blocks -> pool-backed store (through the host tier and back) ->
+    kv_utils.reconstruct_past_from_store gives the cache back exactly."""
+    from pager_hf.kv_utils import real_past_to_blocks, reconstruct_past_from_store, split_full_blocks_and_tail
+
+    g = torch.Generator().manual_seed(8)
+    past = [(torch.randn(2, 4, 70, 32, generator=g).half().cuda(), torch.randn(2, 4, 70, 32, generator=g).half().cuda())
+            for _ in range(3)]
+    full, tail, n = split_full_blocks_and_tail(past, tokens_per_block=16)
+    store = kvs.KVBlockStore(tokens_per_block=16, gpu_capacity_blocks=2, cpu_capacity_blocks=2)
+    for j, (k, v) in enumerate(real_past_to_blocks(full, tokens_per_block=16)):
+        store.put_gpu(j, k, v)
+    store.apply_tiers([1, 0, 1, 0], "cuda")
+    store.apply_tiers([0, 0, 0, 0], "cuda")
+    rec = reconstruct_past_from_store(store=store, num_layers=3, num_blocks=n // 16, tail_past=tail)
+    for layer in range(3):
+        assert torch.equal(rec[layer][0], past[layer][0]) and torch.equal(rec[layer][1], past[layer][1])
+    store.close()

@@ -51,7 +51,7 @@ def plan_host_runs(block_table: torch.Tensor, tokens_per_block: int | None = Non
     ``(src, dst, len)`` of maximal runs of consecutive host slots (one 2D copy
     each)."""
     t = block_table.to("cpu", torch.int32)
-    B, nb = t.shape
+    nb = t.shape[1]
     need = (t >= 0) & ((t & HOST_SLOT_BIT) != 0)
     cols = torch.arange(nb, dtype=torch.int64)[None, :]
     if num_blocks is not None:

@@ -201,7 +201,7 @@ def test_paged_op_options_match_the_reference(mods, case):
     s = build(seed, B, Hq, Hkv, D, tpb, L, nbs, tails, dtype)
     dt = {torch.float16: "f16", torch.bfloat16: "bf16", torch.float32: "f32"}[dtype]
     layer = L - 1
-    out, bm, accum = run_gpu(sa, HostPool, s, layer, **kw)
+    out, bm, _ = run_gpu(sa, HostPool, s, layer, **kw)
     atol = 5e-3 if dtype == torch.bfloat16 else 2e-3
     for b in range(B):
         ref_out, ref_mass = oracle_row(s, b, layer, dt, scale=kw.get("scale"), softcap=kw.get("softcap"))

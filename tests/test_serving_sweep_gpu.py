@@ -2,7 +2,6 @@
 host tier along the way, and every slot returns to the pools at the end."""
 
 import pytest
-import torch
 
 pytestmark = pytest.mark.gpu
 

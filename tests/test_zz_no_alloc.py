@@ -12,8 +12,6 @@ own in a fresh process and after the other tests (the array keeps whatever the
 previous call left in it; nothing in it needs to start at zero).
 """
 
-import ctypes
-
 import numpy as np
 import pytest
 import torch

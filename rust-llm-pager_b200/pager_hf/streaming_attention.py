@@ -14,7 +14,6 @@ and raises if the native library is missing.
 
 from __future__ import annotations
 
-
 import torch
 
 from . import _lib as L

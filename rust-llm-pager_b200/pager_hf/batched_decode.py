@@ -211,3 +211,70 @@ class BatchedDecodeAttention:
         return result
 
 
+
+
+@torch.inference_mode()
+def batched_decode_step(sessions: list, next_input_ids: list[int], device) -> list[torch.Tensor]:
+    """Advance single-row ``PagedModel`` sessions by one token each in one model forward
+    (``batched_decode.py:32-348``); returns each session's last-position logits in order.
+
+    The sessions must share one model, ``tokens_per_block`` and one ``KVPools`` (``PagedModel(...,
+    pools=shared)``), and each must have an active session (a ``generate`` call made).  One fused
+    paged launch per layer covers every session: rows of different lengths, tails of different
+    lengths and per-row sliding windows are fine (the reference requires equal tails and rejects
+    windows, ``:80-108``).  Afterwards each session gets the reference's post-step calls
+    (``:320-338``) on its own pager and store, through ``PagedModel._finish_token``.
+    """
+    from .paged_model import run_decoder_step
+
+    if not sessions:
+        return []
+    first = sessions[0]
+    model, pools, tpb = first.model, first.shared_pools, first.tokens_per_block
+    if pools is None:
+        raise ValueError("batched_decode_step requires sessions created with PagedModel(..., pools=shared_pools).")
+    for s in sessions:
+        if s.model is not model:
+            raise ValueError("batched_decode_step requires every session to share the same underlying model.")
+        if s._store is None:
+            raise ValueError("batched_decode_step requires every session to already have an active generate() session.")
+        if s.shared_pools is not pools:
+            raise ValueError("batched_decode_step requires every session to share the same KVPools.")
+        if s.tokens_per_block != tpb:
+            raise ValueError("batched_decode_step requires every session to share the same tokens_per_block.")
+    if len(next_input_ids) != len(sessions):
+        raise ValueError("one next input id per session")
+    device = torch.device(device)
+    a = first._arch()
+    S = len(sessions)
+    width = max(s._num_blocks for s in sessions) + 1
+    table = torch.full((S, width), -1, dtype=torch.int32)
+    lo, hi, slots, positions, pos_ids = [], [], [], [], []
+    for r, s in enumerate(sessions):
+        nb = s._num_blocks
+        if nb:
+            table[r, :nb] = s._store.block_table(range(nb), device="cpu")[0]
+        table[r, nb] = s._tail_group  # single-row groups: the group is the slot
+        total = s._total + 1  # columns including this step's token
+        pad = int(s._pad[0])
+        lo.append(max(pad, total - int(a["window"])) if a["window"] is not None else pad)
+        hi.append(total)
+        slots.append(s._tail_group)
+        positions.append(s._tail_len)
+        pos_ids.append(total - 1 - pad)  # RoPE position of the new token
+    i32 = dict(dtype=torch.int32, device=device)
+    needs = any(s._needs_attention for s in sessions)
+    mass = torch.zeros(S, width, dtype=torch.float32, device=device) if needs else None
+    plan = PagedDecodePlan(
+        batch=S, num_query_heads=a["hq"], dev_pool=pools.dev_pool, host_pool=pools.host_pool.tensor,
+        num_layers=a["layers"], tokens_per_block=tpb, block_table=table.to(device),
+        num_blocks=torch.tensor([s._num_blocks + 1 for s in sessions], **i32), max_row_tokens=width * tpb,
+        valid_lo=torch.tensor(lo, **i32) if any(lo) else None, valid_hi=torch.tensor(hi, **i32),
+        scale=a["scale"], mass_accum=mass, mass_mode="row_mean" if needs else "none", host_read=first.host_read)
+    input_ids = torch.tensor(next_input_ids, dtype=torch.long, device=device)[:, None]
+    position_ids = torch.tensor(pos_ids, dtype=torch.long, device=device)[:, None]
+    logits = run_decoder_step(model, a, pools, plan, input_ids, position_ids, torch.tensor(slots, **i32),
+                              torch.tensor(positions, **i32))
+    for r, s in enumerate(sessions):
+        s._finish_token(mass[r, :s._num_blocks] if (mass is not None and s._needs_attention) else None)
+    return [logits[r, -1, :] for r in range(S)]

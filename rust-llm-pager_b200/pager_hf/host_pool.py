@@ -28,11 +28,12 @@ class HostPool:
         ptr = ctypes.c_void_p()
         L.check(L.lib().pager_host_pool_alloc(self.nbytes, ctypes.byref(ptr)))
         self._ptr = ptr.value
-        if self.nbytes:
-            raw = (ctypes.c_uint8 * self.nbytes).from_address(self._ptr)
-            self.tensor = torch.frombuffer(raw, dtype=torch.uint8).view(dtype).view(self.shape)
-        else:
-            self.tensor = torch.empty(self.shape, dtype=dtype)
+        with torch.inference_mode(False):  # an ordinary tensor, updatable in and out of inference mode
+            if self.nbytes:
+                raw = (ctypes.c_uint8 * self.nbytes).from_address(self._ptr)
+                self.tensor = torch.frombuffer(raw, dtype=torch.uint8).view(dtype).view(self.shape)
+            else:
+                self.tensor = torch.empty(self.shape, dtype=dtype)
         self._raw_ref = self.tensor
 
     @property

@@ -157,9 +157,13 @@ class KVPools:
     def slot_shape(self):
         return (self.num_layers, 2, self.kv_heads, self.tokens_per_block, self.head_dim)
 
+    # Pool tensors are always created with inference mode off, so that code inside and outside
+    # torch.inference_mode (generate() and a caller's own loop) can both update them in place.
     def _alloc(self, gpu_groups: int, cpu_groups: int, rows: int) -> None:
-        self.dev_pool = torch.empty((gpu_groups * rows,) + self.slot_shape(), dtype=self.dtype, device=self.device)
-        self.host_pool = HostPool((cpu_groups * rows,) + self.slot_shape(), self.dtype)
+        with torch.inference_mode(False):
+            self.dev_pool = torch.empty((gpu_groups * rows,) + self.slot_shape(), dtype=self.dtype,
+                                        device=self.device)
+            self.host_pool = HostPool((cpu_groups * rows,) + self.slot_shape(), self.dtype)
         self.dev_groups = SlotGroups(gpu_groups)
         self.host_groups = SlotGroups(cpu_groups)
         self.rows_per_group = rows
@@ -184,16 +188,19 @@ class KVPools:
 
     def grow_dev(self, groups: int) -> None:
         self.copy_stream.synchronize()
-        new = torch.empty((groups * self.rows_per_group,) + self.slot_shape(), dtype=self.dtype, device=self.device)
-        new[: self.dev_pool.shape[0]].copy_(self.dev_pool)
+        with torch.inference_mode(False):
+            new = torch.empty((groups * self.rows_per_group,) + self.slot_shape(), dtype=self.dtype,
+                              device=self.device)
+            new[: self.dev_pool.shape[0]].copy_(self.dev_pool)
         self.dev_pool = new
         self.dev_groups.grow(groups)
         self.version += 1
 
     def grow_host(self, groups: int) -> None:
         self.copy_stream.synchronize()
-        new = HostPool((groups * self.rows_per_group,) + self.slot_shape(), self.dtype)
-        new.tensor[: self.host_pool.shape[0]].copy_(self.host_pool.tensor)
+        with torch.inference_mode(False):
+            new = HostPool((groups * self.rows_per_group,) + self.slot_shape(), self.dtype)
+            new.tensor[: self.host_pool.shape[0]].copy_(self.host_pool.tensor)
         self.host_pool.close()
         self.host_pool = new
         self.host_groups.grow(groups)
@@ -545,8 +552,9 @@ class KVBlockStore:
         if n == B:
             new_dev, new_host = old_dev, old_host
         else:
-            new_dev = torch.empty((p.dev_groups.capacity * n,) + p.slot_shape(), dtype=p.dtype, device=p.device)
-            new_host = HostPool((p.host_groups.capacity * n,) + p.slot_shape(), p.dtype)
+            with torch.inference_mode(False):
+                new_dev = torch.empty((p.dev_groups.capacity * n,) + p.slot_shape(), dtype=p.dtype, device=p.device)
+                new_host = HostPool((p.host_groups.capacity * n,) + p.slot_shape(), p.dtype)
         for groups, old, new, dev in ((self._dev_group, old_dev, new_dev, True),
                                       (self._host_group, old_host.tensor, new_host.tensor, False)):
             if not groups:

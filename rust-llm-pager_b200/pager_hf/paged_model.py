@@ -67,6 +67,42 @@ def _rope_fn(model):
     return mod.apply_rotary_pos_emb
 
 
+def run_decoder_step(model, arch: dict, pools: KVPools, plan: PagedDecodePlan, input_ids, position_ids, slots,
+                     positions):
+    """One token per row through the decoder: embeddings, then per layer the input norm, q/k/v
+    projections and RoPE from the model, the new K/V written into each row's tail slot
+    (``pager_append_tokens``: row r at token ``positions[r]`` of slot ``slots[r]``), the fused paged
+    attention of ``plan``, o_proj, the residual, the MLP; final norm and lm_head.  Returns logits
+    ``[rows, 1, vocab]``."""
+    B = input_ids.shape[0]
+    a = arch
+    rope = _rope_fn(model)
+    hidden = model.model.embed_tokens(input_ids)
+    cos, sin = model.model.rotary_emb(hidden, position_ids)
+    lib = L.lib()
+    dev = input_ids.device
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    out = torch.empty(B, a["hq"], a["d"], dtype=hidden.dtype, device=dev)
+    for li, layer in enumerate(model.model.layers):
+        residual = hidden
+        h = layer.input_layernorm(hidden)
+        attn = layer.self_attn
+        q = attn.q_proj(h).view(B, 1, -1, a["d"]).transpose(1, 2)
+        k = attn.k_proj(h).view(B, 1, -1, a["d"]).transpose(1, 2)
+        v = attn.v_proj(h).view(B, 1, -1, a["d"]).transpose(1, 2)
+        q, k = rope(q, k, cos, sin)
+        kn = k[:, :, 0].contiguous()
+        vn = v[:, :, 0].contiguous()
+        L.check(lib.pager_append_tokens(pools.dev_pool.data_ptr(), L.DTYPE_CODE[pools.dtype], pools.dev_pool.shape[0],
+                                        a["layers"], li, a["hkv"], pools.tokens_per_block, a["d"], slots.data_ptr(),
+                                        positions.data_ptr(), kn.data_ptr(), vn.data_ptr(), B, stream))
+        plan.run(q[:, :, 0].contiguous(), li, out)
+        hidden = residual + attn.o_proj(out.reshape(B, 1, -1))
+        residual = hidden
+        hidden = residual + layer.mlp(layer.post_attention_layernorm(hidden))
+    return model.lm_head(model.model.norm(hidden))
+
+
 class PagedModel:
     """A HuggingFace causal LM whose KV cache lives in paged device / host pools."""
 
@@ -74,7 +110,7 @@ class PagedModel:
                  rebalance_interval: int = 4, promote_margin: float = 0.05, ram_promote_margin: float = 0.20,
                  policy: str = "sinks_heavy_hitter", tokens_per_block: int = 16, prefill_chunk_tokens: int = 512,
                  use_streaming_attention: bool = True, streaming_group_size_blocks: int = 64,
-                 host_read: str = "auto"):
+                 host_read: str = "auto", pools: KVPools | None = None):
         if not use_streaming_attention:
             raise NotImplementedError("only the streaming (fused paged) attention path is implemented")
         self.model = model
@@ -83,6 +119,11 @@ class PagedModel:
         self.use_streaming_attention = True
         self.streaming_group_size_blocks = streaming_group_size_blocks  # kept for API parity; one launch per layer
         self.host_read = host_read
+        # pools shared with other single-row sessions (``batched_decode_step`` decodes them in one
+        # launch); None: the session allocates its own
+        if pools is not None and (pools.rows_per_group != 1 or pools.tokens_per_block != tokens_per_block):
+            raise ValueError("shared pools must hold single-row blocks of tokens_per_block tokens")
+        self.shared_pools = pools
         self._needs_attention = policy not in _POLICIES_WITHOUT_ATTENTION_SIGNAL
         self._ram_budget = ram_budget
         self._pager_kwargs = dict(vram=vram_budget, ram=ram_budget, recent=recent_window,
@@ -127,7 +168,10 @@ class PagedModel:
     def _release_pools(self):
         if self._store is not None:
             self._store.close()
-        if self._pools is not None:
+        if self._pools is not None and self._pools is self.shared_pools:
+            if self._tail_group is not None:
+                self._pools.dev_groups.give(self._tail_group)
+        elif self._pools is not None:
             self._pools.close()
 
     # ------------------------------------------------------------------ helpers
@@ -195,9 +239,14 @@ class PagedModel:
         n = prefix.shape[1]
         nfull = n // tpb
         budget_blocks = max(1, self._pager_kwargs["vram"] // (16 * 1024 * 1024))
-        self._pools = KVPools(num_layers=a["layers"], kv_heads=a["hkv"], head_dim=a["d"], tokens_per_block=tpb,
-                              dtype=dtype, device=dev, rows_per_group=B, gpu_groups=max(nfull + 2, 2),
-                              cpu_groups=max(4, nfull - min(nfull, budget_blocks) + 2))
+        if self.shared_pools is not None:
+            if B != 1:
+                raise ValueError("a session on shared pools is single-row")
+            self._pools = self.shared_pools
+        else:
+            self._pools = KVPools(num_layers=a["layers"], kv_heads=a["hkv"], head_dim=a["d"], tokens_per_block=tpb,
+                                  dtype=dtype, device=dev, rows_per_group=B, gpu_groups=max(nfull + 2, 2),
+                                  cpu_groups=max(4, nfull - min(nfull, budget_blocks) + 2))
         self._store = KVBlockStore(tpb, self._ram_budget, pools=self._pools)
         keys = [layer.keys for layer in cache.layers]
         values = [layer.values for layer in cache.layers]
@@ -236,7 +285,6 @@ class PagedModel:
     def _forward_step(self, input_ids: torch.Tensor, attention_mask: torch.Tensor):
         """One token per row through the model with paged attention; then blocks, pager, tiers."""
         a = self._arch()
-        m = self.model
         B = input_ids.shape[0]
         dev = input_ids.device
         p = self._pools
@@ -263,45 +311,30 @@ class PagedModel:
         slots = torch.arange(self._tail_group * B, self._tail_group * B + B, **i32)
         positions = torch.full((B,), self._tail_len, **i32)
         position_ids = self._position_ids_from_mask(attention_mask)[:, -1:]
-        rope = _rope_fn(m)
-        hidden = m.model.embed_tokens(input_ids)
-        cos, sin = m.model.rotary_emb(hidden, position_ids)
-        lib = L.lib()
-        stream = torch.cuda.current_stream(dev).cuda_stream
-        out = torch.empty(B, a["hq"], a["d"], dtype=hidden.dtype, device=dev)
-        for li, layer in enumerate(m.model.layers):
-            residual = hidden
-            h = layer.input_layernorm(hidden)
-            attn = layer.self_attn
-            q = attn.q_proj(h).view(B, 1, -1, a["d"]).transpose(1, 2)
-            k = attn.k_proj(h).view(B, 1, -1, a["d"]).transpose(1, 2)
-            v = attn.v_proj(h).view(B, 1, -1, a["d"]).transpose(1, 2)
-            q, k = rope(q, k, cos, sin)
-            kn = k[:, :, 0].contiguous()
-            vn = v[:, :, 0].contiguous()
-            L.check(lib.pager_append_tokens(p.dev_pool.data_ptr(), L.DTYPE_CODE[p.dtype], p.dev_pool.shape[0],
-                                            a["layers"], li, a["hkv"], tpb, a["d"], slots.data_ptr(),
-                                            positions.data_ptr(), kn.data_ptr(), vn.data_ptr(), B, stream))
-            plan.run(q[:, :, 0].contiguous(), li, out)
-            hidden = residual + attn.o_proj(out.reshape(B, 1, -1))
-            residual = hidden
-            hidden = residual + layer.mlp(layer.post_attention_layernorm(hidden))
-        logits = m.lm_head(m.model.norm(hidden))
-        # --- bookkeeping (paged_model.py:1210-1233, :785-798)
-        self._total = total
+        logits = run_decoder_step(self.model, a, p, plan, input_ids, position_ids, slots, positions)
+        return logits, self._finish_token(None if mass is None else mass[:nb])
+
+    def _finish_token(self, mass_row):
+        """After a decoded token (``paged_model.py:1210-1233, :785-798``): roll a full tail into a block
+        (adopted in place), hand the step's block attention to the pager, move blocks to its tiers.
+        ``mass_row``: this session's accumulated block mass over the layers (device tensor) or None."""
+        p = self._pools
+        dev = p.device
+        nb = self._num_blocks
+        self._total += 1
         self._tail_len += 1
         added = []
-        if self._tail_len == tpb:
+        if self._tail_len == self.tokens_per_block:
             self._store.adopt_gpu_group(nb, self._tail_group)
             added.append(nb)
             self._num_blocks = nb + 1
             self._tail_group = p.take_dev_group()
             self._tail_len = 0
-        self._mass_accum = mass[:nb].cpu() if mass is not None else None
+        self._mass_accum = mass_row.cpu() if mass_row is not None else None
         step = {"new_blocks": len(added), "gpu_to_cpu_mb": 0.0, "cpu_to_gpu_mb": 0.0, "gpu_to_cpu_copies": 0,
                 "cpu_to_gpu_copies": 0, "attention_in_gpu": 0.0}
         if self._num_blocks == 0:
-            return logits, step
+            return step
         block_attention = (self._block_attention() if self._needs_attention
                            else [1.0 / self._num_blocks] * self._num_blocks)
         before = self._store.summary()
@@ -317,7 +350,7 @@ class PagedModel:
                     cpu_to_gpu_copies=after["cpu_to_gpu_copies"] - before["cpu_to_gpu_copies"],
                     attention_in_gpu=sum(block_attention[i] for i in self._store.gpu_block_ids()
                                          if i < len(block_attention)))
-        return logits, step
+        return step
 
     def _extend_session(self, input_ids, attention_mask):
         total_len = input_ids.shape[-1]

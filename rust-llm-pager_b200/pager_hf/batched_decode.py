@@ -211,6 +211,57 @@ class BatchedDecodeAttention:
         return result
 
 
+def _validate_sessions(sessions: list, next_input_ids: list[int]) -> None:
+    """The reference's checks (``batched_decode.py:72-108``) that still apply; all run before any device
+    work.  Lifted: equal tail lengths, equal ``streaming_group_size_blocks`` (one launch per layer
+    covers any number of blocks), one kind of policy, sliding-window models."""
+    first = sessions[0]
+    for s in sessions:
+        if s.model is not first.model:
+            raise ValueError("batched_decode_step requires every session to share the same underlying model.")
+        if not s.use_streaming_attention:
+            raise ValueError("batched_decode_step only supports use_streaming_attention=True sessions.")
+        if s._store is None:
+            raise ValueError("batched_decode_step requires every session to already have an active generate() session.")
+        if s.tokens_per_block != first.tokens_per_block:
+            raise ValueError("batched_decode_step requires every session to share the same tokens_per_block.")
+        if s._pad is None or s._pad.shape[0] != 1:
+            raise ValueError("batched_decode_step only supports single-row (batch_size==1) sessions.")
+    if len({id(s) for s in sessions}) != len(sessions):
+        raise ValueError("batched_decode_step got the same session twice.")
+    if len(next_input_ids) != len(sessions):
+        raise ValueError("batched_decode_step needs one next input id per session.")
+
+
+def _group_plan(group: list, arch: dict, pools: KVPools, device: torch.device):
+    """The fused op's plan for single-row sessions that share ``pools``: one block-table row per
+    session (its blocks on either tier, then its tail slot), per-row valid ranges (left padding,
+    sliding window), and the per-row block-mass output when any session scores blocks."""
+    S, tpb = len(group), pools.tokens_per_block
+    width = max(s._num_blocks for s in group) + 1
+    table = torch.full((S, width), -1, dtype=torch.int32)
+    lo, hi, slots, positions = [], [], [], []
+    for r, s in enumerate(group):
+        nb = s._num_blocks
+        if nb:
+            table[r, :nb] = s._store.block_table(range(nb), device="cpu")[0]
+        table[r, nb] = s._tail_group  # single-row groups: the group is the slot
+        total = s._total + 1  # columns including this step's token
+        pad = int(s._pad[0])
+        lo.append(max(pad, total - int(arch["window"])) if arch["window"] is not None else pad)
+        hi.append(total)
+        slots.append(s._tail_group)
+        positions.append(s._tail_len)
+    i32 = dict(dtype=torch.int32, device=device)
+    needs = any(s._needs_attention for s in group)
+    mass = torch.zeros(S, width, dtype=torch.float32, device=device) if needs else None
+    plan = PagedDecodePlan(
+        batch=S, num_query_heads=arch["hq"], dev_pool=pools.dev_pool, host_pool=pools.host_pool.tensor,
+        num_layers=arch["layers"], tokens_per_block=tpb, block_table=table.to(device),
+        num_blocks=torch.tensor([s._num_blocks + 1 for s in group], **i32), max_row_tokens=width * tpb,
+        valid_lo=torch.tensor(lo, **i32) if any(lo) else None, valid_hi=torch.tensor(hi, **i32),
+        scale=arch["scale"], mass_accum=mass, mass_mode="row_mean" if needs else "none", host_read=group[0].host_read)
+    return plan, mass, torch.tensor(slots, **i32), torch.tensor(positions, **i32)
 
 
 @torch.inference_mode()
@@ -218,63 +269,47 @@ def batched_decode_step(sessions: list, next_input_ids: list[int], device) -> li
     """Advance single-row ``PagedModel`` sessions by one token each in one model forward
     (``batched_decode.py:32-348``); returns each session's last-position logits in order.
 
-    The sessions must share one model, ``tokens_per_block`` and one ``KVPools`` (``PagedModel(...,
-    pools=shared)``), and each must have an active session (a ``generate`` call made).  One fused
-    paged launch per layer covers every session: rows of different lengths, tails of different
-    lengths and per-row sliding windows are fine (the reference requires equal tails and rejects
-    windows, ``:80-108``).  Afterwards each session gets the reference's post-step calls
-    (``:320-338``) on its own pager and store, through ``PagedModel._finish_token``.
+    The sessions must share one model and ``tokens_per_block`` and each must have an active session
+    (a ``generate`` call made).  Projections, RoPE, MLP and logits run once over all rows.  Attention
+    runs as one fused paged launch per layer for each set of sessions that share a ``KVPools``: one
+    launch for sessions created with ``PagedModel(..., pools=shared)``, one per session for sessions
+    that allocated their own pools (as the reference's serving scheduler creates them).  Rows of
+    different lengths, tails of different lengths, per-row sliding windows and mixed policies are
+    fine (the reference requires equal tails and one kind of policy and rejects windows, ``:80-108``).
+    Afterwards each session gets the reference's post-step calls (``:320-338``) on its own pager and
+    store, through ``PagedModel._finish_token``, and its primed prefix grows by the token fed, so a
+    later ``generate`` call on it continues from here.
     """
-    from .paged_model import run_decoder_step
+    from .paged_model import AttentionGroup, run_decoder_step
 
     if not sessions:
         return []
-    first = sessions[0]
-    model, pools, tpb = first.model, first.shared_pools, first.tokens_per_block
-    if pools is None:
-        raise ValueError("batched_decode_step requires sessions created with PagedModel(..., pools=shared_pools).")
-    for s in sessions:
-        if s.model is not model:
-            raise ValueError("batched_decode_step requires every session to share the same underlying model.")
-        if s._store is None:
-            raise ValueError("batched_decode_step requires every session to already have an active generate() session.")
-        if s.shared_pools is not pools:
-            raise ValueError("batched_decode_step requires every session to share the same KVPools.")
-        if s.tokens_per_block != tpb:
-            raise ValueError("batched_decode_step requires every session to share the same tokens_per_block.")
-    if len(next_input_ids) != len(sessions):
-        raise ValueError("one next input id per session")
+    _validate_sessions(sessions, next_input_ids)
     device = torch.device(device)
+    if device.type == "cuda" and device.index is None:
+        device = torch.device("cuda", torch.cuda.current_device())
+    by_pools: dict[int, list[int]] = {}
+    for r, s in enumerate(sessions):
+        if s._pools.device != device:
+            raise ValueError(f"batched_decode_step: a session's KV lives on {s._pools.device}, not on {device}.")
+        by_pools.setdefault(id(s._pools), []).append(r)
+    first = sessions[0]
     a = first._arch()
     S = len(sessions)
-    width = max(s._num_blocks for s in sessions) + 1
-    table = torch.full((S, width), -1, dtype=torch.int32)
-    lo, hi, slots, positions, pos_ids = [], [], [], [], []
-    for r, s in enumerate(sessions):
-        nb = s._num_blocks
-        if nb:
-            table[r, :nb] = s._store.block_table(range(nb), device="cpu")[0]
-        table[r, nb] = s._tail_group  # single-row groups: the group is the slot
-        total = s._total + 1  # columns including this step's token
-        pad = int(s._pad[0])
-        lo.append(max(pad, total - int(a["window"])) if a["window"] is not None else pad)
-        hi.append(total)
-        slots.append(s._tail_group)
-        positions.append(s._tail_len)
-        pos_ids.append(total - 1 - pad)  # RoPE position of the new token
-    i32 = dict(dtype=torch.int32, device=device)
-    needs = any(s._needs_attention for s in sessions)
-    mass = torch.zeros(S, width, dtype=torch.float32, device=device) if needs else None
-    plan = PagedDecodePlan(
-        batch=S, num_query_heads=a["hq"], dev_pool=pools.dev_pool, host_pool=pools.host_pool.tensor,
-        num_layers=a["layers"], tokens_per_block=tpb, block_table=table.to(device),
-        num_blocks=torch.tensor([s._num_blocks + 1 for s in sessions], **i32), max_row_tokens=width * tpb,
-        valid_lo=torch.tensor(lo, **i32) if any(lo) else None, valid_hi=torch.tensor(hi, **i32),
-        scale=a["scale"], mass_accum=mass, mass_mode="row_mean" if needs else "none", host_read=first.host_read)
+    groups, masses = [], []
+    for rows in by_pools.values():
+        members = [sessions[r] for r in rows]
+        plan, mass, slots, positions = _group_plan(members, a, members[0]._pools, device)
+        index = None if len(by_pools) == 1 else torch.tensor(rows, dtype=torch.long, device=device)
+        groups.append(AttentionGroup(members[0]._pools, plan, slots, positions, index))
+        masses.append((rows, mass))
+    pos_ids = [s._total - int(s._pad[0]) for s in sessions]  # RoPE position of the new token
     input_ids = torch.tensor(next_input_ids, dtype=torch.long, device=device)[:, None]
     position_ids = torch.tensor(pos_ids, dtype=torch.long, device=device)[:, None]
-    logits = run_decoder_step(model, a, pools, plan, input_ids, position_ids, torch.tensor(slots, **i32),
-                              torch.tensor(positions, **i32))
-    for r, s in enumerate(sessions):
-        s._finish_token(mass[r, :s._num_blocks] if (mass is not None and s._needs_attention) else None)
+    logits = run_decoder_step(first.model, a, groups, input_ids, position_ids)
+    for rows, mass in masses:
+        for i, r in enumerate(rows):
+            s = sessions[r]
+            s._finish_token(mass[i, :s._num_blocks] if (mass is not None and s._needs_attention) else None)
+            s._note_fed_token(int(next_input_ids[r]))
     return [logits[r, -1, :] for r in range(S)]

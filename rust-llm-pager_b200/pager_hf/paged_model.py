@@ -67,13 +67,25 @@ def _rope_fn(model):
     return mod.apply_rotary_pos_emb
 
 
-def run_decoder_step(model, arch: dict, pools: KVPools, plan: PagedDecodePlan, input_ids, position_ids, slots,
-                     positions):
+@dataclass
+class AttentionGroup:
+    """Rows of a decode batch whose KV lives in one ``KVPools``: the fused op's plan over them, each
+    row's tail slot and the token index in it that the row's new K/V goes to.  ``rows``: the rows'
+    indices in the batch (device int64), or None for every row of the batch in order."""
+
+    pools: KVPools
+    plan: PagedDecodePlan
+    slots: torch.Tensor
+    positions: torch.Tensor
+    rows: torch.Tensor | None = None
+
+
+def run_decoder_step(model, arch: dict, groups: list[AttentionGroup], input_ids, position_ids):
     """One token per row through the decoder: embeddings, then per layer the input norm, q/k/v
-    projections and RoPE from the model, the new K/V written into each row's tail slot
-    (``pager_append_tokens``: row r at token ``positions[r]`` of slot ``slots[r]``), the fused paged
-    attention of ``plan``, o_proj, the residual, the MLP; final norm and lm_head.  Returns logits
-    ``[rows, 1, vocab]``."""
+    projections and RoPE from the model for all rows at once; per group of rows sharing pools, the
+    new K/V written into each row's tail slot (``pager_append_tokens``) and one fused paged attention
+    launch of the group's plan; o_proj, the residual and the MLP for all rows; final norm and lm_head.
+    Returns logits ``[rows, 1, vocab]``."""
     B = input_ids.shape[0]
     a = arch
     rope = _rope_fn(model)
@@ -83,6 +95,8 @@ def run_decoder_step(model, arch: dict, pools: KVPools, plan: PagedDecodePlan, i
     dev = input_ids.device
     stream = torch.cuda.current_stream(dev).cuda_stream
     out = torch.empty(B, a["hq"], a["d"], dtype=hidden.dtype, device=dev)
+    parts = [out if g.rows is None else torch.empty(g.rows.numel(), a["hq"], a["d"], dtype=hidden.dtype, device=dev)
+             for g in groups]
     for li, layer in enumerate(model.model.layers):
         residual = hidden
         h = layer.input_layernorm(hidden)
@@ -91,12 +105,20 @@ def run_decoder_step(model, arch: dict, pools: KVPools, plan: PagedDecodePlan, i
         k = attn.k_proj(h).view(B, 1, -1, a["d"]).transpose(1, 2)
         v = attn.v_proj(h).view(B, 1, -1, a["d"]).transpose(1, 2)
         q, k = rope(q, k, cos, sin)
-        kn = k[:, :, 0].contiguous()
-        vn = v[:, :, 0].contiguous()
-        L.check(lib.pager_append_tokens(pools.dev_pool.data_ptr(), L.DTYPE_CODE[pools.dtype], pools.dev_pool.shape[0],
-                                        a["layers"], li, a["hkv"], pools.tokens_per_block, a["d"], slots.data_ptr(),
-                                        positions.data_ptr(), kn.data_ptr(), vn.data_ptr(), B, stream))
-        plan.run(q[:, :, 0].contiguous(), li, out)
+        q, k, v = q[:, :, 0], k[:, :, 0], v[:, :, 0]
+        for g, part in zip(groups, parts):
+            if g.rows is None:
+                gq, gk, gv = q.contiguous(), k.contiguous(), v.contiguous()
+            else:
+                gq, gk, gv = q.index_select(0, g.rows), k.index_select(0, g.rows), v.index_select(0, g.rows)
+            p = g.pools
+            L.check(lib.pager_append_tokens(p.dev_pool.data_ptr(), L.DTYPE_CODE[p.dtype], p.dev_pool.shape[0],
+                                            a["layers"], li, a["hkv"], p.tokens_per_block, a["d"],
+                                            g.slots.data_ptr(), g.positions.data_ptr(), gk.data_ptr(), gv.data_ptr(),
+                                            gk.shape[0], stream))
+            g.plan.run(gq, li, part)
+            if g.rows is not None:
+                out.index_copy_(0, g.rows, part)
         hidden = residual + attn.o_proj(out.reshape(B, 1, -1))
         residual = hidden
         hidden = residual + layer.mlp(layer.post_attention_layernorm(hidden))
@@ -147,6 +169,27 @@ class PagedModel:
         self._mass_accum = None
         self._primed_tokens = 0
         self._primed_prefix = None
+
+    @property
+    def _tail_past(self):
+        """The tail (tokens after the last full block) per layer as ``(key, value)`` views
+        ``[rows, kv_heads, tail_len, head_dim]`` of the session's tail slots: the layout of the
+        reference's ``_tail_past`` (``paged_model.py:638-641``), which its serving scheduler groups
+        sessions by (``serving/scheduler.py:486``).  None without an active session."""
+        if self._store is None:
+            return None
+        p = self._pools
+        tail = p.dev_pool[p.group_slots(self._tail_group)]
+        n = self._tail_len
+        return [(tail[:, layer, 0, :, :n], tail[:, layer, 1, :, :n]) for layer in range(p.num_layers)]
+
+    def _note_fed_token(self, token_id: int) -> None:
+        """A token decoded outside ``generate`` (``batched_decode_step``) is now part of the session:
+        extend the primed prefix so a later ``generate`` call continues after it instead of feeding
+        it again."""
+        tok = torch.tensor([[token_id]], dtype=self._primed_prefix.dtype)
+        self._primed_prefix = torch.cat([self._primed_prefix, tok], dim=1)
+        self._primed_tokens += 1
 
     def _acquire_or_raise(self) -> None:
         if not self._lock.acquire(blocking=False):
@@ -311,7 +354,7 @@ class PagedModel:
         slots = torch.arange(self._tail_group * B, self._tail_group * B + B, **i32)
         positions = torch.full((B,), self._tail_len, **i32)
         position_ids = self._position_ids_from_mask(attention_mask)[:, -1:]
-        logits = run_decoder_step(self.model, a, p, plan, input_ids, position_ids, slots, positions)
+        logits = run_decoder_step(self.model, a, [AttentionGroup(p, plan, slots, positions)], input_ids, position_ids)
         return logits, self._finish_token(None if mass is None else mass[:nb])
 
     def _finish_token(self, mass_row):
@@ -359,7 +402,7 @@ class PagedModel:
                 "input_ids is shorter than the already-primed session "
                 f"({total_len - 1} < {self._primed_tokens} tokens). "
                 "Call reset() to start a new session instead of rewinding one.")
-        if not torch.equal(input_ids[:, :self._primed_tokens].cpu(), self._primed_prefix.cpu()):
+        if not torch.equal(input_ids[:, :self._primed_tokens].cpu(), self._primed_prefix):
             raise ValueError(
                 "input_ids diverges from the already-primed session prefix. generate() expects each call to extend "
                 "the same growing sequence (previous input + previously generated tokens + any new tokens). Call "
@@ -414,7 +457,7 @@ class PagedModel:
                 mask = torch.cat([mask, torch.ones((mask.shape[0], 1), dtype=mask.dtype, device=mask.device)], dim=1)
             full = torch.cat([input_ids, torch.tensor(generated, dtype=input_ids.dtype, device=input_ids.device)],
                              dim=1)
-            self._primed_prefix = full[:, :-1].detach().clone()
+            self._primed_prefix = full[:, :-1].detach().cpu()
             self._primed_tokens = full.shape[-1] - 1
             stats.final_num_blocks = self._num_blocks
             if in_gpu:

@@ -224,13 +224,35 @@ struct CombineParams {
 
 enum { OP_STEP = 0, OP_STATS = 1, OP_FIXED = 2, OP_PAGED = 3 };
 
-__global__ void __launch_bounds__(128) combine_kernel(const CombineParams c) {
+// Weight of a split whose running max is ms once the row's final max is M (the reference's
+// guard, streaming_attention.py:171-172: a split that saw nothing valid contributes nothing).
+__device__ __forceinline__ float split_weight(float ms, float M) {
+  return ms == neg_inf() ? 0.f : (ms == M ? 1.f : exp2f((ms - M) * kLog2e));
+}
+
+// Final softmax statistics of one query row from its splits' partial (m, l), in split order:
+// M = max(m_floor, max_s m_s), L = sum_s l_s * 2^((m_s - M) log2 e), each step rounded on its own
+// (explicit fma), so the combine and the mass pass, which both need them, get identical values.
+template <typename Ptr>
+__device__ __forceinline__ void row_final_stats(Ptr ms, Ptr ls, int nsplit, float m_floor, float& M, float& L) {
+  float mx = m_floor;
+#pragma unroll 8
+  for (int s = 0; s < nsplit; ++s) mx = fmaxf(mx, ms[s]);
+  float acc = 0.f;
+#pragma unroll 8
+  for (int s = 0; s < nsplit; ++s) acc = __fmaf_rn(split_weight(ms[s], mx), ls[s], acc);
+  M = mx;
+  L = acc;
+}
+
+// One query row: merge the splits' (m, l, acc), into the incoming state (drop-in ops) or from
+// scratch into the output (paged op).
+__device__ __forceinline__ void combine_row(const CombineParams& c, int row) {
   __shared__ float w_s[kMaxSplits];
   __shared__ float l_s[kMaxSplits];
   __shared__ float sh_L;
   __shared__ float sh_M;
   __shared__ float sh_win;
-  const int row = blockIdx.x;
   const int b = row / c.num_q_heads;
   if (c.active && c.active[b] == 0) return;
   int t_begin, t_end, nsplit;
@@ -253,20 +275,14 @@ __global__ void __launch_bounds__(128) combine_kernel(const CombineParams c) {
   }
   __syncthreads();
   if (threadIdx.x == 0) {
-    float M = neg_inf();
-    for (int s = 0; s < nsplit; ++s) M = fmaxf(M, w_s[s]);
     const float m_in = c.op == OP_PAGED ? neg_inf() : c.m[row];
-    const float Mt = fmaxf(M, m_in);
+    float Mt, L;
+    row_final_stats(static_cast<const float*>(w_s), static_cast<const float*>(l_s), nsplit, m_in, Mt, L);
+    for (int s = 0; s < nsplit; ++s) w_s[s] = split_weight(w_s[s], Mt);
     // reference guard (streaming_attention.py:171-172): nothing valid yet -> alpha = 0
     float w_in = 0.f;
     if (c.op != OP_PAGED && Mt != neg_inf()) w_in = (m_in == Mt) ? 1.f : exp2f((m_in - Mt) * kLog2e);
-    float L = c.op == OP_PAGED ? 0.f : c.l[row] * w_in;
-    for (int s = 0; s < nsplit; ++s) {
-      const float ms = w_s[s];
-      const float ws = ms == neg_inf() ? 0.f : (ms == Mt ? 1.f : exp2f((ms - Mt) * kLog2e));
-      w_s[s] = ws;
-      L += ws * l_s[s];
-    }
+    if (c.op != OP_PAGED) L = __fmaf_rn(c.l[row], w_in, L);
     sh_L = L;
     sh_M = Mt;
     sh_win = w_in;
@@ -295,6 +311,8 @@ __global__ void __launch_bounds__(128) combine_kernel(const CombineParams c) {
   }
 }
 
+__global__ void __launch_bounds__(128) combine_kernel(const CombineParams c) { combine_row(c, blockIdx.x); }
+
 // accumulate_step: block_mass[b, h, off + j] = sum_{groups of local block j} p / l.
 __global__ void chunk_mass_kernel(const float2* mass_part, int gstride, int group_tokens, int tpb, int tokens,
                                   const float* l, const int* active, int num_q_heads, float* block_mass,
@@ -319,54 +337,118 @@ struct PagedMassParams {
   int gstride, group_shift, tile_shift, tpb, tiles_per_split;
   GeomArgs geom;
   const int* active;
-  const float* m_final;
-  const float* l_final;
+  const float* part_m;  // the splits' partial statistics, [rows, max_splits]
+  const float* part_l;
+  int max_splits;
   int batch, num_q_heads, max_blocks;
   float* block_mass;  // [B, Hq, max_blocks] or null
   float* mass_accum;
   int mass_mode;
 };
 
-__device__ float paged_block_head_mass(const PagedMassParams& p, int b, int r, int j, int t_begin, int t_end) {
-  const long long row = (long long)b * p.num_q_heads + r;
-  const float mf = p.m_final[row];
-  const float lf = p.l_final[row];
-  const int gpb = p.tpb >> p.group_shift;
-  float s = 0.f;
-#pragma unroll 4
-  for (int gi = j * gpb; gi < (j + 1) * gpb; ++gi) {
-    const int tile = (gi << p.group_shift) >> p.tile_shift;
-    if (tile < t_begin || tile >= t_end) continue;  // never loaded: outside the attended range
-    const float2 v = p.mass_part[row * p.gstride + gi];
-    if (v.x != 0.f) s += v.x * exp2f((v.y - mf) * kLog2e);
-  }
-  return lf > 0.f ? s / lf : 0.f;  // nothing valid in the row: no mass (streaming_attention.py:317 defaults l_final to 1)
-}
+// The combine/mass kernel of the paged op runs 256-thread CTAs: the first `rows` CTAs merge one
+// query row each, the rest compute the per-block mass of 32 blocks of one batch row (all rows in
+// batch-mean mode).  The mass CTAs derive each head's final (M, L) from the splits' statistics
+// themselves (a warp reduction; the merge's serial sum may differ in the last bit, far inside the
+// mass tolerance), so neither half waits for the other.
+constexpr int kFinishThreads = 256;
+constexpr int kFinishWarps = kFinishThreads / 32;
+constexpr int kHeadsPerWarp = 4;  // heads a warp handles at once: their loads are issued together
+constexpr int kMassHeadChunk = kFinishWarps * kHeadsPerWarp;
 
-// One CTA per (32 blocks, row): lane <-> block, warp <-> a subset of the query heads,
-// heads summed through shared memory.  In batch-mean mode one CTA walks all rows.
-constexpr int kMassWarps = 8;
-
-__global__ void __launch_bounds__(kMassWarps * 32) paged_mass_kernel(const PagedMassParams p) {
-  __shared__ float red[kMassWarps][32];
+__device__ __forceinline__ void paged_mass_cta(const PagedMassParams& p, int bx, int by) {
+  __shared__ float red[kFinishWarps][32];
+  __shared__ float mf_s[kMassHeadChunk];
+  __shared__ float lf_s[kMassHeadChunk];
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
-  const int j = blockIdx.x * 32 + lane;
+  const int j = bx * 32 + lane;
   const bool batch_mean = p.mass_mode == PAGER_MASS_BATCH_MEAN;
-  const int b_first = batch_mean ? 0 : blockIdx.y;
-  const int b_last = batch_mean ? p.batch : blockIdx.y + 1;
+  const int b_first = batch_mean ? 0 : by;
+  const int b_last = batch_mean ? p.batch : by + 1;
+  const int gpb = p.tpb >> p.group_shift;
   float tot = 0.f;
   for (int b = b_first; b < b_last; ++b) {
-    if (p.active && p.active[b] == 0) continue;
+    if (p.active && p.active[b] == 0) continue;  // uniform across the CTA
     const RowGeom g = row_geom(p.geom, b);
-    if (j >= g.nb || j >= p.max_blocks) continue;
     int tb, te, ns;
     geom_tiles(g, p.tile_shift, p.tiles_per_split, tb, te, ns);
-#pragma unroll 4
-    for (int r = warp; r < p.num_q_heads; r += kMassWarps) {
-      const float v = paged_block_head_mass(p, b, r, j, tb, te);
-      if (p.block_mass) p.block_mass[((long long)b * p.num_q_heads + r) * p.max_blocks + j] = v;
-      tot += v;
+    const long long row0 = (long long)b * p.num_q_heads;
+    for (int r0 = 0; r0 < p.num_q_heads; r0 += kMassHeadChunk) {
+      const int r_end = min(p.num_q_heads, r0 + kMassHeadChunk);
+      // Phase 1: warp w finalizes heads r0 + w + k * kFinishWarps (k < kHeadsPerWarp); lanes walk the
+      // splits keeping an online (max, sum), shuffles merge the lanes.
+      {
+        float mx[kHeadsPerWarp], sm[kHeadsPerWarp];
+#pragma unroll
+        for (int k = 0; k < kHeadsPerWarp; ++k) {
+          mx[k] = neg_inf();
+          sm[k] = 0.f;
+        }
+        for (int s0 = 0; s0 < ns; s0 += 32) {
+          const int s = s0 + lane;
+          float mv[kHeadsPerWarp], lv[kHeadsPerWarp];
+#pragma unroll
+          for (int k = 0; k < kHeadsPerWarp; ++k) {
+            const int r = r0 + warp + k * kFinishWarps;
+            const bool ok = r < r_end && s < ns;
+            const long long pi = (row0 + r) * p.max_splits + s;
+            mv[k] = ok ? p.part_m[pi] : neg_inf();
+            lv[k] = ok ? p.part_l[pi] : 0.f;
+          }
+#pragma unroll
+          for (int k = 0; k < kHeadsPerWarp; ++k) {
+            const float nm = fmaxf(mx[k], mv[k]);
+            sm[k] = sm[k] * split_weight(mx[k], nm) + lv[k] * split_weight(mv[k], nm);
+            mx[k] = nm;
+          }
+        }
+#pragma unroll
+        for (int k = 0; k < kHeadsPerWarp; ++k) {
+          const float M = warp_max(mx[k]);
+          const float L = warp_sum(sm[k] * split_weight(mx[k], M));
+          const int r = r0 + warp + k * kFinishWarps;
+          if (lane == 0 && r < r_end) {
+            mf_s[r - r0] = M;
+            lf_s[r - r0] = L;
+          }
+        }
+      }
+      __syncthreads();
+      // Phase 2: lane <-> block j, the warp's heads at once: mass = sum over the block's groups of
+      // sum(p) * 2^((m_group - M) log2 e) / L (zero for a row with nothing valid,
+      // streaming_attention.py:317 defaults l_final to 1 there).
+      if (j < g.nb && j < p.max_blocks) {
+        float acc[kHeadsPerWarp];
+#pragma unroll
+        for (int k = 0; k < kHeadsPerWarp; ++k) acc[k] = 0.f;
+#pragma unroll 2
+        for (int gi = j * gpb; gi < (j + 1) * gpb; ++gi) {
+          const int tile = (gi << p.group_shift) >> p.tile_shift;
+          if (tile < tb || tile >= te) continue;  // never loaded: outside the attended range
+          float2 v[kHeadsPerWarp];
+#pragma unroll
+          for (int k = 0; k < kHeadsPerWarp; ++k) {
+            const int r = r0 + warp + k * kFinishWarps;
+            v[k] = r < r_end ? p.mass_part[(row0 + r) * p.gstride + gi] : make_float2(0.f, 0.f);
+          }
+#pragma unroll
+          for (int k = 0; k < kHeadsPerWarp; ++k) {
+            const int r = r0 + warp + k * kFinishWarps;
+            if (v[k].x != 0.f) acc[k] += v[k].x * exp2f((v[k].y - mf_s[min(r, r_end - 1) - r0]) * kLog2e);
+          }
+        }
+#pragma unroll
+        for (int k = 0; k < kHeadsPerWarp; ++k) {
+          const int r = r0 + warp + k * kFinishWarps;
+          if (r >= r_end) continue;
+          const float lf = lf_s[r - r0];
+          const float v = lf > 0.f ? acc[k] / lf : 0.f;
+          if (p.block_mass) p.block_mass[(row0 + r) * p.max_blocks + j] = v;
+          tot += v;
+        }
+      }
+      __syncthreads();
     }
   }
   red[warp][lane] = tot;
@@ -374,14 +456,30 @@ __global__ void __launch_bounds__(kMassWarps * 32) paged_mass_kernel(const Paged
   if (warp != 0 || j >= p.max_blocks || p.mass_mode == PAGER_MASS_NONE) return;
   float sum = 0.f;
 #pragma unroll
-  for (int w = 0; w < kMassWarps; ++w) sum += red[w][lane];
+  for (int w = 0; w < kFinishWarps; ++w) sum += red[w][lane];
   if (batch_mean) {
     p.mass_accum[j] += sum / (float)(p.batch * p.num_q_heads);
   } else {
-    const int b = blockIdx.y;
+    const int b = by;
     if (p.active && p.active[b] == 0) return;
     if (j >= row_geom(p.geom, b).nb) return;
     p.mass_accum[(long long)b * p.max_blocks + j] += sum / (float)p.num_q_heads;
+  }
+}
+
+// Paged op, after the split kernel: CTAs [0, rows) merge, the next mass_x * mass_y compute mass.
+// Launched programmatically serialized behind the split kernel, it waits for the split grid before
+// reading its partials and lets the next layer's split kernel be scheduled behind it.
+__global__ void __launch_bounds__(kFinishThreads) paged_finish_kernel(const CombineParams c, const PagedMassParams mp,
+                                                                     int rows, int mass_x) {
+  pdl_wait();
+  pdl_launch_dependents();
+  const int cta = blockIdx.x;
+  if (cta < rows) {
+    combine_row(c, cta);
+  } else {
+    const int m = cta - rows;
+    paged_mass_cta(mp, m % mass_x, m / mass_x);
   }
 }
 
@@ -429,6 +527,26 @@ __global__ void zero_copy_probe_kernel(const uint4* __restrict__ src, uint4* __r
     dst[i + 3 * stride] = d;
   }
   for (; i < n16; i += stride) dst[i] = ld_global_16(src + i);
+}
+
+// ------------------------------------------------------------------ launches
+// Launch with programmatic stream serialization: the kernel may be scheduled while the previous
+// kernel in the stream drains (hiding launch latency between the paged op's kernels and across
+// layers); every kernel launched this way calls pdl_wait() before it touches global memory.
+cudaError_t launch_serialized(const void* fn, dim3 grid, dim3 block, size_t smem, cudaStream_t st, void** args) {
+  cudaLaunchConfig_t cfg;
+  memset(&cfg, 0, sizeof(cfg));
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  memset(attr, 0, sizeof(attr));
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelExC(&cfg, fn, args);
 }
 
 // ------------------------------------------------------------------ scratch layout
@@ -990,7 +1108,7 @@ int pager_paged_decode_attention_staged(const void* q, int q_dtype, const void* 
   cudaStream_t st = (cudaStream_t)stream;
   dim3 grid(pp.plan.max_splits, num_kv_heads, batch);
   void* args[] = {&p, &mk, staged ? &ms : &mk};
-  PAGER_CUDA(cudaLaunchKernel(pp.k.fn, grid, dim3(pp.k.threads), args, pp.k.smem_bytes, st), "split kernel launch");
+  PAGER_CUDA(launch_serialized(pp.k.fn, grid, dim3(pp.k.threads), pp.k.smem_bytes, st, args), "split kernel launch");
 
   CombineParams c;
   memset(&c, 0, sizeof(c));
@@ -1009,12 +1127,10 @@ int pager_paged_decode_attention_staged(const void* q, int q_dtype, const void* 
   c.out_dtype = out_dtype;
   c.m_final = sc.m_final;
   c.l_final = sc.l_final;
-  combine_kernel<<<(unsigned)rows, 128, 0, st>>>(c);
-  PAGER_CUDA(cudaGetLastError(), "combine launch");
-
+  PagedMassParams mp;
+  memset(&mp, 0, sizeof(mp));
+  int mass_x = 1, mass_y = 0;
   if ((block_mass || mass_mode != PAGER_MASS_NONE) && max_blocks > 0) {
-    PagedMassParams mp;
-    memset(&mp, 0, sizeof(mp));
     mp.mass_part = sc.mass_part;
     mp.gstride = (int)pp.gstride;
     mp.group_shift = ilog2(pp.G);
@@ -1023,18 +1139,25 @@ int pager_paged_decode_attention_staged(const void* q, int q_dtype, const void* 
     mp.tiles_per_split = pp.plan.tiles_per_split;
     mp.geom = p.geom;
     mp.active = active;
-    mp.m_final = sc.m_final;
-    mp.l_final = sc.l_final;
+    mp.part_m = sc.part_m;
+    mp.part_l = sc.part_l;
+    mp.max_splits = pp.plan.max_splits;
     mp.batch = batch;
     mp.num_q_heads = num_q_heads;
     mp.max_blocks = max_blocks;
     mp.block_mass = block_mass;
     mp.mass_accum = mass_accum;
     mp.mass_mode = mass_mode;
-    dim3 g2((max_blocks + 31) / 32, mass_mode == PAGER_MASS_BATCH_MEAN ? 1 : batch);
-    paged_mass_kernel<<<g2, kMassWarps * 32, 0, st>>>(mp);
-    PAGER_CUDA(cudaGetLastError(), "mass launch");
+    mass_x = (max_blocks + 31) / 32;
+    mass_y = mass_mode == PAGER_MASS_BATCH_MEAN ? 1 : batch;
   }
+  int rows_i = (int)rows;
+  const long long ctas = rows + (long long)mass_x * mass_y;
+  if (ctas >= (1LL << 31)) return fail(PAGER_ERR_INVALID, "too many rows and blocks for one launch");
+  void* fargs[] = {&c, &mp, &rows_i, &mass_x};
+  PAGER_CUDA(launch_serialized(reinterpret_cast<const void*>(&paged_finish_kernel), dim3((unsigned)ctas),
+                               dim3(kFinishThreads), 0, st, fargs),
+             "combine/mass launch");
   return PAGER_OK;
 }
 

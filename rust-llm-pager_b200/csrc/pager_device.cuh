@@ -45,6 +45,16 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return done != 0;
 }
 
+// ---------------------------------------------------------------- programmatic dependent launch
+// A kernel launched with programmatic stream serialization may be scheduled before the previous
+// kernel in its stream has finished.  pdl_wait() blocks until every grid it depends on has
+// completed and its memory writes are visible; kernels call it before touching global memory.
+// Launched without that attribute (or after a non-kernel stream operation) it returns at once.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+// Lets the next programmatically serialized kernel in the stream be scheduled now; it still waits
+// (pdl_wait) for this grid to complete before it reads anything this grid writes.
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 __device__ __forceinline__ uint64_t global_timer_ns() {
   uint64_t t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));

@@ -1070,6 +1070,11 @@ __global__ void __launch_bounds__(TileCfg<T, D, MODE, BACKEND>::THREADS, TileCfg
   const int split = blockIdx.x;
   const int h = blockIdx.y;
   const int b = blockIdx.z;
+  // Launched programmatically serialized (paged op): the previous kernel in the stream may still
+  // be reading the partials this grid overwrites, or writing q / the pools; wait for it first,
+  // then let the combine/mass kernel that follows be scheduled behind this grid.
+  pdl_wait();
+  pdl_launch_dependents();
   if (p.active && p.active[b] == 0) return;
   bool clamped = false;
   const RowGeom g = row_geom(p.geom, b, &clamped);

@@ -61,4 +61,4 @@ def test_json_line_is_alone_on_stdout_under_torchrun():
 def test_every_workload_lays_out(name):
     lay = bench.WorkloadLayout(name, seed=7)
     assert lay.bytes_per_step == lay.hbm_bytes + lay.host_bytes > 0
-    assert lay.launches_per_step == 3 * lay.L
+    assert lay.launches_per_step == 2 * lay.L

@@ -39,9 +39,9 @@ for _p in (ROOT, os.path.join(ROOT, "rust-llm-pager_b200")):
         sys.path.insert(0, _p)
 
 METRIC = "decode-attn effective KV GB/s (HBM + host tiers) at 32k ctx"
-# (268.82 MB read + 6.80 MB written) / 268.75 MB of K/V per launch, from one ncu capture of the
+# (268.83 MB read + 4.59 MB written) / 268.75 MB of K/V per launch, from one ncu capture of the
 # split kernel on the prof-hbm workload (profiles/split_kernel_paged_hbm_prof-hbm.md).
-NCU_DRAM_PER_HBM_BYTE = (268.82 + 6.80) / 268.75
+NCU_DRAM_PER_HBM_BYTE = (268.83 + 4.59) / 268.75
 
 WORKLOADS = {
     # the serving config's Llama-3-8B geometry at 32k: 40 GB HBM budget, overflow in the pinned host pool

@@ -140,9 +140,10 @@ def test_paged_matches_reference_two_pass(mods, cfg, backend):
     assert lib.device_status(0) == 0
 
 
-def test_batch_mean_mass_mode(mods):
+@pytest.mark.parametrize("hq,hkv", [(14, 2), (48, 16)])
+def test_batch_mean_mass_mode(mods, hq, hkv):
     sa, HostPool, lib = mods
-    s = build(7, 2, 14, 2, 64, 16, 1, [6, 6], [2, 2], torch.float16)
+    s = build(7, 2, hq, hkv, 64, 16, 1, [6, 6], [2, 2], torch.float16)
     _, bm, accum = run_gpu(sa, HostPool, s, 0, mass_mode="batch_mean")
     np.testing.assert_allclose(accum.numpy(), bm.mean(dim=(0, 1)).numpy(), rtol=1e-5, atol=1e-7)
     ref = np.stack([oracle_row(s, b, 0, "f16")[1] for b in range(2)]).mean(axis=(0, 1))
@@ -189,13 +190,19 @@ EXTRA = [
     ("n_rep_1_mha", 16, 2, 4, 4, 64, 32, 2, [6, 2], [1, 30], torch.float16, {}),
     ("fp32_d8", 17, 3, 4, 2, 8, 16, 1, [5, 1, 3], [2, 16, 1], torch.float32, {}),
     ("fp16_d32", 18, 2, 6, 3, 32, 16, 1, [9, 4], [15, 1], torch.float16, {}),
+    # the mass pass finalizes heads in chunks of 32: 48 heads end on a partial chunk, 80 on two more
+    ("heads_48_chunked_mass", 19, 2, 48, 16, 64, 16, 1, [9, 3], [4, 11], torch.float16, {}),
+    ("heads_80_bf16_d128", 20, 1, 80, 8, 128, 64, 1, [5], [7], torch.bfloat16, {}),
+    # one row, two kv heads, 300 blocks: planned at 37 splits, more than a warp's lanes hold at once
+    ("many_splits_one_row", 21, 1, 8, 2, 64, 64, 1, [300], [13], torch.float16, {}),
 ]
 
 
 @pytest.mark.parametrize("case", EXTRA, ids=[c[0] for c in EXTRA])
 def test_paged_op_options_match_the_reference(mods, case):
     """Softcap and custom scale (MMA and FMA), blocks larger than a tile and the smallest blocks,
-    GQA fan-out 16 and plain MHA, fp32 and small head dims."""
+    GQA fan-out 16 and plain MHA, fp32 and small head dims, more query heads than the mass pass
+    finalizes at once, and a row split more ways than a warp has lanes."""
     sa, HostPool, lib = mods
     name, seed, B, Hq, Hkv, D, tpb, L, nbs, tails, dtype, kw = case
     s = build(seed, B, Hq, Hkv, D, tpb, L, nbs, tails, dtype)

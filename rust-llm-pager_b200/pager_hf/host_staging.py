@@ -11,9 +11,11 @@ Host-pool blocks can reach the decode kernel two ways:
   Copies for layer ``l+1`` run on a copy stream while layer ``l`` computes, into
   the other half of a double buffer.
 
-Which one wins depends on the link: ``choose_host_read`` measures both on this
-device (pinned ``cudaMemcpyAsync`` against a zero-copy read kernel, 256 MiB)
-and picks staged reads when the copy engines are faster.  The reference reads
+Which one wins depends on the link and on how the host blocks lie in the pool:
+``choose_host_read`` measures both reads on this device (pinned
+``cudaMemcpyAsync`` against a zero-copy read kernel, 256 MiB) and picks staged
+reads when copying a layer's blocks, one submission per run of consecutive
+slots, is expected to beat reading them zero-copy.  The reference reads
 host blocks with synchronous pageable copies per layer and group
 (``pager_hf/paged_model.py:878-924``).
 """
@@ -111,10 +113,24 @@ def record_link_bandwidth(device, copy_gbs: float, zero_copy_gbs: float) -> None
         _LINK[idx] = {"copy_gbs": float(copy_gbs), "zero_copy_gbs": float(zero_copy_gbs)}
 
 
-def choose_host_read(device) -> str:
-    """``"staged"`` when the copy engines beat zero-copy reads on this device's link, else ``"zero_copy"``."""
+# Host time to submit one 2D copy of a run (cudaMemcpy2DAsync), measured on B200 boxes: a
+# left-padded 16-row batch whose host slots fell into ~570 runs per layer issued 99,616 copies
+# in 8 decode steps for 774 ms of host time (~7.8 us each, command-buffer stalls included).
+COPY_SUBMIT_S = 10e-6
+
+
+def choose_host_read(device, bytes_per_layer: int | None = None, copies_per_layer: int = 1) -> str:
+    """``"staged"`` when copying a layer's host blocks is expected to take less time than reading them
+    zero-copy, else ``"zero_copy"``.  The copies of a layer are submitted while earlier work runs, so
+    staged time = the longer of the copy engines' time (bytes / copy bandwidth) and the host's
+    submissions (one per copy, ``COPY_SUBMIT_S``): a host tier scattered over many short runs of
+    slots is submission-bound.  Without sizes, compares the two links."""
     bw = link_bandwidth(device)
-    return "staged" if bw["copy_gbs"] > bw["zero_copy_gbs"] else "zero_copy"
+    if bytes_per_layer is None:
+        return "staged" if bw["copy_gbs"] > bw["zero_copy_gbs"] else "zero_copy"
+    t_staged = max(bytes_per_layer / (bw["copy_gbs"] * 1e9), copies_per_layer * COPY_SUBMIT_S)
+    t_zero_copy = bytes_per_layer / (bw["zero_copy_gbs"] * 1e9)
+    return "staged" if t_staged < t_zero_copy else "zero_copy"
 
 
 class HostStaging:
@@ -132,8 +148,9 @@ class HostStaging:
 
     def __init__(self, block_table: torch.Tensor, host_pool: torch.Tensor, num_layers: int, device,
                  prefetch_next_step: bool = False, tokens_per_block: int | None = None, num_blocks=None,
-                 valid_lo=None, valid_hi=None, active=None):
-        staged, slots, runs = plan_host_runs(block_table, tokens_per_block, num_blocks, valid_lo, valid_hi, active)
+                 valid_lo=None, valid_hi=None, active=None, plan=None):
+        staged, slots, runs = plan if plan is not None else plan_host_runs(
+            block_table, tokens_per_block, num_blocks, valid_lo, valid_hi, active)
         self.device = torch.device(device)
         self.table = staged.to(self.device)
         self.num_slots = int(slots.numel())

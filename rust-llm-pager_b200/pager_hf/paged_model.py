@@ -141,6 +141,7 @@ class PagedModel:
         self.use_streaming_attention = True
         self.streaming_group_size_blocks = streaming_group_size_blocks  # kept for API parity; one launch per layer
         self.host_read = host_read
+        self.last_host_read: str | None = None  # the host-tier read mode of the last decode step's plan
         # pools shared with other single-row sessions (``batched_decode_step`` decodes them in one
         # launch); None: the session allocates its own
         if pools is not None and (pools.rows_per_group != 1 or pools.tokens_per_block != tokens_per_block):
@@ -351,6 +352,7 @@ class PagedModel:
             valid_lo=lo.to(dev) if bool((lo > 0).any()) else None, valid_hi=torch.full((B,), total, **i32),
             scale=a["scale"], mass_accum=mass, mass_mode="batch_mean" if mass is not None else "none",
             host_read=self.host_read)
+        self.last_host_read = plan.host_read
         slots = torch.arange(self._tail_group * B, self._tail_group * B + B, **i32)
         positions = torch.full((B,), self._tail_len, **i32)
         position_ids = self._position_ids_from_mask(attention_mask)[:, -1:]

@@ -452,14 +452,18 @@ class PagedDecodePlan:
             tbl = self.block_table
             has_host = bool(((tbl >= 0) & ((tbl & L.HOST_SLOT_BIT) != 0)).any())
             if has_host:
-                from .host_staging import HostStaging, choose_host_read
+                from .host_staging import HostStaging, choose_host_read, plan_host_runs
 
-                mode = choose_host_read(device) if host_read == "auto" else "staged"
-                if mode == "staged":
+                plan = plan_host_runs(tbl, self.tpb, self.num_blocks, self.valid_lo, self.valid_hi, self.active)
+                n_slots, n_runs = int(plan[1].numel()), len(plan[2][0])
+                mode = "staged"
+                if host_read == "auto":
+                    chunk = 2 * host_pool.shape[3] * host_pool.shape[4] * host_pool.shape[5] * host_pool.element_size()
+                    mode = choose_host_read(device, n_slots * chunk, n_runs)
+                if mode == "staged" and n_slots > 0:  # with no host block read there is nothing to stage
                     self.staging = HostStaging(tbl, host_pool, self.num_layers, device, prefetch_next_step,
-                                               self.tpb, self.num_blocks, self.valid_lo, self.valid_hi, self.active)
-                    if self.staging.num_slots == 0:  # no host block is read: nothing to stage
-                        self.staging = None
+                                               self.tpb, self.num_blocks, self.valid_lo, self.valid_hi, self.active,
+                                               plan=plan)
         self.host_read = "staged" if self.staging is not None else "zero_copy"
 
     def run(self, q: torch.Tensor, layer: int, out: torch.Tensor, stream: int | None = None) -> torch.Tensor:

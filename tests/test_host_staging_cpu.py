@@ -46,3 +46,28 @@ def test_only_blocks_the_kernel_reads_are_staged():
     assert int(staged[1, 3]) == 7 | H                  # beyond num_blocks
     assert all(int(staged[2, j]) == table[2, j] for j in range(4))  # inactive row
     assert int(staged[1, 2]) & STAGE_SLOT_BIT
+
+
+def test_auto_choice_counts_one_submission_per_copy():
+    """``auto`` stages a host tier that lies in a few long runs of slots and reads a scattered one
+    zero-copy: each run is one copy submission (``COPY_SUBMIT_S`` of host time), overlapped with
+    the copies themselves."""
+    from pager_hf import host_staging as hs
+
+    dev = torch.device("cuda", 7)  # a recorded (fake) link: nothing touches a GPU
+    try:
+        hs.record_link_bandwidth(dev, copy_gbs=55.6, zero_copy_gbs=51.5)
+        assert hs.choose_host_read(dev) == "staged"  # without sizes: the faster link
+        assert hs.choose_host_read(dev, 362 << 20, copies_per_layer=1) == "staged"  # one contiguous run
+        assert hs.choose_host_read(dev, 225 << 20, copies_per_layer=566) == "zero_copy"  # scattered slots
+        # a windowed layer: 8 runs of 2 MiB, submitted while the copies run
+        assert hs.choose_host_read(dev, 16 << 20, copies_per_layer=8) == "staged"
+        # break-even: submissions take as long as zero-copy reads of the same bytes
+        nbytes = 64 << 20
+        k = int(nbytes / 51.5e9 / hs.COPY_SUBMIT_S)
+        assert hs.choose_host_read(dev, nbytes, copies_per_layer=k) == "staged"
+        assert hs.choose_host_read(dev, nbytes, copies_per_layer=k + 2) == "zero_copy"
+        hs.record_link_bandwidth(dev, copy_gbs=40.0, zero_copy_gbs=51.5)
+        assert hs.choose_host_read(dev, 362 << 20, copies_per_layer=1) == "zero_copy"
+    finally:
+        hs._LINK.pop(7, None)

@@ -282,15 +282,17 @@ class PagedModel:
                        past_key_values=cache, use_cache=True)
         n = prefix.shape[1]
         nfull = n // tpb
-        budget_blocks = max(1, self._pager_kwargs["vram"] // (16 * 1024 * 1024))
         if self.shared_pools is not None:
             if B != 1:
                 raise ValueError("a session on shared pools is single-row")
             self._pools = self.shared_pools
         else:
+            # Both tiers get a group for every block (plus the tail and room for new blocks): a
+            # rebalance may demote blocks before its promotions free their host groups, and growing the
+            # pinned host pool mid-decode (a new allocation of twice the size plus a copy) takes seconds.
             self._pools = KVPools(num_layers=a["layers"], kv_heads=a["hkv"], head_dim=a["d"], tokens_per_block=tpb,
                                   dtype=dtype, device=dev, rows_per_group=B, gpu_groups=max(nfull + 2, 2),
-                                  cpu_groups=max(4, nfull - min(nfull, budget_blocks) + 2))
+                                  cpu_groups=max(4, nfull + 2))
         self._store = KVBlockStore(tpb, self._ram_budget, pools=self._pools)
         keys = [layer.keys for layer in cache.layers]
         values = [layer.values for layer in cache.layers]

@@ -125,6 +125,67 @@ def run_decoder_step(model, arch: dict, groups: list[AttentionGroup], input_ids,
     return model.lm_head(model.model.norm(hidden))
 
 
+class _DecodeGraph:
+    """One decode step of a ``PagedModel`` session captured as a CUDA graph.
+
+    Eager decode steps are bound by the host: each layer runs a dozen small modules
+    (norms, projections, RoPE, MLP) plus the paged op, ~800 launches per step for a 24-layer
+    model.  The graph replays them with one launch.  Its inputs live in static device buffers
+    refreshed before each replay: the token ids and position ids, and one packed int32 buffer
+    holding the block table, the rows' valid ranges, tail slots and tail positions (a single host
+    copy per step).  Shapes and pointers the launches bake in -- batch, block count (the table
+    width and the split plan), the pools (their ``version`` changes when they grow) -- form the
+    key; a step with another key captures a new graph (once per ``tokens_per_block`` tokens, when
+    the tail becomes a block).  Host-tier blocks are read zero-copy inside the graph."""
+
+    def __init__(self, pm, arch: dict, key: tuple, B: int, nb: int, dev):
+        p = pm._pools
+        self.key, self.pm, self.arch, self.pools, self.B, self.nb = key, pm, arch, p, B, nb
+        w = nb + 1
+        self.ints = torch.zeros(B * w + 4 * B, dtype=torch.int32, device=dev)
+        self.table = self.ints[: B * w].view(B, w)
+        self.lo, self.hi, self.slots, self.positions = self.ints[B * w:].view(4, B).unbind(0)
+        self.input_ids = torch.zeros(B, 1, dtype=torch.long, device=dev)
+        self.position_ids = torch.zeros(B, 1, dtype=torch.long, device=dev)
+        self.mass = torch.zeros(w, dtype=torch.float32, device=dev) if pm._needs_attention else None
+        self.plan = PagedDecodePlan(
+            batch=B, num_query_heads=arch["hq"], dev_pool=p.dev_pool, host_pool=p.host_pool.tensor,
+            num_layers=arch["layers"], tokens_per_block=pm.tokens_per_block, block_table=self.table,
+            num_blocks=torch.full((B,), w, dtype=torch.int32, device=dev), max_row_tokens=w * pm.tokens_per_block,
+            valid_lo=self.lo, valid_hi=self.hi, scale=arch["scale"], mass_accum=self.mass,
+            mass_mode="batch_mean" if self.mass is not None else "none", host_read="zero_copy")
+        self.graph = None
+        self.logits = None
+
+    def load(self, ints_cpu: torch.Tensor, input_ids: torch.Tensor, position_ids: torch.Tensor) -> None:
+        self.ints.copy_(ints_cpu, non_blocking=False)
+        self.input_ids.copy_(input_ids)
+        self.position_ids.copy_(position_ids)
+
+    def _run(self):
+        if self.mass is not None:
+            self.mass.zero_()
+        group = AttentionGroup(self.pools, self.plan, self.slots, self.positions)
+        return run_decoder_step(self.pm.model, self.arch, [group], self.input_ids, self.position_ids)
+
+    def step(self) -> torch.Tensor:
+        """Run the loaded step: the first time eagerly on a side stream (the step's own values, so
+        its tail write is the one the replay repeats), then captured; afterwards by replay."""
+        if self.graph is None:
+            cur = torch.cuda.current_stream()
+            side = torch.cuda.Stream()
+            side.wait_stream(cur)
+            with torch.cuda.stream(side):
+                self._run()
+            cur.wait_stream(side)
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                self.logits = self._run()
+            self.graph = graph
+        self.graph.replay()
+        return self.logits
+
+
 class PagedModel:
     """A HuggingFace causal LM whose KV cache lives in paged device / host pools."""
 
@@ -132,7 +193,7 @@ class PagedModel:
                  rebalance_interval: int = 4, promote_margin: float = 0.05, ram_promote_margin: float = 0.20,
                  policy: str = "sinks_heavy_hitter", tokens_per_block: int = 16, prefill_chunk_tokens: int = 512,
                  use_streaming_attention: bool = True, streaming_group_size_blocks: int = 64,
-                 host_read: str = "auto", pools: KVPools | None = None):
+                 host_read: str = "auto", pools: KVPools | None = None, decode_graphs: bool = True):
         if not use_streaming_attention:
             raise NotImplementedError("only the streaming (fused paged) attention path is implemented")
         self.model = model
@@ -142,6 +203,9 @@ class PagedModel:
         self.streaming_group_size_blocks = streaming_group_size_blocks  # kept for API parity; one launch per layer
         self.host_read = host_read
         self.last_host_read: str | None = None  # the host-tier read mode of the last decode step's plan
+        # decode steps captured and replayed as CUDA graphs (host tier read zero-copy); staged host
+        # reads keep the eager step
+        self.decode_graphs = bool(decode_graphs) and host_read != "staged"
         # pools shared with other single-row sessions (``batched_decode_step`` decodes them in one
         # launch); None: the session allocates its own
         if pools is not None and (pools.rows_per_group != 1 or pools.tokens_per_block != tokens_per_block):
@@ -158,6 +222,7 @@ class PagedModel:
 
     # ------------------------------------------------------------------ session state
     def _clear_session(self):
+        self._graph = None
         self._pools = None
         self._store = None
         self._rust_pager = None
@@ -345,6 +410,8 @@ class PagedModel:
         lo = self._pad.clone()
         if a["window"] is not None:
             lo = torch.clamp(lo, min=max(0, total - int(a["window"])))
+        if self.decode_graphs:
+            return self._graph_step(a, B, nb, table, lo, total, input_ids, attention_mask)
         i32 = dict(dtype=torch.int32, device=dev)
         mass = torch.zeros(nb + 1, dtype=torch.float32, device=dev) if self._needs_attention else None
         plan = PagedDecodePlan(
@@ -360,6 +427,22 @@ class PagedModel:
         position_ids = self._position_ids_from_mask(attention_mask)[:, -1:]
         logits = run_decoder_step(self.model, a, [AttentionGroup(p, plan, slots, positions)], input_ids, position_ids)
         return logits, self._finish_token(None if mass is None else mass[:nb])
+
+    def _graph_step(self, a, B, nb, table, lo, total, input_ids, attention_mask):
+        """``_forward_step`` through a captured graph (``_DecodeGraph``); same inputs, same result."""
+        p = self._pools
+        key = (B, nb, id(p), p.version, self._needs_attention)
+        if self._graph is None or self._graph.key != key:
+            self._graph = None  # release the previous graph's memory before capturing the next
+            self._graph = _DecodeGraph(self, a, key, B, nb, input_ids.device)
+        g = self._graph
+        ints = torch.cat([table.reshape(-1), lo.to("cpu", torch.int32), torch.full((B,), total, dtype=torch.int32),
+                          torch.arange(self._tail_group * B, self._tail_group * B + B, dtype=torch.int32),
+                          torch.full((B,), self._tail_len, dtype=torch.int32)])
+        g.load(ints, input_ids, self._position_ids_from_mask(attention_mask)[:, -1:])
+        logits = g.step()
+        self.last_host_read = "zero_copy"
+        return logits, self._finish_token(None if g.mass is None else g.mass[:nb])
 
     def _finish_token(self, mass_row):
         """After a decoded token (``paged_model.py:1210-1233, :785-798``): roll a full tail into a block

@@ -165,3 +165,27 @@ def test_baseline_config2_geometry_greedy_parity():
                     recent_window=-(-nblocks // 10) - 1, policy="recent_only", tokens_per_block=64)
     _assert_greedy_match(pm.generate(ids, mask, 32), want[0], logits)
     assert len(pm._store.gpu_block_ids()) <= -(-nblocks // 10) + 1
+
+
+def test_captured_decode_steps_match_eager_steps():
+    """Decode steps replayed from CUDA graphs (the default) give the same tokens and pager decisions
+    as eager steps: a left-padded two-row batch, heavy-hitter scoring from the kernel's mass, tails
+    rolled into blocks several times (each a new capture)."""
+    from pager_hf.paged_model import PagedModel
+
+    model = _model("qwen2")
+    g = torch.Generator().manual_seed(5)
+    ids = torch.randint(0, 2000, (2, 200), generator=g).cuda()
+    mask = torch.ones_like(ids)
+    mask[1, :37] = 0
+    runs = {}
+    for graphs in (False, True):
+        pm = PagedModel(model, vram_budget=3 * BLOCK, ram_budget=64 * BLOCK, recent_window=1, policy="heavy_hitter",
+                        tokens_per_block=16, decode_graphs=graphs)
+        toks = pm.generate(ids, mask, 40)
+        runs[graphs] = (toks, sorted(pm._store.gpu_block_ids()), pm.last_run_stats.total_new_blocks,
+                        pm.last_host_read)
+        pm.reset()
+    assert runs[True][0] == runs[False][0]
+    assert runs[True][1:3] == runs[False][1:3]
+    assert runs[True][3] == "zero_copy"

@@ -132,26 +132,33 @@ class _DecodeGraph:
     (norms, projections, RoPE, MLP) plus the paged op, ~800 launches per step for a 24-layer
     model.  The graph replays them with one launch.  Its inputs live in static device buffers
     refreshed before each replay: the token ids and position ids, and one packed int32 buffer
-    holding the block table, the rows' valid ranges, tail slots and tail positions (a single host
-    copy per step).  Shapes and pointers the launches bake in -- batch, block count (the table
-    width and the split plan), the pools (their ``version`` changes when they grow) -- form the
-    key; a step with another key captures a new graph (once per ``tokens_per_block`` tokens, when
-    the tail becomes a block).  Host-tier blocks are read zero-copy inside the graph."""
+    holding the block table, the rows' block counts, valid ranges, tail slots and tail positions
+    (a single host copy per step).  Shapes and pointers the launches bake in -- batch, table width
+    (``width`` block columns, a multiple of ``WIDTH_STEP`` at least the blocks plus the tail; it
+    also bounds the split plan), the pools (their ``version`` changes when they grow) -- form the
+    key, so a new graph is captured once per ``WIDTH_STEP`` blocks; columns past a row's blocks
+    are absent.  Host-tier blocks are read zero-copy inside the graph."""
 
-    def __init__(self, pm, arch: dict, key: tuple, B: int, nb: int, dev):
+    WIDTH_STEP = 64
+
+    @classmethod
+    def width_for(cls, nb: int) -> int:
+        return -(-(nb + 1) // cls.WIDTH_STEP) * cls.WIDTH_STEP
+
+    def __init__(self, pm, arch: dict, key: tuple, B: int, width: int, dev):
         p = pm._pools
-        self.key, self.pm, self.arch, self.pools, self.B, self.nb = key, pm, arch, p, B, nb
-        w = nb + 1
-        self.ints = torch.zeros(B * w + 4 * B, dtype=torch.int32, device=dev)
+        self.key, self.pm, self.arch, self.pools, self.B, self.width = key, pm, arch, p, B, width
+        w = width
+        self.ints = torch.zeros(B * w + 5 * B, dtype=torch.int32, device=dev)
         self.table = self.ints[: B * w].view(B, w)
-        self.lo, self.hi, self.slots, self.positions = self.ints[B * w:].view(4, B).unbind(0)
+        self.num_blocks, self.lo, self.hi, self.slots, self.positions = self.ints[B * w:].view(5, B).unbind(0)
         self.input_ids = torch.zeros(B, 1, dtype=torch.long, device=dev)
         self.position_ids = torch.zeros(B, 1, dtype=torch.long, device=dev)
         self.mass = torch.zeros(w, dtype=torch.float32, device=dev) if pm._needs_attention else None
         self.plan = PagedDecodePlan(
             batch=B, num_query_heads=arch["hq"], dev_pool=p.dev_pool, host_pool=p.host_pool.tensor,
             num_layers=arch["layers"], tokens_per_block=pm.tokens_per_block, block_table=self.table,
-            num_blocks=torch.full((B,), w, dtype=torch.int32, device=dev), max_row_tokens=w * pm.tokens_per_block,
+            num_blocks=self.num_blocks, max_row_tokens=w * pm.tokens_per_block,
             valid_lo=self.lo, valid_hi=self.hi, scale=arch["scale"], mass_accum=self.mass,
             mass_mode="batch_mean" if self.mass is not None else "none", host_read="zero_copy")
         self.graph = None
@@ -431,12 +438,16 @@ class PagedModel:
     def _graph_step(self, a, B, nb, table, lo, total, input_ids, attention_mask):
         """``_forward_step`` through a captured graph (``_DecodeGraph``); same inputs, same result."""
         p = self._pools
-        key = (B, nb, id(p), p.version, self._needs_attention)
+        width = _DecodeGraph.width_for(nb)
+        key = (B, width, id(p), p.version, self._needs_attention)
         if self._graph is None or self._graph.key != key:
             self._graph = None  # release the previous graph's memory before capturing the next
-            self._graph = _DecodeGraph(self, a, key, B, nb, input_ids.device)
+            self._graph = _DecodeGraph(self, a, key, B, width, input_ids.device)
         g = self._graph
-        ints = torch.cat([table.reshape(-1), lo.to("cpu", torch.int32), torch.full((B,), total, dtype=torch.int32),
+        wide = torch.full((B, width), -1, dtype=torch.int32)
+        wide[:, : nb + 1] = table
+        ints = torch.cat([wide.reshape(-1), torch.full((B,), nb + 1, dtype=torch.int32),
+                          lo.to("cpu", torch.int32), torch.full((B,), total, dtype=torch.int32),
                           torch.arange(self._tail_group * B, self._tail_group * B + B, dtype=torch.int32),
                           torch.full((B,), self._tail_len, dtype=torch.int32)])
         g.load(ints, input_ids, self._position_ids_from_mask(attention_mask)[:, -1:])

@@ -214,8 +214,6 @@ struct CombineParams {
   float* acc;
   void* out;
   int out_dtype;
-  float* m_final;
-  float* l_final;
 };
 
 enum { OP_STEP = 0, OP_STATS = 1, OP_FIXED = 2, OP_PAGED = 3 };
@@ -296,14 +294,9 @@ __device__ __forceinline__ void combine_row(const CombineParams& c, int row) {
         store_any(c.out, (long long)row * D + d, c.out_dtype, a / L);
     }
   }
-  if (threadIdx.x == 0) {
-    if (c.op == OP_PAGED) {
-      c.m_final[row] = sh_M;
-      c.l_final[row] = L;
-    } else {
-      c.m[row] = sh_M;
-      c.l[row] = L;
-    }
+  if (threadIdx.x == 0 && c.op != OP_PAGED) {
+    c.m[row] = sh_M;
+    c.l[row] = L;
   }
 }
 
@@ -551,15 +544,12 @@ struct Scratch {
   float* part_l;
   float* part_acc;
   float2* mass_part;
-  float* m_final;
-  float* l_final;
   size_t bytes;
 };
 
 size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
-Scratch layout_scratch(char* base, long long rows, int max_splits, int head_dim, long long mass_groups,
-                       bool finals) {
+Scratch layout_scratch(char* base, long long rows, int max_splits, int head_dim, long long mass_groups) {
   Scratch s;
   size_t off = 0;
   auto take = [&](size_t n) {
@@ -571,8 +561,6 @@ Scratch layout_scratch(char* base, long long rows, int max_splits, int head_dim,
   s.part_l = reinterpret_cast<float*>(take(sizeof(float) * rows * max_splits));
   s.part_acc = reinterpret_cast<float*>(take(sizeof(float) * rows * max_splits * head_dim));
   s.mass_part = reinterpret_cast<float2*>(take(sizeof(float2) * rows * (mass_groups > 0 ? mass_groups : 0)));
-  s.m_final = reinterpret_cast<float*>(take(finals ? sizeof(float) * rows : 0));
-  s.l_final = reinterpret_cast<float*>(take(finals ? sizeof(float) * rows : 0));
   s.bytes = off;
   return s;
 }
@@ -666,7 +654,7 @@ int run_chunk(const ChunkArgs& a) {
   rc = chunk_plan(a, &k, &plan, &mass_groups, &G);
   if (rc) return rc;
   const long long rows = (long long)a.batch * a.hq;
-  Scratch sc = layout_scratch(static_cast<char*>(a.scratch), rows, plan.max_splits, a.head_dim, mass_groups, false);
+  Scratch sc = layout_scratch(static_cast<char*>(a.scratch), rows, plan.max_splits, a.head_dim, mass_groups);
   if (!a.scratch || a.scratch_bytes < sc.bytes)
     return fail(PAGER_ERR_SCRATCH, "scratch too small: need %zu bytes, got %zu", sc.bytes, a.scratch_bytes);
   DevInfo* di;
@@ -754,7 +742,7 @@ size_t chunk_scratch(const ChunkArgs& a) {
   long long mass_groups;
   int G;
   if (chunk_plan(a, &k, &plan, &mass_groups, &G)) return 0;
-  return layout_scratch(nullptr, (long long)a.batch * a.hq, plan.max_splits, a.head_dim, mass_groups, false).bytes;
+  return layout_scratch(nullptr, (long long)a.batch * a.hq, plan.max_splits, a.head_dim, mass_groups).bytes;
 }
 
 struct PagedPlan {
@@ -960,9 +948,9 @@ size_t pager_paged_decode_scratch_bytes(int batch, int num_q_heads, int num_kv_h
   size_t extra = 0;
   if (!paged_plan(batch, num_q_heads, num_kv_heads, head_dim, kv_dtype, tokens_per_block, max_row_tokens,
                   PAGER_BACKEND_FMA, &pf))
-    extra = layout_scratch(nullptr, (long long)batch * num_q_heads, pf.plan.max_splits, head_dim, pf.gstride, true).bytes;
+    extra = layout_scratch(nullptr, (long long)batch * num_q_heads, pf.plan.max_splits, head_dim, pf.gstride).bytes;
   const size_t base =
-      layout_scratch(nullptr, (long long)batch * num_q_heads, pp.plan.max_splits, head_dim, pp.gstride, true).bytes;
+      layout_scratch(nullptr, (long long)batch * num_q_heads, pp.plan.max_splits, head_dim, pp.gstride).bytes;
   return base > extra ? base : extra;
 }
 
@@ -1025,7 +1013,7 @@ int pager_paged_decode_attention_staged(const void* q, int q_dtype, const void* 
   rc = paged_plan(batch, num_q_heads, num_kv_heads, head_dim, kv_dtype, tokens_per_block, max_row_tokens, backend, &pp);
   if (rc) return rc;
   const long long rows = (long long)batch * num_q_heads;
-  Scratch sc = layout_scratch(static_cast<char*>(scratch), rows, pp.plan.max_splits, head_dim, pp.gstride, true);
+  Scratch sc = layout_scratch(static_cast<char*>(scratch), rows, pp.plan.max_splits, head_dim, pp.gstride);
   if (!scratch || scratch_bytes < sc.bytes)
     return fail(PAGER_ERR_SCRATCH, "scratch too small: need %zu bytes, got %zu", sc.bytes, scratch_bytes);
   DevInfo* di;
@@ -1121,8 +1109,6 @@ int pager_paged_decode_attention_staged(const void* q, int q_dtype, const void* 
   c.op = OP_PAGED;
   c.out = out;
   c.out_dtype = out_dtype;
-  c.m_final = sc.m_final;
-  c.l_final = sc.l_final;
   PagedMassParams mp;
   memset(&mp, 0, sizeof(mp));
   int mass_x = 1, mass_y = 0;

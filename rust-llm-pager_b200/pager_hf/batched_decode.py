@@ -264,6 +264,112 @@ def _group_plan(group: list, arch: dict, pools: KVPools, device: torch.device):
     return plan, mass, torch.tensor(slots, **i32), torch.tensor(positions, **i32)
 
 
+def _group_ints(group: list, arch: dict, width: int) -> torch.Tensor:
+    """The per-step int32 inputs of one pools group, packed as a captured step reads them: the block
+    table ``[rows, width]`` (each row's blocks, its tail slot, then absent columns), then per row the
+    block count (blocks + tail), valid range ``[lo, hi)``, tail slot and tail position."""
+    S = len(group)
+    table = torch.full((S, width), -1, dtype=torch.int32)
+    cols = torch.zeros(5, S, dtype=torch.int32)
+    for r, s in enumerate(group):
+        nb = s._num_blocks
+        if nb:
+            table[r, :nb] = s._store.block_table(range(nb), device="cpu")[0]
+        table[r, nb] = s._tail_group
+        total = s._total + 1
+        pad = int(s._pad[0])
+        cols[0, r] = nb + 1
+        cols[1, r] = max(pad, total - int(arch["window"])) if arch["window"] is not None else pad
+        cols[2, r] = total
+        cols[3, r] = s._tail_group
+        cols[4, r] = s._tail_len
+    return torch.cat([table.reshape(-1), cols.reshape(-1)])
+
+
+class _BatchedGraph:
+    """``batched_decode_step`` for one ordered set of sessions captured as a CUDA graph (see
+    ``paged_model._DecodeGraph``): per pools group a packed int32 input buffer (``_group_ints``) and a
+    mass buffer, the token and position ids of all rows, one plan per group with zero-copy host reads.
+    The key -- the sessions, and per group the pools, their version and the table width (blocks plus
+    tail, rounded up to ``_DecodeGraph.WIDTH_STEP``) -- changes when a session joins or leaves, a pool
+    grows, or a session's blocks cross a width step."""
+
+    def __init__(self, key, sessions, by_pools, arch, widths, device):
+        from .paged_model import AttentionGroup
+
+        self.key, self.arch = key, arch
+        self.model = sessions[0].model
+        S = len(sessions)
+        self.input_ids = torch.zeros(S, 1, dtype=torch.long, device=device)
+        self.position_ids = torch.zeros(S, 1, dtype=torch.long, device=device)
+        self.groups, self.buffers = [], []
+        for (rows, width) in zip(by_pools, widths):
+            members = [sessions[r] for r in rows]
+            pools = members[0]._pools
+            n = len(rows)
+            ints = torch.zeros(n * width + 5 * n, dtype=torch.int32, device=device)
+            table = ints[: n * width].view(n, width)
+            nbs, lo, hi, slots, positions = ints[n * width:].view(5, n).unbind(0)
+            needs = any(s._needs_attention for s in members)
+            mass = torch.zeros(n, width, dtype=torch.float32, device=device) if needs else None
+            plan = PagedDecodePlan(
+                batch=n, num_query_heads=arch["hq"], dev_pool=pools.dev_pool, host_pool=pools.host_pool.tensor,
+                num_layers=arch["layers"], tokens_per_block=pools.tokens_per_block, block_table=table, num_blocks=nbs,
+                max_row_tokens=width * pools.tokens_per_block, valid_lo=lo, valid_hi=hi, scale=arch["scale"],
+                mass_accum=mass, mass_mode="row_mean" if needs else "none", host_read="zero_copy")
+            index = None if len(by_pools) == 1 else torch.tensor(rows, dtype=torch.long, device=device)
+            self.groups.append(AttentionGroup(pools, plan, slots, positions, index))
+            self.buffers.append((rows, width, ints, mass))
+        self.graph = None
+        self.logits = None
+
+    def _run(self):
+        from .paged_model import run_decoder_step
+
+        for _, _, _, mass in self.buffers:
+            if mass is not None:
+                mass.zero_()
+        return run_decoder_step(self.model, self.arch, self.groups, self.input_ids, self.position_ids)
+
+    def step(self, sessions, next_input_ids, pos_ids):
+        for rows, width, ints, _ in self.buffers:
+            ints.copy_(_group_ints([sessions[r] for r in rows], self.arch, width))
+        self.input_ids.copy_(torch.tensor(next_input_ids, dtype=torch.long)[:, None])
+        self.position_ids.copy_(torch.tensor(pos_ids, dtype=torch.long)[:, None])
+        if self.graph is None:
+            cur = torch.cuda.current_stream()
+            side = torch.cuda.Stream()
+            side.wait_stream(cur)
+            with torch.cuda.stream(side):
+                self._run()
+            cur.wait_stream(side)
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                self.logits = self._run()
+            self.graph = graph
+        self.graph.replay()
+        return self.logits
+
+
+_BATCHED_GRAPH: list = []  # the last captured batched step (one at a time: each holds its own memory)
+
+
+def _batched_graph_for(sessions, by_pools, arch, device):
+    from .paged_model import _DecodeGraph
+
+    groups = list(by_pools.values())
+    widths = [_DecodeGraph.width_for(max(sessions[r]._num_blocks for r in rows)) for rows in groups]
+    key = (tuple(id(s) for s in sessions),
+           tuple((id(sessions[rows[0]]._pools), sessions[rows[0]]._pools.version, w,
+                  any(sessions[r]._needs_attention for r in rows)) for rows, w in zip(groups, widths)))
+    if _BATCHED_GRAPH and _BATCHED_GRAPH[0].key == key:
+        return _BATCHED_GRAPH[0]
+    _BATCHED_GRAPH.clear()  # release the previous graph's memory before capturing the next
+    g = _BatchedGraph(key, sessions, groups, arch, widths, device)
+    _BATCHED_GRAPH.append(g)
+    return g
+
+
 @torch.inference_mode()
 def batched_decode_step(sessions: list, next_input_ids: list[int], device) -> list[torch.Tensor]:
     """Advance single-row ``PagedModel`` sessions by one token each in one model forward
@@ -296,6 +402,17 @@ def batched_decode_step(sessions: list, next_input_ids: list[int], device) -> li
     first = sessions[0]
     a = first._arch()
     S = len(sessions)
+    pos_ids = [s._total - int(s._pad[0]) for s in sessions]  # RoPE position of the new token
+    if all(getattr(s, "decode_graphs", False) for s in sessions):
+        g = _batched_graph_for(sessions, by_pools, a, device)
+        logits = g.step(sessions, next_input_ids, pos_ids)
+        for rows, _, _, mass in g.buffers:
+            for i, r in enumerate(rows):
+                s = sessions[r]
+                s._finish_token(mass[i, :s._num_blocks] if (mass is not None and s._needs_attention) else None)
+                s._note_fed_token(int(next_input_ids[r]))
+                s.last_host_read = "zero_copy"
+        return [logits[r, -1, :] for r in range(S)]
     groups, masses = [], []
     for rows in by_pools.values():
         members = [sessions[r] for r in rows]
@@ -303,7 +420,6 @@ def batched_decode_step(sessions: list, next_input_ids: list[int], device) -> li
         index = None if len(by_pools) == 1 else torch.tensor(rows, dtype=torch.long, device=device)
         groups.append(AttentionGroup(members[0]._pools, plan, slots, positions, index))
         masses.append((rows, mass))
-    pos_ids = [s._total - int(s._pad[0]) for s in sessions]  # RoPE position of the new token
     input_ids = torch.tensor(next_input_ids, dtype=torch.long, device=device)[:, None]
     position_ids = torch.tensor(pos_ids, dtype=torch.long, device=device)[:, None]
     logits = run_decoder_step(first.model, a, groups, input_ids, position_ids)

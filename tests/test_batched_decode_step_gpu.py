@@ -99,3 +99,42 @@ def test_scheduler_style_private_pool_sessions_with_a_generate_fallback():
         s.reset()
     shared.close()
     assert batched_decode_step([], [], "cuda") == []
+
+
+def test_captured_batched_steps_match_eager_batched_steps():
+    """Batched steps replayed from a CUDA graph (sessions created with the default ``decode_graphs``)
+    give the same tokens and tiers as eager batched steps: two pool groups (three sessions sharing
+    pools, one on its own), mixed policies, and a session leaving mid-way (a new capture)."""
+    from test_paged_model_gpu import _model
+
+    from pager_hf.batched_decode import batched_decode_step
+    from pager_hf.kv_block_store import KVPools
+    from pager_hf.paged_model import PagedModel
+
+    model = _model("qwen2")
+    cfg = model.config
+    g = torch.Generator().manual_seed(21)
+    prompts = [torch.randint(0, 2000, (1, n), generator=g).cuda() for n in (120, 61, 35, 90)]
+    policies = ["sinks_heavy_hitter", "recent_only", "heavy_hitter", "sinks_heavy_hitter"]
+    runs = {}
+    for graphs in (False, True):
+        pools = KVPools(num_layers=cfg.num_hidden_layers, kv_heads=cfg.num_key_value_heads, head_dim=64,
+                        tokens_per_block=16, dtype=torch.float16, device="cuda", gpu_groups=16, cpu_groups=16)
+        sessions, tokens = [], []
+        for i, (ids, pol) in enumerate(zip(prompts, policies)):
+            pm = PagedModel(model, vram_budget=2 * BLOCK, ram_budget=1000 * BLOCK, recent_window=1, policy=pol,
+                            tokens_per_block=16, pools=pools if i < 3 else None, decode_graphs=graphs)
+            tokens.append(pm.generate(ids, torch.ones_like(ids), 1))
+            sessions.append(pm)
+        live = list(range(4))
+        for step in range(20):
+            if step == 12:
+                live.remove(1)  # a session leaves the batch
+            logits = batched_decode_step([sessions[r] for r in live], [tokens[r][-1] for r in live], "cuda")
+            for r, lg in zip(live, logits):
+                tokens[r].append(int(lg.argmax()))
+        runs[graphs] = (tokens, [sorted(s._store.gpu_block_ids()) for s in sessions])
+        for s in sessions:
+            s.reset()
+        pools.close()
+    assert runs[True] == runs[False]

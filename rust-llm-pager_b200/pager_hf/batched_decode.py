@@ -320,6 +320,7 @@ class _BatchedGraph:
             index = None if len(by_pools) == 1 else torch.tensor(rows, dtype=torch.long, device=device)
             self.groups.append(AttentionGroup(pools, plan, slots, positions, index))
             self.buffers.append((rows, width, ints, mass))
+        self.device = torch.device(device)
         self.graph = None
         self.logits = None
 
@@ -336,22 +337,25 @@ class _BatchedGraph:
             ints.copy_(_group_ints([sessions[r] for r in rows], self.arch, width))
         self.input_ids.copy_(torch.tensor(next_input_ids, dtype=torch.long)[:, None])
         self.position_ids.copy_(torch.tensor(pos_ids, dtype=torch.long)[:, None])
-        if self.graph is None:
-            cur = torch.cuda.current_stream()
-            side = torch.cuda.Stream()
-            side.wait_stream(cur)
-            with torch.cuda.stream(side):
-                self._run()
-            cur.wait_stream(side)
-            graph = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(graph):
-                self.logits = self._run()
-            self.graph = graph
-        self.graph.replay()
+        with torch.cuda.device(self.device):
+            if self.graph is None:
+                cur = torch.cuda.current_stream()
+                side = torch.cuda.Stream()
+                side.wait_stream(cur)
+                with torch.cuda.stream(side):
+                    self._run()
+                cur.wait_stream(side)
+                graph = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(graph, capture_error_mode="thread_local"):
+                    self.logits = self._run()
+                self.graph = graph
+            self.graph.replay()
         return self.logits
 
 
-_BATCHED_GRAPH: list = []  # the last captured batched step (one at a time: each holds its own memory)
+# The last captured batched step per device (one at a time per device: each holds its own memory;
+# per device, so that scheduler threads driving different GPUs keep their own).
+_BATCHED_GRAPH: dict = {}
 
 
 def _batched_graph_for(sessions, by_pools, arch, device):
@@ -362,11 +366,13 @@ def _batched_graph_for(sessions, by_pools, arch, device):
     key = (tuple(id(s) for s in sessions),
            tuple((id(sessions[rows[0]]._pools), sessions[rows[0]]._pools.version, w,
                   any(sessions[r]._needs_attention for r in rows)) for rows, w in zip(groups, widths)))
-    if _BATCHED_GRAPH and _BATCHED_GRAPH[0].key == key:
-        return _BATCHED_GRAPH[0]
-    _BATCHED_GRAPH.clear()  # release the previous graph's memory before capturing the next
+    dev = torch.device(device).index
+    cached = _BATCHED_GRAPH.get(dev)
+    if cached is not None and cached.key == key:
+        return cached
+    _BATCHED_GRAPH.pop(dev, None)  # release the previous graph's memory before capturing the next
     g = _BatchedGraph(key, sessions, groups, arch, widths, device)
-    _BATCHED_GRAPH.append(g)
+    _BATCHED_GRAPH[dev] = g
     return g
 
 

@@ -161,6 +161,7 @@ class _DecodeGraph:
             num_blocks=self.num_blocks, max_row_tokens=w * pm.tokens_per_block,
             valid_lo=self.lo, valid_hi=self.hi, scale=arch["scale"], mass_accum=self.mass,
             mass_mode="batch_mean" if self.mass is not None else "none", host_read="zero_copy")
+        self.device = torch.device(dev)
         self.graph = None
         self.logits = None
 
@@ -177,19 +178,21 @@ class _DecodeGraph:
 
     def step(self) -> torch.Tensor:
         """Run the loaded step: the first time eagerly on a side stream (the step's own values, so
-        its tail write is the one the replay repeats), then captured; afterwards by replay."""
-        if self.graph is None:
-            cur = torch.cuda.current_stream()
-            side = torch.cuda.Stream()
-            side.wait_stream(cur)
-            with torch.cuda.stream(side):
-                self._run()
-            cur.wait_stream(side)
-            graph = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(graph):
-                self.logits = self._run()
-            self.graph = graph
-        self.graph.replay()
+        its tail write is the one the replay repeats), then captured; afterwards by replay.  The
+        capture is thread-local: threads driving other GPUs in the same process are not affected."""
+        with torch.cuda.device(self.device):
+            if self.graph is None:
+                cur = torch.cuda.current_stream()
+                side = torch.cuda.Stream()
+                side.wait_stream(cur)
+                with torch.cuda.stream(side):
+                    self._run()
+                cur.wait_stream(side)
+                graph = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(graph, capture_error_mode="thread_local"):
+                    self.logits = self._run()
+                self.graph = graph
+            self.graph.replay()
         return self.logits
 
 

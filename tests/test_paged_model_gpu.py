@@ -189,3 +189,42 @@ def test_captured_decode_steps_match_eager_steps():
     assert runs[True][0] == runs[False][0]
     assert runs[True][1:3] == runs[False][1:3]
     assert runs[True][3] == "zero_copy"
+
+
+def test_sessions_in_two_threads_capture_and_replay_concurrently():
+    """Two threads, each driving its own session (the serving scheduler's one thread per session or
+    device), decode at the same time while their first steps capture graphs; each thread's tokens
+    equal a sequential run's."""
+    import threading
+
+    from pager_hf.paged_model import PagedModel
+
+    model = _model("qwen2")
+    g = torch.Generator().manual_seed(8)
+    prompts = [torch.randint(0, 2000, (1, n), generator=g).cuda() for n in (170, 90)]
+
+    def run(ids, out, i):
+        torch.cuda.set_device(0)
+        pm = PagedModel(model, vram_budget=2 * BLOCK, ram_budget=1000 * BLOCK, recent_window=1,
+                        policy="sinks_heavy_hitter", tokens_per_block=16)
+        out[i] = pm.generate(ids, torch.ones_like(ids), 30)
+        pm.reset()
+
+    sequential = [None, None]
+    for i, ids in enumerate(prompts):
+        run(ids, sequential, i)
+    concurrent, errors = [None, None], []
+
+    def guarded(ids, i):
+        try:
+            run(ids, concurrent, i)
+        except Exception as e:  # noqa: BLE001 - reported by the assertion below
+            errors.append(e)
+
+    threads = [threading.Thread(target=guarded, args=(ids, i)) for i, ids in enumerate(prompts)]
+    for t in threads:
+        t.start()
+    for t in threads:
+        t.join(timeout=300)
+    assert not errors, errors
+    assert concurrent == sequential

@@ -62,3 +62,18 @@ def test_every_workload_lays_out(name):
     lay = bench.WorkloadLayout(name, seed=7)
     assert lay.bytes_per_step == lay.hbm_bytes + lay.host_bytes > 0
     assert lay.launches_per_step == 2 * lay.L
+
+
+def test_reference_gpu_arm_reports_unavailable_without_the_install(tmp_path, monkeypatch, capsys):
+    """Without the reference installed under baseline/_ref, the GPU comparison arm prints one
+    ``unavailable`` line and succeeds, leaving the import path alone."""
+    import argparse
+    import json
+
+    monkeypatch.setattr(bench, "REF_INSTALL", str(tmp_path / "missing"))
+    before = list(sys.path)
+    args = argparse.Namespace(workload="hbm-32k", steps=1, warmup=1, gpus=1)
+    assert bench.run_reference_gpu_arm(args) == 0
+    line = json.loads(capsys.readouterr().out.strip())
+    assert line["impl"] == "reference-gpu" and "baseline/_ref" in line["unavailable"]
+    assert sys.path == before

@@ -234,13 +234,16 @@ def _validate_sessions(sessions: list, next_input_ids: list[int]) -> None:
 
 
 def _group_plan(group: list, arch: dict, pools: KVPools, device: torch.device):
-    """The fused op's plan for single-row sessions that share ``pools``: one block-table row per
-    session (its blocks on either tier, then its tail slot), per-row valid ranges (left padding,
-    sliding window), and the per-row block-mass output when any session scores blocks."""
+    """The fused op's plans for single-row sessions that share ``pools`` (one per distinct sliding
+    window of the model): one block-table row per session (its blocks on either tier, then its tail
+    slot), per-row valid ranges (left padding, sliding window), and the per-row block-mass output
+    when any session scores blocks."""
+    from .paged_model import window_lo
+
     S, tpb = len(group), pools.tokens_per_block
     width = max(s._num_blocks for s in group) + 1
     table = torch.full((S, width), -1, dtype=torch.int32)
-    lo, hi, slots, positions = [], [], [], []
+    los, hi, slots, positions = [[] for _ in arch["windows"]], [], [], []
     for r, s in enumerate(group):
         nb = s._num_blocks
         if nb:
@@ -248,29 +251,36 @@ def _group_plan(group: list, arch: dict, pools: KVPools, device: torch.device):
         table[r, nb] = s._tail_group  # single-row groups: the group is the slot
         total = s._total + 1  # columns including this step's token
         pad = int(s._pad[0])
-        lo.append(max(pad, total - int(arch["window"])) if arch["window"] is not None else pad)
+        for lo, w in zip(los, arch["windows"]):
+            lo.append(window_lo(pad, total, w))
         hi.append(total)
         slots.append(s._tail_group)
         positions.append(s._tail_len)
     i32 = dict(dtype=torch.int32, device=device)
     needs = any(s._needs_attention for s in group)
     mass = torch.zeros(S, width, dtype=torch.float32, device=device) if needs else None
-    plan = PagedDecodePlan(
+    table_dev = table.to(device)
+    num_blocks = torch.tensor([s._num_blocks + 1 for s in group], **i32)
+    valid_hi = torch.tensor(hi, **i32)
+    plans = [PagedDecodePlan(
         batch=S, num_query_heads=arch["hq"], dev_pool=pools.dev_pool, host_pool=pools.host_pool.tensor,
-        num_layers=arch["layers"], tokens_per_block=tpb, block_table=table.to(device),
-        num_blocks=torch.tensor([s._num_blocks + 1 for s in group], **i32), max_row_tokens=width * tpb,
-        valid_lo=torch.tensor(lo, **i32) if any(lo) else None, valid_hi=torch.tensor(hi, **i32),
-        scale=arch["scale"], mass_accum=mass, mass_mode="row_mean" if needs else "none", host_read=group[0].host_read)
-    return plan, mass, torch.tensor(slots, **i32), torch.tensor(positions, **i32)
+        num_layers=arch["layers"], tokens_per_block=tpb, block_table=table_dev, num_blocks=num_blocks,
+        max_row_tokens=width * tpb, valid_lo=torch.tensor(lo, **i32) if any(lo) else None, valid_hi=valid_hi,
+        scale=arch["scale"], softcap=arch["softcap"], mass_accum=mass, mass_mode="row_mean" if needs else "none",
+        host_read=group[0].host_read) for lo in los]
+    return plans, mass, torch.tensor(slots, **i32), torch.tensor(positions, **i32)
 
 
 def _group_ints(group: list, arch: dict, width: int) -> torch.Tensor:
     """The per-step int32 inputs of one pools group, packed as a captured step reads them: the block
     table ``[rows, width]`` (each row's blocks, its tail slot, then absent columns), then per row the
-    block count (blocks + tail), valid range ``[lo, hi)``, tail slot and tail position."""
-    S = len(group)
+    block count (blocks + tail), range end, tail slot, tail position and the first attended column
+    for each distinct sliding window."""
+    from .paged_model import window_lo
+
+    S, nw = len(group), len(arch["windows"])
     table = torch.full((S, width), -1, dtype=torch.int32)
-    cols = torch.zeros(5, S, dtype=torch.int32)
+    cols = torch.zeros(4 + nw, S, dtype=torch.int32)
     for r, s in enumerate(group):
         nb = s._num_blocks
         if nb:
@@ -279,10 +289,11 @@ def _group_ints(group: list, arch: dict, width: int) -> torch.Tensor:
         total = s._total + 1
         pad = int(s._pad[0])
         cols[0, r] = nb + 1
-        cols[1, r] = max(pad, total - int(arch["window"])) if arch["window"] is not None else pad
-        cols[2, r] = total
-        cols[3, r] = s._tail_group
-        cols[4, r] = s._tail_len
+        cols[1, r] = total
+        cols[2, r] = s._tail_group
+        cols[3, r] = s._tail_len
+        for i, w in enumerate(arch["windows"]):
+            cols[4 + i, r] = window_lo(pad, total, w)
     return torch.cat([table.reshape(-1), cols.reshape(-1)])
 
 
@@ -306,19 +317,21 @@ class _BatchedGraph:
         for (rows, width) in zip(by_pools, widths):
             members = [sessions[r] for r in rows]
             pools = members[0]._pools
-            n = len(rows)
-            ints = torch.zeros(n * width + 5 * n, dtype=torch.int32, device=device)
+            n, nw = len(rows), len(arch["windows"])
+            ints = torch.zeros(n * width + (4 + nw) * n, dtype=torch.int32, device=device)
             table = ints[: n * width].view(n, width)
-            nbs, lo, hi, slots, positions = ints[n * width:].view(5, n).unbind(0)
+            cols = ints[n * width:].view(4 + nw, n).unbind(0)
+            nbs, hi, slots, positions = cols[:4]
             needs = any(s._needs_attention for s in members)
             mass = torch.zeros(n, width, dtype=torch.float32, device=device) if needs else None
-            plan = PagedDecodePlan(
+            plans = [PagedDecodePlan(
                 batch=n, num_query_heads=arch["hq"], dev_pool=pools.dev_pool, host_pool=pools.host_pool.tensor,
                 num_layers=arch["layers"], tokens_per_block=pools.tokens_per_block, block_table=table, num_blocks=nbs,
                 max_row_tokens=width * pools.tokens_per_block, valid_lo=lo, valid_hi=hi, scale=arch["scale"],
-                mass_accum=mass, mass_mode="row_mean" if needs else "none", host_read="zero_copy")
+                softcap=arch["softcap"], mass_accum=mass, mass_mode="row_mean" if needs else "none",
+                host_read="zero_copy") for lo in cols[4:]]
             index = None if len(by_pools) == 1 else torch.tensor(rows, dtype=torch.long, device=device)
-            self.groups.append(AttentionGroup(pools, plan, slots, positions, index))
+            self.groups.append(AttentionGroup(pools, plans, slots, positions, index))
             self.buffers.append((rows, width, ints, mass))
         self.device = torch.device(device)
         self.graph = None
@@ -422,9 +435,9 @@ def batched_decode_step(sessions: list, next_input_ids: list[int], device) -> li
     groups, masses = [], []
     for rows in by_pools.values():
         members = [sessions[r] for r in rows]
-        plan, mass, slots, positions = _group_plan(members, a, members[0]._pools, device)
+        plans, mass, slots, positions = _group_plan(members, a, members[0]._pools, device)
         index = None if len(by_pools) == 1 else torch.tensor(rows, dtype=torch.long, device=device)
-        groups.append(AttentionGroup(members[0]._pools, plan, slots, positions, index))
+        groups.append(AttentionGroup(members[0]._pools, plans, slots, positions, index))
         masses.append((rows, mass))
     input_ids = torch.tensor(next_input_ids, dtype=torch.long, device=device)[:, None]
     position_ids = torch.tensor(pos_ids, dtype=torch.long, device=device)[:, None]

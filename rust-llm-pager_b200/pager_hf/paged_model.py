@@ -44,7 +44,14 @@ from .streaming_attention import PagedDecodePlan
 logger = logging.getLogger(__name__)
 
 _POLICIES_WITHOUT_ATTENTION_SIGNAL = frozenset({"recent_only", "sinks_recent"})
-_SUPPORTED_MODEL_TYPES = frozenset({"qwen2", "llama", "mistral"})
+# The families the reference verified its patched forward on (``paged_model.py:81-85``).
+_SUPPORTED_MODEL_TYPES = frozenset({"qwen2", "qwen2_moe", "starcoder2", "llama", "mistral", "gemma", "phi3", "gemma2"})
+# Families whose attention takes its window from the config (every layer); the others keep a
+# per-layer ``sliding_window`` on the attention module (Gemma2 and Qwen2 alternate by layer type).
+_CONFIG_WINDOW_MODEL_TYPES = frozenset({"mistral", "phi3", "starcoder2"})
+# Families whose decode step cannot be captured in a CUDA graph: Qwen2-MoE's sparse block routes
+# tokens to experts with offsets copied from host memory each step.
+_EAGER_ONLY_MODEL_TYPES = frozenset({"qwen2_moe"})
 
 
 @dataclass
@@ -69,12 +76,13 @@ def _rope_fn(model):
 
 @dataclass
 class AttentionGroup:
-    """Rows of a decode batch whose KV lives in one ``KVPools``: the fused op's plan over them, each
-    row's tail slot and the token index in it that the row's new K/V goes to.  ``rows``: the rows'
-    indices in the batch (device int64), or None for every row of the batch in order."""
+    """Rows of a decode batch whose KV lives in one ``KVPools``: the fused op's plans over them (one
+    per distinct sliding window of the model, ``arch["windows"]``; layers use the plan of their
+    window), each row's tail slot and the token index in it that the row's new K/V goes to.
+    ``rows``: the rows' indices in the batch (device int64), or None for every row in order."""
 
     pools: KVPools
-    plan: PagedDecodePlan
+    plans: list
     slots: torch.Tensor
     positions: torch.Tensor
     rows: torch.Tensor | None = None
@@ -82,9 +90,11 @@ class AttentionGroup:
 
 def run_decoder_step(model, arch: dict, groups: list[AttentionGroup], input_ids, position_ids):
     """One token per row through the decoder: embeddings, then per layer the input norm, q/k/v
-    projections and RoPE from the model for all rows at once; per group of rows sharing pools, the
-    new K/V written into each row's tail slot (``pager_append_tokens``) and one fused paged attention
-    launch of the group's plan; o_proj, the residual and the MLP for all rows; final norm and lm_head.
+    projections (fused ``qkv_proj`` for Phi3) and RoPE from the model for all rows at once; per group
+    of rows sharing pools, the new K/V written into each row's tail slot (``pager_append_tokens``)
+    and one fused paged attention launch of the group's plan for this layer's window; o_proj, the
+    residual and the MLP for all rows (Gemma2: normalized attention output and MLP between its
+    pre/post feed-forward norms); final norm, lm_head and Gemma2's final logit softcap.
     Returns logits ``[rows, 1, vocab]``."""
     B = input_ids.shape[0]
     a = arch
@@ -101,9 +111,15 @@ def run_decoder_step(model, arch: dict, groups: list[AttentionGroup], input_ids,
         residual = hidden
         h = layer.input_layernorm(hidden)
         attn = layer.self_attn
-        q = attn.q_proj(h).view(B, 1, -1, a["d"]).transpose(1, 2)
-        k = attn.k_proj(h).view(B, 1, -1, a["d"]).transpose(1, 2)
-        v = attn.v_proj(h).view(B, 1, -1, a["d"]).transpose(1, 2)
+        if a["qkv_fused"]:
+            qkv = attn.qkv_proj(h)
+            nq, nkv = a["hq"] * a["d"], a["hkv"] * a["d"]
+            q, k, v = qkv[..., :nq], qkv[..., nq:nq + nkv], qkv[..., nq + nkv:]
+        else:
+            q, k, v = attn.q_proj(h), attn.k_proj(h), attn.v_proj(h)
+        q = q.view(B, 1, -1, a["d"]).transpose(1, 2)
+        k = k.view(B, 1, -1, a["d"]).transpose(1, 2)
+        v = v.view(B, 1, -1, a["d"]).transpose(1, 2)
         q, k = rope(q, k, cos, sin)
         q, k, v = q[:, :, 0], k[:, :, 0], v[:, :, 0]
         for g, part in zip(groups, parts):
@@ -116,13 +132,26 @@ def run_decoder_step(model, arch: dict, groups: list[AttentionGroup], input_ids,
                                             a["layers"], li, a["hkv"], p.tokens_per_block, a["d"],
                                             g.slots.data_ptr(), g.positions.data_ptr(), gk.data_ptr(), gv.data_ptr(),
                                             gk.shape[0], stream))
-            g.plan.run(gq, li, part)
+            g.plans[a["layer_window"][li]].run(gq, li, part)
             if g.rows is not None:
                 out.index_copy_(0, g.rows, part)
-        hidden = residual + attn.o_proj(out.reshape(B, 1, -1))
-        residual = hidden
-        hidden = residual + layer.mlp(layer.post_attention_layernorm(hidden))
-    return model.lm_head(model.model.norm(hidden))
+        attn_out = attn.o_proj(out.reshape(B, 1, -1))
+        if a["sandwich_norms"]:  # Gemma2DecoderLayer
+            hidden = residual + layer.post_attention_layernorm(attn_out)
+            hidden = hidden + layer.post_feedforward_layernorm(layer.mlp(layer.pre_feedforward_layernorm(hidden)))
+        else:
+            hidden = residual + attn_out
+            hidden = hidden + layer.mlp(layer.post_attention_layernorm(hidden))
+    logits = model.lm_head(model.model.norm(hidden))
+    if a["final_softcap"]:
+        logits = torch.tanh(logits / a["final_softcap"]) * a["final_softcap"]
+    return logits
+
+
+def window_lo(pad: int, total: int, window) -> int:
+    """First attended column of a row: after its left padding and, with a sliding window, within the
+    last ``window`` columns (``paged_model.py:975-980``)."""
+    return max(pad, total - int(window)) if window is not None else pad
 
 
 class _DecodeGraph:
@@ -132,8 +161,8 @@ class _DecodeGraph:
     (norms, projections, RoPE, MLP) plus the paged op, ~800 launches per step for a 24-layer
     model.  The graph replays them with one launch.  Its inputs live in static device buffers
     refreshed before each replay: the token ids and position ids, and one packed int32 buffer
-    holding the block table, the rows' block counts, valid ranges, tail slots and tail positions
-    (a single host copy per step).  Shapes and pointers the launches bake in -- batch, table width
+    holding the block table, the rows' block counts, range ends, tail slots, tail positions and
+    first attended columns (one per distinct sliding window) -- a single host copy per step.  Shapes and pointers the launches bake in -- batch, table width
     (``width`` block columns, a multiple of ``WIDTH_STEP`` at least the blocks plus the tail; it
     also bounds the split plan), the pools (their ``version`` changes when they grow) -- form the
     key, so a new graph is captured once per ``WIDTH_STEP`` blocks; columns past a row's blocks
@@ -148,19 +177,21 @@ class _DecodeGraph:
     def __init__(self, pm, arch: dict, key: tuple, B: int, width: int, dev):
         p = pm._pools
         self.key, self.pm, self.arch, self.pools, self.B, self.width = key, pm, arch, p, B, width
-        w = width
-        self.ints = torch.zeros(B * w + 5 * B, dtype=torch.int32, device=dev)
+        w, nw = width, len(arch["windows"])
+        self.ints = torch.zeros(B * w + (4 + nw) * B, dtype=torch.int32, device=dev)
         self.table = self.ints[: B * w].view(B, w)
-        self.num_blocks, self.lo, self.hi, self.slots, self.positions = self.ints[B * w:].view(5, B).unbind(0)
+        cols = self.ints[B * w:].view(4 + nw, B).unbind(0)
+        self.num_blocks, self.hi, self.slots, self.positions = cols[:4]
+        self.los = cols[4:]  # first attended column per row, one per distinct window
         self.input_ids = torch.zeros(B, 1, dtype=torch.long, device=dev)
         self.position_ids = torch.zeros(B, 1, dtype=torch.long, device=dev)
         self.mass = torch.zeros(w, dtype=torch.float32, device=dev) if pm._needs_attention else None
-        self.plan = PagedDecodePlan(
+        self.plans = [PagedDecodePlan(
             batch=B, num_query_heads=arch["hq"], dev_pool=p.dev_pool, host_pool=p.host_pool.tensor,
             num_layers=arch["layers"], tokens_per_block=pm.tokens_per_block, block_table=self.table,
-            num_blocks=self.num_blocks, max_row_tokens=w * pm.tokens_per_block,
-            valid_lo=self.lo, valid_hi=self.hi, scale=arch["scale"], mass_accum=self.mass,
-            mass_mode="batch_mean" if self.mass is not None else "none", host_read="zero_copy")
+            num_blocks=self.num_blocks, max_row_tokens=w * pm.tokens_per_block, valid_lo=lo, valid_hi=self.hi,
+            scale=arch["scale"], softcap=arch["softcap"], mass_accum=self.mass,
+            mass_mode="batch_mean" if self.mass is not None else "none", host_read="zero_copy") for lo in self.los]
         self.device = torch.device(dev)
         self.graph = None
         self.logits = None
@@ -173,7 +204,7 @@ class _DecodeGraph:
     def _run(self):
         if self.mass is not None:
             self.mass.zero_()
-        group = AttentionGroup(self.pools, self.plan, self.slots, self.positions)
+        group = AttentionGroup(self.pools, self.plans, self.slots, self.positions)
         return run_decoder_step(self.pm.model, self.arch, [group], self.input_ids, self.position_ids)
 
     def step(self) -> torch.Tensor:
@@ -214,8 +245,10 @@ class PagedModel:
         self.host_read = host_read
         self.last_host_read: str | None = None  # the host-tier read mode of the last decode step's plan
         # decode steps captured and replayed as CUDA graphs (host tier read zero-copy); staged host
-        # reads keep the eager step
-        self.decode_graphs = bool(decode_graphs) and host_read != "staged"
+        # reads and models whose step cannot be captured keep the eager step
+        self.decode_graphs = (bool(decode_graphs) and host_read != "staged"
+                              and getattr(getattr(model, "config", None), "model_type", None)
+                              not in _EAGER_ONLY_MODEL_TYPES)
         # pools shared with other single-row sessions (``batched_decode_step`` decodes them in one
         # launch); None: the session allocates its own
         if pools is not None and (pools.rows_per_group != 1 or pools.tokens_per_block != tokens_per_block):
@@ -330,12 +363,22 @@ class PagedModel:
         model_type = getattr(cfg, "model_type", None)
         if model_type not in _SUPPORTED_MODEL_TYPES:
             raise NotImplementedError(f"PagedModel doesn't recognize model_type={model_type!r}.")
-        attn = self.model.model.layers[0].self_attn
+        layers = self.model.model.layers
+        attn = layers[0].self_attn
         head_dim = getattr(attn, "head_dim", cfg.hidden_size // cfg.num_attention_heads)
-        window = getattr(cfg, "sliding_window", None) if model_type == "mistral" else getattr(attn, "sliding_window",
-                                                                                              None)
-        return dict(layers=len(self.model.model.layers), hq=cfg.num_attention_heads,
-                    hkv=cfg.num_key_value_heads, d=head_dim, scale=attn.scaling, window=window)
+        per_layer = []
+        for layer in layers:
+            if model_type in _CONFIG_WINDOW_MODEL_TYPES:
+                w = getattr(cfg, "sliding_window", None)
+            else:
+                w = getattr(layer.self_attn, "sliding_window", None)
+            per_layer.append(int(w) if w else None)
+        windows = sorted(set(per_layer), key=lambda w: (w is not None, w or 0))  # None (global) first
+        return dict(layers=len(layers), hq=cfg.num_attention_heads, hkv=cfg.num_key_value_heads, d=head_dim,
+                    scale=attn.scaling, windows=windows, layer_window=[windows.index(w) for w in per_layer],
+                    softcap=getattr(attn, "attn_logit_softcapping", None) or None,
+                    final_softcap=getattr(cfg, "final_logit_softcapping", None) or None,
+                    qkv_fused=hasattr(attn, "qkv_proj"), sandwich_norms=hasattr(layers[0], "pre_feedforward_layernorm"))
 
     # ------------------------------------------------------------------ session start
     def _start_session(self, input_ids, attention_mask):
@@ -417,28 +460,29 @@ class PagedModel:
         if nb:
             table[:, :nb] = self._store.block_table(range(nb), device="cpu")
         table[:, nb] = torch.arange(self._tail_group * B, self._tail_group * B + B, dtype=torch.int32)
-        lo = self._pad.clone()
-        if a["window"] is not None:
-            lo = torch.clamp(lo, min=max(0, total - int(a["window"])))
+        pad = self._pad.to("cpu", torch.int32)
+        # first attended column per row, one row of values per distinct sliding window
+        los = [torch.tensor([window_lo(int(x), total, w) for x in pad], dtype=torch.int32) for w in a["windows"]]
         if self.decode_graphs:
-            return self._graph_step(a, B, nb, table, lo, total, input_ids, attention_mask)
+            return self._graph_step(a, B, nb, table, los, total, input_ids, attention_mask)
         i32 = dict(dtype=torch.int32, device=dev)
         mass = torch.zeros(nb + 1, dtype=torch.float32, device=dev) if self._needs_attention else None
-        plan = PagedDecodePlan(
+        table_dev = table.to(dev)
+        plans = [PagedDecodePlan(
             batch=B, num_query_heads=a["hq"], dev_pool=p.dev_pool, host_pool=p.host_pool.tensor,
-            num_layers=a["layers"], tokens_per_block=tpb, block_table=table.to(dev),
+            num_layers=a["layers"], tokens_per_block=tpb, block_table=table_dev,
             num_blocks=torch.full((B,), nb + 1, **i32), max_row_tokens=(nb + 1) * tpb,
             valid_lo=lo.to(dev) if bool((lo > 0).any()) else None, valid_hi=torch.full((B,), total, **i32),
-            scale=a["scale"], mass_accum=mass, mass_mode="batch_mean" if mass is not None else "none",
-            host_read=self.host_read)
-        self.last_host_read = plan.host_read
+            scale=a["scale"], softcap=a["softcap"], mass_accum=mass,
+            mass_mode="batch_mean" if mass is not None else "none", host_read=self.host_read) for lo in los]
+        self.last_host_read = plans[0].host_read
         slots = torch.arange(self._tail_group * B, self._tail_group * B + B, **i32)
         positions = torch.full((B,), self._tail_len, **i32)
         position_ids = self._position_ids_from_mask(attention_mask)[:, -1:]
-        logits = run_decoder_step(self.model, a, [AttentionGroup(p, plan, slots, positions)], input_ids, position_ids)
+        logits = run_decoder_step(self.model, a, [AttentionGroup(p, plans, slots, positions)], input_ids, position_ids)
         return logits, self._finish_token(None if mass is None else mass[:nb])
 
-    def _graph_step(self, a, B, nb, table, lo, total, input_ids, attention_mask):
+    def _graph_step(self, a, B, nb, table, los, total, input_ids, attention_mask):
         """``_forward_step`` through a captured graph (``_DecodeGraph``); same inputs, same result."""
         p = self._pools
         width = _DecodeGraph.width_for(nb)
@@ -450,9 +494,9 @@ class PagedModel:
         wide = torch.full((B, width), -1, dtype=torch.int32)
         wide[:, : nb + 1] = table
         ints = torch.cat([wide.reshape(-1), torch.full((B,), nb + 1, dtype=torch.int32),
-                          lo.to("cpu", torch.int32), torch.full((B,), total, dtype=torch.int32),
+                          torch.full((B,), total, dtype=torch.int32),
                           torch.arange(self._tail_group * B, self._tail_group * B + B, dtype=torch.int32),
-                          torch.full((B,), self._tail_len, dtype=torch.int32)])
+                          torch.full((B,), self._tail_len, dtype=torch.int32)] + los)
         g.load(ints, input_ids, self._position_ids_from_mask(attention_mask)[:, -1:])
         logits = g.step()
         self.last_host_read = "zero_copy"

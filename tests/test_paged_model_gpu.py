@@ -228,3 +228,52 @@ def test_sessions_in_two_threads_capture_and_replay_concurrently():
         t.join(timeout=300)
     assert not errors, errors
     assert concurrent == sequential
+
+
+def _family_model(kind):
+    """Small random-init models of the other families the reference verified (``paged_model.py:81-85``)."""
+    import transformers as T
+
+    torch.manual_seed(0)
+    common = dict(hidden_size=256, intermediate_size=512, num_hidden_layers=4, num_attention_heads=4,
+                  num_key_value_heads=2, head_dim=64, vocab_size=2000, max_position_embeddings=4096,
+                  initializer_range=0.02)
+    extra = {
+        # sliding layers alternate with global ones; the window is shorter than the prompts
+        "gemma2": dict(sliding_window=64, query_pre_attn_scalar=64),
+        "phi3": dict(pad_token_id=0, sliding_window=None),
+        "starcoder2": dict(sliding_window=None),
+        # every expert active: the routing weights stay continuous in the hidden state, so a 1-ulp
+        # difference in attention cannot switch experts
+        "qwen2_moe": dict(moe_intermediate_size=128, shared_expert_intermediate_size=256, num_experts=4,
+                          num_experts_per_tok=4),
+        "gemma": {},
+    }[kind]
+    cls = {"gemma": (T.GemmaConfig, T.GemmaForCausalLM), "gemma2": (T.Gemma2Config, T.Gemma2ForCausalLM),
+           "phi3": (T.Phi3Config, T.Phi3ForCausalLM), "starcoder2": (T.Starcoder2Config, T.Starcoder2ForCausalLM),
+           "qwen2_moe": (T.Qwen2MoeConfig, T.Qwen2MoeForCausalLM)}[kind]
+    m = cls[1](cls[0](**common, **extra))
+    return m.to(device="cuda", dtype=torch.float16).eval()
+
+
+@pytest.mark.parametrize("kind", ["gemma", "gemma2", "phi3", "starcoder2", "qwen2_moe"])
+def test_greedy_tokens_match_unpaged_for_the_other_families(kind):
+    """Gemma (scaled embeddings), Gemma2 (alternating sliding/global layers, attention and final logit
+    softcaps, extra feed-forward norms), Phi3 (fused qkv projection), Starcoder2 (biased projections,
+    LayerNorm) and Qwen2-MoE (sparse MoE feed-forward, whose steps stay eager: its expert routing
+    cannot be captured): greedy tokens of captured decode steps, and of eager ones, match unpaged HF
+    greedy decoding with most blocks in the host tier."""
+    from pager_hf.paged_model import PagedModel
+
+    model = _family_model(kind)
+    g = torch.Generator().manual_seed(11)
+    ids = torch.randint(0, 2000, (1, 150), generator=g).cuda()
+    mask = torch.ones_like(ids)
+    want, logits = _hf_greedy(model, ids, mask, 24)
+    for graphs in (True, False):
+        pm = PagedModel(model, vram_budget=2 * BLOCK, ram_budget=1000 * BLOCK, recent_window=1,
+                        policy="sinks_heavy_hitter", tokens_per_block=16, decode_graphs=graphs)
+        assert pm.decode_graphs == (graphs and kind != "qwen2_moe")
+        _assert_greedy_match(pm.generate(ids, mask, 24), want[0], logits)
+        assert pm._store.cpu_block_ids(), "no block reached the host tier"
+        pm.reset()

@@ -567,7 +567,7 @@ Scratch layout_scratch(char* base, long long rows, int max_splits, int head_dim,
 
 int backend_for(int requested, int kv_dtype, int head_dim) {
   if (requested == PAGER_BACKEND_MMA || requested == PAGER_BACKEND_FMA) return requested;
-  if (kv_dtype != PAGER_DTYPE_F32 && (head_dim == 64 || head_dim == 128)) return PAGER_BACKEND_MMA;
+  if (kv_dtype != PAGER_DTYPE_F32 && (head_dim == 64 || head_dim == 128 || head_dim == 256)) return PAGER_BACKEND_MMA;
   return PAGER_BACKEND_FMA;
 }
 

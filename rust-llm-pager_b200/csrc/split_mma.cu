@@ -1,4 +1,4 @@
-// Tensor-core (mma.sync m16n8k16, fp32 accumulate) split kernels: fp16 / bf16 KV, head_dim 64 / 128.
+// Tensor-core (mma.sync m16n8k16, fp32 accumulate) split kernels: fp16 / bf16 KV, head_dim 64 / 128 / 256.
 #include "split_inst.cuh"
 
 namespace pager {
@@ -7,6 +7,7 @@ bool lookup_split_mma(int kv_dtype, int head_dim, int mode, SplitKernelInfo* out
     switch (head_dim) {
       PAGER_MODE_CASES(__half, 64, BACKEND_MMA)
       PAGER_MODE_CASES(__half, 128, BACKEND_MMA)
+      PAGER_MODE_CASES(__half, 256, BACKEND_MMA)
       default: return false;
     }
   }
@@ -14,6 +15,7 @@ bool lookup_split_mma(int kv_dtype, int head_dim, int mode, SplitKernelInfo* out
     switch (head_dim) {
       PAGER_MODE_CASES(__nv_bfloat16, 64, BACKEND_MMA)
       PAGER_MODE_CASES(__nv_bfloat16, 128, BACKEND_MMA)
+      PAGER_MODE_CASES(__nv_bfloat16, 256, BACKEND_MMA)
       default: return false;
     }
   }

@@ -81,6 +81,9 @@ CASES = {
     # TinyLlama geometry (n_rep 8), a general 0/1 mask with holes, tpb 32
     "gqa8_d64_f16_holes": dict(kind="two_pass", seed=12, B=2, Hq=32, Hkv=4, D=64, tpb=32, nb=7, tail=3,
                                group_blocks=4, dtype="f16", holes=0.25),
+    # Gemma geometry (head_dim 256, n_rep 2), left-padded rows, two-pass with block mass
+    "gemma_d256_f16_padded": dict(kind="two_pass", seed=15, B=2, Hq=8, Hkv=4, D=256, tpb=16, nb=6, tail=5,
+                                  group_blocks=2, dtype="f16", pad_prefix=[0, 20]),
     # cross-session batched decode (batched_decode.py): block counts 6, 2, 0; tail 4 (+1 new token)
     "batched_sessions_f16": dict(kind="batched", seed=13, Hq=14, Hkv=2, D=64, tpb=16, nbs=[6, 2, 0], tail=4,
                                  group_blocks=4, dtype="f16"),

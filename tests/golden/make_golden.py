@@ -135,12 +135,18 @@ def run_batched(sa, ref_tests, name, c):
 
 
 def main():
-    if len(sys.argv) != 2:
-        sys.exit("usage: python tests/golden/make_golden.py /path/to/rust-llm-pager")
+    if len(sys.argv) < 2:
+        sys.exit("usage: python tests/golden/make_golden.py /path/to/rust-llm-pager [case ...]")
     ref_root = sys.argv[1]
+    only = set(sys.argv[2:])
+    unknown = only - set(CASES)
+    if unknown:
+        sys.exit(f"unknown cases: {sorted(unknown)}")
     sa, ref_tests = _load_reference(ref_root)
     runners = {"steps": run_steps, "two_pass": run_two_pass, "batched": run_batched}
     for name, c in CASES.items():
+        if only and name not in only:
+            continue
         res = runners[c["kind"]](sa, ref_tests, name, c)
         np.savez_compressed(os.path.join(HERE, f"{name}.npz"), **res)
         print(f"{name}: {sorted(res)}")

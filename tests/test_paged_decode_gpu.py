@@ -114,6 +114,8 @@ CFGS = [
     (3, 2, 32, 4, 64, 32, 1, [7, 6], [3, 30], torch.float16, set(), [0, 40], [200, 150]),
     (4, 1, 14, 2, 64, 64, 1, [64], [1], torch.float32, set(), None, None),
     (5, 2, 32, 8, 128, 16, 2, [12, 1], [16, 2], torch.float16, {(0, 0), (0, 11)}, None, None),
+    # Gemma geometry: head_dim 256 (tensor cores under "auto"), n_rep 2, a left-padded row
+    (6, 2, 8, 4, 256, 32, 2, [7, 3], [5, 20], torch.bfloat16, set(), [10, 0], None),
 ]
 
 
@@ -183,7 +185,8 @@ def test_row_with_nothing_to_read_next_to_full_rows(mods):
 EXTRA = [
     # (name, seed, B, Hq, Hkv, D, tpb, L, nbs, tails, dtype, kw) -- kw: scale / softcap / backend
     ("softcap_mma_d128", 11, 2, 16, 8, 128, 64, 2, [6, 3], [9, 2], torch.bfloat16, dict(scale=0.0625, softcap=50.0)),
-    ("softcap_fma_d256", 12, 2, 8, 4, 256, 32, 1, [5, 2], [4, 31], torch.bfloat16, dict(scale=1 / 16, softcap=30.0)),
+    ("softcap_d256", 12, 2, 8, 4, 256, 32, 1, [5, 2], [4, 31], torch.bfloat16, dict(scale=1 / 16, softcap=30.0)),
+    ("fp16_d256_n_rep_8", 22, 2, 16, 2, 256, 64, 1, [6, 4], [9, 63], torch.float16, {}),
     ("blocks_of_256", 13, 2, 8, 2, 64, 256, 1, [3, 2], [200, 17], torch.float16, {}),
     ("blocks_of_8", 14, 2, 8, 2, 64, 8, 1, [40, 7], [5, 8], torch.float16, {}),
     ("n_rep_16", 15, 2, 32, 2, 128, 64, 1, [4, 5], [3, 60], torch.float16, {}),

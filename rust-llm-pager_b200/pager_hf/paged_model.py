@@ -162,11 +162,12 @@ class _DecodeGraph:
     model.  The graph replays them with one launch.  Its inputs live in static device buffers
     refreshed before each replay: the token ids and position ids, and one packed int32 buffer
     holding the block table, the rows' block counts, range ends, tail slots, tail positions and
-    first attended columns (one per distinct sliding window) -- a single host copy per step.  Shapes and pointers the launches bake in -- batch, table width
-    (``width`` block columns, a multiple of ``WIDTH_STEP`` at least the blocks plus the tail; it
-    also bounds the split plan), the pools (their ``version`` changes when they grow) -- form the
-    key, so a new graph is captured once per ``WIDTH_STEP`` blocks; columns past a row's blocks
-    are absent.  Host-tier blocks are read zero-copy inside the graph."""
+    first attended columns (one per distinct sliding window) -- a single host copy per step.
+    Shapes and pointers the launches bake in -- batch, table width (``width`` block columns, a
+    multiple of ``WIDTH_STEP`` at least the blocks plus the tail; it also bounds the split plan),
+    the pools (their ``version`` changes when they grow) -- form the key, so a new graph is
+    captured once per ``WIDTH_STEP`` blocks; columns past a row's blocks are absent.  Host-tier
+    blocks are read zero-copy inside the graph."""
 
     WIDTH_STEP = 64
 

@@ -367,7 +367,9 @@ class _BatchedGraph:
 
 
 # The last captured batched step per device (one at a time per device: each holds its own memory;
-# per device, so that scheduler threads driving different GPUs keep their own).
+# per device, so that scheduler threads driving different GPUs keep their own).  A cached graph keeps
+# its sessions' pools referenced until a batched step of another composition on that device
+# replaces it.
 _BATCHED_GRAPH: dict = {}
 
 
@@ -376,7 +378,8 @@ def _batched_graph_for(sessions, by_pools, arch, device):
 
     groups = list(by_pools.values())
     widths = [_DecodeGraph.width_for(max(sessions[r]._num_blocks for r in rows)) for rows in groups]
-    key = (tuple(id(s) for s in sessions),
+    # a cached graph references its model and pools, so their ids cannot be reused while it is cached
+    key = (id(sessions[0].model), tuple(id(s) for s in sessions),
            tuple((id(sessions[rows[0]]._pools), sessions[rows[0]]._pools.version, w,
                   any(sessions[r]._needs_attention for r in rows)) for rows, w in zip(groups, widths)))
     dev = torch.device(device).index

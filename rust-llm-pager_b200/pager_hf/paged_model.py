@@ -302,7 +302,11 @@ class PagedModel:
         self._primed_tokens += 1
 
     def _acquire_or_raise(self) -> None:
+        """Single-flight guard (``paged_model.py:270-282``): a second concurrent call is logged and
+        rejected instead of waiting."""
         if not self._lock.acquire(blocking=False):
+            logger.warning("PagedModel call rejected: another generate() or reset() is already in flight on "
+                           "this instance.")
             raise RuntimeError(
                 "Another generate() or reset() call is already running on this PagedModel instance. It holds one "
                 "mutable session, so concurrent calls from another thread would corrupt its state rather than run "

@@ -545,6 +545,16 @@ class PagedModel:
                                          if i < len(block_attention)))
         return step
 
+    def _reorder_rows(self, rows: list[int]) -> None:
+        """Row i of the session continues old row ``rows[i]`` (``paged_model.py:612-622``): every block's
+        rows on both tiers (``KVBlockStore.reorder_batch_rows``), the tail slots and the left padding."""
+        self._store.reorder_batch_rows(rows)
+        p = self._pools
+        idx = torch.tensor(rows, dtype=torch.long, device=p.device)
+        tail = p.dev_pool[p.group_slots(self._tail_group)]
+        tail.copy_(tail.index_select(0, idx))
+        self._pad = self._pad.index_select(0, idx.to(self._pad.device))
+
     def _extend_session(self, input_ids, attention_mask):
         total_len = input_ids.shape[-1]
         if total_len - 1 < self._primed_tokens:
@@ -616,5 +626,110 @@ class PagedModel:
                 stats.max_attention_in_gpu = max(in_gpu)
             self.last_run_stats = stats
             return generated[0] if batch_size == 1 else generated
+        finally:
+            self._lock.release()
+
+    @torch.inference_mode()
+    def generate_beam_search(self, input_ids: torch.Tensor, attention_mask: torch.Tensor, num_beams: int,
+                             max_new_tokens: int, *, eos_token_id: int | None = None, length_penalty: float = 1.0,
+                             num_return_sequences: int = 1, do_sample: bool = False, temperature: float = 1.0,
+                             top_k: int | None = None, top_p: float | None = None,
+                             generator: torch.Generator | None = None):
+        """Beam search (``paged_model.py:409-610``): ``num_beams`` hypotheses per prompt, each a row of
+        the session with its own KV history, advanced together one token per step; each step keeps the
+        ``num_beams`` best continuations over all beams of a prompt (or samples them without replacement
+        under ``do_sample``, after temperature / top-k / top-p), and the rows are reordered to their
+        parents (``_reorder_rows``).  Only the first beam of a prompt starts live (the others at -inf);
+        a beam that emitted ``eos_token_id`` may only repeat it at no score change.  Final candidates
+        are ranked per prompt by score / length ** ``length_penalty``.  Every call starts a fresh
+        session and ends it.  Returns, like ``generate``: one list of tokens for one prompt and one
+        sequence, a list of lists for several prompts or several sequences, a list of lists of lists
+        for both."""
+        self._acquire_or_raise()
+        try:
+            batch = input_ids.shape[0]
+            if num_beams < 1:
+                raise ValueError(f"num_beams must be >= 1, got {num_beams}")
+            if not 1 <= num_return_sequences <= num_beams:
+                raise ValueError(f"num_return_sequences must be between 1 and num_beams ({num_beams}), got "
+                                 f"{num_return_sequences}")
+            if do_sample:
+                if temperature <= 0:
+                    raise ValueError(f"temperature must be > 0 for sampling, got {temperature}.")
+                if top_k is not None and top_k < 1:
+                    raise ValueError(f"top_k must be >= 1, got {top_k}.")
+                if top_p is not None and not (0.0 < top_p <= 1.0):
+                    raise ValueError(f"top_p must be in (0, 1], got {top_p}.")
+            self._validate_left_padded(attention_mask)
+            if self._store is not None:  # beam search starts its own session
+                self._release_pools()
+                self._clear_session()
+            device = input_ids.device
+            rows = batch * num_beams
+            ids = input_ids.repeat_interleave(num_beams, dim=0)
+            mask = attention_mask.repeat_interleave(num_beams, dim=0)
+            self._start_session(ids, mask)
+            try:
+                nxt = ids[:, -1:]
+                scores = torch.full((rows,), float("-inf"), dtype=torch.float32, device=device)
+                scores[0::num_beams] = 0.0
+                tokens: list[list[int]] = [[] for _ in range(rows)]
+                finished = [False] * rows
+                group_base = torch.arange(batch, device=device).unsqueeze(1) * num_beams
+                for _ in range(max_new_tokens):
+                    logits, _ = self._forward_step(nxt, mask)
+                    logp = torch.log_softmax(logits[:, -1, :].float(), dim=-1)
+                    vocab = logp.shape[-1]
+                    if eos_token_id is not None and any(finished):
+                        done = torch.tensor(finished, device=device)
+                        frozen = torch.full((vocab,), float("-inf"), device=device)
+                        frozen[eos_token_id] = 0.0
+                        logp = torch.where(done[:, None], frozen[None, :], logp)
+                    cand = logp
+                    if do_sample:
+                        cand = logp / temperature
+                        if top_k is not None:
+                            kth = torch.topk(cand, min(top_k, vocab), dim=-1).values[:, -1, None]
+                            cand = cand.masked_fill(cand < kth, float("-inf"))
+                        if top_p is not None:
+                            srt, order = torch.sort(cand, descending=True, dim=-1)
+                            pr = torch.softmax(srt, dim=-1)
+                            srt = srt.masked_fill(torch.cumsum(pr, dim=-1) - pr > top_p, float("-inf"))
+                            cand = torch.full_like(cand, float("-inf")).scatter(-1, order, srt)
+                        cand = torch.log_softmax(cand, dim=-1)
+                    joint = (scores[:, None] + cand).view(batch, num_beams * vocab)
+                    if do_sample:
+                        pick = torch.multinomial(torch.softmax(joint, dim=-1), num_beams, replacement=False,
+                                                 generator=generator)
+                        best = torch.gather(joint, 1, pick)
+                    else:
+                        best, pick = torch.topk(joint, num_beams, dim=-1)
+                    parents = (pick // vocab + group_base).flatten().tolist()
+                    chosen = (pick % vocab).flatten().tolist()
+                    tokens = [tokens[par] + [tok] for par, tok in zip(parents, chosen)]
+                    finished = [finished[par] or (eos_token_id is not None and tok == eos_token_id)
+                                for par, tok in zip(parents, chosen)]
+                    scores = best.flatten()
+                    self._reorder_rows(parents)
+                    nxt = torch.tensor(chosen, dtype=input_ids.dtype, device=device).unsqueeze(1)
+                    mask = torch.cat([mask[parents], torch.ones((rows, 1), dtype=mask.dtype, device=device)], dim=1)
+                    if all(finished):
+                        break
+            finally:
+                self._release_pools()
+                self._clear_session()
+            results = []
+            for g in range(batch):
+                ranked = []
+                for r in range(g * num_beams, (g + 1) * num_beams):
+                    seq = tokens[r]
+                    if eos_token_id is not None and eos_token_id in seq:
+                        seq = seq[: seq.index(eos_token_id) + 1]
+                    ranked.append((float(scores[r]) / (max(len(seq), 1) ** length_penalty), seq))
+                ranked.sort(key=lambda item: item[0], reverse=True)
+                results.append([seq for _, seq in ranked[:num_return_sequences]])
+            if batch == 1:
+                return results[0][0] if num_return_sequences == 1 else results[0]
+            return [r[0] for r in results] if num_return_sequences == 1 else results
         finally:
             self._lock.release()

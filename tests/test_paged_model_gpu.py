@@ -277,3 +277,45 @@ def test_greedy_tokens_match_unpaged_for_the_other_families(kind):
         _assert_greedy_match(pm.generate(ids, mask, 24), want[0], logits)
         assert pm._store.cpu_block_ids(), "no block reached the host tier"
         pm.reset()
+
+
+def test_beam_search_with_one_beam_is_greedy_decoding():
+    from pager_hf.paged_model import PagedModel
+
+    model = _model("qwen2")
+    g = torch.Generator().manual_seed(41)
+    ids = torch.randint(0, 2000, (1, 120), generator=g).cuda()
+    mask = torch.ones_like(ids)
+    kw = dict(vram_budget=2 * BLOCK, ram_budget=1000 * BLOCK, recent_window=1, policy="sinks_heavy_hitter",
+              tokens_per_block=16)
+    beam = PagedModel(model, **kw).generate_beam_search(ids, mask, num_beams=1, max_new_tokens=20,
+                                                        length_penalty=0.0)
+    assert beam == PagedModel(model, **kw).generate(ids, mask, 20)
+
+
+def test_beam_search_matches_hf_beam_search_in_fp32():
+    """num_beams hypotheses per prompt, rows reordered to their parents every step across both KV
+    tiers and the tail; with fp32 weights (no near-ties at output precision) the result equals
+    transformers' own beam search at length_penalty 0, the setting the reference verified."""
+    from pager_hf.paged_model import PagedModel
+
+    model = _model("qwen2").float()
+    g = torch.Generator().manual_seed(43)
+    lens = [90, 57]
+    T = max(lens)
+    ids = torch.zeros(2, T, dtype=torch.long)
+    mask = torch.zeros(2, T, dtype=torch.long)
+    for b, n in enumerate(lens):
+        ids[b, T - n:] = torch.randint(0, 2000, (n,), generator=g)
+        mask[b, T - n:] = 1
+    ids, mask = ids.cuda(), mask.cuda()
+    pm = PagedModel(model, vram_budget=2 * BLOCK, ram_budget=1000 * BLOCK, recent_window=1,
+                    policy="sinks_heavy_hitter", tokens_per_block=16)
+    got = pm.generate_beam_search(ids, mask, num_beams=3, max_new_tokens=12, length_penalty=0.0)
+    with torch.inference_mode():
+        ref = model.generate(input_ids=ids, attention_mask=mask, num_beams=3, max_new_tokens=12, do_sample=False,
+                             length_penalty=0.0, early_stopping=False, num_return_sequences=1, pad_token_id=0)
+    assert got == ref[:, T:].tolist()
+    three = pm.generate_beam_search(ids[:1], mask[:1], num_beams=3, max_new_tokens=12, length_penalty=0.0,
+                                    num_return_sequences=3)
+    assert len(three) == 3 and three[0] == got[0]

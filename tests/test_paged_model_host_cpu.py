@@ -93,3 +93,22 @@ def test_a_low_temperature_favours_the_argmax():
     gen = torch.Generator().manual_seed(0)
     picks = [_draw(torch.tensor([[3.0, 2.9, 2.8]]), gen, temperature=0.05) for _ in range(20)]
     assert picks.count(0) >= 15
+
+
+# -- beam search arguments (paged_model.py:480-495 of the reference): refused before the model is touched
+@pytest.mark.parametrize("kw,exc", [
+    (dict(num_beams=0, max_new_tokens=2), ValueError),
+    (dict(num_beams=2, max_new_tokens=2, num_return_sequences=3), ValueError),
+    (dict(num_beams=2, max_new_tokens=2, do_sample=True, temperature=0.0), ValueError),
+    (dict(num_beams=2, max_new_tokens=2, do_sample=True, top_k=0), ValueError),
+    (dict(num_beams=2, max_new_tokens=2, do_sample=True, top_p=1.5), ValueError),
+])
+def test_beam_search_argument_checks(kw, exc):
+    pm = _pm()
+    with pytest.raises(exc):
+        pm.generate_beam_search(torch.zeros(1, 2, dtype=torch.long), torch.ones(1, 2, dtype=torch.long), **kw)
+    assert not pm._lock.locked()
+    with pytest.raises(NotImplementedError):  # right padding
+        pm.generate_beam_search(torch.zeros(1, 2, dtype=torch.long), torch.tensor([[1, 0]]), num_beams=2,
+                                max_new_tokens=2)
+    assert not pm._lock.locked()

@@ -488,6 +488,8 @@ class ReferenceGpuWorkload:
         self.window = lay.window
         self.cols = cols
         self.scale = 1.0 / math.sqrt(D)
+        self.two_pass = False
+        self.mass_accum = torch.zeros(nb, dtype=torch.float32, device=device)
 
     def _layer(self, layer: int):
         import torch
@@ -514,9 +516,50 @@ class ReferenceGpuWorkload:
         sa.streaming_attention_step(q, full_tail_key, full_tail_value, m, l, acc, valid=tail_valid, scale=self.scale)
         self.out[layer] = sa.streaming_attention_finalize(acc, l, q.dtype)
 
+    def _layer_two_pass(self, layer: int):
+        """The two-pass sequence the reference runs for mass-scoring placements (heavy_hitter,
+        sinks_heavy_hitter; ``paged_model.py:993-1050``): a stats pass over every gathered group and
+        the tail, then each group gathered again for ``accumulate_step`` (writing ``block_mass``), the
+        tail folded with the final statistics, and the batch-and-head mean of the mass accumulated."""
+        import torch
+
+        sa, lay, device = self.sa, self.lay, self.device
+        q = self.q[layer]
+        m, l, acc = sa.streaming_attention_state_init(lay.B, lay.Hq, lay.D, device)
+        padding_mask = self.padding_mask
+        if self.window is not None:
+            col_positions = torch.arange(padding_mask.shape[1], device=device)
+            window_valid = (col_positions > (self.cols - 1 - self.window)).unsqueeze(0)
+            padding_mask = padding_mask.to(torch.int32) * window_valid.to(torch.int32)
+        full_tail_key = torch.cat([self.tail_k[layer], self.new_k[layer]], dim=2)
+        full_tail_value = torch.cat([self.tail_v[layer], self.new_v[layer]], dim=2)
+        tail_valid = padding_mask[:, self.full_tokens:].to(torch.int32)
+        ids, G, tpb = self.block_ids, self.group, lay.tpb
+        for i in range(0, len(ids), G):
+            group_ids = ids[i: i + G]
+            gk, gv, _, _ = self.gather(layer_idx=layer, block_ids=group_ids, device=device)
+            gvalid = padding_mask[:, i * tpb: (i + len(group_ids)) * tpb].to(torch.int32)
+            sa.streaming_attention_stats_step(q, gk, m, l, valid=gvalid, scale=self.scale)
+            del gk, gv
+        sa.streaming_attention_stats_step(q, full_tail_key, m, l, valid=tail_valid, scale=self.scale)
+        block_mass = torch.zeros(lay.B, lay.Hq, max(len(ids), 1), dtype=torch.float32, device=device)
+        for i in range(0, len(ids), G):
+            group_ids = ids[i: i + G]
+            gk, gv, _, _ = self.gather(layer_idx=layer, block_ids=group_ids, device=device)
+            gvalid = padding_mask[:, i * tpb: (i + len(group_ids)) * tpb].to(torch.int32)
+            sa.streaming_attention_accumulate_step(q, gk, gv, m, l, acc, block_mass, i, tpb, valid=gvalid,
+                                                   scale=self.scale)
+            del gk, gv
+        sa.streaming_attention_fold_fixed_step(q, full_tail_key, full_tail_value, m, l, acc, valid=tail_valid,
+                                               scale=self.scale)
+        self.mass_accum += block_mass.mean(dim=(0, 1))[: len(ids)]
+        self.out[layer] = sa.streaming_attention_finalize(acc, l, q.dtype)
+
     def step(self):
+        if self.two_pass:
+            self.mass_accum.zero_()
         for layer in range(self.lay.L):
-            self._layer(layer)
+            (self._layer_two_pass if self.two_pass else self._layer)(layer)
 
 
 def _import_reference_gpu_path():
@@ -566,6 +609,7 @@ def run_reference_gpu_arm(args):
         return ref_pm.PagedModel._gather_layer_kv_group(holder, **kw)
 
     wl = ReferenceGpuWorkload(args.workload, device, seed=1234, sa=ref_sa, gather=gather)
+    wl.two_pass = bool(getattr(args, "ref_mass", False))
     holder._store = wl.store
     for _ in range(max(args.warmup, 1)):
         wl.step()
@@ -601,10 +645,11 @@ def run_reference_gpu_arm(args):
                 "h2d_bytes_per_step": q_host.numel() * q_host.element_size(),
                 "d2h_bytes_per_step": out_host.numel() * out_host.element_size()},
         "clocks": clk.summary(),
+        "reference_path": ("two-pass with block mass (paged_model.py:993-1050)" if wl.two_pass
+                           else "single pass, no mass (paged_model.py:1055-1072)"),
         "note": "the reference's KVBlockStore, PagedModel._gather_layer_kv_group and Triton streaming_attention_* "
-                "from the unmodified package in baseline/_ref, in the single-pass per-layer order of "
-                "paged_model.py:1055-1072 (the workloads' placements need no attention mass); the Rust pager "
-                "is not on this path",
+                "from the unmodified package in baseline/_ref, in the per-layer order of the reference_path; "
+                "the Rust pager is not on this path",
     }
     print(json.dumps(line), flush=True)
     return 0
@@ -760,6 +805,9 @@ def main():
                     help="ours; reference = the reference's algorithm on the host cores; reference-gpu = the "
                          "reference's own Triton path from baseline/_ref on the same GPU (comparison)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--ref-mass", action="store_true",
+                    help="reference-gpu: the reference's two-pass path that also writes the per-block mass "
+                         "(what its heavy-hitter placements run; ours always emits the mass)")
     ap.add_argument("--host-read", default="auto", choices=["auto", "zero_copy", "staged"],
                     help="host tier: zero-copy kernel reads, copy-engine staging, or pick from the measured link")
     args = ap.parse_args()

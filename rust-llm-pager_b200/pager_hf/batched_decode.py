@@ -225,7 +225,8 @@ def _validate_sessions(sessions: list, next_input_ids: list[int]) -> None:
             raise ValueError("batched_decode_step requires every session to already have an active generate() session.")
         if s.tokens_per_block != first.tokens_per_block:
             raise ValueError("batched_decode_step requires every session to share the same tokens_per_block.")
-        if s._pad is None or s._pad.shape[0] != 1:
+        tail = s._tail_past
+        if not tail or tail[0][0].shape[0] != 1:  # the session's row count, as the reference reads it
             raise ValueError("batched_decode_step only supports single-row (batch_size==1) sessions.")
     if len({id(s) for s in sessions}) != len(sessions):
         raise ValueError("batched_decode_step got the same session twice.")

@@ -286,12 +286,20 @@ class PagedModel:
         ``[rows, kv_heads, tail_len, head_dim]`` of the session's tail slots: the layout of the
         reference's ``_tail_past`` (``paged_model.py:638-641``), which its serving scheduler groups
         sessions by (``serving/scheduler.py:486``).  None without an active session."""
-        if self._store is None:
+        if getattr(self, "_tail_past_override", None) is not None:
+            return self._tail_past_override
+        if self._store is None or self._pools is None:
             return None
         p = self._pools
         tail = p.dev_pool[p.group_slots(self._tail_group)]
         n = self._tail_len
         return [(tail[:, layer, 0, :, :n], tail[:, layer, 1, :, :n]) for layer in range(p.num_layers)]
+
+    @_tail_past.setter
+    def _tail_past(self, value):
+        """Assignable like the reference's attribute (its tests build fake sessions by setting it);
+        an assigned value is returned instead of the view until it is set back to None."""
+        self._tail_past_override = value
 
     def _note_fed_token(self, token_id: int) -> None:
         """A token decoded outside ``generate`` (``batched_decode_step``) is now part of the session:

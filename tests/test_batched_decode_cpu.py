@@ -21,6 +21,7 @@ def make_fake_session(**overrides) -> PagedModel:
     pm._num_blocks = 1
     pm._tail_len = 3
     pm._pad = torch.zeros(1, dtype=torch.int32)
+    pm._tail_past = [(torch.zeros(1, 2, 3, 4), torch.zeros(1, 2, 3, 4))]  # one row, tail of 3 tokens
     for key, value in overrides.items():
         setattr(pm, key, value)
     return pm
@@ -62,7 +63,8 @@ def test_rejects_mismatched_tokens_per_block():
 
 
 def test_rejects_batch_size_greater_than_one():
-    a = make_fake_session(_pad=torch.zeros(2, dtype=torch.int32))
+    a = make_fake_session(_pad=torch.zeros(2, dtype=torch.int32),
+                          _tail_past=[(torch.zeros(2, 2, 3, 4), torch.zeros(2, 2, 3, 4))])
     with pytest.raises(ValueError, match="single-row"):
         batched_decode_step([a], [1], torch.device("cpu"))
 

@@ -267,6 +267,7 @@ class PagedModel:
     # ------------------------------------------------------------------ session state
     def _clear_session(self):
         self._graph = None
+        self._tail_past_override = None
         self._pools = None
         self._store = None
         self._rust_pager = None

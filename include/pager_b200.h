@@ -49,7 +49,7 @@ enum {
 #define PAGER_HOST_SLOT_BIT 0x40000000
 
 /* Compute backends for the split kernel (PAGER_BACKEND_AUTO picks tensor-core
- * mma for fp16/bf16 at head_dim 64/128 and CUDA-core FMA otherwise). */
+ * mma for fp16/bf16 at head_dim 64/128/256 and CUDA-core FMA otherwise). */
 enum { PAGER_BACKEND_AUTO = 0, PAGER_BACKEND_MMA = 1, PAGER_BACKEND_FMA = 2 };
 
 /* Mass accumulation modes of pager_paged_decode_attention. */

@@ -30,7 +30,9 @@ PAGER_ERR_CUDA = 3
 PAGER_ERR_SCRATCH = 4
 PAGER_ERR_TIMEOUT = 5
 
+# block-table entry tags (include/pager_b200.h PAGER_HOST_SLOT_BIT / PAGER_STAGE_SLOT_BIT)
 HOST_SLOT_BIT = 0x40000000
+STAGE_SLOT_BIT = 0x20000000
 
 BACKEND_AUTO, BACKEND_MMA, BACKEND_FMA = 0, 1, 2
 MASS_NONE, MASS_ROW_MEAN, MASS_BATCH_MEAN = 0, 1, 2

@@ -30,8 +30,8 @@ import torch
 
 from . import _lib as L
 
-HOST_SLOT_BIT = 0x40000000
-STAGE_SLOT_BIT = 0x20000000
+HOST_SLOT_BIT = L.HOST_SLOT_BIT
+STAGE_SLOT_BIT = L.STAGE_SLOT_BIT
 
 _LINK: dict[int, dict] = {}
 _LINK_LOCK = threading.Lock()

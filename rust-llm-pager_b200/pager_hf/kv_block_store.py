@@ -45,13 +45,13 @@ from dataclasses import dataclass
 import numpy as np
 import torch
 
+from ._lib import HOST_SLOT_BIT
 from .host_pool import HostPool
 
 logger = logging.getLogger(__name__)
 
 # kv_block_store.py:10-13: warn once CPU-resident bytes pass this fraction of ram_budget_bytes
 _RAM_BUDGET_WARNING_THRESHOLD = 0.8
-HOST_SLOT_BIT = 0x40000000
 
 
 @dataclass

@@ -65,3 +65,27 @@ def test_module_surface_matches_reference():
                  "streaming_attention_finalize", "_validate_n_rep", "_default_valid", "_default_active"):
         assert callable(getattr(sa, name))
     assert sa._BLOCK_KV == 64 and sa._M_TILE == 16 and sa._MIN_DOT_DIM == 16
+
+
+def test_python_constants_match_the_header():
+    """Status codes, dtype / backend / mass-mode codes and block-table tags of ``_lib`` equal the
+    values ``include/pager_b200.h`` defines, so the ctypes binding and the C ABI cannot drift."""
+    import re
+
+    from pager_hf import _lib as L
+    from pager_hf import host_staging, kv_block_store
+
+    hdr = open(L.HEADER_PATH).read()
+    defined = {name: int(val, 0) for name, val in re.findall(r"\b(PAGER_[A-Z0-9_]+)\s*=\s*(\w+)", hdr)}
+    defined.update({name: int(val, 0) for name, val in re.findall(r"#define (PAGER_\w+_BIT) (0x[0-9a-fA-F]+)", hdr)})
+    for name in ("PAGER_OK", "PAGER_ERR_INVALID", "PAGER_ERR_UNSUPPORTED", "PAGER_ERR_CUDA", "PAGER_ERR_SCRATCH",
+                 "PAGER_ERR_TIMEOUT"):
+        assert getattr(L, name) == defined[name], name
+    assert (L.BACKEND_AUTO, L.BACKEND_MMA, L.BACKEND_FMA) == (
+        defined["PAGER_BACKEND_AUTO"], defined["PAGER_BACKEND_MMA"], defined["PAGER_BACKEND_FMA"])
+    assert (L.MASS_NONE, L.MASS_ROW_MEAN, L.MASS_BATCH_MEAN) == (
+        defined["PAGER_MASS_NONE"], defined["PAGER_MASS_ROW_MEAN"], defined["PAGER_MASS_BATCH_MEAN"])
+    assert L.DTYPE_CODE == {torch.float32: defined["PAGER_DTYPE_F32"], torch.float16: defined["PAGER_DTYPE_F16"],
+                            torch.bfloat16: defined["PAGER_DTYPE_BF16"]}
+    assert L.HOST_SLOT_BIT == host_staging.HOST_SLOT_BIT == kv_block_store.HOST_SLOT_BIT == defined["PAGER_HOST_SLOT_BIT"]
+    assert L.STAGE_SLOT_BIT == host_staging.STAGE_SLOT_BIT == defined["PAGER_STAGE_SLOT_BIT"]

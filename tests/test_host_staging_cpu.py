@@ -71,3 +71,38 @@ def test_auto_choice_counts_one_submission_per_copy():
         assert hs.choose_host_read(dev, 362 << 20, copies_per_layer=1) == "zero_copy"
     finally:
         hs._LINK.pop(7, None)
+
+
+def test_plan_properties_on_random_tables():
+    """Over seeded random tables (device, host and absent entries; per-row num_blocks, token windows
+    and active flags): every entry the kernel reads from the host tier is renamed to a staging slot
+    that the runs fill from the same host slot; every other entry is unchanged; the runs are maximal
+    and fill the staging buffer densely in ascending host-slot order."""
+    H = HOST_SLOT_BIT
+    rng = np.random.default_rng(7)
+    for _ in range(200):
+        B, nb, tpb = int(rng.integers(1, 6)), int(rng.integers(1, 24)), int(rng.choice([1, 16, 64]))
+        kind = rng.integers(0, 3, (B, nb))
+        slot = rng.integers(0, 40, (B, nb))
+        table = torch.tensor(np.where(kind == 0, -1, np.where(kind == 1, slot, slot | H)), dtype=torch.int32)
+        num_blocks = torch.tensor(rng.integers(0, nb + 1, B), dtype=torch.int32)
+        hi = torch.tensor(rng.integers(0, nb * tpb + 1, B), dtype=torch.int32)
+        lo = torch.tensor([int(rng.integers(0, int(h) + 1)) for h in hi], dtype=torch.int32)
+        active = torch.tensor(rng.integers(0, 2, B), dtype=torch.int32)
+        staged, slots, (src, dst, ln) = plan_host_runs(table, tpb, num_blocks, lo, hi, active)
+
+        stage_of = np.full(int(ln.sum()), -1)  # host slot each staging slot receives
+        for s, d, n in zip(src, dst, ln):
+            stage_of[d:d + n] = np.arange(s, s + n)
+        assert stage_of.tolist() == slots.tolist() and np.all(np.diff(stage_of) > 0)
+        assert np.all(src[1:] != src[:-1] + ln[:-1]) and np.all(dst == np.concatenate(([0], np.cumsum(ln)[:-1])))
+
+        for b in range(B):
+            for j in range(nb):
+                e, g = int(table[b, j]), int(staged[b, j])
+                read = (e >= 0 and e & H and j < num_blocks[b] and (j + 1) * tpb > lo[b] and j * tpb < hi[b]
+                        and active[b])
+                if read:
+                    assert g & STAGE_SLOT_BIT and stage_of[g & (STAGE_SLOT_BIT - 1)] == e & (H - 1)
+                else:
+                    assert g == e

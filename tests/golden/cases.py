@@ -84,19 +84,17 @@ CASES = {
     # Gemma geometry (head_dim 256, n_rep 2), left-padded rows, two-pass with block mass
     "gemma_d256_f16_padded": dict(kind="two_pass", seed=15, B=2, Hq=8, Hkv=4, D=256, tpb=16, nb=6, tail=5,
                                   group_blocks=2, dtype="f16", pad_prefix=[0, 20]),
-    # Oracle pins (``oracle_pin``) at the shapes the fused paged op's GPU parity cases compare with the
-    # oracle: GQA fan-out 16, plain MHA, head_dim 32 / 16 / 8, fp32.  The drop-in functions' GPU test
-    # does not replay these.
+    # the shapes the fused paged op's GPU parity cases compare with the oracle: GQA fan-out 16
+    # (the most _validate_n_rep allows), plain MHA, head_dim 32 / 16 / 8, fp32
     "pin_n_rep_16_d128_f16": dict(kind="two_pass", seed=31, B=2, Hq=32, Hkv=2, D=128, tpb=64, nb=4, tail=7,
-                                  group_blocks=2, dtype="f16", pad_prefix=[0, 90], oracle_pin=True),
+                                  group_blocks=2, dtype="f16", pad_prefix=[0, 90]),
     "pin_mha_d64_f16_holes": dict(kind="two_pass", seed=32, B=2, Hq=4, Hkv=4, D=64, tpb=32, nb=5, tail=11,
-                                  group_blocks=2, dtype="f16", holes=0.2, oracle_pin=True),
+                                  group_blocks=2, dtype="f16", holes=0.2),
     "pin_d32_f16": dict(kind="two_pass", seed=33, B=2, Hq=6, Hkv=3, D=32, tpb=16, nb=9, tail=15,
-                        group_blocks=4, dtype="f16", oracle_pin=True),
+                        group_blocks=4, dtype="f16"),
     "pin_d8_f32": dict(kind="two_pass", seed=34, B=3, Hq=4, Hkv=2, D=8, tpb=16, nb=5, tail=2,
-                       group_blocks=2, dtype="f32", oracle_pin=True),
-    "pin_d16_f32_steps": dict(kind="steps", seed=35, B=2, Hq=8, Hkv=2, D=16, T=80, group=40, dtype="f32",
-                              oracle_pin=True),
+                       group_blocks=2, dtype="f32"),
+    "pin_d16_f32_steps": dict(kind="steps", seed=35, B=2, Hq=8, Hkv=2, D=16, T=80, group=40, dtype="f32"),
     # cross-session batched decode (batched_decode.py): block counts 6, 2, 0; tail 4 (+1 new token)
     "batched_sessions_f16": dict(kind="batched", seed=13, Hq=14, Hkv=2, D=64, tpb=16, nbs=[6, 2, 0], tail=4,
                                  group_blocks=4, dtype="f16"),

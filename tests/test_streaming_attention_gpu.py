@@ -43,7 +43,7 @@ def backend(request, sa):
     sa.set_backend("auto")
 
 
-@pytest.mark.parametrize("name", [n for n, c in CASES.items() if not c.get("oracle_pin")])
+@pytest.mark.parametrize("name", list(CASES))
 def test_golden_case(sa, backend, name):
     c = CASES[name]
     g = gio.load(name)

@@ -85,7 +85,7 @@ CASES = {
     "gemma_d256_f16_padded": dict(kind="two_pass", seed=15, B=2, Hq=8, Hkv=4, D=256, tpb=16, nb=6, tail=5,
                                   group_blocks=2, dtype="f16", pad_prefix=[0, 20]),
     # the shapes the fused paged op's GPU parity cases compare with the oracle: GQA fan-out 16
-    # (the most _validate_n_rep allows), plain MHA, head_dim 32 / 16 / 8, fp32
+    # (the most _validate_n_rep allows), plain MHA, head_dim 8 to 256 across fp16, bf16 and fp32
     "pin_n_rep_16_d128_f16": dict(kind="two_pass", seed=31, B=2, Hq=32, Hkv=2, D=128, tpb=64, nb=4, tail=7,
                                   group_blocks=2, dtype="f16", pad_prefix=[0, 90]),
     "pin_mha_d64_f16_holes": dict(kind="two_pass", seed=32, B=2, Hq=4, Hkv=4, D=64, tpb=32, nb=5, tail=11,
@@ -95,6 +95,11 @@ CASES = {
     "pin_d8_f32": dict(kind="two_pass", seed=34, B=3, Hq=4, Hkv=2, D=8, tpb=16, nb=5, tail=2,
                        group_blocks=2, dtype="f32"),
     "pin_d16_f32_steps": dict(kind="steps", seed=35, B=2, Hq=8, Hkv=2, D=16, T=80, group=40, dtype="f32"),
+    "pin_d8_f16_steps": dict(kind="steps", seed=36, B=2, Hq=6, Hkv=2, D=8, T=72, group=24, dtype="f16"),
+    "pin_d256_f32": dict(kind="two_pass", seed=37, B=1, Hq=4, Hkv=2, D=256, tpb=16, nb=3, tail=9,
+                         group_blocks=2, dtype="f32"),
+    "pin_d32_bf16_as_f32": dict(kind="two_pass", seed=38, B=2, Hq=8, Hkv=2, D=32, tpb=32, nb=4, tail=6,
+                                group_blocks=3, dtype="bf16", pad_prefix=[0, 40]),
     # cross-session batched decode (batched_decode.py): block counts 6, 2, 0; tail 4 (+1 new token)
     "batched_sessions_f16": dict(kind="batched", seed=13, Hq=14, Hkv=2, D=64, tpb=16, nbs=[6, 2, 0], tail=4,
                                  group_blocks=4, dtype="f16"),

@@ -193,6 +193,8 @@ EXTRA = [
     ("n_rep_1_mha", 16, 2, 4, 4, 64, 32, 2, [6, 2], [1, 30], torch.float16, {}),
     ("fp32_d8", 17, 3, 4, 2, 8, 16, 1, [5, 1, 3], [2, 16, 1], torch.float32, {}),
     ("fp16_d32", 18, 2, 6, 3, 32, 16, 1, [9, 4], [15, 1], torch.float16, {}),
+    ("bf16_d16", 23, 2, 8, 2, 16, 16, 1, [7, 3], [12, 0], torch.bfloat16, {}),
+    ("fp32_d256_softcap", 24, 1, 4, 2, 256, 16, 1, [5], [3], torch.float32, dict(softcap=20.0)),
     # the mass pass finalizes heads in chunks of 32: 48 heads end on a partial chunk, 80 on two more
     ("heads_48_chunked_mass", 19, 2, 48, 16, 64, 16, 1, [9, 3], [4, 11], torch.float16, {}),
     ("heads_80_bf16_d128", 20, 1, 80, 8, 128, 64, 1, [5], [7], torch.bfloat16, {}),

@@ -742,7 +742,7 @@ def run_ours(args):
     achieved = bytes_per_launch / (launch_ms / 1000) / 1e9
     t_hbm = wl.hbm_bytes / wl.L / (hbm_peak * 1e9)
     t_link = wl.host_bytes / wl.L / (h2d * 1e9) if wl.host_bytes else 0.0
-    t_roof = t_hbm + t_link  # the north star's combined roofline: HBM time plus link time
+    t_roof = t_hbm + t_link  # combined roofline: HBM time plus host-link time
     combined_peak = bytes_per_launch / t_roof / 1e9
     # DRAM traffic per launch: the ncu capture of the split kernel on the small HBM-resident case read
     # and wrote NCU_DRAM_PER_HBM_BYTE bytes per algorithmic HBM byte; scaled here to the bytes this

@@ -1,6 +1,6 @@
 """Greedy generation through ``pager_hf.paged_model.PagedModel`` matches unpaged HF greedy decoding.
 
-The north star's end-to-end criterion: greedy token IDs from
+The end-to-end criterion: greedy token IDs from
 ``PagedModel.generate`` on random-init weights match exactly.  The unpaged
 reference is the model's own forward with a ``DynamicCache`` (transformers'
 stock attention), one token at a time with argmax -- the reference project's

@@ -77,3 +77,17 @@ def test_reference_gpu_arm_reports_unavailable_without_the_install(tmp_path, mon
     line = json.loads(capsys.readouterr().out.strip())
     assert line["impl"] == "reference-gpu" and "baseline/_ref" in line["unavailable"]
     assert sys.path == before
+
+
+def test_reference_arms_do_no_work_on_ranks_other_than_zero(monkeypatch, capsys):
+    """Under torchrun only rank 0 runs and prints the reference arms; the other ranks exit 0 at once."""
+    import argparse
+
+    monkeypatch.setenv("WORLD_SIZE", "2")
+    monkeypatch.setenv("RANK", "1")
+    monkeypatch.setenv("LOCAL_RANK", "1")
+    monkeypatch.setattr(bench, "CpuOracleArm", lambda *a, **k: pytest.fail("rank 1 started the CPU arm"))
+    args = argparse.Namespace(workload="cfg5-32k", gpus=2, steps=3, warmup=3)
+    assert bench.run_reference_arm(args) == 0
+    assert bench.run_reference_gpu_arm(args) == 0
+    assert capsys.readouterr().out == ""

@@ -64,6 +64,16 @@ int pager_version(void);
 /* Reads (and clears) the device-side status word written by bounded waits. */
 int pager_device_status(int device, int* status_out);
 
+/* Stream-ordered form of pager_device_status for decode loops (the reference surfaces a failed
+ * step per request, pager_hf/serving/scheduler.py:520-524): enqueues on `stream` a copy of the
+ * current device's status word into *host_dst (page-locked host memory, so the copy is
+ * asynchronous and can be captured in a CUDA graph), then a reset of the word to 0.  *host_dst is
+ * valid once the stream has reached that point (e.g. after the step's synchronisation):
+ * 0 = no fault, PAGER_ERR_TIMEOUT (5) = a bounded wait ran out, 6 = a block-table entry or a
+ * tail write named a slot outside its pool and was skipped.  The word is per device: a kernel on
+ * another stream may set it between the copy and the reset. */
+int pager_status_snapshot_async(int32_t* host_dst, void* stream);
+
 /* ---- streaming_attention_state_init (pager_hf/streaming_attention.py:444-449) */
 int pager_attn_state_init(float* m, float* l, float* acc, int64_t rows, int head_dim, void* stream);
 

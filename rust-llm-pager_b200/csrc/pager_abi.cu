@@ -775,6 +775,18 @@ int paged_plan(int batch, int hq, int hkv, int head_dim, int kv_dtype, int tpb, 
 
 void set_last_error(const char* msg) { t_err = msg; }
 
+// Scratch bytes the paged op needs with the compute backend a call passes (0 when the
+// arguments are rejected); pager_paged_decode_scratch_bytes sizes for the larger of two plans.
+size_t paged_scratch_bytes_for_backend(int batch, int num_q_heads, int num_kv_heads, int head_dim, int kv_dtype,
+                                       int tokens_per_block, int max_row_tokens, int backend) {
+  if (check_geometry(batch, num_q_heads, num_kv_heads, head_dim, kv_dtype, kv_dtype)) return 0;
+  if (batch <= 0 || max_row_tokens <= 0 || !is_pow2(tokens_per_block) || tokens_per_block < 8) return 0;
+  PagedPlan pp;
+  if (paged_plan(batch, num_q_heads, num_kv_heads, head_dim, kv_dtype, tokens_per_block, max_row_tokens, backend, &pp))
+    return 0;
+  return layout_scratch(nullptr, (long long)batch * num_q_heads, pp.plan.max_splits, head_dim, pp.gstride).bytes;
+}
+
 // Device status word of the current device, for kernels compiled in other files.
 int current_status_word(int** out) {
   DevInfo* d = nullptr;
@@ -805,6 +817,17 @@ int pager_device_status(int device, int* status_out) {
   cudaSetDevice(prev);
   if (e != cudaSuccess) return cuda_fail(e, "status read");
   *status_out = v;
+  return PAGER_OK;
+}
+
+int pager_status_snapshot_async(int32_t* host_dst, void* stream) {
+  if (!host_dst) return fail(PAGER_ERR_INVALID, "host_dst is null");
+  DevInfo* di;
+  const int rc = device_info(&di);
+  if (rc) return rc;
+  cudaStream_t st = (cudaStream_t)stream;
+  PAGER_CUDA(cudaMemcpyAsync(host_dst, di->status, sizeof(int), cudaMemcpyDeviceToHost, st), "status snapshot");
+  PAGER_CUDA(cudaMemsetAsync(di->status, 0, sizeof(int), st), "status reset");
   return PAGER_OK;
 }
 

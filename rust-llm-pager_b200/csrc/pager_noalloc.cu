@@ -11,8 +11,9 @@
 // Limits and sharing:
 //   * the array holds PAGER_NOALLOC_SCRATCH_BYTES (32 MiB) and is reserved on
 //     every GPU that loads the library, for as long as the process runs;
-//   * a call whose scratch requirement (pager_paged_decode_scratch_bytes) is
-//     larger is rejected with PAGER_ERR_SCRATCH;
+//   * a call whose scratch requirement for the backend it passes (the size
+//     pager_paged_decode_scratch_bytes gives covers every backend) is larger is
+//     rejected with PAGER_ERR_SCRATCH;
 //   * every call on a device uses the same array and leaves its contents
 //     behind; nothing in it needs to start at zero (every value the kernels
 //     read was written earlier in the same call), but calls that overlap on the
@@ -30,6 +31,8 @@
 
 namespace pager {
 void set_last_error(const char* msg);  // pager_abi.cu: the message pager_last_error() returns
+size_t paged_scratch_bytes_for_backend(int batch, int num_q_heads, int num_kv_heads, int head_dim, int kv_dtype,
+                                       int tokens_per_block, int max_row_tokens, int backend);  // pager_abi.cu
 }
 
 namespace {
@@ -78,8 +81,10 @@ int pager_paged_decode_attention_noalloc(const void* q, int q_dtype, const void*
                                          float softcap, int max_row_tokens, void* out, int out_dtype,
                                          float* block_mass, float* mass_accum, int mass_mode, int backend,
                                          void* stream) {
-  const size_t need = pager_paged_decode_scratch_bytes(batch, num_q_heads, num_kv_heads, head_dim, kv_dtype,
-                                                       tokens_per_block, max_blocks, max_row_tokens);
+  // sized for the backend this call asks for (the regular entry checks the same plan); a call whose
+  // arguments are rejected sizes to 0 here and gets the regular entry's own error below
+  const size_t need = pager::paged_scratch_bytes_for_backend(batch, num_q_heads, num_kv_heads, head_dim, kv_dtype,
+                                                             tokens_per_block, max_row_tokens, backend);
   if (need > kNoallocBytes) {
     char buf[256];
     snprintf(buf, sizeof(buf),

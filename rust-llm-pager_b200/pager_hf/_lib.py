@@ -49,6 +49,7 @@ _SIGNATURES = {
     "pager_last_error": (ctypes.c_char_p, []),
     "pager_version": (_i, []),
     "pager_device_status": (_i, [_i, ctypes.POINTER(_i)]),
+    "pager_status_snapshot_async": (_i, [_vp, _vp]),
     "pager_attn_state_init": (_i, [_vp, _vp, _vp, _i64, _i, _vp]),
     "pager_attn_finalize": (_i, [_vp, _vp, _vp, _i, _i64, _i, _vp]),
     "pager_attn_chunk_scratch_bytes": (_sz, [_i, _i, _i, _i, _i, _i, _i, _i]),
@@ -135,6 +136,72 @@ def device_status(device: int) -> int:
     out = _i(0)
     check(lib().pager_device_status(device, ctypes.byref(out)))
     return out.value
+
+
+STATUS_TIMEOUT = 5
+STATUS_BAD_SLOT = 6
+_STATUS_TEXT = {
+    STATUS_TIMEOUT: "a bounded wait in a decode kernel ran out (a copy or a stage never arrived); the step's "
+                    "attention is incomplete",
+    STATUS_BAD_SLOT: "a block-table entry or a tail write named a slot outside its pool; that block was skipped, so "
+                     "the step's attention is wrong",
+}
+
+
+class DeviceStatusError(RuntimeError):
+    """A decode step's kernels reported a fault through the device status word (``code``: 5 for a
+    timed-out wait, 6 for a slot outside its pool).  The kernels never dereference such a slot and
+    always finish, so the CUDA context stays usable; the step's result must not be used."""
+
+    def __init__(self, code: int, where: str = "decode step"):
+        self.code = int(code)
+        super().__init__(f"{where}: device status {self.code}: {_STATUS_TEXT.get(self.code, 'unknown fault')}")
+
+
+class StatusWatch:
+    """Per-step check of a device's status word at a synchronisation the step already has.
+
+    ``enqueue(stream)`` queues, behind the step's kernels, a copy of the word into a page-locked
+    host int and a reset of the word (``pager_status_snapshot_async``); once the stream has been
+    synchronised, ``check()`` raises ``DeviceStatusError`` if the step set it.  One watch per
+    (thread, device): ``watch_for(device)``."""
+
+    def __init__(self, device: torch.device):
+        self.device = torch.device(device)
+        self.host = torch.zeros(1, dtype=torch.int32).pin_memory()
+
+    def enqueue(self, stream: int | None = None) -> None:
+        with torch.cuda.device(self.device):
+            s = torch.cuda.current_stream(self.device).cuda_stream if stream is None else stream
+            check(lib().pager_status_snapshot_async(self.host.data_ptr(), s))
+
+    def check(self, where: str = "decode step") -> None:
+        code = int(self.host[0])
+        if code:
+            self.host[0] = 0
+            raise DeviceStatusError(code, where)
+
+    def sync_and_check(self, where: str = "decode step") -> None:
+        """Enqueue, wait for the current stream, check: for a step with no later synchronisation."""
+        self.enqueue()
+        torch.cuda.current_stream(self.device).synchronize()
+        self.check(where)
+
+
+_watches = threading.local()
+
+
+def watch_for(device) -> StatusWatch:
+    device = torch.device(device)
+    if device.index is None:
+        device = torch.device("cuda", torch.cuda.current_device())
+    table = getattr(_watches, "table", None)
+    if table is None:
+        table = _watches.table = {}
+    w = table.get(device.index)
+    if w is None:
+        w = table[device.index] = StatusWatch(device)
+    return w
 
 
 def ptr(t: torch.Tensor | None) -> int | None:

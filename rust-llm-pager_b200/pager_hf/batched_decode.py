@@ -177,9 +177,12 @@ class BatchedDecodeAttention:
     def finish(self, apply_tiers: bool = True) -> list[list[float]]:
         """Advance every session by the decoded token (``batched_decode.py:320-338``): roll a full
         tail into a block, hand the step's block attention to the pager, move blocks to the tiers
-        it picks.  Returns each session's block attention list."""
+        it picks.  Returns each session's block attention list.  Raises ``DeviceStatusError`` (before
+        any session changes) when the step's kernels flagged a timed-out wait or a slot outside its
+        pool."""
         p = self.pools
         tpb = p.tokens_per_block
+        L.watch_for(self.device).sync_and_check("batched decode attention step")
         mass = self.mass.cpu() if self.mass is not None else None
         result = []
         for r, s in enumerate(self.sessions):
@@ -429,13 +432,17 @@ def batched_decode_step(sessions: list, next_input_ids: list[int], device) -> li
     if all(getattr(s, "decode_graphs", False) for s in sessions):
         g = _batched_graph_for(sessions, by_pools, a, device)
         logits = g.step(sessions, next_input_ids, pos_ids)
+        L.watch_for(device).sync_and_check("batched_decode_step")
         for rows, _, _, mass in g.buffers:
             for i, r in enumerate(rows):
                 s = sessions[r]
                 s._finish_token(mass[i, :s._num_blocks] if (mass is not None and s._needs_attention) else None)
                 s._note_fed_token(int(next_input_ids[r]))
                 s.last_host_read = "zero_copy"
-        return [logits[r, -1, :] for r in range(S)]
+        # the graph's logits buffer is overwritten by the next replay: hand out a copy, as the eager
+        # path (and the reference) hand out fresh tensors
+        last = logits[:, -1, :].clone()
+        return [last[r] for r in range(S)]
     groups, masses = [], []
     for rows in by_pools.values():
         members = [sessions[r] for r in rows]
@@ -446,6 +453,7 @@ def batched_decode_step(sessions: list, next_input_ids: list[int], device) -> li
     input_ids = torch.tensor(next_input_ids, dtype=torch.long, device=device)[:, None]
     position_ids = torch.tensor(pos_ids, dtype=torch.long, device=device)[:, None]
     logits = run_decoder_step(first.model, a, groups, input_ids, position_ids)
+    L.watch_for(device).sync_and_check("batched_decode_step")
     for rows, mass in masses:
         for i, r in enumerate(rows):
             s = sessions[r]

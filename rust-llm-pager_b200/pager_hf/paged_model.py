@@ -494,6 +494,7 @@ class PagedModel:
         positions = torch.full((B,), self._tail_len, **i32)
         position_ids = self._position_ids_from_mask(attention_mask)[:, -1:]
         logits = run_decoder_step(self.model, a, [AttentionGroup(p, plans, slots, positions)], input_ids, position_ids)
+        L.watch_for(dev).sync_and_check("PagedModel decode step")
         return logits, self._finish_token(None if mass is None else mass[:nb])
 
     def _graph_step(self, a, B, nb, table, los, total, input_ids, attention_mask):
@@ -514,6 +515,7 @@ class PagedModel:
         g.load(ints, input_ids, self._position_ids_from_mask(attention_mask)[:, -1:])
         logits = g.step()
         self.last_host_read = "zero_copy"
+        L.watch_for(input_ids.device).sync_and_check("PagedModel decode step")
         return logits, self._finish_token(None if g.mass is None else g.mass[:nb])
 
     def _finish_token(self, mass_row):

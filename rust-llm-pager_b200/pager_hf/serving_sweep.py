@@ -42,6 +42,7 @@ from dataclasses import dataclass, field
 import numpy as np
 import torch
 
+from ._lib import DeviceStatusError
 from .batched_decode import BatchedDecodeAttention, DecodeSession
 from .kv_block_store import KVPools
 from .request_shard import local_requests, shard_requests
@@ -94,6 +95,7 @@ class ShardStats:
     waits: list = field(default_factory=list)
     peak_sessions: int = 0
     host_blocks_peak: int = 0
+    errors: list = field(default_factory=list)  # {"rid", "error"} per request failed by a faulted step
 
 
 class ShardRunner:
@@ -207,7 +209,17 @@ class ShardRunner:
             plan = BatchedDecodeAttention([a.session for a in active], self.g["hq"])
             for layer in range(self.g["layers"]):
                 plan.layer(layer, self.q[layer, :S], self.kn[layer, :S], self.vn[layer, :S])
-            plan.finish()
+            try:
+                plan.finish()
+            except DeviceStatusError as e:
+                # a faulted step fails the requests it served, each with the reason, as the reference's
+                # scheduler sets req.error and finishes a request whose step raised (scheduler.py:520-524)
+                for a in active:
+                    st.errors.append({"rid": a.req.rid, "error": str(e)})
+                    a.session.close()
+                active = []
+                step_time += time.perf_counter() - ts
+                continue
             torch.cuda.synchronize(self.device)
             step_time += time.perf_counter() - ts
             st.steps += 1
@@ -244,6 +256,7 @@ def summarize(stats: list[ShardStats]) -> dict:
             "decode_tokens_per_s": tokens / wall if wall else None, "kv_gbs": kv / wall / 1e9 if wall else None,
             "latency_s": {"mean": sum(lat) / len(lat) if lat else None, "p50": pct(0.5), "p90": pct(0.9)},
             "mean_step_ms": 1000 * sum(s.step_s for s in stats) / max(1, sum(s.steps for s in stats)),
+            "errors": [e for s in stats for e in s.errors],
             "per_rank": [{"rank": s.rank, "requests": s.requests, "tokens": s.tokens, "wall_s": s.wall_s,
                           "peak_sessions": s.peak_sessions, "host_blocks_peak": s.host_blocks_peak}
                          for s in stats]}

@@ -45,7 +45,7 @@ def _setup(seed, B, Hq, Hkv, D, tpb, L, nbs, tails, dtype):
         dtype=dtype)
 
 
-def _args(s, layer, out, block_mass, accum):
+def _args(s, layer, out, block_mass, accum, backend=0):
     from pager_hf import _lib
 
     code = _lib.DTYPE_CODE[s["dtype"]]
@@ -53,10 +53,10 @@ def _args(s, layer, out, block_mass, accum):
             s["host"].shape[0], code, s["L"], layer, s["Hkv"], s["tpb"], s["D"], s["table"].data_ptr(),
             s["table"].shape[1], s["nbs"].data_ptr(), s["tk"].data_ptr(), s["tv"].data_ptr(), s["tails"].data_ptr(),
             s["tk"].shape[2], None, None, None, s["B"], s["Hq"], 1.0 / s["D"] ** 0.5, 0.0, s["max_row"],
-            out.data_ptr(), code, block_mass.data_ptr(), accum.data_ptr(), _lib.MASS_ROW_MEAN, _lib.BACKEND_AUTO]
+            out.data_ptr(), code, block_mass.data_ptr(), accum.data_ptr(), _lib.MASS_ROW_MEAN, backend]
 
 
-def _regular(s, layer):
+def _regular(s, layer, backend=0):
     from pager_hf import _lib
 
     lib = _lib.lib()
@@ -67,19 +67,20 @@ def _regular(s, layer):
                                                   s["tpb"], s["table"].shape[1], s["max_row"])
     scratch = torch.empty(nbytes, dtype=torch.uint8, device="cuda")
     stream = torch.cuda.current_stream().cuda_stream
-    _lib.check(lib.pager_paged_decode_attention(*_args(s, layer, out, bm, acc), scratch.data_ptr(), nbytes, stream))
+    _lib.check(lib.pager_paged_decode_attention(*_args(s, layer, out, bm, acc, backend), scratch.data_ptr(), nbytes,
+                                                stream))
     torch.cuda.synchronize()
     return out.float().cpu(), bm.cpu(), acc.cpu()
 
 
-def _noalloc(s, layer):
+def _noalloc(s, layer, backend=0):
     from pager_hf import _lib
 
     out = torch.empty(s["B"], s["Hq"], s["D"], dtype=s["dtype"], device="cuda")
     bm = torch.zeros(s["B"], s["Hq"], s["table"].shape[1], device="cuda")
     acc = torch.zeros(s["B"], s["table"].shape[1], device="cuda")
     stream = torch.cuda.current_stream().cuda_stream
-    _lib.check(_lib.lib().pager_paged_decode_attention_noalloc(*_args(s, layer, out, bm, acc), stream))
+    _lib.check(_lib.lib().pager_paged_decode_attention_noalloc(*_args(s, layer, out, bm, acc, backend), stream))
     torch.cuda.synchronize()
     return out.float().cpu(), bm.cpu(), acc.cpu()
 
@@ -101,6 +102,24 @@ def test_noalloc_matches_regular_entry_on_two_calls_in_a_row():
     finally:
         first["host"].close()
         second["host"].close()
+
+
+def test_noalloc_with_an_explicit_backend_matches_regular_entry():
+    """The size check follows the backend a call asks for: tensor-core and CUDA-core calls both run
+    and agree with the regular entry on the same backend."""
+    from pager_hf import _lib
+
+    s = _setup(34, 2, 14, 2, 64, 16, 3, [11, 3], [5, 16], torch.float16)
+    try:
+        for backend in (_lib.BACKEND_MMA, _lib.BACKEND_FMA):
+            ref_out, ref_bm, ref_acc = _regular(s, 1, backend)
+            out, bm, acc = _noalloc(s, 1, backend)
+            np.testing.assert_allclose(out.numpy(), ref_out.numpy(), rtol=0, atol=2e-3)
+            np.testing.assert_allclose(bm.numpy(), ref_bm.numpy(), rtol=1e-4, atol=1e-6)
+            np.testing.assert_allclose(acc.numpy(), ref_acc.numpy(), rtol=1e-4, atol=1e-6)
+        assert _lib.device_status(0) == 0
+    finally:
+        s["host"].close()
 
 
 def test_noalloc_rejects_calls_beyond_its_scratch_array():

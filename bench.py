@@ -16,10 +16,19 @@ request stay in HBM (recent_only placement) and the rest sit in the pinned
 host pool.  KV values are seeded synthetic data (no checkpoints offline).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--workload NAME] [--impl ours|reference]
+                    [--rounding running|final|one_pass] [--no-extras]
 
 N > 1 runs one process per GPU (torchrun); requests are sharded across GPUs
 (weak scaling, no collective on the data path); the timed region is bracketed
 by barriers and its time is the max over ranks.
+
+``--rounding``: how p is rounded before P.V.  "running" (default) rounds exactly
+as the reference's one-pass path does for this workload's recent_only placement
+(a K pass, a scan and a V pass); "one_pass" is the fused one-pass kernel.  At
+N = 1 the line also carries, unless ``--no-extras``: the HBM-resident ``hbm-32k``
+workload timed on its own (``kernel_hbm_32k``, against the measured HBM peak)
+and model-level decode tokens/s of ``PagedModel.generate`` on BASELINE config 4
+at 32k (``model_decode``).
 """
 
 from __future__ import annotations
@@ -214,7 +223,7 @@ class WorkloadLayout:
         self.bytes_per_step = self.hbm_bytes + self.host_bytes
         self.launches_per_step = self.L * 2  # split kernel + combine/mass kernel per layer
 
-    def config(self, world: int, host_read: str) -> dict:
+    def config(self, world: int) -> dict:
         w = self.w
         return {
             "workload": self.name, "model": w["model"], "batch_per_gpu": self.B, "global_batch": self.B * world,
@@ -224,7 +233,6 @@ class WorkloadLayout:
             "hbm_bytes_per_step": self.hbm_bytes, "host_bytes_per_step": self.host_bytes,
             "l2": "inputs larger than L2 (KV per step >> 126 MB), no flush",
             "parallelism": f"request-sharded x{world}, no collectives on the data path",
-            "host_read": host_read,
         }
 
 
@@ -270,15 +278,20 @@ class Workload(WorkloadLayout):
             n = min(chunk, flat.numel() - s)
             flat[s:s + n].copy_(src[:n], non_blocking=False)
 
-    def build_plan(self, host_read: str):
+    def build_plan(self, host_read: str, rounding: str = "running"):
         from pager_hf.streaming_attention import PagedDecodePlan
 
+        # the reference's chunks for its rounding: groups of 64 blocks (PagedModel's default
+        # streaming_group_size_blocks), then the tail
         self.plan = PagedDecodePlan(
             batch=self.B, num_query_heads=self.Hq, dev_pool=self.dev_pool,
             host_pool=None if self.host is None else self.host.tensor, num_layers=self.L, tokens_per_block=self.tpb,
             block_table=self.table, num_blocks=self.num_blocks, max_row_tokens=self.max_row_tokens,
             tail_k=self.tail_k, tail_v=self.tail_v, tail_len=self.tail_len, valid_lo=self.valid_lo,
-            mass_accum=self.mass, mass_mode="row_mean", host_read=host_read, prefetch_next_step=True)
+            mass_accum=self.mass, mass_mode="row_mean", host_read=host_read, prefetch_next_step=True,
+            rounding=rounding, ref_group_tokens=64 * self.tpb)
+        # kernels per layer: split + combine/mass, or scores + reference max + values + combine/mass
+        self.launches_per_step = self.L * (2 if self.plan.rounding == 0 else 4)
 
     def invalidate_staging(self):
         if self.plan.staging is not None:
@@ -390,11 +403,63 @@ class CpuOracleArm:
         self.pool.join()
 
 
+class CpuTorchArm:
+    """The reference's torch decode-attention path on the host cores: its dense test oracle
+    (tests/test_streaming_attention.py:20-40, restated in oracle/streaming_attention_torch.py) on one
+    (request, layer) unit of the workload at the full context, with ``torch.set_num_threads`` = every
+    host core.  A sample is ``reps`` calls."""
+
+    def __init__(self, wl_name: str, threads: int | None = None, reps: int = 2):
+        import torch
+
+        from oracle import streaming_attention_torch as ort
+
+        w = WORKLOADS[wl_name]
+        self.w, self.reps, self.ort = w, reps, ort
+        self.procs = threads or os.cpu_count() or 1
+        torch.set_num_threads(self.procs)
+        nb = w["context"] // w["tpb"]
+        T = nb * w["tpb"] + 32  # the blocks plus a 32-token tail
+        window = w.get("window")
+        lo = max(0, T - window) if window else 0
+        dt = torch.bfloat16 if w["dtype"] == "bf16" else torch.float16
+        g = torch.Generator().manual_seed(1000)
+        self.q = torch.randn(1, w["hq"], w["d"], generator=g).to(dt)
+        self.k = torch.randn(1, w["hkv"], T, w["d"], generator=g).to(dt)
+        self.v = torch.randn(1, w["hkv"], T, w["d"], generator=g).to(dt)
+        self.valid = torch.ones(1, T, dtype=torch.int32)
+        self.valid[:, :lo] = 0
+        self.n_rep, self.tpb = w["hq"] // w["hkv"], w["tpb"]
+        self.bytes = (T - lo) * 2 * w["hkv"] * w["d"] * 2  # attended K and V bytes
+        self.units = reps
+        self._call()  # warm-up
+
+    def _call(self):
+        self.ort.dense_reference(self.q, self.k, self.v, self.n_rep, self.tpb, valid=self.valid)
+
+    def sample(self):
+        t0 = time.perf_counter()
+        for _ in range(self.reps):
+            self._call()
+        return self.bytes * self.reps, time.perf_counter() - t0
+
+    def close(self):
+        pass
+
+
 def sample_desc(arm):
     w = arm.w
+    if isinstance(arm, CpuTorchArm):
+        return (f"{arm.reps} calls per sample, each one (request, layer) of the workload at {w['context']} tokens: "
+                f"the reference's dense torch decode attention with per-block mass (its test oracle restated), "
+                f"torch.set_num_threads({arm.procs})")
     return (f"{arm.procs} processes x {arm.reps} calls, each one (request, layer) of the workload at "
             f"{w['context']} tokens; numpy restatement of the reference's dense decode attention with "
             f"per-block mass, 1 BLAS thread per process")
+
+
+def cpu_arm(wl_name: str, kind: str):
+    return CpuTorchArm(wl_name) if kind == "torch" else CpuOracleArm(wl_name)
 
 
 # ----------------------------------------------------------------------------- arms
@@ -402,7 +467,7 @@ def run_reference_arm(args):
     world, rank, _ = _dist_env()
     if world > 1 and rank != 0:
         return 0
-    arm = CpuOracleArm(args.workload)
+    arm = cpu_arm(args.workload, args.cpu_arm)
     try:
         for _ in range(args.warmup):
             arm.sample()
@@ -415,15 +480,20 @@ def run_reference_arm(args):
         arm.close()
     gbs = tot_b / tot_t / 1e9
     w = WORKLOADS[args.workload]
+    lay = WorkloadLayout(args.workload, seed=1234)
     line = {
         "impl": "reference", "metric": METRIC, "value": gbs, "unit": "GB/s", "n_gpus": args.gpus, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": 1000 * tot_t / args.steps, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": w["dtype"], "data": "synthetic (seeded random KV)",
-        "config": WorkloadLayout(args.workload, seed=1234).config(args.gpus, "n/a (CPU)"),
+        "warmup": args.warmup,
+        # one step = the whole workload step (every request and layer), at the rate the samples measured
+        "ms_per_step": 1000 * lay.bytes_per_step / (gbs * 1e9), "sample_ms": 1000 * tot_t / args.steps,
+        "units_per_step": lay.B * lay.L, "units_per_sample": getattr(arm, "units", arm.procs * arm.reps),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": w["dtype"],
+        "data": "synthetic (seeded random KV)", "config": lay.config(args.gpus), "host_read": "n/a (CPU)",
         "cpu_baseline": {"value": gbs, "unit": "GB/s", "cores": arm.procs, "kind": "port", "sample": sample_desc(arm)},
         "e2e": {"value": gbs, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-        "note": "reference path = the reference's Triton/torch algorithm restated on the CPU (oracle/); the "
-                "reference ships no compiled CPU implementation",
+        "note": "reference path = the reference's torch decode attention (its dense test oracle, "
+                "tests/test_streaming_attention.py:20-40) on the host cores; the reference ships no compiled CPU "
+                "implementation",
     }
     print(json.dumps(line), flush=True)
     return 0
@@ -639,7 +709,7 @@ def run_reference_gpu_arm(args):
         "impl": "reference-gpu", "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": 1, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": w["dtype"], "data": "synthetic: seeded random KV in the workload's geometry",
-        "config": lay.config(1, "reference: pageable CPU blocks gathered with synchronous .to(device)"),
+        "config": lay.config(1), "host_read": "reference: pageable CPU blocks gathered with synchronous .to(device)",
         "decode_tokens_per_s": lay.B / (ms_step / 1000),
         "e2e": {"value": lay.bytes_per_step / (e2e_step / 1000) / 1e9, "unit": "GB/s", "ms_per_step": e2e_step,
                 "h2d_bytes_per_step": q_host.numel() * q_host.element_size(),
@@ -691,7 +761,7 @@ def run_ours(args):
         from pager_hf.host_staging import record_link_bandwidth
 
         record_link_bandwidth(device, link["copy_gbs"], link["zero_copy_gbs"])
-    wl.build_plan(args.host_read)
+    wl.build_plan(args.host_read, args.rounding)
 
     # warm-up (also first-call setup: occupancy queries, smem attributes)
     for _ in range(max(args.warmup, 1)):
@@ -746,24 +816,32 @@ def run_ours(args):
     combined_peak = bytes_per_launch / t_roof / 1e9
     # DRAM traffic per launch: the ncu capture of the split kernel on the small HBM-resident case read
     # and wrote NCU_DRAM_PER_HBM_BYTE bytes per algorithmic HBM byte; scaled here to the bytes this
-    # launch's kernel reads from DRAM: the HBM tier, plus the staged copies of host blocks when the
-    # host tier is staged (zero-copy host reads cross the link, not DRAM).
-    kernel_dram_bytes = wl.hbm_bytes + (wl.host_bytes if wl.plan.host_read == "staged" else 0)
-    traffic = kernel_dram_bytes / wl.L * NCU_DRAM_PER_HBM_BYTE
+    # launch's kernels read from DRAM -- the HBM tier, plus the staged copies of host blocks when the
+    # host tier is staged (zero-copy host reads cross the link, not DRAM) -- and to those copies
+    # themselves: the copy engines write every staged host byte into device memory first.
+    staged = wl.plan.host_read == "staged"
+    kernel_dram_bytes = (wl.hbm_bytes + (wl.host_bytes if staged else 0)) / wl.L * NCU_DRAM_PER_HBM_BYTE
+    copy_engine_writes = wl.host_bytes / wl.L if staged else 0.0
+    traffic = kernel_dram_bytes + copy_engine_writes
     clocks = clk.summary()
     line = {
         "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": w["dtype"],
         "data": "synthetic: seeded random KV in the workload's geometry (no checkpoints offline)",
-        "config": wl.config(world, wl.plan.host_read),
+        "config": wl.config(world), "host_read": wl.plan.host_read, "rounding": args.rounding,
         "decode_tokens_per_s": tokens_per_s,
         "roofline": {
             "bound": "hbm", "achieved": achieved, "peak": combined_peak, "unit": "GB/s",
             "frac": achieved / combined_peak, "traffic": traffic,
             "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of split_kernel on prof-hbm "
-                              f"({NCU_DRAM_PER_HBM_BYTE:.4f} B per algorithmic HBM byte), scaled to this launch",
-            "kernel": "paged decode attention per layer (split-KV kernel + combine/mass kernel, back to back)",
+                              f"({NCU_DRAM_PER_HBM_BYTE:.4f} B per algorithmic HBM byte) scaled to the bytes this "
+                              "launch reads from DRAM (HBM tier + staged copies), plus the copy engines' writes of "
+                              f"the staged host blocks ({copy_engine_writes:.0f} B per launch)",
+            "traffic_per_algorithmic_byte": traffic / (wl.bytes_per_step / wl.L),
+            "kernel": ("paged decode attention per layer: " + ("split-KV kernel + combine/mass kernel"
+                       if wl.plan.rounding == 0 else "scores pass + reference-max scan + values pass + combine/mass")
+                       + ", back to back"),
             "peak_kind": f"combined roofline: HBM {hbm_peak:.0f} GB/s ({peak_src}) + host link {h2d:.1f} GB/s "
                          f"(measured live); peak = bytes / (hbm_bytes/HBM + host_bytes/link)",
             "launch_ms": launch_ms, "bytes_per_launch": bytes_per_launch,
@@ -779,13 +857,19 @@ def run_ours(args):
         "clocks": clocks,
     }
     wl.close()
+    del wl
     if world > 1:
         dist.barrier(device_ids=[local])
         dist.destroy_process_group()
     if rank == 0:
+        if world == 1 and not args.no_extras:
+            if args.workload != "hbm-32k":
+                line["kernel_hbm_32k"] = kernel_only_measurement("hbm-32k", device, args.rounding, hbm_peak, peak_src)
+            line["model_decode"] = model_level_decode(device)
         if world == 1 and not args.no_cpu_baseline:
-            arm = CpuOracleArm(args.workload)
+            arm = cpu_arm(args.workload, args.cpu_arm)
             try:
+                arm.sample()
                 b, t_cpu = arm.sample()
             finally:
                 arm.close()
@@ -793,6 +877,62 @@ def run_ours(args):
                                     "sample": sample_desc(arm)}
         print(json.dumps(line), file=out, flush=True)
     return 0
+
+
+def kernel_only_measurement(name: str, device, rounding: str, hbm_peak: float, peak_src: str, steps: int = 5):
+    """The fused op alone on an HBM-resident workload (no host tier), against the measured HBM peak:
+    the kernel-bound figure beside a headline that the host link bounds."""
+    import torch
+
+    wl = Workload(name, device, seed=4321)
+    try:
+        wl.build_plan("zero_copy", rounding)
+        for _ in range(2):
+            wl.step()
+        torch.cuda.synchronize(device)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            wl.step()
+        e1.record()
+        e1.synchronize()
+        ms = e0.elapsed_time(e1) / steps
+        gbs = wl.bytes_per_step / (ms / 1000) / 1e9
+        return {"workload": name, "value": gbs, "unit": "GB/s", "ms_per_step": ms, "launch_ms": ms / wl.L,
+                "peak": hbm_peak, "frac": gbs / hbm_peak, "peak_kind": f"HBM copy peak, {peak_src}",
+                "rounding": rounding, "decode_tokens_per_s": wl.B / (ms / 1000), "steps": steps}
+    finally:
+        wl.close()
+        del wl
+        torch.cuda.empty_cache()
+
+
+def model_level_decode(device, config: str = "cfg4", new_tokens: int = 32):
+    """Model-level decode through ``PagedModel.generate``: BASELINE config 4 (random-init Mistral-7B
+    architecture, 8 rows x 32,768 tokens, window 4096, 5 % of blocks resident, sinks_recent, bf16),
+    ``new_tokens`` greedy tokens after the prompt's prefill, with the default reference rounding and
+    CUDA-graph steps.  Wall clock around the decode call, device synchronised on both sides; every
+    step reads its argmax back to the host, as generate() does."""
+    import torch
+
+    from pager_hf import generate_bench as gb
+
+    c = gb.CONFIGS[config]
+    model = gb.build_model(c)
+    try:
+        ids, mask, lens = gb.build_prompt(c)
+        toks, dt, peak, prefill_s, stats, resident, nb, host_read = gb.paged_decode(model, c, ids, mask, new_tokens)
+        B = ids.shape[0]
+        return {"config": f"{config}: random-init {c['family']} ({c['num_hidden_layers']} layers, hidden "
+                          f"{c['hidden_size']}), {B} rows x {max(lens)} tokens, window {c.get('sliding_window')}, "
+                          f"{c['policy']}, {int(100 * c['resident'])}% of blocks resident",
+                "decode_tokens_per_s": B * new_tokens / dt, "ms_per_step": 1000 * dt / new_tokens,
+                "new_tokens": new_tokens, "kv_gbs": gb.kv_bytes_per_step(c, lens, new_tokens // 2) / (dt / new_tokens) / 1e9,
+                "prefill_s": prefill_s, "peak_gpu_gb": peak / 1e9, "host_read": host_read,
+                "rounding": "reference (running max per 64-token tile)", "dtype": c.get("dtype", "f16")}
+    finally:
+        del model
+        torch.cuda.empty_cache()
 
 
 def main():
@@ -805,6 +945,14 @@ def main():
                     help="ours; reference = the reference's algorithm on the host cores; reference-gpu = the "
                          "reference's own Triton path from baseline/_ref on the same GPU (comparison)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extras", action="store_true",
+                    help="skip the kernel-only hbm-32k figure and the model-level decode of config 4 (N = 1 only)")
+    ap.add_argument("--rounding", default="running", choices=["running", "final", "one_pass"],
+                    help="rounding of p before P.V: the reference's one-pass rule (running max per 64-token tile), "
+                         "its two-pass rule (final max), or the fused one-pass kernel")
+    ap.add_argument("--cpu-arm", default="torch", choices=["torch", "numpy"],
+                    help="CPU baseline: the reference's dense torch path with all host threads, or the numpy "
+                         "restatement in one single-threaded process per core")
     ap.add_argument("--ref-mass", action="store_true",
                     help="reference-gpu: the reference's two-pass path that also writes the per-block mass "
                          "(what its heavy-hitter placements run; ours always emits the mass)")

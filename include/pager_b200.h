@@ -194,6 +194,45 @@ int pager_paged_decode_attention_staged(const void* q, int q_dtype, const void* 
                                         int mass_mode, int backend, void* scratch, size_t scratch_bytes,
                                         void* stream);
 
+/* ---- Reference-exact rounding of P.
+ *      The reference rounds p = exp(s - m) to the KV dtype before its P.V product
+ *      (pager_hf/streaming_attention.py:177-178; :346-347 and :427-428 in its two-pass path),
+ *      with m its running max after each 64-token tile of the chunks it is handed
+ *      (PagedModel._build_streaming_layer_forward, paged_model.py:1055-1072, for recent_only /
+ *      sinks_recent) or the row's final max (the two-pass path of the heavy-hitter policies,
+ *      paged_model.py:993-1039).  A one-pass split-KV kernel rounds against maxima the reference
+ *      never uses, which moves about half of the bf16/fp16 outputs by an ulp.  These modes run two
+ *      passes instead -- K to fp32 scores and group maxima, a scan to the reference's maxima, then
+ *      V -- reading every K and V byte once (plus 2 * n_rep * 4 bytes of scores per token and KV
+ *      head), and round p exactly as the reference does:
+ *        PAGER_ROUND_ONE_PASS  the one-pass kernel (pager_paged_decode_attention_staged)
+ *        PAGER_ROUND_RUNNING   the reference's one-pass path: m = running max after the reference
+ *                              tile holding the token; tiles are 64 tokens from the start of each
+ *                              chunk: chunks of ref_group_tokens tokens (<= 0: one chunk) of a
+ *                              numbering in which row b's token j sits at ref_shift[b] + j (NULL:
+ *                              j), then the tail chunk from row-local token ref_tail_start[b]
+ *                              (NULL: num_blocks[b] * tokens_per_block).  tokens_per_block >= 16.
+ *        PAGER_ROUND_FINAL     the reference's two-pass path: m = the row's final max.
+ *      fp16/bf16 KV at head_dim 64/128/256 (tensor-core kernels); fp32 KV rounds p to fp32, a
+ *      no-op, so every mode runs the one pass there.  Other arguments as
+ *      pager_paged_decode_attention_staged; scratch per pager_paged_decode_scratch_bytes_rounded. */
+enum { PAGER_ROUND_ONE_PASS = 0, PAGER_ROUND_RUNNING = 1, PAGER_ROUND_FINAL = 2 };
+size_t pager_paged_decode_scratch_bytes_rounded(int batch, int num_q_heads, int num_kv_heads, int head_dim,
+                                                int kv_dtype, int tokens_per_block, int max_row_tokens,
+                                                int rounding);
+int pager_paged_decode_attention_rounded(const void* q, int q_dtype, const void* dev_pool, int dev_slots,
+                                         const void* host_pool, int host_slots, const void* stage_pool,
+                                         int stage_slots, int kv_dtype, int num_layers, int layer, int num_kv_heads,
+                                         int tokens_per_block, int head_dim, const int32_t* block_table,
+                                         int max_blocks, const int32_t* num_blocks, const void* tail_k,
+                                         const void* tail_v, const int32_t* tail_len, int tail_cap,
+                                         const int32_t* valid_lo, const int32_t* valid_hi, const int32_t* active,
+                                         int batch, int num_q_heads, float scale, float softcap, int max_row_tokens,
+                                         void* out, int out_dtype, float* block_mass, float* mass_accum,
+                                         int mass_mode, int backend, int rounding, int ref_group_tokens,
+                                         const int32_t* ref_shift, const int32_t* ref_tail_start, void* scratch,
+                                         size_t scratch_bytes, void* stream);
+
 /* Copy one layer of host-pool blocks into a staging buffer, one cudaMemcpy2DAsync per run:
  * run r copies run_len[r] consecutive host slots starting at run_src[r] into consecutive staging
  * slots starting at run_dst[r]; from each host slot it takes chunk_bytes at layer_offset_bytes

@@ -303,6 +303,36 @@ def two_pass_decode(
     return finalize(acc, l, out_dtype), block_mass[:, :, :num_blocks], m, l
 
 
+def single_pass_decode(
+    q, k, v, tail_k, tail_v, num_blocks, tokens_per_block, group_size_blocks,
+    valid=None, tail_valid=None, scale=None, softcap=None, v_dtype="f32", out_dtype="f32",
+):
+    """The reference's per-layer decode sequence for the policies without an attention signal.
+
+    Follows ``_build_streaming_layer_forward`` in pager_hf/paged_model.py:1055-1072 (recent_only,
+    sinks_recent): one ``streaming_attention_step`` per group of ``group_size_blocks`` blocks
+    (:1055-1067), then one over the tail including the new token (:1068-1070), then finalize
+    (:1072).  Each step walks its chunk in 64-token tiles from the chunk's start, so p is rounded
+    against the running max after each such tile.  ``k``/``v`` hold the ``num_blocks *
+    tokens_per_block`` block tokens; a row padded in front with empty blocks (the combined
+    numbering of batched_decode.py:185-234) passes them with valid = 0.  Returns (out, m, l).
+    """
+    batch, hq, d = q.shape
+    full = num_blocks * tokens_per_block
+    if valid is None:
+        valid = np.ones((batch, full), dtype=np.int32)
+    if tail_valid is None:
+        tail_valid = np.ones((batch, tail_k.shape[2]), dtype=np.int32)
+    m, l, acc = state_init(batch, hq, d)
+    gt = group_size_blocks * tokens_per_block
+    for g0 in range(0, full, gt):
+        g1 = min(g0 + gt, full)
+        step(q, k[:, :, g0:g1], v[:, :, g0:g1], m, l, acc, valid=valid[:, g0:g1], scale=scale, softcap=softcap,
+             v_dtype=v_dtype)
+    step(q, tail_k, tail_v, m, l, acc, valid=tail_valid, scale=scale, softcap=softcap, v_dtype=v_dtype)
+    return finalize(acc, l, out_dtype), m, l
+
+
 def gather_paged_kv(pool_k, pool_v, block_table_row, layer):
     """Gather one row's blocks into contiguous [Hkv, nb*tpb, D] K and V.
 

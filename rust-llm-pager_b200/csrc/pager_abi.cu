@@ -18,6 +18,7 @@
 namespace pager {
 
 __device__ int g_status;
+const void* append_kernel_fn(int i);  // pager_append.cu
 
 bool lookup_split_mma(int kv_dtype, int head_dim, int mode, SplitKernelInfo* out);
 bool lookup_split_fma_f32(int head_dim, int mode, SplitKernelInfo* out);
@@ -59,6 +60,8 @@ int cuda_fail(cudaError_t e, const char* what) {
 constexpr unsigned long long kWaitLimitNs = 4000000000ull;  // 4 s per bounded device wait
 constexpr int kMaxSplits = 1024;
 
+void preload_kernels();  // below: loads every kernel of the library on the current device
+
 struct DevInfo {
   bool init = false;
   int sms = 0;
@@ -79,6 +82,7 @@ int device_info(DevInfo** out) {
     void* p = nullptr;
     PAGER_CUDA(cudaGetSymbolAddress(&p, g_status), "status symbol");
     d.status = static_cast<int*>(p);
+    preload_kernels();
     d.init = true;
   }
   *out = &d;
@@ -703,7 +707,9 @@ int run_chunk(const ChunkArgs& a) {
   p.status = di->status;
 
   dim3 grid(plan.max_splits, a.hkv, a.batch);
-  void* args[] = {&p, &mk, &mv};
+  CUtensorMap unused;
+  memset(&unused, 0, sizeof(unused));
+  void* args[] = {&p, &mk, &mv, &unused, &unused};
   PAGER_CUDA(cudaLaunchKernel(k.fn, grid, dim3(k.threads), args, k.smem_bytes, a.stream), "split kernel launch");
 
   CombineParams c;
@@ -753,9 +759,9 @@ struct PagedPlan {
 };
 
 int paged_plan(int batch, int hq, int hkv, int head_dim, int kv_dtype, int tpb, int max_row_tokens, int backend,
-               PagedPlan* out) {
+               PagedPlan* out, int mode = MODE_ONLINE) {
   const int be = backend_for(backend, kv_dtype, head_dim);
-  if (!lookup_split_kernel(kv_dtype, head_dim, MODE_ONLINE, be, &out->k))
+  if (!lookup_split_kernel(kv_dtype, head_dim, mode, be, &out->k))
     return fail(PAGER_ERR_UNSUPPORTED, "no split kernel for dtype %d head_dim %d backend %d", kv_dtype, head_dim, be);
   DevInfo* di;
   int rc = device_info(&di);
@@ -994,6 +1000,441 @@ int pager_paged_decode_attention(const void* q, int q_dtype, const void* dev_poo
                                              backend, scratch, scratch_bytes, stream);
 }
 
+}  // extern "C"
+
+namespace pager {
+namespace {
+
+// Every argument of the paged entry points (see include/pager_b200.h).
+struct PagedArgs {
+  const void* q;
+  int q_dtype;
+  const void* dev_pool;
+  int dev_slots;
+  const void* host_pool;
+  int host_slots;
+  const void* stage_pool;
+  int stage_slots;
+  int kv_dtype, num_layers, layer, num_kv_heads, tokens_per_block, head_dim;
+  const int32_t* block_table;
+  int max_blocks;
+  const int32_t* num_blocks;
+  const void* tail_k;
+  const void* tail_v;
+  const int32_t* tail_len;
+  int tail_cap;
+  const int32_t* valid_lo;
+  const int32_t* valid_hi;
+  const int32_t* active;
+  int batch, num_q_heads;
+  float scale, softcap;
+  int max_row_tokens;
+  void* out;
+  int out_dtype;
+  float* block_mass;
+  float* mass_accum;
+  int mass_mode, backend;
+  int rounding, ref_group_tokens;
+  const int32_t* ref_shift;
+  const int32_t* ref_tail_start;
+  void* scratch;
+  size_t scratch_bytes;
+  void* stream;
+};
+
+// The reference's tile of row-local token j: its one-pass kernel walks each chunk it is given in
+// 64-token tiles from the chunk's start (streaming_attention.py:143), the chunks being groups of
+// `gs_tok` tokens of the combined block numbering (paged_model.py:993-1072; in batched_decode.py
+// :238-285 a row's blocks sit `shift` tokens into that numbering) and then the tail from
+// `tail_start`.  Keys are unique per tile and increase along the row.
+__device__ __forceinline__ int ref_tile_key(int j, int shift, int tail_start, int gs_tok) {
+  if (j >= tail_start) return 0x40000000 + ((j - tail_start) >> 6);
+  const int c = shift + j;
+  if (gs_tok <= 0) return c >> 6;
+  const int grp = c / gs_tok;
+  return grp * ((gs_tok + 63) >> 6) + ((c - grp * gs_tok) >> 6);
+}
+
+struct RefMaxParams {
+  GeomArgs geom;
+  const int* active;
+  int rows, num_q_heads, tile_shift, tiles_per_split, group_shift, gstride, mstride, tpb;
+  int rule;  // PAGER_ROUND_RUNNING or PAGER_ROUND_FINAL
+  int ref_group_tokens;
+  const int* ref_shift;
+  const int* ref_tail_start;
+  float* gmax;  // in: the SCORES pass's group maxima; out: their inclusive prefix max
+  float* mref;  // out: [rows, mstride], kRefSlots entries per tile
+};
+
+constexpr int kRefMaxWarps = 8;
+
+// Between the SCORES and VALUES passes: per query row (one warp), the max each group's p is
+// formed against -- the reference's running max once its tile is folded in (the inclusive prefix
+// max of the group maxima up to the tile's last group), or the row's final max.
+__global__ void __launch_bounds__(kRefMaxWarps * 32) ref_max_kernel(const RefMaxParams p) {
+  pdl_wait();
+  pdl_launch_dependents();
+  const int lane = threadIdx.x & 31;
+  const int row = blockIdx.x * kRefMaxWarps + (threadIdx.x >> 5);
+  if (row >= p.rows) return;
+  const int b = row / p.num_q_heads;
+  if (p.active && p.active[b] == 0) return;
+  const RowGeom g = row_geom(p.geom, b);
+  int tb, te, ns;
+  geom_tiles(g, p.tile_shift, p.tiles_per_split, tb, te, ns);
+  if (ns == 0) return;
+  const int g0 = (tb << p.tile_shift) >> p.group_shift;
+  const int g1 = (te << p.tile_shift) >> p.group_shift;
+  float* gm = p.gmax + (long long)row * p.gstride;
+  float* mr = p.mref + (long long)row * p.mstride;
+  float carry = neg_inf();
+  for (int c0 = g0; c0 < g1; c0 += 32) {
+    const int gi = c0 + lane;
+    float v = gi < g1 ? gm[gi] : neg_inf();
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const float t = __shfl_up_sync(0xffffffffu, v, o);
+      if (lane >= o) v = fmaxf(v, t);
+    }
+    v = fmaxf(v, carry);
+    if (gi < g1) gm[gi] = v;
+    carry = __shfl_sync(0xffffffffu, v, 31);
+  }
+  __syncwarp();  // every lane's prefix values are visible to the others
+  const int shift = p.ref_shift ? p.ref_shift[b] : 0;
+  const int tail_start = p.ref_tail_start ? p.ref_tail_start[b] : g.nb * p.tpb;
+  const int G = 1 << p.group_shift;
+  const int per_tile = 1 << (p.tile_shift - p.group_shift);
+  for (int gi = g0 + lane; gi < g1; gi += 32) {
+    float M = carry;  // the final max
+    if (p.rule == PAGER_ROUND_RUNNING) {
+      const int key = ref_tile_key(gi * G, shift, tail_start, p.ref_group_tokens);
+      int e = gi;  // the last group of the same reference tile (a tile spans at most 64 / G groups)
+      while (e + 1 < g1 && ref_tile_key((e + 1) * G, shift, tail_start, p.ref_group_tokens) == key) ++e;
+      M = gm[e];
+    }
+    const int tile = gi / per_tile;
+    mr[(long long)tile * kRefSlots + (gi - tile * per_tile)] = M;
+  }
+}
+
+// Loads every kernel of the library on the current device, at the library's first call there.
+// With lazy module loading (the CUDA 12 default) a kernel is otherwise loaded at its first launch;
+// a load while another thread captures a CUDA graph on the device fails and invalidates that
+// capture, which a serving process with one scheduler thread per session can run into.
+void preload_kernels() {
+  cudaFuncAttributes fa;
+  const int dims[] = {8, 16, 32, 64, 128, 256};
+  for (int dt = 0; dt < 3; ++dt)
+    for (int d : dims)
+      for (int mode = 0; mode <= MODE_VALUES; ++mode)
+        for (int be : {BACKEND_MMA, BACKEND_FMA}) {
+          SplitKernelInfo k;
+          if (lookup_split_kernel(dt, d, mode, be, &k)) cudaFuncGetAttributes(&fa, k.fn);
+        }
+  const void* fns[] = {reinterpret_cast<const void*>(&combine_kernel), reinterpret_cast<const void*>(&chunk_mass_kernel),
+                       reinterpret_cast<const void*>(&paged_finish_kernel), reinterpret_cast<const void*>(&finalize_kernel),
+                       reinterpret_cast<const void*>(&state_init_kernel), reinterpret_cast<const void*>(&ref_max_kernel),
+                       reinterpret_cast<const void*>(&zero_copy_probe_kernel),
+                       reinterpret_cast<const void*>(&bounded_wait_selftest_kernel), append_kernel_fn(0),
+                       append_kernel_fn(1), append_kernel_fn(2)};
+  for (const void* f : fns) cudaFuncGetAttributes(&fa, f);
+  (void)cudaGetLastError();  // a kernel this build lacks is reported at its launch, not here
+}
+
+// 2D fp32 view [d1][d0], box b0 x b1, no swizzle (score and reference-max tiles).
+int encode_2d_f32(CUtensorMap* map, const void* base, uint64_t d0, uint64_t d1, uint32_t b0, uint32_t b1) {
+  EncodeTiledFn enc;
+  int rc = get_encoder(&enc);
+  if (rc) return rc;
+  cuuint64_t dims[2] = {d0, d1};
+  cuuint64_t strides[1] = {d0 * 4};
+  cuuint32_t box[2] = {b0, b1};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void*>(base), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(PAGER_ERR_INVALID, "cuTensorMapEncodeTiled failed (%d) for a %llu x %llu fp32 view", (int)r,
+                (unsigned long long)d0, (unsigned long long)d1);
+  return PAGER_OK;
+}
+
+// Whether a call runs the two reference-rounding passes: fp32 KV rounds p to fp32, which changes
+// nothing, so the one pass already is the reference's arithmetic there.
+bool exact_rounding(int rounding, int kv_dtype) { return rounding != PAGER_ROUND_ONE_PASS && kv_dtype != PAGER_DTYPE_F32; }
+
+struct PagedLayout {
+  PagedPlan pv;  // the pass that folds V (ONLINE, or VALUES with exact rounding)
+  PagedPlan ps;  // SCORES (exact rounding only)
+  long long s_stride, mstride;
+  Scratch sc;
+  float* scores;
+  float* gmax;
+  float* mref;
+  size_t bytes;
+};
+
+int paged_layout(int batch, int hq, int hkv, int head_dim, int kv_dtype, int tpb, int max_row_tokens, int backend,
+                 int rounding, char* base, PagedLayout* L) {
+  const bool exact = exact_rounding(rounding, kv_dtype);
+  int rc = paged_plan(batch, hq, hkv, head_dim, kv_dtype, tpb, max_row_tokens, backend, &L->pv,
+                      exact ? MODE_VALUES : MODE_ONLINE);
+  if (rc) return rc;
+  const long long rows = (long long)batch * hq;
+  L->sc = layout_scratch(base, rows, L->pv.plan.max_splits, head_dim, L->pv.gstride);
+  size_t off = L->sc.bytes;
+  L->scores = L->gmax = L->mref = nullptr;
+  L->s_stride = L->mstride = 0;
+  if (exact) {
+    rc = paged_plan(batch, hq, hkv, head_dim, kv_dtype, tpb, max_row_tokens, backend, &L->ps, MODE_SCORES);
+    if (rc) return rc;
+    const long long tiles = L->pv.gstride * L->pv.G / L->pv.k.tile;
+    L->s_stride = tiles * L->pv.k.tile;
+    L->mstride = tiles * kRefSlots;
+    auto take = [&](size_t n) {
+      char* p = base ? base + off : nullptr;
+      off += align256(n);
+      return reinterpret_cast<float*>(p);
+    };
+    L->scores = take(sizeof(float) * rows * L->s_stride);
+    L->gmax = take(sizeof(float) * rows * L->pv.gstride);
+    L->mref = take(sizeof(float) * rows * L->mstride);
+  }
+  L->bytes = off;
+  return PAGER_OK;
+}
+
+int run_paged(const PagedArgs& a) {
+  int rc = check_geometry(a.batch, a.num_q_heads, a.num_kv_heads, a.head_dim, a.kv_dtype, a.q_dtype);
+  if (rc) return rc;
+  if (a.batch == 0) return PAGER_OK;
+  if (!dtype_ok(a.out_dtype)) return fail(PAGER_ERR_INVALID, "bad out dtype");
+  if (!is_pow2(a.tokens_per_block) || a.tokens_per_block < 8)
+    return fail(PAGER_ERR_UNSUPPORTED, "tokens_per_block must be a power of two >= 8, got %d", a.tokens_per_block);
+  if (a.num_layers <= 0 || a.layer < 0 || a.layer >= a.num_layers)
+    return fail(PAGER_ERR_INVALID, "layer %d out of range for %d layers", a.layer, a.num_layers);
+  if (!a.q || !a.out || !a.num_blocks || a.max_blocks < 0 || (a.max_blocks > 0 && !a.block_table))
+    return fail(PAGER_ERR_INVALID, "null tensor pointer");
+  if (a.max_row_tokens <= 0) return fail(PAGER_ERR_INVALID, "max_row_tokens must be positive");
+  if (a.tail_len && (!a.tail_k || !a.tail_v || a.tail_cap <= 0)) return fail(PAGER_ERR_INVALID, "tail tensors missing");
+  if ((a.dev_pool && !aligned16(a.dev_pool)) || (a.host_pool && !aligned16(a.host_pool)) ||
+      (a.tail_k && !aligned16(a.tail_k)) || (a.tail_v && !aligned16(a.tail_v)))
+    return fail(PAGER_ERR_INVALID, "pools and tail tensors must be 16-byte aligned");
+  if (a.dev_slots < 0 || a.host_slots < 0 || a.stage_slots < 0) return fail(PAGER_ERR_INVALID, "negative pool capacity");
+  if (a.dev_slots >= (1 << 29) || a.host_slots >= (1 << 29) || a.stage_slots >= (1 << 29))
+    return fail(PAGER_ERR_INVALID, "pool capacity must stay below 2^29 slots (block-table tag bits)");
+  if ((long long)a.dev_slots * a.num_layers * 2 * a.num_kv_heads >= (1LL << 31) ||
+      (long long)a.host_slots * a.num_layers * 2 * a.num_kv_heads >= (1LL << 31) ||
+      (long long)a.stage_slots * 2 * a.num_kv_heads >= (1LL << 31))
+    return fail(PAGER_ERR_INVALID, "pool too large: slots * layers * 2 * kv_heads must stay below 2^31");
+  if (a.stage_pool && !aligned16(a.stage_pool)) return fail(PAGER_ERR_INVALID, "staging buffer must be 16-byte aligned");
+  if (a.mass_mode != PAGER_MASS_NONE && a.mass_mode != PAGER_MASS_ROW_MEAN && a.mass_mode != PAGER_MASS_BATCH_MEAN)
+    return fail(PAGER_ERR_INVALID, "unknown mass mode %d", a.mass_mode);
+  if (a.mass_mode != PAGER_MASS_NONE && !a.mass_accum) return fail(PAGER_ERR_INVALID, "mass_accum is null");
+  if (a.rounding != PAGER_ROUND_ONE_PASS && a.rounding != PAGER_ROUND_RUNNING && a.rounding != PAGER_ROUND_FINAL)
+    return fail(PAGER_ERR_INVALID, "unknown rounding mode %d", a.rounding);
+  const bool exact = exact_rounding(a.rounding, a.kv_dtype);
+  if (exact) {
+    if (backend_for(a.backend, a.kv_dtype, a.head_dim) != PAGER_BACKEND_MMA)
+      return fail(PAGER_ERR_UNSUPPORTED,
+                  "reference rounding runs on the tensor-core kernels (fp16/bf16 KV, head_dim 64, 128 or 256); got "
+                  "dtype %d head_dim %d backend %d",
+                  a.kv_dtype, a.head_dim, a.backend);
+    if (a.rounding == PAGER_ROUND_RUNNING && a.tokens_per_block < 16)
+      return fail(PAGER_ERR_UNSUPPORTED, "running-max reference rounding needs tokens_per_block >= 16, got %d",
+                  a.tokens_per_block);
+  }
+
+  PagedLayout lay;
+  rc = paged_layout(a.batch, a.num_q_heads, a.num_kv_heads, a.head_dim, a.kv_dtype, a.tokens_per_block,
+                    a.max_row_tokens, a.backend, a.rounding, static_cast<char*>(a.scratch), &lay);
+  if (rc) return rc;
+  if (!a.scratch || a.scratch_bytes < lay.bytes)
+    return fail(PAGER_ERR_SCRATCH, "scratch too small: need %zu bytes, got %zu", lay.bytes, a.scratch_bytes);
+  const PagedPlan& pp = lay.pv;
+  const Scratch& sc = lay.sc;
+  const long long rows = (long long)a.batch * a.num_q_heads;
+  DevInfo* di;
+  rc = device_info(&di);
+  if (rc) return rc;
+
+  const long long row_bytes = (long long)a.head_dim * dtype_size(a.kv_dtype);
+  const long long layer_stride = 2LL * a.num_kv_heads * a.tokens_per_block * row_bytes;
+  const int br = a.tokens_per_block < pp.k.tile ? a.tokens_per_block : pp.k.tile;
+  CUtensorMap mk;
+  memset(&mk, 0, sizeof(mk));
+  if (a.dev_pool && a.dev_slots > 0) {
+    const uint64_t z = (uint64_t)a.dev_slots * a.num_layers * 2 * a.num_kv_heads;
+    rc = encode_3d(&mk, a.kv_dtype, a.dev_pool, a.head_dim, a.tokens_per_block, z, pp.k.panel_elts, br,
+                   pp.k.panel_bytes);
+    if (rc) return rc;
+  }
+  CUtensorMap ms;  // staging buffer [stage_slots, 2, Hkv, tpb, D]: one layer of copied host blocks
+  memset(&ms, 0, sizeof(ms));
+  const bool staged = a.stage_pool && a.stage_slots > 0;
+  if (staged) {
+    const uint64_t z = (uint64_t)a.stage_slots * 2 * a.num_kv_heads;
+    rc = encode_3d(&ms, a.kv_dtype, a.stage_pool, a.head_dim, a.tokens_per_block, z, pp.k.panel_elts, br,
+                   pp.k.panel_bytes);
+    if (rc) return rc;
+  }
+  CUtensorMap mS, mM;  // exact rounding: score tiles [n_rep][TILE] and reference maxima [n_rep][kRefSlots]
+  memset(&mS, 0, sizeof(mS));
+  memset(&mM, 0, sizeof(mM));
+  const int n_rep = a.num_q_heads / a.num_kv_heads;
+  if (exact) {
+    rc = encode_2d_f32(&mS, lay.scores, (uint64_t)lay.s_stride, (uint64_t)rows, (uint32_t)pp.k.tile, (uint32_t)n_rep);
+    if (rc) return rc;
+    rc = encode_2d_f32(&mM, lay.mref, (uint64_t)lay.mstride, (uint64_t)rows, (uint32_t)kRefSlots, (uint32_t)n_rep);
+    if (rc) return rc;
+  }
+  SplitParams p;
+  memset(&p, 0, sizeof(p));
+  p.q = a.q;
+  p.q_dtype = a.q_dtype;
+  p.batch = a.batch;
+  p.num_q_heads = a.num_q_heads;
+  p.num_kv_heads = a.num_kv_heads;
+  p.n_rep = n_rep;
+  p.scale = a.scale;
+  p.softcap = a.softcap > 0.f ? a.softcap : 0.f;
+  p.source = SRC_PAGED;
+  p.dev_pool = (a.dev_pool && a.dev_slots > 0) ? static_cast<const char*>(a.dev_pool) : nullptr;
+  p.host_pool = (a.host_pool && a.host_slots > 0) ? static_cast<const char*>(a.host_pool) : nullptr;
+  p.stage_pool = staged ? static_cast<const char*>(a.stage_pool) : nullptr;
+  p.stage_slots = staged ? a.stage_slots : 0;
+  p.slot_stride_bytes = layer_stride * a.num_layers;
+  p.layer_stride_bytes = layer_stride;
+  p.num_layers = a.num_layers;
+  p.layer = a.layer;
+  p.tpb = a.tokens_per_block;
+  p.log2_tpb = ilog2(a.tokens_per_block);
+  p.dev_slots = a.dev_slots;
+  p.host_slots = a.host_slots;
+  p.block_table = a.block_table;
+  p.max_blocks = a.max_blocks;
+  p.tail_k = static_cast<const char*>(a.tail_k);
+  p.tail_v = static_cast<const char*>(a.tail_v);
+  p.tail_cap = a.tail_cap;
+  p.geom.source = SRC_PAGED;
+  p.geom.tpb = a.tokens_per_block;
+  p.geom.num_blocks = a.num_blocks;
+  p.geom.max_blocks = a.max_blocks;
+  p.geom.tail_len = a.tail_len;
+  p.geom.tail_cap = a.tail_len ? a.tail_cap : 0;
+  p.geom.max_tokens = a.max_row_tokens;
+  p.geom.valid_lo = a.valid_lo;
+  p.geom.valid_hi = a.valid_hi;
+  p.active = a.active;
+  p.part_m = sc.part_m;
+  p.part_l = sc.part_l;
+  p.part_acc = sc.part_acc;
+  p.mass_part = sc.mass_part;
+  p.mass_gstride = (int)pp.gstride;
+  p.group_tokens = pp.G;
+  p.log2_group = ilog2(pp.G);
+  p.scores = lay.scores;
+  p.s_stride = lay.s_stride;
+  p.gmax = lay.gmax;
+  p.wait_limit_ns = kWaitLimitNs;
+  p.status = di->status;
+
+  cudaStream_t st = (cudaStream_t)a.stream;
+  CUtensorMap* map2 = staged ? &ms : &mk;
+  if (exact) {
+    SplitParams ps = p;  // SCORES: its own split plan over the same tiles
+    ps.tiles_per_split = lay.ps.plan.tiles_per_split;
+    ps.max_splits = lay.ps.plan.max_splits;
+    dim3 grid_s(lay.ps.plan.max_splits, a.num_kv_heads, a.batch);
+    void* sargs[] = {&ps, &mk, map2, &mS, &mM};
+    PAGER_CUDA(launch_serialized(lay.ps.k.fn, grid_s, dim3(lay.ps.k.threads), lay.ps.k.smem_bytes, st, sargs),
+               "scores kernel launch");
+    RefMaxParams rp;
+    memset(&rp, 0, sizeof(rp));
+    rp.geom = p.geom;
+    rp.active = a.active;
+    rp.rows = (int)rows;
+    rp.num_q_heads = a.num_q_heads;
+    rp.tile_shift = ilog2(pp.k.tile);
+    rp.tiles_per_split = pp.plan.tiles_per_split;
+    rp.group_shift = ilog2(pp.G);
+    rp.gstride = (int)pp.gstride;
+    rp.mstride = (int)lay.mstride;
+    rp.tpb = a.tokens_per_block;
+    rp.rule = a.rounding;
+    rp.ref_group_tokens = a.ref_group_tokens;
+    rp.ref_shift = a.ref_shift;
+    rp.ref_tail_start = a.ref_tail_start;
+    rp.gmax = lay.gmax;
+    rp.mref = lay.mref;
+    void* rargs[] = {&rp};
+    PAGER_CUDA(launch_serialized(reinterpret_cast<const void*>(&ref_max_kernel),
+                                 dim3((unsigned)((rows + kRefMaxWarps - 1) / kRefMaxWarps)), dim3(kRefMaxWarps * 32), 0,
+                                 st, rargs),
+               "reference-max launch");
+  }
+  p.tiles_per_split = pp.plan.tiles_per_split;
+  p.max_splits = pp.plan.max_splits;
+  dim3 grid(pp.plan.max_splits, a.num_kv_heads, a.batch);
+  void* args[] = {&p, &mk, map2, &mS, &mM};
+  PAGER_CUDA(launch_serialized(pp.k.fn, grid, dim3(pp.k.threads), pp.k.smem_bytes, st, args), "split kernel launch");
+
+  CombineParams c;
+  memset(&c, 0, sizeof(c));
+  c.num_q_heads = a.num_q_heads;
+  c.head_dim = a.head_dim;
+  c.tile_shift = ilog2(pp.k.tile);
+  c.tiles_per_split = pp.plan.tiles_per_split;
+  c.max_splits = pp.plan.max_splits;
+  c.geom = p.geom;
+  c.active = a.active;
+  c.part_m = sc.part_m;
+  c.part_l = sc.part_l;
+  c.part_acc = sc.part_acc;
+  c.op = OP_PAGED;
+  c.out = a.out;
+  c.out_dtype = a.out_dtype;
+  PagedMassParams mp;
+  memset(&mp, 0, sizeof(mp));
+  int mass_x = 1, mass_y = 0;
+  if ((a.block_mass || a.mass_mode != PAGER_MASS_NONE) && a.max_blocks > 0) {
+    mp.mass_part = sc.mass_part;
+    mp.gstride = (int)pp.gstride;
+    mp.group_shift = ilog2(pp.G);
+    mp.tile_shift = ilog2(pp.k.tile);
+    mp.tpb = a.tokens_per_block;
+    mp.tiles_per_split = pp.plan.tiles_per_split;
+    mp.geom = p.geom;
+    mp.active = a.active;
+    mp.part_m = sc.part_m;
+    mp.part_l = sc.part_l;
+    mp.max_splits = pp.plan.max_splits;
+    mp.batch = a.batch;
+    mp.num_q_heads = a.num_q_heads;
+    mp.max_blocks = a.max_blocks;
+    mp.block_mass = a.block_mass;
+    mp.mass_accum = a.mass_accum;
+    mp.mass_mode = a.mass_mode;
+    mass_x = (a.max_blocks + 31) / 32;
+    mass_y = a.mass_mode == PAGER_MASS_BATCH_MEAN ? 1 : a.batch;
+  }
+  int rows_i = (int)rows;
+  const long long ctas = rows + (long long)mass_x * mass_y;
+  if (ctas >= (1LL << 31)) return fail(PAGER_ERR_INVALID, "too many rows and blocks for one launch");
+  void* fargs[] = {&c, &mp, &rows_i, &mass_x};
+  PAGER_CUDA(launch_serialized(reinterpret_cast<const void*>(&paged_finish_kernel), dim3((unsigned)ctas),
+                               dim3(kFinishThreads), 0, st, fargs),
+             "combine/mass launch");
+  return PAGER_OK;
+}
+
+}  // namespace
+}  // namespace pager
+
+extern "C" {
+
 int pager_paged_decode_attention_staged(const void* q, int q_dtype, const void* dev_pool, int dev_slots,
                                         const void* host_pool, int host_slots, const void* stage_pool,
                                         int stage_slots, int kv_dtype, int num_layers, int layer, int num_kv_heads,
@@ -1005,165 +1446,85 @@ int pager_paged_decode_attention_staged(const void* q, int q_dtype, const void* 
                                         void* out, int out_dtype, float* block_mass, float* mass_accum,
                                         int mass_mode, int backend, void* scratch, size_t scratch_bytes,
                                         void* stream) {
-  int rc = check_geometry(batch, num_q_heads, num_kv_heads, head_dim, kv_dtype, q_dtype);
-  if (rc) return rc;
-  if (batch == 0) return PAGER_OK;
-  if (!dtype_ok(out_dtype)) return fail(PAGER_ERR_INVALID, "bad out dtype");
-  if (!is_pow2(tokens_per_block) || tokens_per_block < 8)
-    return fail(PAGER_ERR_UNSUPPORTED, "tokens_per_block must be a power of two >= 8, got %d", tokens_per_block);
-  if (num_layers <= 0 || layer < 0 || layer >= num_layers)
-    return fail(PAGER_ERR_INVALID, "layer %d out of range for %d layers", layer, num_layers);
-  if (!q || !out || !num_blocks || max_blocks < 0 || (max_blocks > 0 && !block_table))
-    return fail(PAGER_ERR_INVALID, "null tensor pointer");
-  if (max_row_tokens <= 0) return fail(PAGER_ERR_INVALID, "max_row_tokens must be positive");
-  if (tail_len && (!tail_k || !tail_v || tail_cap <= 0)) return fail(PAGER_ERR_INVALID, "tail tensors missing");
-  if ((dev_pool && !aligned16(dev_pool)) || (host_pool && !aligned16(host_pool)) || (tail_k && !aligned16(tail_k)) ||
-      (tail_v && !aligned16(tail_v)))
-    return fail(PAGER_ERR_INVALID, "pools and tail tensors must be 16-byte aligned");
-  if (dev_slots < 0 || host_slots < 0 || stage_slots < 0) return fail(PAGER_ERR_INVALID, "negative pool capacity");
-  if (dev_slots >= (1 << 29) || host_slots >= (1 << 29) || stage_slots >= (1 << 29))
-    return fail(PAGER_ERR_INVALID, "pool capacity must stay below 2^29 slots (block-table tag bits)");
-  if ((long long)dev_slots * num_layers * 2 * num_kv_heads >= (1LL << 31) ||
-      (long long)host_slots * num_layers * 2 * num_kv_heads >= (1LL << 31) ||
-      (long long)stage_slots * 2 * num_kv_heads >= (1LL << 31))
-    return fail(PAGER_ERR_INVALID, "pool too large: slots * layers * 2 * kv_heads must stay below 2^31");
-  if (stage_pool && !aligned16(stage_pool)) return fail(PAGER_ERR_INVALID, "staging buffer must be 16-byte aligned");
-  if (mass_mode != PAGER_MASS_NONE && mass_mode != PAGER_MASS_ROW_MEAN && mass_mode != PAGER_MASS_BATCH_MEAN)
-    return fail(PAGER_ERR_INVALID, "unknown mass mode %d", mass_mode);
-  if (mass_mode != PAGER_MASS_NONE && !mass_accum) return fail(PAGER_ERR_INVALID, "mass_accum is null");
+  return pager_paged_decode_attention_rounded(
+      q, q_dtype, dev_pool, dev_slots, host_pool, host_slots, stage_pool, stage_slots, kv_dtype, num_layers, layer,
+      num_kv_heads, tokens_per_block, head_dim, block_table, max_blocks, num_blocks, tail_k, tail_v, tail_len,
+      tail_cap, valid_lo, valid_hi, active, batch, num_q_heads, scale, softcap, max_row_tokens, out, out_dtype,
+      block_mass, mass_accum, mass_mode, backend, PAGER_ROUND_ONE_PASS, 0, nullptr, nullptr, scratch, scratch_bytes,
+      stream);
+}
 
-  PagedPlan pp;
-  rc = paged_plan(batch, num_q_heads, num_kv_heads, head_dim, kv_dtype, tokens_per_block, max_row_tokens, backend, &pp);
-  if (rc) return rc;
-  const long long rows = (long long)batch * num_q_heads;
-  Scratch sc = layout_scratch(static_cast<char*>(scratch), rows, pp.plan.max_splits, head_dim, pp.gstride);
-  if (!scratch || scratch_bytes < sc.bytes)
-    return fail(PAGER_ERR_SCRATCH, "scratch too small: need %zu bytes, got %zu", sc.bytes, scratch_bytes);
-  DevInfo* di;
-  rc = device_info(&di);
-  if (rc) return rc;
+size_t pager_paged_decode_scratch_bytes_rounded(int batch, int num_q_heads, int num_kv_heads, int head_dim,
+                                                int kv_dtype, int tokens_per_block, int max_row_tokens,
+                                                int rounding) {
+  if (!exact_rounding(rounding, kv_dtype))
+    return pager_paged_decode_scratch_bytes(batch, num_q_heads, num_kv_heads, head_dim, kv_dtype, tokens_per_block,
+                                            0, max_row_tokens);
+  if (check_geometry(batch, num_q_heads, num_kv_heads, head_dim, kv_dtype, kv_dtype)) return 0;
+  if (batch <= 0 || max_row_tokens <= 0 || !is_pow2(tokens_per_block) || tokens_per_block < 8) return 0;
+  PagedLayout lay;
+  if (paged_layout(batch, num_q_heads, num_kv_heads, head_dim, kv_dtype, tokens_per_block, max_row_tokens,
+                   PAGER_BACKEND_MMA, rounding, nullptr, &lay))
+    return 0;
+  return lay.bytes;
+}
 
-  const long long row_bytes = (long long)head_dim * dtype_size(kv_dtype);
-  const long long layer_stride = 2LL * num_kv_heads * tokens_per_block * row_bytes;
-  CUtensorMap mk;
-  memset(&mk, 0, sizeof(mk));
-  if (dev_pool && dev_slots > 0) {
-    const uint64_t z = (uint64_t)dev_slots * num_layers * 2 * num_kv_heads;
-    const int br = tokens_per_block < pp.k.tile ? tokens_per_block : pp.k.tile;
-    rc = encode_3d(&mk, kv_dtype, dev_pool, head_dim, tokens_per_block, z, pp.k.panel_elts, br, pp.k.panel_bytes);
-    if (rc) return rc;
-  }
-  CUtensorMap ms;  // staging buffer [stage_slots, 2, Hkv, tpb, D]: one layer of copied host blocks
-  memset(&ms, 0, sizeof(ms));
-  const bool staged = stage_pool && stage_slots > 0;
-  if (staged) {
-    const uint64_t z = (uint64_t)stage_slots * 2 * num_kv_heads;
-    const int br = tokens_per_block < pp.k.tile ? tokens_per_block : pp.k.tile;
-    rc = encode_3d(&ms, kv_dtype, stage_pool, head_dim, tokens_per_block, z, pp.k.panel_elts, br, pp.k.panel_bytes);
-    if (rc) return rc;
-  }
-  SplitParams p;
-  memset(&p, 0, sizeof(p));
-  p.q = q;
-  p.q_dtype = q_dtype;
-  p.batch = batch;
-  p.num_q_heads = num_q_heads;
-  p.num_kv_heads = num_kv_heads;
-  p.n_rep = num_q_heads / num_kv_heads;
-  p.scale = scale;
-  p.softcap = softcap > 0.f ? softcap : 0.f;
-  p.source = SRC_PAGED;
-  p.dev_pool = (dev_pool && dev_slots > 0) ? static_cast<const char*>(dev_pool) : nullptr;
-  p.host_pool = (host_pool && host_slots > 0) ? static_cast<const char*>(host_pool) : nullptr;
-  p.stage_pool = staged ? static_cast<const char*>(stage_pool) : nullptr;
-  p.stage_slots = staged ? stage_slots : 0;
-  p.slot_stride_bytes = layer_stride * num_layers;
-  p.layer_stride_bytes = layer_stride;
-  p.num_layers = num_layers;
-  p.layer = layer;
-  p.tpb = tokens_per_block;
-  p.log2_tpb = ilog2(tokens_per_block);
-  p.dev_slots = dev_slots;
-  p.host_slots = host_slots;
-  p.block_table = block_table;
-  p.max_blocks = max_blocks;
-  p.tail_k = static_cast<const char*>(tail_k);
-  p.tail_v = static_cast<const char*>(tail_v);
-  p.tail_cap = tail_cap;
-  p.geom.source = SRC_PAGED;
-  p.geom.tpb = tokens_per_block;
-  p.geom.num_blocks = num_blocks;
-  p.geom.max_blocks = max_blocks;
-  p.geom.tail_len = tail_len;
-  p.geom.tail_cap = tail_len ? tail_cap : 0;
-  p.geom.max_tokens = max_row_tokens;
-  p.geom.valid_lo = valid_lo;
-  p.geom.valid_hi = valid_hi;
-  p.active = active;
-  p.tiles_per_split = pp.plan.tiles_per_split;
-  p.max_splits = pp.plan.max_splits;
-  p.part_m = sc.part_m;
-  p.part_l = sc.part_l;
-  p.part_acc = sc.part_acc;
-  p.mass_part = sc.mass_part;
-  p.mass_gstride = (int)pp.gstride;
-  p.group_tokens = pp.G;
-  p.log2_group = ilog2(pp.G);
-  p.wait_limit_ns = kWaitLimitNs;
-  p.status = di->status;
-
-  cudaStream_t st = (cudaStream_t)stream;
-  dim3 grid(pp.plan.max_splits, num_kv_heads, batch);
-  void* args[] = {&p, &mk, staged ? &ms : &mk};
-  PAGER_CUDA(launch_serialized(pp.k.fn, grid, dim3(pp.k.threads), pp.k.smem_bytes, st, args), "split kernel launch");
-
-  CombineParams c;
-  memset(&c, 0, sizeof(c));
-  c.num_q_heads = num_q_heads;
-  c.head_dim = head_dim;
-  c.tile_shift = ilog2(pp.k.tile);
-  c.tiles_per_split = pp.plan.tiles_per_split;
-  c.max_splits = pp.plan.max_splits;
-  c.geom = p.geom;
-  c.active = active;
-  c.part_m = sc.part_m;
-  c.part_l = sc.part_l;
-  c.part_acc = sc.part_acc;
-  c.op = OP_PAGED;
-  c.out = out;
-  c.out_dtype = out_dtype;
-  PagedMassParams mp;
-  memset(&mp, 0, sizeof(mp));
-  int mass_x = 1, mass_y = 0;
-  if ((block_mass || mass_mode != PAGER_MASS_NONE) && max_blocks > 0) {
-    mp.mass_part = sc.mass_part;
-    mp.gstride = (int)pp.gstride;
-    mp.group_shift = ilog2(pp.G);
-    mp.tile_shift = ilog2(pp.k.tile);
-    mp.tpb = tokens_per_block;
-    mp.tiles_per_split = pp.plan.tiles_per_split;
-    mp.geom = p.geom;
-    mp.active = active;
-    mp.part_m = sc.part_m;
-    mp.part_l = sc.part_l;
-    mp.max_splits = pp.plan.max_splits;
-    mp.batch = batch;
-    mp.num_q_heads = num_q_heads;
-    mp.max_blocks = max_blocks;
-    mp.block_mass = block_mass;
-    mp.mass_accum = mass_accum;
-    mp.mass_mode = mass_mode;
-    mass_x = (max_blocks + 31) / 32;
-    mass_y = mass_mode == PAGER_MASS_BATCH_MEAN ? 1 : batch;
-  }
-  int rows_i = (int)rows;
-  const long long ctas = rows + (long long)mass_x * mass_y;
-  if (ctas >= (1LL << 31)) return fail(PAGER_ERR_INVALID, "too many rows and blocks for one launch");
-  void* fargs[] = {&c, &mp, &rows_i, &mass_x};
-  PAGER_CUDA(launch_serialized(reinterpret_cast<const void*>(&paged_finish_kernel), dim3((unsigned)ctas),
-                               dim3(kFinishThreads), 0, st, fargs),
-             "combine/mass launch");
-  return PAGER_OK;
+int pager_paged_decode_attention_rounded(const void* q, int q_dtype, const void* dev_pool, int dev_slots,
+                                         const void* host_pool, int host_slots, const void* stage_pool,
+                                         int stage_slots, int kv_dtype, int num_layers, int layer, int num_kv_heads,
+                                         int tokens_per_block, int head_dim, const int32_t* block_table,
+                                         int max_blocks, const int32_t* num_blocks, const void* tail_k,
+                                         const void* tail_v, const int32_t* tail_len, int tail_cap,
+                                         const int32_t* valid_lo, const int32_t* valid_hi, const int32_t* active,
+                                         int batch, int num_q_heads, float scale, float softcap, int max_row_tokens,
+                                         void* out, int out_dtype, float* block_mass, float* mass_accum,
+                                         int mass_mode, int backend, int rounding, int ref_group_tokens,
+                                         const int32_t* ref_shift, const int32_t* ref_tail_start, void* scratch,
+                                         size_t scratch_bytes, void* stream) {
+  PagedArgs a;
+  a.q = q;
+  a.q_dtype = q_dtype;
+  a.dev_pool = dev_pool;
+  a.dev_slots = dev_slots;
+  a.host_pool = host_pool;
+  a.host_slots = host_slots;
+  a.stage_pool = stage_pool;
+  a.stage_slots = stage_slots;
+  a.kv_dtype = kv_dtype;
+  a.num_layers = num_layers;
+  a.layer = layer;
+  a.num_kv_heads = num_kv_heads;
+  a.tokens_per_block = tokens_per_block;
+  a.head_dim = head_dim;
+  a.block_table = block_table;
+  a.max_blocks = max_blocks;
+  a.num_blocks = num_blocks;
+  a.tail_k = tail_k;
+  a.tail_v = tail_v;
+  a.tail_len = tail_len;
+  a.tail_cap = tail_cap;
+  a.valid_lo = valid_lo;
+  a.valid_hi = valid_hi;
+  a.active = active;
+  a.batch = batch;
+  a.num_q_heads = num_q_heads;
+  a.scale = scale;
+  a.softcap = softcap;
+  a.max_row_tokens = max_row_tokens;
+  a.out = out;
+  a.out_dtype = out_dtype;
+  a.block_mass = block_mass;
+  a.mass_accum = mass_accum;
+  a.mass_mode = mass_mode;
+  a.backend = backend;
+  a.rounding = rounding;
+  a.ref_group_tokens = ref_group_tokens;
+  a.ref_shift = ref_shift;
+  a.ref_tail_start = ref_tail_start;
+  a.scratch = scratch;
+  a.scratch_bytes = scratch_bytes;
+  a.stream = stream;
+  return run_paged(a);
 }
 
 int pager_selftest_bounded_wait(unsigned long long limit_ns, unsigned long long* waited_ns, void* stream) {

@@ -68,6 +68,16 @@ int fail(int code, const char* msg) {
 
 }  // namespace
 
+namespace pager {
+// The append kernels (by copy unit: 16, 4, 2 bytes), for the library's load of every kernel at its
+// first call on a device.
+const void* append_kernel_fn(int i) {
+  return i == 0 ? reinterpret_cast<const void*>(&append_tokens_kernel<16>)
+                : (i == 1 ? reinterpret_cast<const void*>(&append_tokens_kernel<4>)
+                          : reinterpret_cast<const void*>(&append_tokens_kernel<2>));
+}
+}  // namespace pager
+
 extern "C" int pager_append_tokens(void* pool, int dtype, int pool_slots, int num_layers, int layer,
                                    int num_kv_heads, int tokens_per_block, int head_dim, const int32_t* slots,
                                    const int32_t* positions, const void* k_new, const void* v_new, int batch,

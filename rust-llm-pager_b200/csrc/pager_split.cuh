@@ -19,6 +19,19 @@
 // partials (sum of p over `group_tokens` tokens, with the running max it is
 // relative to), from which the per-block mass is assembled without a second
 // pass over KV.
+//
+// Reference-exact rounding of P (the reference rounds p = exp(s - m) to the
+// value dtype before P.V, with m its running max at each 64-token tile in
+// sequence order, or the final max in its two-pass path; a split-KV pass
+// cannot know either, so its roundings differ in about half of the bf16
+// outputs).  Two more modes do the same arithmetic in two passes without
+// reading K twice:
+//   SCORES  K only: writes the masked fp32 scores of every attended tile and
+//           the max of every `group_tokens` group; a small scan kernel turns
+//           the group maxima into the reference's max for each group.
+//   VALUES  V only: the producer brings each tile's scores and reference
+//           maxima in by TMA next to the V tile; p is formed against the
+//           reference max of its group, rounded, and folded like ONLINE.
 #pragma once
 
 #include <type_traits>
@@ -27,7 +40,7 @@
 
 namespace pager {
 
-enum Mode { MODE_ONLINE = 0, MODE_STATS = 1, MODE_FIXED = 2 };
+enum Mode { MODE_ONLINE = 0, MODE_STATS = 1, MODE_FIXED = 2, MODE_SCORES = 3, MODE_VALUES = 4 };
 enum Source { SRC_CONTIG = 0, SRC_PAGED = 1 };
 enum Backend { BACKEND_MMA = 1, BACKEND_FMA = 2 };
 
@@ -139,9 +152,15 @@ struct SplitParams {
   int mass_gstride;
   int group_tokens;  // 0: no mass partials
   int log2_group;
+  // MODE_SCORES outputs (MODE_VALUES reads them back through its tensor maps)
+  float* scores;       // [B*Hq, s_stride]: masked scores of every attended tile
+  long long s_stride;  // tokens per score row (the plan's tiles * TILE)
+  float* gmax;         // [B*Hq, mass_gstride]: max score of every group_tokens group
   unsigned long long wait_limit_ns;
   int* status;
 };
+
+constexpr int kRefSlots = 8;  // reference-max entries per tile in the VALUES pass (groups per tile <= 8)
 
 constexpr int kTableCache = 1024;  // block-table entries cached in shared memory per CTA
 
@@ -160,7 +179,13 @@ struct TileCfg {
   static constexpr int SWZ_MASK = CPP - 1;
   static constexpr int PANEL_TILE_BYTES = TILE * PANEL_BYTES;
   static constexpr int TENSOR_BYTES = TILE * ROW_BYTES;
-  static constexpr int STAGE_BYTES = (MODE == MODE_STATS ? 1 : 2) * TENSOR_BYTES;
+  static constexpr bool KONLY = MODE == MODE_STATS || MODE == MODE_SCORES;  // K tiles only
+  static constexpr bool VONLY = MODE == MODE_VALUES;                         // V tiles only
+  static constexpr int STAGE_BYTES = (KONLY || VONLY ? 1 : 2) * TENSOR_BYTES;
+  // VALUES: a second ring beside the tensor ring holds each stage's score tile [n_rep][TILE] and
+  // reference maxima [n_rep][kRefSlots] (fp32, no swizzle), filled by the same full barrier.
+  static constexpr int AUX_S_BYTES = VONLY ? kMaxRep * TILE * 4 : 0;
+  static constexpr int AUX_BYTES = VONLY ? (AUX_S_BYTES + kMaxRep * kRefSlots * 4 + 127) / 128 * 128 : 0;
   // Shared memory outside the stage ring: Q (bf16/fp16 for mma, fp32 for fma), the fma
   // path's P buffer, the block-table cache, barriers.
   // CTA shape.  Tensor-core configs: 3 consumer warps + 1 producer warp in 128 threads, two CTAs
@@ -172,16 +197,16 @@ struct TileCfg {
   static constexpr int THREADS = (NCW + NPW) * 32;
   static constexpr int MIN_BLOCKS = BACKEND == BACKEND_MMA ? 2 : 1;
   static constexpr int SMEM_BUDGET = BACKEND == BACKEND_MMA ? 110 * 1024 : 225 * 1024;
-  static constexpr int Q_BYTES = BACKEND == BACKEND_FMA ? kMaxRep * D * 4 : kMaxRep * D * ELT;
+  static constexpr int Q_BYTES = VONLY ? 0 : (BACKEND == BACKEND_FMA ? kMaxRep * D * 4 : kMaxRep * D * ELT);
   static constexpr int P_BYTES = BACKEND == BACKEND_FMA ? NCW * TILE * kMaxRep * 4 : 0;
   static constexpr int EXTRA = Q_BYTES + P_BYTES + kTableCache * 4 + 1536;
   // A deep ring: each consumer warp holds a stage while it computes, the rest stay in flight.
   // Even, so that with two producer warps each stage is always filled by the same one.
-  static constexpr int STAGES_RAW = ((SMEM_BUDGET - EXTRA) / STAGE_BYTES) & ~1;
+  static constexpr int STAGES_RAW = ((SMEM_BUDGET - EXTRA) / (STAGE_BYTES + AUX_BYTES)) & ~1;
   static constexpr int STAGES = STAGES_RAW > 16 ? 16 : STAGES_RAW;
   static_assert(STAGES >= NCW && STAGES % 2 == 0, "stage ring too shallow for the consumer warps");
   static constexpr int STAGE_AREA = STAGES * STAGE_BYTES;
-  static constexpr int MERGE_BYTES = NCW * kMaxRep * (2 + (MODE == MODE_STATS ? 0 : D)) * 4;
+  static constexpr int MERGE_BYTES = NCW * kMaxRep * (2 + (KONLY ? 0 : D)) * 4;
   static_assert(MERGE_BYTES <= STAGE_AREA, "merge region must fit in the stage ring");
   static_assert((TILE & (TILE - 1)) == 0 && TILE >= 16 && TILE <= 64, "tile");
 };
@@ -305,7 +330,7 @@ __device__ __forceinline__ void sw_copy_rows(uint32_t tile_base, int row0, const
 // over the host link) and tail rows -- are copied into the stage by the
 // consumer warp that owns the tile, with 16-byte loads.  `mask` has one bit per
 // segment of min(TILE, tokens_per_block) rows.
-template <class Cfg, bool kNeedV>
+template <class Cfg, bool kNeedK, bool kNeedV>
 __device__ __forceinline__ void copy_sw_segments(const SplitParams& p, const TableCache& tc, const RowGeom& g, int b,
                                                  int h, int t0, uint32_t mask, uint8_t* kbuf, uint8_t* vbuf) {
   // Slow path (host-pool blocks, tail rows): fields are read from the parameter block here
@@ -337,7 +362,7 @@ __device__ __forceinline__ void copy_sw_segments(const SplitParams& p, const Tab
       vdelta = p.tail_v - p.tail_k;
       n = min(br, g.ntok - tok);
     }
-    sw_copy_rows<Cfg>(kaddr, sg * br, ksrc, n);
+    if (kNeedK) sw_copy_rows<Cfg>(kaddr, sg * br, ksrc, n);
     if (kNeedV) sw_copy_rows<Cfg>(vaddr, sg * br, ksrc + vdelta, n);
   }
   __syncwarp();
@@ -351,17 +376,23 @@ __device__ __forceinline__ void copy_sw_segments(const SplitParams& p, const Tab
 // holding data) and arrive on the stage's full barrier (release).
 template <class Cfg, int MODE>
 __device__ void run_producer(const SplitParams& p, const TableCache& tc, const CUtensorMap* mapk,
-                             const CUtensorMap* mapv, uint8_t* stages, uint64_t* full, uint64_t* empty,
-                             volatile int* infos, int b, int h, int tile0, int ntiles, const RowGeom& g,
-                             volatile int* abort_flag, int producer) {
+                             const CUtensorMap* mapv, const CUtensorMap* maps, const CUtensorMap* mapm,
+                             uint8_t* stages, uint8_t* aux, uint64_t* full, uint64_t* empty, volatile int* infos,
+                             int b, int h, int tile0, int ntiles, const RowGeom& g, volatile int* abort_flag,
+                             int producer) {
   if ((threadIdx.x & 31) != 0) return;
-  constexpr bool kNeedV = MODE != MODE_STATS;
+  constexpr bool kNeedK = !Cfg::VONLY;
+  constexpr bool kNeedV = !Cfg::KONLY;
   const Hot k = load_hot(p);
+  // VALUES: the tile's scores [n_rep][TILE] and reference maxima [n_rep][kRefSlots] (rows of the query
+  // heads of KV head h), fetched with the V tile under the same full barrier
+  const int aux_row0 = b * p.num_q_heads + h * p.n_rep;
+  const uint32_t aux_tx = Cfg::VONLY ? (uint32_t)p.n_rep * (Cfg::TILE + kRefSlots) * 4u : 0u;
   const int zc = b * k.hkv + h;  // contiguous source: (row, kv head) plane
   const int br = min(Cfg::TILE, k.tpb);
   const int nseg = Cfg::TILE / br;
   const int block_tokens = g.nb * k.tpb;
-  const uint32_t seg_bytes = (uint32_t)br * Cfg::ROW_BYTES * (kNeedV ? 2u : 1u);
+  const uint32_t seg_bytes = (uint32_t)br * Cfg::ROW_BYTES * ((kNeedK ? 1u : 0u) + (kNeedV ? 1u : 0u));
   int last = -1;
   for (int i = producer; i < ntiles; i += Cfg::NPW) {
     const int s = i % Cfg::STAGES;
@@ -372,16 +403,22 @@ __device__ void run_producer(const SplitParams& p, const TableCache& tc, const C
       break;
     }
     uint8_t* kbuf = stages + s * Cfg::STAGE_BYTES;
-    uint8_t* vbuf = kbuf + Cfg::TENSOR_BYTES;
+    uint8_t* vbuf = Cfg::VONLY ? kbuf : kbuf + Cfg::TENSOR_BYTES;
     const int t0 = (tile0 + i) * Cfg::TILE;
     uint32_t sw_mask = 0;
     uint32_t present = 0;  // segments whose rows hold data (device, host or tail)
+    if (Cfg::VONLY) {
+      uint8_t* a = aux + s * Cfg::AUX_BYTES;
+      mbar_expect_tx(&full[s], aux_tx);
+      tma_load_2d(a, maps, t0, aux_row0, &full[s]);
+      tma_load_2d(a + Cfg::AUX_S_BYTES, mapm, (tile0 + i) * kRefSlots, aux_row0, &full[s]);
+    }
     if (k.source == SRC_CONTIG) {
       present = 1u;  // one segment: the whole tile
       mbar_expect_tx(&full[s], (uint32_t)Cfg::STAGE_BYTES);
 #pragma unroll
       for (int pn = 0; pn < Cfg::NPANEL; ++pn) {
-        tma_load_3d(kbuf + pn * Cfg::PANEL_TILE_BYTES, mapk, pn * Cfg::PANEL_ELTS, t0, zc, &full[s]);
+        if (kNeedK) tma_load_3d(kbuf + pn * Cfg::PANEL_TILE_BYTES, mapk, pn * Cfg::PANEL_ELTS, t0, zc, &full[s]);
         if (kNeedV) tma_load_3d(vbuf + pn * Cfg::PANEL_TILE_BYTES, mapv, pn * Cfg::PANEL_ELTS, t0, zc, &full[s]);
       }
     } else {
@@ -413,7 +450,7 @@ __device__ void run_producer(const SplitParams& p, const TableCache& tc, const C
 #pragma unroll
         for (int pn = 0; pn < Cfg::NPANEL; ++pn) {
           const int off = pn * Cfg::PANEL_TILE_BYTES + sg * br * Cfg::PANEL_BYTES;
-          tma_load_3d(kbuf + off, map, pn * Cfg::PANEL_ELTS, y, zk, &full[s]);
+          if (kNeedK) tma_load_3d(kbuf + off, map, pn * Cfg::PANEL_ELTS, y, zk, &full[s]);
           if (kNeedV) tma_load_3d(vbuf + off, map, pn * Cfg::PANEL_ELTS, y, zk + k.hkv, &full[s]);
         }
       }
@@ -562,27 +599,28 @@ __device__ void merge_and_store(const SplitParams& p, float* mw, int b, int h, i
       p.part_l[o] = L;
     }
   }
-  if constexpr (MODE == MODE_STATS) return;
-  for (int idx = tid; idx < n_rep * D; idx += NCW * 32) {
-    const int r = idx / D;
-    const int d = idx % D;
-    float A = 0.f;
-    if (MODE == MODE_FIXED) {
+  if constexpr (MODE != MODE_STATS) {
+    for (int idx = tid; idx < n_rep * D; idx += NCW * 32) {
+      const int r = idx / D;
+      const int d = idx % D;
+      float A = 0.f;
+      if (MODE == MODE_FIXED) {
 #pragma unroll
-      for (int w = 0; w < NCW; ++w) A += acc_w[(w * kMaxRep + r) * D + d];
-    } else {
-      float M = neg_inf();
+        for (int w = 0; w < NCW; ++w) A += acc_w[(w * kMaxRep + r) * D + d];
+      } else {
+        float M = neg_inf();
 #pragma unroll
-      for (int w = 0; w < NCW; ++w) M = fmaxf(M, m_w[w * kMaxRep + r]);
+        for (int w = 0; w < NCW; ++w) M = fmaxf(M, m_w[w * kMaxRep + r]);
 #pragma unroll
-      for (int w = 0; w < NCW; ++w) {
-        const float mwr = m_w[w * kMaxRep + r];
-        const float wt = mwr == neg_inf() ? 0.f : fast_exp2((mwr - M) * kLog2e);
-        A += wt * acc_w[(w * kMaxRep + r) * D + d];
+        for (int w = 0; w < NCW; ++w) {
+          const float mwr = m_w[w * kMaxRep + r];
+          const float wt = mwr == neg_inf() ? 0.f : fast_exp2((mwr - M) * kLog2e);
+          A += wt * acc_w[(w * kMaxRep + r) * D + d];
+        }
       }
+      const long long o = ((long long)b * p.num_q_heads + qh0 + r) * p.max_splits + split;
+      p.part_acc[o * D + d] = A;
     }
-    const long long o = ((long long)b * p.num_q_heads + qh0 + r) * p.max_splits + split;
-    p.part_acc[o * D + d] = A;
   }
 }
 
@@ -651,7 +689,7 @@ __device__ void run_consumer_mma(const SplitParams& p, const TableCache& tc, uin
     const int t0 = (tile0 + i) * Cfg::TILE;
     uint8_t* kbuf = stages + s * Cfg::STAGE_BYTES;
     uint8_t* vbuf = kbuf + Cfg::TENSOR_BYTES;
-    if (swm & 0xffu) copy_sw_segments<Cfg, MODE != MODE_STATS>(p, tc, g, b, h, t0, swm & 0xffu, kbuf, vbuf);
+    if (swm & 0xffu) copy_sw_segments<Cfg, true, !Cfg::KONLY>(p, tc, g, b, h, t0, swm & 0xffu, kbuf, vbuf);
     uint32_t vlo, vhi;
     tile_bits_fast<Cfg::TILE>(valid, valid_stride, b, t0, g, swm >> 8, seg_rows, vlo, vhi);
     const uint64_t vmask = ((uint64_t)vhi << 32) | vlo;
@@ -691,6 +729,46 @@ __device__ void run_consumer_mma(const SplitParams& p, const TableCache& tc, uin
         if (!all_valid && !((tmask >> (8 * j + (e & 1))) & 1ull)) x = neg_inf();
         sc[j][e] = x;
       }
+    }
+    if constexpr (MODE == MODE_SCORES) {
+      // the masked scores of the tile, and the max of each group_tokens group, per query head
+      float* const srow = p.scores + (long long)(b * num_q_heads + qh0) * p.s_stride + t0 + 2 * tq;
+#pragma unroll
+      for (int rr = 0; rr < 2; ++rr) {
+        const int row = gr + 8 * rr;
+        if (row < n_rep) {
+#pragma unroll
+          for (int j = 0; j < NT_S; ++j)
+            *reinterpret_cast<float2*>(srow + (long long)row * p.s_stride + 8 * j) =
+                make_float2(sc[j][2 * rr], sc[j][2 * rr + 1]);
+        }
+      }
+      const int ntg = G >> 3;  // S n-tiles per group
+      for (int gi = 0; gi < Cfg::TILE / G; ++gi) {
+        float gm[2] = {neg_inf(), neg_inf()};
+#pragma unroll
+        for (int j = 0; j < NT_S; ++j) {
+          if (j / ntg == gi) {
+            gm[0] = fmaxf(gm[0], fmaxf(sc[j][0], sc[j][1]));
+            gm[1] = fmaxf(gm[1], fmaxf(sc[j][2], sc[j][3]));
+          }
+        }
+#pragma unroll
+        for (int rr = 0; rr < 2; ++rr) {
+          gm[rr] = fmaxf(gm[rr], __shfl_xor_sync(0xffffffffu, gm[rr], 1));
+          gm[rr] = fmaxf(gm[rr], __shfl_xor_sync(0xffffffffu, gm[rr], 2));
+        }
+        if (tq == 0) {
+          const long long gidx = (t0 >> log2_group) + gi;
+#pragma unroll
+          for (int rr = 0; rr < 2; ++rr) {
+            const int row = gr + 8 * rr;
+            if (row < n_rep) p.gmax[((long long)b * num_q_heads + qh0 + row) * mass_gstride + gidx] = gm[rr];
+          }
+        }
+      }
+      release_stage(&empty[s], (swm & 0xffu) != 0);
+      continue;
     }
     float mref[2];
     if (MODE != MODE_FIXED) {
@@ -796,6 +874,7 @@ __device__ void run_consumer_mma(const SplitParams& p, const TableCache& tc, uin
     }
     release_stage(&empty[s], wrote);
   }
+  if constexpr (MODE == MODE_SCORES) return;  // no partial state: the VALUES pass folds the tiles
 
   // per-row l from the quad's partial sums
 #pragma unroll
@@ -826,6 +905,201 @@ __device__ void run_consumer_mma(const SplitParams& p, const TableCache& tc, uin
   }
   named_bar_sync(1, Cfg::NCW * 32);
   merge_and_store<D, MODE, Cfg::NCW>(p, mw, b, h, split);
+}
+
+
+// ------------------------------------------------------------------ tensor-core consumer, VALUES pass
+// The tile's scores and each group's reference max (the reference's running max at that group's
+// 64-token tile, or its final max) arrive by TMA in the auxiliary ring.  p = exp(s - M) against the
+// group's M, rounded to the KV dtype before O += P V (streaming_attention.py:177-178, :346-347),
+// l and the mass partials from the unrounded p.  M never decreases along a row and a warp visits
+// its tiles in order, so the warp keeps O and l relative to the latest M and rescales them when M
+// grows (at most once per group; G >= 16 puts every 16-token k-step in one group, and under the
+// final-max rule all groups share M).  The split's (m, l, acc) then merge like ONLINE partials.
+template <typename T, int D>
+__device__ void run_consumer_mma_values(const SplitParams& p, const TableCache& tc, uint8_t* stages, uint8_t* aux,
+                                        uint64_t* full, uint64_t* empty, volatile int* infos, int b, int h,
+                                        int tile0, int ntiles, const RowGeom& g, volatile int* abort_flag,
+                                        int split) {
+  using Cfg = TileCfg<T, D, MODE_VALUES, BACKEND_MMA>;
+  using Op = MmaOp<T>;
+  static_assert(Cfg::PANEL_BYTES == 128, "mma path expects 128-byte panels");
+  constexpr int NT_O = D / 8;
+  constexpr int NT_S = Cfg::TILE / 8;
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const int gr = lane >> 2;
+  const int tq = lane & 3;
+  const int n_rep = p.n_rep;
+  const int qh0 = h * n_rep;
+  const int l7 = lane & 7;
+  const int seg_rows = p.source == SRC_CONTIG ? Cfg::TILE : min(Cfg::TILE, p.tpb);
+  const int* const valid = p.valid;
+  const long long valid_stride = p.valid_stride;
+  const uint64_t wait_limit = p.wait_limit_ns;
+  int* const status = p.status;
+  float2* const mass_part = p.mass_part;
+  const int num_q_heads = p.num_q_heads;
+  const int mass_gstride = p.mass_gstride;
+  const int log2_group = p.log2_group;
+  const int G = p.group_tokens;
+  const uint64_t full_mask = Cfg::TILE == 64 ? ~0ull : ((1ull << Cfg::TILE) - 1ull);
+
+  float o[NT_O][4];
+#pragma unroll
+  for (int n = 0; n < NT_O; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+  float m_r[2] = {neg_inf(), neg_inf()};
+  float l_r[2] = {0.f, 0.f};
+
+  for (int i = warp; i < ntiles; i += Cfg::NCW) {
+    const int s = i % Cfg::STAGES;
+    if (*abort_flag) break;
+    uint32_t swm;
+    if (!consumer_wait(wait_limit, status, &full[s], &empty[s], &infos[s], i / Cfg::STAGES, abort_flag, &swm)) break;
+    const int t0 = (tile0 + i) * Cfg::TILE;
+    uint8_t* vbuf = stages + s * Cfg::STAGE_BYTES;
+    const float* s_sm = reinterpret_cast<const float*>(aux + s * Cfg::AUX_BYTES);  // [n_rep][TILE]
+    const float* m_sm = s_sm + Cfg::AUX_S_BYTES / 4;                               // [n_rep][kRefSlots]
+    if (swm & 0xffu) copy_sw_segments<Cfg, false, true>(p, tc, g, b, h, t0, swm & 0xffu, vbuf, vbuf);
+    uint32_t vlo, vhi;
+    tile_bits_fast<Cfg::TILE>(valid, valid_stride, b, t0, g, swm >> 8, seg_rows, vlo, vhi);
+    bool wrote = (swm & 0xffu) != 0;
+    if ((((uint64_t)vhi << 32) | vlo) != full_mask) wrote |= zero_masked_rows<Cfg>(vbuf, vlo, vhi);
+
+    // scores of rows gr and gr + 8 (masked tokens hold -inf), columns 8j + 2tq + {0, 1}
+    float sc[NT_S][4];
+#pragma unroll
+    for (int rr = 0; rr < 2; ++rr) {
+      const int row = gr + 8 * rr;
+#pragma unroll
+      for (int j = 0; j < NT_S; ++j) {
+        float2 v = make_float2(neg_inf(), neg_inf());
+        if (row < n_rep) v = *reinterpret_cast<const float2*>(s_sm + row * Cfg::TILE + 8 * j + 2 * tq);
+        sc[j][2 * rr] = v.x;
+        sc[j][2 * rr + 1] = v.y;
+      }
+    }
+    float gsum[2] = {0.f, 0.f};  // this lane's sum of p over the current mass group
+    const uint32_t vaddr = smem_u32(vbuf);
+#pragma unroll
+    for (int kt = 0; kt < Cfg::TILE / 16; ++kt) {
+      const int gi = (16 * kt) / G;  // the k-step's group within the tile
+      float alpha[2];
+      bool changed = false;
+#pragma unroll
+      for (int rr = 0; rr < 2; ++rr) {
+        const int row = gr + 8 * rr;
+        const float mn = row < n_rep ? m_sm[row * kRefSlots + gi] : neg_inf();
+        alpha[rr] = 1.f;
+        if (mn > m_r[rr]) {
+          alpha[rr] = m_r[rr] == neg_inf() ? 0.f : fast_exp2((m_r[rr] - mn) * kLog2e);
+          m_r[rr] = mn;
+          changed = true;
+        }
+      }
+      if (__any_sync(0xffffffffu, changed)) {
+#pragma unroll
+        for (int rr = 0; rr < 2; ++rr) {
+          l_r[rr] *= alpha[rr];
+#pragma unroll
+          for (int n = 0; n < NT_O; ++n) {
+            o[n][2 * rr] *= alpha[rr];
+            o[n][2 * rr + 1] *= alpha[rr];
+          }
+        }
+      }
+      float mref[2];
+#pragma unroll
+      for (int rr = 0; rr < 2; ++rr) mref[rr] = m_r[rr] == neg_inf() ? 0.f : m_r[rr] * kLog2e;
+#pragma unroll
+      for (int jj = 2 * kt; jj < 2 * kt + 2; ++jj) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) sc[jj][e] = fast_exp2(fmaf(sc[jj][e], kLog2e, -mref[e >> 1]));
+        l_r[0] += sc[jj][0] + sc[jj][1];
+        l_r[1] += sc[jj][2] + sc[jj][3];
+        gsum[0] += sc[jj][0] + sc[jj][1];
+        gsum[1] += sc[jj][2] + sc[jj][3];
+      }
+      uint32_t pa[4];
+      pa[0] = Op::pack(sc[2 * kt][0], sc[2 * kt][1]);
+      pa[1] = Op::pack(sc[2 * kt][2], sc[2 * kt][3]);
+      pa[2] = Op::pack(sc[2 * kt + 1][0], sc[2 * kt + 1][1]);
+      pa[3] = Op::pack(sc[2 * kt + 1][2], sc[2 * kt + 1][3]);
+#pragma unroll
+      for (int np = 0; np < NT_O / 2; ++np) {
+        uint32_t b0, b1, b2, b3;
+        const int c = 2 * np + (lane >> 4);
+        const uint32_t voff =
+            (c >> 3) * Cfg::PANEL_TILE_BYTES + (((lane >> 3) & 1) * 8 + l7) * 128 + (((c & 7) ^ l7) << 4);
+        ldmatrix_x4_trans(vaddr + voff + kt * 16 * 128, b0, b1, b2, b3);
+        Op::run(o[2 * np], pa, b0, b1);
+        Op::run(o[2 * np + 1], pa, b2, b3);
+      }
+      // a mass group ends after this k-step: (sum p, the group's reference max)
+      if (G > 0 && ((16 * (kt + 1)) % G == 0 || G < 16)) {
+        // G == 8 (final-max rule only): this k-step holds two groups; split the sum by n-tile
+        const int ngs = G < 16 ? 2 : 1;
+#pragma unroll
+        for (int q2 = 0; q2 < 2; ++q2) {
+          if (q2 >= ngs) break;
+          float gs[2];
+          if (ngs == 2) {
+            const int jj = 2 * kt + q2;
+            gs[0] = sc[jj][0] + sc[jj][1];
+            gs[1] = sc[jj][2] + sc[jj][3];
+          } else {
+            gs[0] = gsum[0];
+            gs[1] = gsum[1];
+          }
+#pragma unroll
+          for (int rr = 0; rr < 2; ++rr) {
+            gs[rr] += __shfl_xor_sync(0xffffffffu, gs[rr], 1);
+            gs[rr] += __shfl_xor_sync(0xffffffffu, gs[rr], 2);
+          }
+          const int gl = ngs == 2 ? 2 * kt + q2 : gi;  // group index within the tile
+          if (tq == 0) {
+            const long long gidx = (t0 >> log2_group) + gl;
+#pragma unroll
+            for (int rr = 0; rr < 2; ++rr) {
+              const int row = gr + 8 * rr;
+              if (row < n_rep)
+                mass_part[((long long)b * num_q_heads + qh0 + row) * mass_gstride + gidx] =
+                    make_float2(gs[rr], m_sm[row * kRefSlots + gl]);
+            }
+          }
+        }
+        gsum[0] = gsum[1] = 0.f;
+      }
+    }
+    release_stage(&empty[s], wrote);
+  }
+
+#pragma unroll
+  for (int rr = 0; rr < 2; ++rr) {
+    l_r[rr] += __shfl_xor_sync(0xffffffffu, l_r[rr], 1);
+    l_r[rr] += __shfl_xor_sync(0xffffffffu, l_r[rr], 2);
+  }
+  named_bar_sync(1, Cfg::NCW * 32);
+  float* mw = reinterpret_cast<float*>(stages);
+  float* m_w = mw;
+  float* l_w = mw + Cfg::NCW * kMaxRep;
+  float* acc_w = mw + 2 * Cfg::NCW * kMaxRep;
+  if (tq == 0) {
+    m_w[warp * kMaxRep + gr] = m_r[0];
+    m_w[warp * kMaxRep + gr + 8] = m_r[1];
+    l_w[warp * kMaxRep + gr] = l_r[0];
+    l_w[warp * kMaxRep + gr + 8] = l_r[1];
+  }
+#pragma unroll
+  for (int n = 0; n < NT_O; ++n) {
+    const int col = 8 * n + 2 * tq;
+    acc_w[(warp * kMaxRep + gr) * D + col] = o[n][0];
+    acc_w[(warp * kMaxRep + gr) * D + col + 1] = o[n][1];
+    acc_w[(warp * kMaxRep + gr + 8) * D + col] = o[n][2];
+    acc_w[(warp * kMaxRep + gr + 8) * D + col + 1] = o[n][3];
+  }
+  named_bar_sync(1, Cfg::NCW * 32);
+  merge_and_store<D, MODE_ONLINE, Cfg::NCW>(p, mw, b, h, split);
 }
 
 // ------------------------------------------------------------------ CUDA-core consumer
@@ -885,7 +1159,7 @@ __device__ void run_consumer_fma(const SplitParams& p, const TableCache& tc, uin
     const int t0 = (tile0 + i) * TILE;
     uint8_t* kbuf = stages + s * Cfg::STAGE_BYTES;
     uint8_t* vbuf = kbuf + Cfg::TENSOR_BYTES;
-    if (swm & 0xffu) copy_sw_segments<Cfg, MODE != MODE_STATS>(p, tc, g, b, h, t0, swm & 0xffu, kbuf, vbuf);
+    if (swm & 0xffu) copy_sw_segments<Cfg, true, !Cfg::KONLY>(p, tc, g, b, h, t0, swm & 0xffu, kbuf, vbuf);
     uint32_t vlo, vhi;
     tile_bits_fast<TILE>(valid, valid_stride, b, t0, g, swm >> 8, seg_rows, vlo, vhi);
     const uint32_t kaddr = smem_u32(kbuf);
@@ -1050,7 +1324,8 @@ __device__ void run_consumer_fma(const SplitParams& p, const TableCache& tc, uin
 template <typename T, int D, int MODE, int BACKEND>
 struct SplitSmem {
   using Cfg = TileCfg<T, D, MODE, BACKEND>;
-  static constexpr int BAR_OFF = Cfg::STAGE_AREA;
+  static constexpr int AUX_OFF = Cfg::STAGE_AREA;  // VALUES: score / reference-max ring (128-byte stages)
+  static constexpr int BAR_OFF = AUX_OFF + Cfg::STAGES * Cfg::AUX_BYTES;
   static constexpr int FLAG_OFF = BAR_OFF + 2 * Cfg::STAGES * 8;
   static constexpr int INFO_OFF = FLAG_OFF + 16;
   static constexpr int TBL_OFF = (INFO_OFF + 4 * Cfg::STAGES + 15) / 16 * 16;
@@ -1062,9 +1337,9 @@ struct SplitSmem {
 
 template <typename T, int D, int MODE, int BACKEND>
 __global__ void __launch_bounds__(TileCfg<T, D, MODE, BACKEND>::THREADS, TileCfg<T, D, MODE, BACKEND>::MIN_BLOCKS)
-    split_kernel(const __grid_constant__ SplitParams p,
-                                                         const __grid_constant__ CUtensorMap mapk,
-                                                         const __grid_constant__ CUtensorMap mapv) {
+    split_kernel(const __grid_constant__ SplitParams p, const __grid_constant__ CUtensorMap mapk,
+                 const __grid_constant__ CUtensorMap mapv, const __grid_constant__ CUtensorMap maps,
+                 const __grid_constant__ CUtensorMap mapm) {
   using Cfg = TileCfg<T, D, MODE, BACKEND>;
   using L = SplitSmem<T, D, MODE, BACKEND>;
   const int split = blockIdx.x;
@@ -1088,6 +1363,7 @@ __global__ void __launch_bounds__(TileCfg<T, D, MODE, BACKEND>::THREADS, TileCfg
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* stages = smem;
+  uint8_t* aux = smem + L::AUX_OFF;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::BAR_OFF);
   uint64_t* empty = full + Cfg::STAGES;
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::FLAG_OFF);
@@ -1102,9 +1378,14 @@ __global__ void __launch_bounds__(TileCfg<T, D, MODE, BACKEND>::THREADS, TileCfg
     }
     *abort_flag = 0;
     mbar_fence_init();
-    if (p.source == SRC_CONTIG || p.dev_pool != nullptr) tma_prefetch_desc(&mapk);
-    if ((p.source == SRC_CONTIG && MODE != MODE_STATS) || (p.source == SRC_PAGED && p.stage_pool != nullptr))
+    if ((p.source == SRC_CONTIG && !Cfg::VONLY) || (p.source == SRC_PAGED && p.dev_pool != nullptr))
+      tma_prefetch_desc(&mapk);
+    if ((p.source == SRC_CONTIG && !Cfg::KONLY) || (p.source == SRC_PAGED && p.stage_pool != nullptr))
       tma_prefetch_desc(&mapv);
+    if (Cfg::VONLY) {
+      tma_prefetch_desc(&maps);
+      tma_prefetch_desc(&mapm);
+    }
   }
   float* q_sm = reinterpret_cast<float*>(smem + L::Q_OFF);
   T* q_smem_t = reinterpret_cast<T*>(smem + L::Q_OFF);
@@ -1119,7 +1400,7 @@ __global__ void __launch_bounds__(TileCfg<T, D, MODE, BACKEND>::THREADS, TileCfg
     tc.n = max(0, min(blk1 - blk0, kTableCache));
     for (int i = threadIdx.x; i < tc.n; i += Cfg::THREADS) tbl[i] = p.block_table[(long long)b * p.max_blocks + blk0 + i];
   }
-  if (warp < Cfg::NCW) {
+  if (warp < Cfg::NCW && !Cfg::VONLY) {
     const long long qbase = ((long long)b * p.num_q_heads + (long long)h * p.n_rep) * D;
     for (int idx = threadIdx.x; idx < kMaxRep * D; idx += Cfg::NCW * 32) {
       const int r = idx / D;
@@ -1139,10 +1420,13 @@ __global__ void __launch_bounds__(TileCfg<T, D, MODE, BACKEND>::THREADS, TileCfg
   __syncthreads();
 
   if (warp >= Cfg::NCW) {
-    run_producer<Cfg, MODE>(p, tc, &mapk, &mapv, stages, full, empty, infos, b, h, tile0, ntiles, g, abort_flag,
-                            warp - Cfg::NCW);
+    run_producer<Cfg, MODE>(p, tc, &mapk, &mapv, &maps, &mapm, stages, aux, full, empty, infos, b, h, tile0, ntiles,
+                            g, abort_flag, warp - Cfg::NCW);
   } else {
-    if constexpr (BACKEND == BACKEND_MMA) {
+    if constexpr (BACKEND == BACKEND_MMA && MODE == MODE_VALUES) {
+      run_consumer_mma_values<T, D>(p, tc, stages, aux, full, empty, infos, b, h, tile0, ntiles, g, abort_flag,
+                                    split);
+    } else if constexpr (BACKEND == BACKEND_MMA) {
       run_consumer_mma<T, D, MODE>(p, tc, stages, full, empty, infos, b, h, tile0, ntiles, g, abort_flag, split,
                                    q_smem_t);
     } else {

@@ -11,3 +11,15 @@
       case pager::MODE_FIXED: *out = pager::split_kernel_info<T, D, pager::MODE_FIXED, BE>(); return true;   \
       default: return false;                                                         \
     }
+
+// The two passes of reference-exact rounding (tensor-core kernels only).
+#define PAGER_EXACT_MODE_CASES(T, D)                                                 \
+  case D:                                                                            \
+    switch (mode) {                                                                  \
+      case pager::MODE_ONLINE: *out = pager::split_kernel_info<T, D, pager::MODE_ONLINE, pager::BACKEND_MMA>(); return true; \
+      case pager::MODE_STATS: *out = pager::split_kernel_info<T, D, pager::MODE_STATS, pager::BACKEND_MMA>(); return true;   \
+      case pager::MODE_FIXED: *out = pager::split_kernel_info<T, D, pager::MODE_FIXED, pager::BACKEND_MMA>(); return true;   \
+      case pager::MODE_SCORES: *out = pager::split_kernel_info<T, D, pager::MODE_SCORES, pager::BACKEND_MMA>(); return true; \
+      case pager::MODE_VALUES: *out = pager::split_kernel_info<T, D, pager::MODE_VALUES, pager::BACKEND_MMA>(); return true; \
+      default: return false;                                                         \
+    }

@@ -35,6 +35,10 @@ HOST_SLOT_BIT = 0x40000000
 STAGE_SLOT_BIT = 0x20000000
 
 BACKEND_AUTO, BACKEND_MMA, BACKEND_FMA = 0, 1, 2
+# rounding of p before P.V (include/pager_b200.h PAGER_ROUND_*): the one-pass kernel, or the reference's
+# own rounding against its running max per 64-token tile (its one-pass path) / its final max (two-pass)
+ROUND_ONE_PASS, ROUND_RUNNING, ROUND_FINAL = 0, 1, 2
+ROUNDING_CODE = {"one_pass": ROUND_ONE_PASS, "running": ROUND_RUNNING, "final": ROUND_FINAL}
 MASS_NONE, MASS_ROW_MEAN, MASS_BATCH_MEAN = 0, 1, 2
 
 DTYPE_CODE = {torch.float32: 0, torch.float16: 1, torch.bfloat16: 2}
@@ -72,6 +76,10 @@ _SIGNATURES = {
     "pager_paged_decode_attention_staged": (_i, [_vp, _i, _vp, _i, _vp, _i, _vp, _i, _i, _i, _i, _i, _i, _i, _vp,
                                                  _i, _vp, _vp, _vp, _vp, _i, _vp, _vp, _vp, _i, _i, _f, _f, _i,
                                                  _vp, _i, _vp, _vp, _i, _i, _vp, _sz, _vp]),
+    "pager_paged_decode_scratch_bytes_rounded": (_sz, [_i, _i, _i, _i, _i, _i, _i, _i]),
+    "pager_paged_decode_attention_rounded": (_i, [_vp, _i, _vp, _i, _vp, _i, _vp, _i, _i, _i, _i, _i, _i, _i, _vp,
+                                                  _i, _vp, _vp, _vp, _vp, _i, _vp, _vp, _vp, _i, _i, _f, _f, _i,
+                                                  _vp, _i, _vp, _vp, _i, _i, _i, _i, _vp, _vp, _vp, _sz, _vp]),
     "pager_stage_host_blocks": (_i, [_vp, _vp, _i64, _i64, _i64, _vp, _vp, _vp, _i, _vp]),
     "pager_selftest_bounded_wait": (_i, [ctypes.c_ulonglong, ctypes.POINTER(ctypes.c_ulonglong), _vp]),
     "pager_host_pool_alloc": (_i, [_sz, ctypes.POINTER(_vp)]),

@@ -237,11 +237,25 @@ def _validate_sessions(sessions: list, next_input_ids: list[int]) -> None:
         raise ValueError("batched_decode_step needs one next input id per session.")
 
 
-def _group_plan(group: list, arch: dict, pools: KVPools, device: torch.device):
+def _group_rounding(group: list, arch: dict) -> str:
+    """The rounding of p for a set of sessions decoded in one launch: the reference's batched path
+    runs its two-pass sequence when the sessions score blocks and its one-pass sequence otherwise
+    (batched_decode.py:236-285); with mixed policies (which the reference rejects) the two-pass one."""
+    from .paged_model import step_rounding
+
+    first = group[0]
+    return step_rounding(getattr(first, "attention_rounding", "reference"), any(s._needs_attention for s in group), first.model.dtype,
+                         arch["d"], first.tokens_per_block)
+
+
+def _group_plan(group: list, arch: dict, pools: KVPools, device: torch.device, max_nb: int):
     """The fused op's plans for single-row sessions that share ``pools`` (one per distinct sliding
     window of the model): one block-table row per session (its blocks on either tier, then its tail
     slot), per-row valid ranges (left padding, sliding window), and the per-row block-mass output
-    when any session scores blocks."""
+    when any session scores blocks.  For the reference rounding of p each row sits
+    ``(max_nb - blocks) * tokens_per_block`` tokens into the reference's combined block numbering
+    (sessions with fewer blocks are padded in front, ``max_nb`` being the most blocks of any session
+    in the step, batched_decode.py:185-234)."""
     from .paged_model import window_lo
 
     S, tpb = len(group), pools.tokens_per_block
@@ -266,25 +280,31 @@ def _group_plan(group: list, arch: dict, pools: KVPools, device: torch.device):
     table_dev = table.to(device)
     num_blocks = torch.tensor([s._num_blocks + 1 for s in group], **i32)
     valid_hi = torch.tensor(hi, **i32)
+    shift = torch.tensor([(max_nb - s._num_blocks) * tpb for s in group], **i32)
+    tail_start = torch.tensor([s._num_blocks * tpb for s in group], **i32)
     plans = [PagedDecodePlan(
         batch=S, num_query_heads=arch["hq"], dev_pool=pools.dev_pool, host_pool=pools.host_pool.tensor,
         num_layers=arch["layers"], tokens_per_block=tpb, block_table=table_dev, num_blocks=num_blocks,
         max_row_tokens=width * tpb, valid_lo=torch.tensor(lo, **i32) if any(lo) else None, valid_hi=valid_hi,
         scale=arch["scale"], softcap=arch["softcap"], mass_accum=mass, mass_mode="row_mean" if needs else "none",
-        host_read=group[0].host_read) for lo in los]
+        host_read=group[0].host_read, rounding=_group_rounding(group, arch),
+        ref_group_tokens=group[0].streaming_group_size_blocks * tpb, ref_shift=shift, ref_tail_start=tail_start)
+        for lo in los]
     return plans, mass, torch.tensor(slots, **i32), torch.tensor(positions, **i32)
 
 
-def _group_ints(group: list, arch: dict, width: int) -> torch.Tensor:
+def _group_ints(group: list, arch: dict, width: int, max_nb: int) -> torch.Tensor:
     """The per-step int32 inputs of one pools group, packed as a captured step reads them: the block
     table ``[rows, width]`` (each row's blocks, its tail slot, then absent columns), then per row the
-    block count (blocks + tail), range end, tail slot, tail position and the first attended column
-    for each distinct sliding window."""
+    block count (blocks + tail), range end, tail slot, tail position, offset into the reference's
+    combined block numbering, first tail token (``_group_plan``) and the first attended column for
+    each distinct sliding window."""
     from .paged_model import window_lo
 
     S, nw = len(group), len(arch["windows"])
+    tpb = group[0].tokens_per_block
     table = torch.full((S, width), -1, dtype=torch.int32)
-    cols = torch.zeros(4 + nw, S, dtype=torch.int32)
+    cols = torch.zeros(6 + nw, S, dtype=torch.int32)
     for r, s in enumerate(group):
         nb = s._num_blocks
         if nb:
@@ -296,8 +316,10 @@ def _group_ints(group: list, arch: dict, width: int) -> torch.Tensor:
         cols[1, r] = total
         cols[2, r] = s._tail_group
         cols[3, r] = s._tail_len
+        cols[4, r] = (max_nb - nb) * tpb
+        cols[5, r] = nb * tpb
         for i, w in enumerate(arch["windows"]):
-            cols[4 + i, r] = window_lo(pad, total, w)
+            cols[6 + i, r] = window_lo(pad, total, w)
     return torch.cat([table.reshape(-1), cols.reshape(-1)])
 
 
@@ -322,10 +344,10 @@ class _BatchedGraph:
             members = [sessions[r] for r in rows]
             pools = members[0]._pools
             n, nw = len(rows), len(arch["windows"])
-            ints = torch.zeros(n * width + (4 + nw) * n, dtype=torch.int32, device=device)
+            ints = torch.zeros(n * width + (6 + nw) * n, dtype=torch.int32, device=device)
             table = ints[: n * width].view(n, width)
-            cols = ints[n * width:].view(4 + nw, n).unbind(0)
-            nbs, hi, slots, positions = cols[:4]
+            cols = ints[n * width:].view(6 + nw, n).unbind(0)
+            nbs, hi, slots, positions, shift, tail_start = cols[:6]
             needs = any(s._needs_attention for s in members)
             mass = torch.zeros(n, width, dtype=torch.float32, device=device) if needs else None
             plans = [PagedDecodePlan(
@@ -333,7 +355,9 @@ class _BatchedGraph:
                 num_layers=arch["layers"], tokens_per_block=pools.tokens_per_block, block_table=table, num_blocks=nbs,
                 max_row_tokens=width * pools.tokens_per_block, valid_lo=lo, valid_hi=hi, scale=arch["scale"],
                 softcap=arch["softcap"], mass_accum=mass, mass_mode="row_mean" if needs else "none",
-                host_read="zero_copy") for lo in cols[4:]]
+                host_read="zero_copy", rounding=_group_rounding(members, arch),
+                ref_group_tokens=members[0].streaming_group_size_blocks * pools.tokens_per_block, ref_shift=shift,
+                ref_tail_start=tail_start) for lo in cols[6:]]
             index = None if len(by_pools) == 1 else torch.tensor(rows, dtype=torch.long, device=device)
             self.groups.append(AttentionGroup(pools, plans, slots, positions, index))
             self.buffers.append((rows, width, ints, mass))
@@ -350,8 +374,9 @@ class _BatchedGraph:
         return run_decoder_step(self.model, self.arch, self.groups, self.input_ids, self.position_ids)
 
     def step(self, sessions, next_input_ids, pos_ids):
+        max_nb = max(s._num_blocks for s in sessions)
         for rows, width, ints, _ in self.buffers:
-            ints.copy_(_group_ints([sessions[r] for r in rows], self.arch, width))
+            ints.copy_(_group_ints([sessions[r] for r in rows], self.arch, width, max_nb))
         self.input_ids.copy_(torch.tensor(next_input_ids, dtype=torch.long)[:, None])
         self.position_ids.copy_(torch.tensor(pos_ids, dtype=torch.long)[:, None])
         with torch.cuda.device(self.device):
@@ -444,9 +469,10 @@ def batched_decode_step(sessions: list, next_input_ids: list[int], device) -> li
         last = logits[:, -1, :].clone()
         return [last[r] for r in range(S)]
     groups, masses = [], []
+    max_nb = max(s._num_blocks for s in sessions)
     for rows in by_pools.values():
         members = [sessions[r] for r in rows]
-        plans, mass, slots, positions = _group_plan(members, a, members[0]._pools, device)
+        plans, mass, slots, positions = _group_plan(members, a, members[0]._pools, device, max_nb)
         index = None if len(by_pools) == 1 else torch.tensor(rows, dtype=torch.long, device=device)
         groups.append(AttentionGroup(members[0]._pools, plans, slots, positions, index))
         masses.append((rows, mass))

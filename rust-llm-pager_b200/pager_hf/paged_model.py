@@ -148,6 +148,25 @@ def run_decoder_step(model, arch: dict, groups: list[AttentionGroup], input_ids,
     return logits
 
 
+_EXACT_HEAD_DIMS = frozenset({64, 128, 256})  # head_dims of the tensor-core kernels that round p exactly
+
+
+def step_rounding(mode: str, needs_attention: bool, dtype, head_dim: int, tokens_per_block: int) -> str:
+    """The fused op's ``rounding`` for a decode step.  ``mode="reference"``: p is rounded as the
+    reference rounds it -- against its running max per 64-token tile ("running") in the one-pass
+    path it runs for policies without an attention signal (paged_model.py:1055-1072), against the
+    row's final max ("final") in the two-pass path of the heavy-hitter policies (:993-1039).  The
+    fp32 path rounds nothing either way, and head_dims below 64 (CUDA-core kernels) keep the one
+    pass; ``mode="one_pass"`` always does."""
+    if mode not in ("reference", "one_pass"):
+        raise ValueError(f"attention_rounding must be 'reference' or 'one_pass', got {mode!r}")
+    if mode == "one_pass" or dtype == torch.float32 or head_dim not in _EXACT_HEAD_DIMS:
+        return "one_pass"
+    if needs_attention:
+        return "final"
+    return "running" if tokens_per_block >= 16 else "one_pass"
+
+
 def window_lo(pad: int, total: int, window) -> int:
     """First attended column of a row: after its left padding and, with a sliding window, within the
     last ``window`` columns (``paged_model.py:975-980``)."""
@@ -161,8 +180,9 @@ class _DecodeGraph:
     (norms, projections, RoPE, MLP) plus the paged op, ~800 launches per step for a 24-layer
     model.  The graph replays them with one launch.  Its inputs live in static device buffers
     refreshed before each replay: the token ids and position ids, and one packed int32 buffer
-    holding the block table, the rows' block counts, range ends, tail slots, tail positions and
-    first attended columns (one per distinct sliding window) -- a single host copy per step.
+    holding the block table, the rows' block counts, range ends, tail slots, tail positions, first
+    tail tokens (where the reference's tail chunk starts, for its rounding of p) and first attended
+    columns (one per distinct sliding window) -- a single host copy per step.
     Shapes and pointers the launches bake in -- batch, table width (``width`` block columns, a
     multiple of ``WIDTH_STEP`` at least the blocks plus the tail; it also bounds the split plan),
     the pools (their ``version`` changes when they grow) -- form the key, so a new graph is
@@ -179,11 +199,11 @@ class _DecodeGraph:
         p = pm._pools
         self.key, self.pm, self.arch, self.pools, self.B, self.width = key, pm, arch, p, B, width
         w, nw = width, len(arch["windows"])
-        self.ints = torch.zeros(B * w + (4 + nw) * B, dtype=torch.int32, device=dev)
+        self.ints = torch.zeros(B * w + (5 + nw) * B, dtype=torch.int32, device=dev)
         self.table = self.ints[: B * w].view(B, w)
-        cols = self.ints[B * w:].view(4 + nw, B).unbind(0)
-        self.num_blocks, self.hi, self.slots, self.positions = cols[:4]
-        self.los = cols[4:]  # first attended column per row, one per distinct window
+        cols = self.ints[B * w:].view(5 + nw, B).unbind(0)
+        self.num_blocks, self.hi, self.slots, self.positions, self.tail_start = cols[:5]
+        self.los = cols[5:]  # first attended column per row, one per distinct window
         self.input_ids = torch.zeros(B, 1, dtype=torch.long, device=dev)
         self.position_ids = torch.zeros(B, 1, dtype=torch.long, device=dev)
         self.mass = torch.zeros(w, dtype=torch.float32, device=dev) if pm._needs_attention else None
@@ -192,7 +212,9 @@ class _DecodeGraph:
             num_layers=arch["layers"], tokens_per_block=pm.tokens_per_block, block_table=self.table,
             num_blocks=self.num_blocks, max_row_tokens=w * pm.tokens_per_block, valid_lo=lo, valid_hi=self.hi,
             scale=arch["scale"], softcap=arch["softcap"], mass_accum=self.mass,
-            mass_mode="batch_mean" if self.mass is not None else "none", host_read="zero_copy") for lo in self.los]
+            mass_mode="batch_mean" if self.mass is not None else "none", host_read="zero_copy",
+            rounding=pm._rounding(arch), ref_group_tokens=pm._ref_group_tokens(), ref_tail_start=self.tail_start)
+            for lo in self.los]
         self.device = torch.device(dev)
         self.graph = None
         self.logits = None
@@ -235,14 +257,19 @@ class PagedModel:
                  rebalance_interval: int = 4, promote_margin: float = 0.05, ram_promote_margin: float = 0.20,
                  policy: str = "sinks_heavy_hitter", tokens_per_block: int = 16, prefill_chunk_tokens: int = 512,
                  use_streaming_attention: bool = True, streaming_group_size_blocks: int = 64,
-                 host_read: str = "auto", pools: KVPools | None = None, decode_graphs: bool = True):
+                 host_read: str = "auto", pools: KVPools | None = None, decode_graphs: bool = True,
+                 attention_rounding: str = "reference"):
         if not use_streaming_attention:
             raise NotImplementedError("only the streaming (fused paged) attention path is implemented")
         self.model = model
         self.tokens_per_block = tokens_per_block
         self.prefill_chunk_tokens = prefill_chunk_tokens
         self.use_streaming_attention = True
-        self.streaming_group_size_blocks = streaming_group_size_blocks  # kept for API parity; one launch per layer
+        # one launch per layer covers every group; the reference's groups still set the tiles its
+        # one-pass path rounds p over, which the "reference" rounding reproduces
+        self.streaming_group_size_blocks = streaming_group_size_blocks
+        step_rounding(attention_rounding, False, torch.float16, 64, tokens_per_block)  # validates the name
+        self.attention_rounding = attention_rounding
         self.host_read = host_read
         self.last_host_read: str | None = None  # the host-tier read mode of the last decode step's plan
         # decode steps captured and replayed as CUDA graphs (host tier read zero-copy); staged host
@@ -372,6 +399,14 @@ class PagedModel:
         probs = torch.softmax(logits, dim=-1)
         return torch.multinomial(probs, num_samples=1, generator=generator)
 
+    def _rounding(self, arch: dict) -> str:
+        """The fused op's rounding of p for this session's decode steps (``step_rounding``)."""
+        return step_rounding(self.attention_rounding, self._needs_attention, self.model.dtype, arch["d"],
+                             self.tokens_per_block)
+
+    def _ref_group_tokens(self) -> int:
+        return self.streaming_group_size_blocks * self.tokens_per_block
+
     def _arch(self):
         cfg = self.model.config
         model_type = getattr(cfg, "model_type", None)
@@ -488,7 +523,9 @@ class PagedModel:
             num_blocks=torch.full((B,), nb + 1, **i32), max_row_tokens=(nb + 1) * tpb,
             valid_lo=lo.to(dev) if bool((lo > 0).any()) else None, valid_hi=torch.full((B,), total, **i32),
             scale=a["scale"], softcap=a["softcap"], mass_accum=mass,
-            mass_mode="batch_mean" if mass is not None else "none", host_read=self.host_read) for lo in los]
+            mass_mode="batch_mean" if mass is not None else "none", host_read=self.host_read,
+            rounding=self._rounding(a), ref_group_tokens=self._ref_group_tokens(),
+            ref_tail_start=torch.full((B,), nb * tpb, **i32)) for lo in los]
         self.last_host_read = plans[0].host_read
         slots = torch.arange(self._tail_group * B, self._tail_group * B + B, **i32)
         positions = torch.full((B,), self._tail_len, **i32)
@@ -511,7 +548,8 @@ class PagedModel:
         ints = torch.cat([wide.reshape(-1), torch.full((B,), nb + 1, dtype=torch.int32),
                           torch.full((B,), total, dtype=torch.int32),
                           torch.arange(self._tail_group * B, self._tail_group * B + B, dtype=torch.int32),
-                          torch.full((B,), self._tail_len, dtype=torch.int32)] + los)
+                          torch.full((B,), self._tail_len, dtype=torch.int32),
+                          torch.full((B,), nb * self.tokens_per_block, dtype=torch.int32)] + los)
         g.load(ints, input_ids, self._position_ids_from_mask(attention_mask)[:, -1:])
         logits = g.step()
         self.last_host_read = "zero_copy"

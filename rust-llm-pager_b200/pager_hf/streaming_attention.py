@@ -302,6 +302,10 @@ def paged_decode_attention(
     mass_accum: torch.Tensor | None = None,
     mass_mode: str = "none",
     scratch: torch.Tensor | None = None,
+    rounding: str = "one_pass",
+    ref_group_tokens: int = 0,
+    ref_shift: torch.Tensor | None = None,
+    ref_tail_start: torch.Tensor | None = None,
 ) -> torch.Tensor:
     """Fused decode attention over a block table, in one pass.
 
@@ -320,6 +324,18 @@ def paged_decode_attention(
     [B, Hq, max_blocks] receives sum(p over block)/l per head (the two-pass
     reference's block_mass); ``mass_accum`` += the head mean ("row_mean",
     [B, max_blocks]) or the batch-and-head mean ("batch_mean", [max_blocks]).
+
+    ``rounding``: how p is rounded to the KV dtype before P.V.  "one_pass" is the
+    fused one-pass kernel (p against split-local running maxima).  "running" and
+    "final" round exactly as the reference does -- against its running max after
+    each 64-token tile of the chunks it is handed (its one-pass path for
+    recent_only / sinks_recent), or against the row's final max (its two-pass path
+    for the heavy-hitter policies) -- by a K pass to scores, a scan and a V pass
+    (include/pager_b200.h, PAGER_ROUND_*).  The reference's chunks for "running":
+    groups of ``ref_group_tokens`` tokens (streaming_group_size_blocks *
+    tokens_per_block; 0: one chunk) of a numbering in which row b's token j sits at
+    ``ref_shift[b] + j``, then the tail chunk from row token ``ref_tail_start[b]``
+    (default num_blocks[b] * tokens_per_block).
     """
     if q.dim() != 3:
         raise ValueError(f"q must be [batch, heads, dim], got {tuple(q.shape)}")
@@ -373,21 +389,31 @@ def paged_decode_attention(
         _state(mass_accum, "mass_accum", (max_blocks,))
     q = q.contiguous()
     kvd = _dtype_code(pool, "pool")
+    rcode = _rounding_code(rounding)
+    ref_shift, ref_tail_start = _mask(ref_shift), _mask(ref_tail_start)
+    _require_cuda(ref_shift=ref_shift, ref_tail_start=ref_tail_start)
     lib = L.lib()
     with torch.cuda.device(q.device):
-        nbytes = lib.pager_paged_decode_scratch_bytes(B, Hq, Hkv, D, kvd, tokens_per_block, max_blocks,
-                                                      int(max_row_tokens))
+        nbytes = lib.pager_paged_decode_scratch_bytes_rounded(B, Hq, Hkv, D, kvd, tokens_per_block,
+                                                              int(max_row_tokens), rcode)
         if scratch is None or scratch.numel() < nbytes:
             scratch = _scratch(nbytes, q.device)
-        L.check(lib.pager_paged_decode_attention(
+        L.check(lib.pager_paged_decode_attention_rounded(
             q.data_ptr(), _dtype_code(q, "q"), L.ptr(dev_pool), 0 if dev_pool is None else dev_pool.shape[0],
-            L.ptr(host_pool), 0 if host_pool is None else host_pool.shape[0], kvd, num_layers, layer, Hkv,
+            L.ptr(host_pool), 0 if host_pool is None else host_pool.shape[0], None, 0, kvd, num_layers, layer, Hkv,
             tokens_per_block, D, block_table.data_ptr(), max_blocks, num_blocks.data_ptr(), L.ptr(tail_k),
             L.ptr(tail_v), L.ptr(tail_len), tail_cap, L.ptr(valid_lo), L.ptr(valid_hi), L.ptr(active), B, Hq,
             float(scale), float(softcap or 0.0), int(max_row_tokens), out.data_ptr(), _dtype_code(out, "out"),
-            L.ptr(block_mass), L.ptr(mass_accum), mode, _BACKEND, scratch.data_ptr(), scratch.numel(),
-            L.stream_of(q)))
+            L.ptr(block_mass), L.ptr(mass_accum), mode, _BACKEND, rcode, int(ref_group_tokens), L.ptr(ref_shift),
+            L.ptr(ref_tail_start), scratch.data_ptr(), scratch.numel(), L.stream_of(q)))
     return out
+
+
+def _rounding_code(rounding: str) -> int:
+    try:
+        return L.ROUNDING_CODE[rounding]
+    except KeyError:
+        raise ValueError(f"rounding must be 'one_pass', 'running' or 'final', got {rounding!r}") from None
 
 
 class PagedDecodePlan:
@@ -403,7 +429,8 @@ class PagedDecodePlan:
     def __init__(self, *, batch, num_query_heads, dev_pool, host_pool, num_layers, tokens_per_block, block_table,
                  num_blocks, max_row_tokens, tail_k=None, tail_v=None, tail_len=None, valid_lo=None, valid_hi=None,
                  active=None, scale=None, softcap=None, q_dtype=None, block_mass=None, mass_accum=None,
-                 mass_mode="none", host_read="auto", prefetch_next_step=False):
+                 mass_mode="none", host_read="auto", prefetch_next_step=False, rounding="one_pass",
+                 ref_group_tokens=0, ref_shift=None, ref_tail_start=None):
         pool = dev_pool if dev_pool is not None else host_pool
         if pool is None or pool.dim() != 6:
             raise ValueError("a [slots, layers, 2, kv_heads, tokens_per_block, head_dim] pool is required")
@@ -418,9 +445,13 @@ class PagedDecodePlan:
                       block_mass=block_mass, mass_accum=mass_accum)
         if block_table.dtype != torch.int32 or tuple(block_table.shape[:1]) != (self.B,):
             raise ValueError("block_table must be int32 [batch, max_blocks]")
+        _require_cuda(ref_shift=ref_shift, ref_tail_start=ref_tail_start)
         self._keep = [block_table.contiguous(), _mask(num_blocks), _mask(tail_len), _mask(valid_lo), _mask(valid_hi),
-                      _mask(active), dev_pool, host_pool]
-        self.block_table, self.num_blocks, self.tail_len, self.valid_lo, self.valid_hi, self.active = self._keep[:6]
+                      _mask(active), _mask(ref_shift), _mask(ref_tail_start), dev_pool, host_pool]
+        (self.block_table, self.num_blocks, self.tail_len, self.valid_lo, self.valid_hi, self.active, self.ref_shift,
+         self.ref_tail_start) = self._keep[:8]
+        self.rounding = _rounding_code(rounding)
+        self.ref_group_tokens = int(ref_group_tokens)
         self.tail_k = None if tail_k is None else _aligned(tail_k)
         self.tail_v = None if tail_v is None else _aligned(tail_v)
         self._keep += [self.tail_k, self.tail_v]
@@ -436,11 +467,11 @@ class PagedDecodePlan:
         self.mass_mode = _MASS_MODES[mass_mode]
         lib = L.lib()
         with torch.cuda.device(device):
-            nbytes = lib.pager_paged_decode_scratch_bytes(self.B, self.Hq, self.Hkv, self.D, self.kv_dtype, self.tpb,
-                                                          self.max_blocks, self.max_row_tokens)
+            nbytes = lib.pager_paged_decode_scratch_bytes_rounded(self.B, self.Hq, self.Hkv, self.D, self.kv_dtype,
+                                                                  self.tpb, self.max_row_tokens, self.rounding)
         self.scratch = _scratch(nbytes, device)
         self.device = device
-        self._fn = lib.pager_paged_decode_attention_staged
+        self._fn = lib.pager_paged_decode_attention_rounded
         self._static = (
             L.ptr(dev_pool), 0 if dev_pool is None else dev_pool.shape[0], L.ptr(host_pool),
             0 if host_pool is None else host_pool.shape[0], self.kv_dtype, self.num_layers)
@@ -482,7 +513,8 @@ class PagedDecodePlan:
             L.ptr(self.tail_v), L.ptr(self.tail_len), 0 if self.tail_k is None else self.tail_k.shape[2],
             L.ptr(self.valid_lo), L.ptr(self.valid_hi), L.ptr(self.active), self.B, self.Hq, self.scale, self.softcap,
             self.max_row_tokens, out.data_ptr(), L.DTYPE_CODE[out.dtype], L.ptr(self.block_mass),
-            L.ptr(self.mass_accum), self.mass_mode, _BACKEND, self.scratch.data_ptr(), self.scratch.numel(), sh)
+            L.ptr(self.mass_accum), self.mass_mode, _BACKEND, self.rounding, self.ref_group_tokens,
+            L.ptr(self.ref_shift), L.ptr(self.ref_tail_start), self.scratch.data_ptr(), self.scratch.numel(), sh)
         if stg is not None:
             stg.after_kernel(layer, st)
         if rc:

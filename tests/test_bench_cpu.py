@@ -39,11 +39,26 @@ def test_window_counts_only_tokens_inside_the_window():
     assert all(lo == lay.nb * lay.tpb + t - window for lo, t in zip(lay.lo, lay.tails))
 
 
-def test_both_arms_report_the_same_config_keys():
-    cfg = bench.WorkloadLayout("cfg5-32k", seed=1234).config(2, "staged")
+def test_both_arms_report_the_same_config():
+    """The config is the workload's alone (the host-tier read mode is a key of its own), so the GPU
+    arm and the CPU reference arm report identical configs."""
+    cfg = bench.WorkloadLayout("cfg5-32k", seed=1234).config(2)
     assert cfg["global_batch"] == 2 * cfg["batch_per_gpu"]
     for key in ("workload", "model", "context", "hbm_bytes_per_step", "host_bytes_per_step", "l2", "parallelism"):
         assert key in cfg
+    assert "host_read" not in cfg
+    assert cfg == bench.WorkloadLayout("cfg5-32k", seed=1234).config(2)
+
+
+def test_cpu_torch_arm_times_the_reference_dense_path(monkeypatch):
+    """The CPU baseline runs the reference's dense torch path on one (request, layer) unit with every
+    host thread, and reports the attended KV bytes of each call."""
+    monkeypatch.setitem(bench.WORKLOADS, "tiny", dict(model="tiny", layers=2, hq=8, hkv=2, d=64, dtype="bf16",
+                                                     tpb=64, batch=2, context=1024, hbm_budget_gb=1.0, window=None))
+    arm = bench.CpuTorchArm("tiny", threads=2, reps=3)
+    b, t = arm.sample()
+    assert b == 3 * (1024 + 32) * 2 * 2 * 64 * 2 and t > 0
+    assert "torch.set_num_threads(2)" in bench.sample_desc(arm)
 
 
 def test_json_line_is_alone_on_stdout_under_torchrun():
@@ -87,7 +102,8 @@ def test_reference_arms_do_no_work_on_ranks_other_than_zero(monkeypatch, capsys)
     monkeypatch.setenv("RANK", "1")
     monkeypatch.setenv("LOCAL_RANK", "1")
     monkeypatch.setattr(bench, "CpuOracleArm", lambda *a, **k: pytest.fail("rank 1 started the CPU arm"))
-    args = argparse.Namespace(workload="cfg5-32k", gpus=2, steps=3, warmup=3)
+    monkeypatch.setattr(bench, "CpuTorchArm", lambda *a, **k: pytest.fail("rank 1 started the CPU arm"))
+    args = argparse.Namespace(workload="cfg5-32k", gpus=2, steps=3, warmup=3, cpu_arm="torch")
     assert bench.run_reference_arm(args) == 0
     assert bench.run_reference_gpu_arm(args) == 0
     assert capsys.readouterr().out == ""

@@ -1,0 +1,169 @@
+"""Reference-exact rounding of P in the fused paged op (``rounding="running"`` / ``"final"``).
+
+The reference rounds p = exp(s - m) to the KV dtype before its P.V product, with m its running max
+after each 64-token tile of the chunks it is handed (its one-pass path, paged_model.py:1055-1072)
+or the row's final max (its two-pass path, :993-1039).  The SCORES -> reference-max -> VALUES
+passes round against exactly those maxima, so in the output dtype they agree with the numpy
+oracle of those sequences (oracle/streaming_attention_oracle.py: ``single_pass_decode``,
+``two_pass_decode``) everywhere except where fp32 association moves a value across a rounding
+boundary -- as the reference's own Triton kernels agree with that oracle (a few percent of the
+fp16/bf16 outputs, fewer in bf16).  The one-pass kernel differs from it in about half of them.
+
+Tolerances: output max-abs 2e-3 in fp16 and bf16 alike, per-block mass 1e-4 relative, and at
+most 6 % of the rounded outputs different from the oracle's.
+"""
+
+import numpy as np
+import pytest
+import torch
+from test_paged_decode_gpu import HOST, build
+
+from oracle import streaming_attention_oracle as orc
+
+pytestmark = pytest.mark.gpu
+
+DT = {torch.float16: "f16", torch.bfloat16: "bf16"}
+
+
+def _np(t):
+    return t.detach().float().cpu().numpy()
+
+
+def gathered_row(s, b, layer, shift_blocks=0):
+    """Row b's KV as the reference's per-layer gather lays it out: ``shift_blocks`` empty blocks in
+    front (batched_decode.py:185-234 pads shorter sessions that way), then the row's blocks (absent
+    ones empty and masked), then the tail; with the valid mask of the row's range."""
+    tpb, nb, tl = s["tpb"], s["nbs"][b], s["tails"][b]
+    Hkv, D = s["dev"].shape[3], s["dev"].shape[5]
+    n = (shift_blocks + nb) * tpb
+    k = np.zeros((1, Hkv, n, D), np.float32)
+    v = np.zeros_like(k)
+    valid = np.zeros((1, n + tl), np.int32)
+    o = shift_blocks * tpb
+    for j in range(nb):
+        e = int(s["table"][b, j])
+        if e < 0:
+            continue
+        pool = s["host"] if e & HOST else s["dev"]
+        slot = e & (HOST - 1)
+        k[0, :, o + j * tpb:o + (j + 1) * tpb] = _np(pool[slot, layer, 0])
+        v[0, :, o + j * tpb:o + (j + 1) * tpb] = _np(pool[slot, layer, 1])
+        valid[0, o + j * tpb:o + (j + 1) * tpb] = 1
+    valid[0, n:] = 1
+    lo = 0 if s["lo"] is None else s["lo"][b]
+    hi = nb * tpb + tl if s["hi"] is None else min(s["hi"][b], nb * tpb + tl)
+    valid[0, :o + lo] = 0
+    valid[0, o + hi:] = 0
+    return k, v, valid, _np(s["tk"][b:b + 1, :, :tl]), _np(s["tv"][b:b + 1, :, :tl]), _np(s["q"][b:b + 1])
+
+
+def run_op(s, layer, rounding, group_blocks=0, shift_blocks=None, staged=False):
+    from pager_hf import streaming_attention as sa
+    from pager_hf.host_pool import HostPool
+
+    B, Hq = s["q"].shape[:2]
+    hp = HostPool(s["host"].shape, s["host"].dtype)
+    hp.tensor.copy_(s["host"])
+    dev = s["dev"].cuda()
+    max_blocks = s["table"].shape[1]
+    bm = torch.zeros(B, Hq, max_blocks, device="cuda")
+    max_row = max(nb * s["tpb"] + t for nb, t in zip(s["nbs"], s["tails"]))
+    cu = lambda x: None if x is None else torch.tensor(x, dtype=torch.int32, device="cuda")
+    shift = None if shift_blocks is None else cu([x * s["tpb"] for x in shift_blocks])
+    out = torch.empty(B, Hq, s["q"].shape[2], dtype=s["q"].dtype, device="cuda")
+    try:
+        plan = sa.PagedDecodePlan(
+            batch=B, num_query_heads=Hq, dev_pool=dev, host_pool=hp.tensor, num_layers=s["L"],
+            tokens_per_block=s["tpb"], block_table=s["table"].cuda(), num_blocks=cu(s["nbs"]), max_row_tokens=max_row,
+            tail_k=s["tk"].cuda(), tail_v=s["tv"].cuda(), tail_len=cu(s["tails"]), valid_lo=cu(s["lo"]),
+            valid_hi=cu(s["hi"]), block_mass=bm, host_read="staged" if staged else "zero_copy", rounding=rounding,
+            ref_group_tokens=group_blocks * s["tpb"], ref_shift=shift)
+        assert plan.host_read == ("staged" if staged else "zero_copy")
+        plan.run(s["q"].cuda(), layer, out)
+        torch.cuda.synchronize()
+        return out.float().cpu(), bm.cpu()
+    finally:
+        hp.close()
+
+
+def _check(out, ref, dtype, what):
+    np.testing.assert_allclose(out, ref, rtol=0, atol=2e-3, err_msg=what)
+    differ = float((out != ref).mean())
+    assert differ <= 0.06, f"{what}: {differ:.3f} of the rounded outputs differ from the reference sequence"
+    return differ
+
+
+CASES = [
+    # (seed, B, Hq, Hkv, D, tpb, L, nbs, tails, dtype, absent, lo, hi, group_blocks)
+    (11, 2, 32, 8, 128, 64, 2, [9, 5], [17, 64], torch.bfloat16, set(), None, None, 64),
+    (12, 3, 14, 2, 64, 16, 2, [21, 6, 0], [7, 3, 16], torch.float16, {(0, 3)}, [0, 20, 0], None, 4),
+    (13, 2, 32, 4, 64, 32, 1, [17, 6], [3, 30], torch.bfloat16, set(), [100, 0], [500, 150], 3),
+    (14, 2, 8, 4, 256, 16, 2, [13, 3], [5, 9], torch.bfloat16, set(), [10, 0], None, 2),
+    (15, 2, 32, 8, 128, 16, 1, [40, 1], [15, 2], torch.float16, {(0, 0), (0, 11)}, None, None, 64),
+]
+
+
+@pytest.mark.parametrize("case", CASES, ids=[f"case{c[0]}" for c in CASES])
+def test_running_rounding_matches_the_single_pass_sequence(case):
+    seed, B, Hq, Hkv, D, tpb, L, nbs, tails, dtype, absent, lo, hi, gs = case
+    s = build(seed, B, Hq, Hkv, D, tpb, L, nbs, tails, dtype, absent=absent, lo=lo, hi=hi)
+    layer = L - 1
+    out, _ = run_op(s, layer, "running", group_blocks=gs)
+    one, _ = run_op(s, layer, "one_pass")
+    for b in range(B):
+        k, v, valid, tk, tv, q = gathered_row(s, b, layer)
+        nb = nbs[b]
+        ref, _, _ = orc.single_pass_decode(q, k, v, tk, tv, nb, tpb, gs, valid=valid[:, :nb * tpb],
+                                           tail_valid=valid[:, nb * tpb:], v_dtype=DT[dtype], out_dtype=DT[dtype])
+        _check(out[b].numpy(), ref[0], dtype, f"row {b}")
+        np.testing.assert_allclose(one[b].numpy(), ref[0], rtol=0, atol=5e-3)  # one pass: same values, other rounding
+
+
+@pytest.mark.parametrize("case", CASES, ids=[f"case{c[0]}" for c in CASES])
+def test_final_rounding_matches_the_two_pass_sequence(case):
+    seed, B, Hq, Hkv, D, tpb, L, nbs, tails, dtype, absent, lo, hi, gs = case
+    s = build(seed, B, Hq, Hkv, D, tpb, L, nbs, tails, dtype, absent=absent, lo=lo, hi=hi)
+    layer = 0
+    out, bm = run_op(s, layer, "final")
+    for b in range(B):
+        k, v, valid, tk, tv, q = gathered_row(s, b, layer)
+        nb = nbs[b]
+        ref, mass, _, _ = orc.two_pass_decode(q, k, v, tk, tv, nb, tpb, max(nb, 1), valid=valid[:, :nb * tpb],
+                                              tail_valid=valid[:, nb * tpb:], v_dtype=DT[dtype], out_dtype=DT[dtype])
+        _check(out[b].numpy(), ref[0], dtype, f"row {b}")
+        np.testing.assert_allclose(bm[b, :, :nb].numpy(), mass[0, :, :nb], rtol=1e-4, atol=1e-6)
+
+
+def test_batched_rows_round_in_the_combined_numbering():
+    """Rows of different lengths in one launch, each ``ref_shift`` tokens into the combined block
+    numbering of the reference's cross-session path (shorter sessions padded in front), with groups
+    of 3 blocks (48 tokens: chunk boundaries off the 64-token grid)."""
+    nbs, tails, tpb, gs = [12, 5, 9], [4, 4, 4], 16, 3
+    s = build(21, 3, 16, 2, 64, tpb, 2, nbs, tails, torch.float16, host_every=3)
+    shift = [max(nbs) - nb for nb in nbs]
+    out, _ = run_op(s, 1, "running", group_blocks=gs, shift_blocks=shift)
+    for b in range(3):
+        k, v, valid, tk, tv, q = gathered_row(s, b, 1, shift_blocks=shift[b])
+        n = max(nbs)
+        ref, _, _ = orc.single_pass_decode(q, k, v, tk, tv, n, tpb, gs, valid=valid[:, :n * tpb],
+                                           tail_valid=valid[:, n * tpb:], v_dtype="f16", out_dtype="f16")
+        _check(out[b].numpy(), ref[0], torch.float16, f"row {b}")
+
+
+@pytest.mark.parametrize("rounding", ["running", "final"])
+def test_staged_host_reads_give_the_same_bits(rounding):
+    s = build(31, 2, 32, 8, 128, 64, 2, [10, 7], [33, 5], torch.bfloat16, host_every=2)
+    zc, zbm = run_op(s, 1, rounding, group_blocks=64)
+    st, sbm = run_op(s, 1, rounding, group_blocks=64, staged=True)
+    assert torch.equal(zc, st)
+    assert torch.equal(zbm, sbm)
+
+
+def test_exact_rounding_arguments_are_checked():
+    from pager_hf import streaming_attention as sa
+
+    s = build(41, 1, 8, 2, 64, 8, 1, [4], [3], torch.float16)
+    with pytest.raises(NotImplementedError, match="tokens_per_block >= 16"):
+        run_op(s, 0, "running")
+    with pytest.raises(ValueError, match="rounding must be"):
+        sa._rounding_code("nearest")

@@ -611,6 +611,13 @@ struct ChunkArgs {
   cudaStream_t stream;
 };
 
+// streaming_attention_step on fp16/bf16 KV with the tensor-core kernels rounds p exactly as the
+// reference's one-pass kernel does (scores pass, scan seeded with the incoming m, values pass);
+// defined below, beside the scan kernel.
+bool chunk_exact(const ChunkArgs& a);
+int run_chunk_exact(const ChunkArgs& a);
+size_t chunk_exact_scratch(const ChunkArgs& a);
+
 int chunk_plan(const ChunkArgs& a, SplitKernelInfo* k, Plan* plan, long long* mass_groups, int* group_tokens) {
   const int mode = a.op == 0 ? MODE_ONLINE : (a.op == 1 ? MODE_STATS : MODE_FIXED);
   const int be = backend_for(a.backend, a.kv_dtype, a.head_dim);
@@ -651,6 +658,7 @@ int run_chunk(const ChunkArgs& a) {
       return fail(PAGER_ERR_INVALID, "block_mass has %d blocks; offset %d + %d local blocks overflows it", a.max_blocks,
                   a.block_id_offset, nloc);
   }
+  if (chunk_exact(a)) return run_chunk_exact(a);
   SplitKernelInfo k;
   Plan plan;
   long long mass_groups;
@@ -743,6 +751,7 @@ int run_chunk(const ChunkArgs& a) {
 size_t chunk_scratch(const ChunkArgs& a) {
   if (check_geometry(a.batch, a.hq, a.hkv, a.head_dim, a.kv_dtype, a.q_dtype)) return 0;
   if (a.batch <= 0 || a.tokens <= 0) return 0;
+  if (chunk_exact(a)) return chunk_exact_scratch(a);
   SplitKernelInfo k;
   Plan plan;
   long long mass_groups;
@@ -1058,6 +1067,7 @@ __device__ __forceinline__ int ref_tile_key(int j, int shift, int tail_start, in
 struct RefMaxParams {
   GeomArgs geom;
   const int* active;
+  const float* m_in;  // incoming running max per query row (drop-in step), or null: -inf
   int rows, num_q_heads, tile_shift, tiles_per_split, group_shift, gstride, mstride, tpb;
   int rule;  // PAGER_ROUND_RUNNING or PAGER_ROUND_FINAL
   int ref_group_tokens;
@@ -1088,7 +1098,7 @@ __global__ void __launch_bounds__(kRefMaxWarps * 32) ref_max_kernel(const RefMax
   const int g1 = (te << p.tile_shift) >> p.group_shift;
   float* gm = p.gmax + (long long)row * p.gstride;
   float* mr = p.mref + (long long)row * p.mstride;
-  float carry = neg_inf();
+  float carry = p.m_in ? p.m_in[row] : neg_inf();
   for (int c0 = g0; c0 < g1; c0 += 32) {
     const int gi = c0 + lane;
     float v = gi < g1 ? gm[gi] : neg_inf();
@@ -1158,6 +1168,167 @@ int encode_2d_f32(CUtensorMap* map, const void* base, uint64_t d0, uint64_t d1, 
   if (r != CUDA_SUCCESS)
     return fail(PAGER_ERR_INVALID, "cuTensorMapEncodeTiled failed (%d) for a %llu x %llu fp32 view", (int)r,
                 (unsigned long long)d0, (unsigned long long)d1);
+  return PAGER_OK;
+}
+
+// ---- the drop-in streaming_attention_step with the reference's rounding
+// The reference's one-pass kernel folds a chunk in 64-token tiles from the chunk's start, its
+// running max starting at the incoming m (streaming_attention.py:143-181).  Here the scores pass
+// writes each tile's scores and max (one group per tile: tiles are at most 64 tokens and aligned
+// to the reference's), the scan turns them into the reference's running max seeded with m, and
+// the values pass folds V; the splits then merge into the incoming (m, l, acc) as before.
+struct ChunkExactLayout {
+  SplitKernelInfo ks, kv;
+  Plan ps, pv;
+  long long tiles;
+  Scratch sc;
+  float* scores;
+  float* gmax;
+  float* mref;
+  size_t bytes;
+};
+
+bool chunk_exact(const ChunkArgs& a) {
+  return a.op == 0 && a.kv_dtype != PAGER_DTYPE_F32 && backend_for(a.backend, a.kv_dtype, a.head_dim) == BACKEND_MMA;
+}
+
+int chunk_exact_layout(const ChunkArgs& a, char* base, ChunkExactLayout* L) {
+  if (!lookup_split_kernel(a.kv_dtype, a.head_dim, MODE_SCORES, BACKEND_MMA, &L->ks) ||
+      !lookup_split_kernel(a.kv_dtype, a.head_dim, MODE_VALUES, BACKEND_MMA, &L->kv))
+    return fail(PAGER_ERR_UNSUPPORTED, "no exact-rounding kernels for dtype %d head_dim %d", a.kv_dtype, a.head_dim);
+  DevInfo* di;
+  int rc = device_info(&di);
+  if (rc) return rc;
+  int per_s = 1, per_v = 1;
+  rc = ctas_per_sm(L->ks, &per_s);
+  if (rc) return rc;
+  rc = ctas_per_sm(L->kv, &per_v);
+  if (rc) return rc;
+  L->tiles = (a.tokens + L->kv.tile - 1) / L->kv.tile;
+  L->ps = plan_splits((long long)a.batch * a.hkv, (int)L->tiles, di->sms, per_s, 1 << 30);
+  L->pv = plan_splits((long long)a.batch * a.hkv, (int)L->tiles, di->sms, per_v, 1 << 30);
+  const long long rows = (long long)a.batch * a.hq;
+  L->sc = layout_scratch(base, rows, L->pv.max_splits, a.head_dim, L->tiles);
+  size_t off = L->sc.bytes;
+  auto take = [&](size_t n) {
+    char* p = base ? base + off : nullptr;
+    off += align256(n);
+    return reinterpret_cast<float*>(p);
+  };
+  L->scores = take(sizeof(float) * rows * L->tiles * L->kv.tile);
+  L->gmax = take(sizeof(float) * rows * L->tiles);
+  L->mref = take(sizeof(float) * rows * L->tiles * kRefSlots);
+  L->bytes = off;
+  return PAGER_OK;
+}
+
+size_t chunk_exact_scratch(const ChunkArgs& a) {
+  ChunkExactLayout L;
+  return chunk_exact_layout(a, nullptr, &L) ? 0 : L.bytes;
+}
+
+int run_chunk_exact(const ChunkArgs& a) {
+  ChunkExactLayout lay;
+  int rc = chunk_exact_layout(a, static_cast<char*>(a.scratch), &lay);
+  if (rc) return rc;
+  if (!a.scratch || a.scratch_bytes < lay.bytes)
+    return fail(PAGER_ERR_SCRATCH, "scratch too small: need %zu bytes, got %zu", lay.bytes, a.scratch_bytes);
+  DevInfo* di;
+  rc = device_info(&di);
+  if (rc) return rc;
+  const long long rows = (long long)a.batch * a.hq;
+  const int n_rep = a.hq / a.hkv;
+  const int tile = lay.kv.tile;
+  CUtensorMap mk, mv, mS, mM;
+  const uint64_t z = (uint64_t)a.batch * a.hkv;
+  rc = encode_3d(&mk, a.kv_dtype, a.k, a.head_dim, a.tokens, z, lay.ks.panel_elts, tile, lay.ks.panel_bytes);
+  if (rc) return rc;
+  rc = encode_3d(&mv, a.kv_dtype, a.v, a.head_dim, a.tokens, z, lay.kv.panel_elts, tile, lay.kv.panel_bytes);
+  if (rc) return rc;
+  rc = encode_2d_f32(&mS, lay.scores, (uint64_t)(lay.tiles * tile), (uint64_t)rows, (uint32_t)tile, (uint32_t)n_rep);
+  if (rc) return rc;
+  rc = encode_2d_f32(&mM, lay.mref, (uint64_t)(lay.tiles * kRefSlots), (uint64_t)rows, (uint32_t)kRefSlots,
+                     (uint32_t)n_rep);
+  if (rc) return rc;
+  SplitParams p;
+  memset(&p, 0, sizeof(p));
+  p.q = a.q;
+  p.q_dtype = a.q_dtype;
+  p.batch = a.batch;
+  p.num_q_heads = a.hq;
+  p.num_kv_heads = a.hkv;
+  p.n_rep = n_rep;
+  p.scale = a.scale;
+  p.softcap = a.softcap > 0.f ? a.softcap : 0.f;
+  p.source = SRC_CONTIG;
+  p.geom.source = SRC_CONTIG;
+  p.geom.tokens = a.tokens;
+  p.geom.max_tokens = a.tokens;
+  p.valid = a.valid;
+  p.valid_stride = a.tokens;
+  p.active = a.active;
+  p.part_m = lay.sc.part_m;
+  p.part_l = lay.sc.part_l;
+  p.part_acc = lay.sc.part_acc;
+  p.mass_part = lay.sc.mass_part;
+  p.mass_gstride = (int)lay.tiles;
+  p.group_tokens = tile;
+  p.log2_group = ilog2(tile);
+  p.scores = lay.scores;
+  p.s_stride = lay.tiles * tile;
+  p.gmax = lay.gmax;
+  p.wait_limit_ns = kWaitLimitNs;
+  p.status = di->status;
+  SplitParams ps = p;
+  ps.tiles_per_split = lay.ps.tiles_per_split;
+  ps.max_splits = lay.ps.max_splits;
+  void* sargs[] = {&ps, &mk, &mv, &mS, &mM};
+  PAGER_CUDA(cudaLaunchKernel(lay.ks.fn, dim3(lay.ps.max_splits, a.hkv, a.batch), dim3(lay.ks.threads), sargs,
+                              lay.ks.smem_bytes, a.stream),
+             "scores kernel launch");
+  RefMaxParams rp;
+  memset(&rp, 0, sizeof(rp));
+  rp.geom = p.geom;
+  rp.active = a.active;
+  rp.m_in = a.m;
+  rp.rows = (int)rows;
+  rp.num_q_heads = a.hq;
+  rp.tile_shift = ilog2(tile);
+  rp.tiles_per_split = lay.pv.tiles_per_split;
+  rp.group_shift = ilog2(tile);
+  rp.gstride = (int)lay.tiles;
+  rp.mstride = (int)(lay.tiles * kRefSlots);
+  rp.tpb = tile;
+  rp.rule = PAGER_ROUND_RUNNING;
+  rp.ref_tail_start = nullptr;  // a chunk has no blocks: 64-token tiles from its first token
+  rp.gmax = lay.gmax;
+  rp.mref = lay.mref;
+  ref_max_kernel<<<(unsigned)((rows + kRefMaxWarps - 1) / kRefMaxWarps), kRefMaxWarps * 32, 0, a.stream>>>(rp);
+  PAGER_CUDA(cudaGetLastError(), "reference-max launch");
+  p.tiles_per_split = lay.pv.tiles_per_split;
+  p.max_splits = lay.pv.max_splits;
+  void* vargs[] = {&p, &mk, &mv, &mS, &mM};
+  PAGER_CUDA(cudaLaunchKernel(lay.kv.fn, dim3(lay.pv.max_splits, a.hkv, a.batch), dim3(lay.kv.threads), vargs,
+                              lay.kv.smem_bytes, a.stream),
+             "values kernel launch");
+  CombineParams c;
+  memset(&c, 0, sizeof(c));
+  c.num_q_heads = a.hq;
+  c.head_dim = a.head_dim;
+  c.tile_shift = ilog2(tile);
+  c.tiles_per_split = lay.pv.tiles_per_split;
+  c.max_splits = lay.pv.max_splits;
+  c.geom = p.geom;
+  c.active = a.active;
+  c.part_m = lay.sc.part_m;
+  c.part_l = lay.sc.part_l;
+  c.part_acc = lay.sc.part_acc;
+  c.op = OP_STEP;
+  c.m = a.m;
+  c.l = a.l;
+  c.acc = a.acc;
+  combine_kernel<<<(unsigned)rows, 128, 0, a.stream>>>(c);
+  PAGER_CUDA(cudaGetLastError(), "combine launch");
   return PAGER_OK;
 }
 

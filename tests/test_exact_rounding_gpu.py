@@ -9,8 +9,8 @@ oracle of those sequences (oracle/streaming_attention_oracle.py: ``single_pass_d
 boundary -- as the reference's own Triton kernels agree with that oracle (a few percent of the
 fp16/bf16 outputs, fewer in bf16).  The one-pass kernel differs from it in about half of them.
 
-Tolerances: output max-abs 2e-3 in fp16 and bf16 alike, per-block mass 1e-4 relative, and at
-most 6 % of the rounded outputs different from the oracle's.
+Tolerances: outputs within 2e-3 (or one ulp of the output dtype where that is larger), per-block
+mass 1e-4 relative, and at most 6 % of the rounded outputs different from the oracle's.
 """
 
 import numpy as np
@@ -87,7 +87,10 @@ def run_op(s, layer, rounding, group_blocks=0, shift_blocks=None, staged=False):
 
 
 def _check(out, ref, dtype, what):
-    np.testing.assert_allclose(out, ref, rtol=0, atol=2e-3, err_msg=what)
+    # within 2e-3, or one ulp of the output dtype where that is larger (bf16: 3.9e-3 between 0.5 and 1)
+    tol = np.maximum(2e-3, float(torch.finfo(dtype).eps) * np.abs(ref))
+    worst = float((np.abs(out - ref) / tol).max())
+    assert worst <= 1.0, f"{what}: a difference of {worst:.2f} x max(2e-3, 1 ulp)"
     differ = float((out != ref).mean())
     assert differ <= 0.06, f"{what}: {differ:.3f} of the rounded outputs differ from the reference sequence"
     return differ
@@ -167,3 +170,71 @@ def test_exact_rounding_arguments_are_checked():
         run_op(s, 0, "running")
     with pytest.raises(ValueError, match="rounding must be"):
         sa._rounding_code("nearest")
+
+
+def _chunks(seed, B, Hq, Hkv, D, dtype, sizes):
+    g = torch.Generator().manual_seed(seed)
+    q = torch.randn(B, Hq, D, generator=g).to(dtype)
+    chunks = []
+    for n in sizes:
+        k = torch.randn(B, Hkv, n, D, generator=g).to(dtype)
+        v = torch.randn(B, Hkv, n, D, generator=g).to(dtype)
+        valid = (torch.rand(B, n, generator=g) > 0.1).to(torch.int32)
+        chunks.append((k, v, valid))
+    return q, chunks
+
+
+@pytest.mark.parametrize("dtype,D,Hq,Hkv", [(torch.bfloat16, 128, 32, 8), (torch.float16, 64, 14, 2),
+                                            (torch.bfloat16, 256, 8, 4)])
+def test_drop_in_step_rounds_like_the_reference_step_kernel(dtype, D, Hq, Hkv):
+    """``streaming_attention_step`` folds chunks into a running state as the reference's one-pass
+    kernel does (64-token tiles from each chunk's start, its running max starting at the incoming m),
+    so a sequence of calls -- a long chunk, a ragged one with a holed mask, a short tail -- ends at
+    the oracle's state and, after finalize, at its rounded outputs."""
+    from pager_hf import streaming_attention as sa
+
+    B = 3
+    q, chunks = _chunks(51, B, Hq, Hkv, D, dtype, (4096, 1000, 17))
+    m, l, acc = sa.streaming_attention_state_init(B, Hq, D, "cuda")
+    om, ol, oacc = orc.state_init(B, Hq, D)
+    for k, v, valid in chunks:
+        sa.streaming_attention_step(q.cuda(), k.cuda(), v.cuda(), m, l, acc, valid=valid.cuda())
+        orc.step(_np(q), _np(k), _np(v), om, ol, oacc, valid=valid.numpy(), v_dtype=DT[dtype])
+    out = sa.streaming_attention_finalize(acc, l, dtype).float().cpu().numpy()
+    ref = orc.finalize(oacc, ol, DT[dtype])
+    np.testing.assert_allclose(m.cpu().numpy(), om, rtol=1e-6, atol=1e-6)
+    np.testing.assert_allclose(l.cpu().numpy(), ol, rtol=2e-5)
+    for b in range(B):
+        _check(out[b], ref[b], dtype, f"row {b}")
+
+
+def test_drop_in_step_agrees_with_the_reference_triton_kernel():
+    """The same call sequence through the reference's own ``streaming_attention_step`` (its Triton
+    kernel on this GPU, from the offline install of the reference): the rounded outputs agree in all
+    but the few percent where fp32 association differs -- as closely as the reference agrees with its
+    own restatement.  Skipped where the install is absent."""
+    import importlib.util
+    import os
+
+    path = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "baseline", "_ref", "pager_hf",
+                        "streaming_attention.py")
+    if not os.path.isfile(path):
+        pytest.skip("the reference is not installed under baseline/_ref")
+    spec = importlib.util.spec_from_file_location("reference_streaming_attention", path)
+    ref_sa = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(ref_sa)
+    from pager_hf import streaming_attention as sa
+
+    for dtype, D, Hq, Hkv in [(torch.bfloat16, 128, 32, 8), (torch.float16, 64, 14, 2)]:
+        B = 4
+        q, chunks = _chunks(52, B, Hq, Hkv, D, dtype, (4096, 18))
+        outs = []
+        for mod in (sa, ref_sa):
+            m, l, acc = mod.streaming_attention_state_init(B, Hq, D, torch.device("cuda"))
+            for k, v, valid in chunks:
+                mod.streaming_attention_step(q.cuda(), k.cuda(), v.cuda(), m, l, acc, valid=valid.cuda())
+            outs.append(mod.streaming_attention_finalize(acc, l, dtype).float().cpu().numpy())
+        differ = float((outs[0] != outs[1]).mean())
+        print(f"{dtype} D{D}: {differ:.4f} of the rounded outputs differ from the reference's Triton kernel")
+        np.testing.assert_allclose(outs[0], outs[1], rtol=0, atol=4e-3)
+        assert differ <= 0.06

@@ -1077,19 +1077,25 @@ struct RefMaxParams {
   float* mref;  // out: [rows, mstride], kRefSlots entries per tile
 };
 
-constexpr int kRefMaxWarps = 8;
+constexpr int kRefMaxThreads = 256;
+constexpr int kRefMaxPer = 4;  // consecutive groups per thread in each chunk of the prefix scan
 
-// Between the SCORES and VALUES passes: per query row (one warp), the max each group's p is
-// formed against -- the reference's running max once its tile is folded in (the inclusive prefix
-// max of the group maxima up to the tile's last group), or the row's final max.
-__global__ void __launch_bounds__(kRefMaxWarps * 32) ref_max_kernel(const RefMaxParams p) {
+// Between the SCORES and VALUES passes: per query row (one CTA), the max each group's p is formed
+// against -- the reference's running max once its tile is folded in (the inclusive prefix max of
+// the group maxima up to the tile's last group), or the row's final max.  The prefix max runs as a
+// block-wide scan over chunks of kRefMaxThreads * kRefMaxPer groups, written back over the group
+// maxima; each group then reads the prefix at its reference tile's last group.
+__global__ void __launch_bounds__(kRefMaxThreads) ref_max_kernel(const RefMaxParams p) {
+  __shared__ float warp_tot[kRefMaxThreads / 32];
+  __shared__ float chunk_tot;
   pdl_wait();
   pdl_launch_dependents();
-  const int lane = threadIdx.x & 31;
-  const int row = blockIdx.x * kRefMaxWarps + (threadIdx.x >> 5);
-  if (row >= p.rows) return;
+  const int row = blockIdx.x;
+  const int tid = threadIdx.x;
+  const int lane = tid & 31;
+  const int warp = tid >> 5;
   const int b = row / p.num_q_heads;
-  if (p.active && p.active[b] == 0) return;
+  if (p.active && p.active[b] == 0) return;  // uniform across the CTA
   const RowGeom g = row_geom(p.geom, b);
   int tb, te, ns;
   geom_tiles(g, p.tile_shift, p.tiles_per_split, tb, te, ns);
@@ -1099,25 +1105,45 @@ __global__ void __launch_bounds__(kRefMaxWarps * 32) ref_max_kernel(const RefMax
   float* gm = p.gmax + (long long)row * p.gstride;
   float* mr = p.mref + (long long)row * p.mstride;
   float carry = p.m_in ? p.m_in[row] : neg_inf();
-  for (int c0 = g0; c0 < g1; c0 += 32) {
-    const int gi = c0 + lane;
-    float v = gi < g1 ? gm[gi] : neg_inf();
+  for (int c0 = g0; c0 < g1; c0 += kRefMaxThreads * kRefMaxPer) {
+    float v[kRefMaxPer];
+    float run = neg_inf();
+#pragma unroll
+    for (int i = 0; i < kRefMaxPer; ++i) {
+      const int gi = c0 + tid * kRefMaxPer + i;
+      v[i] = gi < g1 ? gm[gi] : neg_inf();
+      run = fmaxf(run, v[i]);
+      v[i] = run;  // inclusive prefix within this thread's groups
+    }
+    float incl = run;  // inclusive scan of the threads' maxima across the warp
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
-      const float t = __shfl_up_sync(0xffffffffu, v, o);
-      if (lane >= o) v = fmaxf(v, t);
+      const float t = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl = fmaxf(incl, t);
     }
-    v = fmaxf(v, carry);
-    if (gi < g1) gm[gi] = v;
-    carry = __shfl_sync(0xffffffffu, v, 31);
+    if (lane == 31) warp_tot[warp] = incl;
+    __syncthreads();
+    float before = carry;  // everything before this thread's groups
+    for (int w = 0; w < warp; ++w) before = fmaxf(before, warp_tot[w]);
+    const float excl = __shfl_up_sync(0xffffffffu, incl, 1);
+    if (lane > 0) before = fmaxf(before, excl);
+#pragma unroll
+    for (int i = 0; i < kRefMaxPer; ++i) {
+      const int gi = c0 + tid * kRefMaxPer + i;
+      if (gi < g1) gm[gi] = fmaxf(before, v[i]);
+    }
+    if (tid == kRefMaxThreads - 1) chunk_tot = fmaxf(before, run);
+    __syncthreads();
+    carry = chunk_tot;
+    __syncthreads();
   }
-  __syncwarp();  // every lane's prefix values are visible to the others
+  // carry: the row's final max; the prefix values written above are visible to the whole CTA
   const int shift = p.ref_shift ? p.ref_shift[b] : 0;
   const int tail_start = p.ref_tail_start ? p.ref_tail_start[b] : g.nb * p.tpb;
   const int G = 1 << p.group_shift;
   const int per_tile = 1 << (p.tile_shift - p.group_shift);
-  for (int gi = g0 + lane; gi < g1; gi += 32) {
-    float M = carry;  // the final max
+  for (int gi = g0 + tid; gi < g1; gi += kRefMaxThreads) {
+    float M = carry;
     if (p.rule == PAGER_ROUND_RUNNING) {
       const int key = ref_tile_key(gi * G, shift, tail_start, p.ref_group_tokens);
       int e = gi;  // the last group of the same reference tile (a tile spans at most 64 / G groups)
@@ -1196,6 +1222,7 @@ int chunk_exact_layout(const ChunkArgs& a, char* base, ChunkExactLayout* L) {
   if (!lookup_split_kernel(a.kv_dtype, a.head_dim, MODE_SCORES, BACKEND_MMA, &L->ks) ||
       !lookup_split_kernel(a.kv_dtype, a.head_dim, MODE_VALUES, BACKEND_MMA, &L->kv))
     return fail(PAGER_ERR_UNSUPPORTED, "no exact-rounding kernels for dtype %d head_dim %d", a.kv_dtype, a.head_dim);
+  if (L->ks.tile != L->kv.tile) return fail(PAGER_ERR_CUDA, "scores and values passes disagree on the tile");
   DevInfo* di;
   int rc = device_info(&di);
   if (rc) return rc;
@@ -1303,7 +1330,7 @@ int run_chunk_exact(const ChunkArgs& a) {
   rp.ref_tail_start = nullptr;  // a chunk has no blocks: 64-token tiles from its first token
   rp.gmax = lay.gmax;
   rp.mref = lay.mref;
-  ref_max_kernel<<<(unsigned)((rows + kRefMaxWarps - 1) / kRefMaxWarps), kRefMaxWarps * 32, 0, a.stream>>>(rp);
+  ref_max_kernel<<<(unsigned)rows, kRefMaxThreads, 0, a.stream>>>(rp);
   PAGER_CUDA(cudaGetLastError(), "reference-max launch");
   p.tiles_per_split = lay.pv.tiles_per_split;
   p.max_splits = lay.pv.max_splits;
@@ -1361,6 +1388,7 @@ int paged_layout(int batch, int hq, int hkv, int head_dim, int kv_dtype, int tpb
   if (exact) {
     rc = paged_plan(batch, hq, hkv, head_dim, kv_dtype, tpb, max_row_tokens, backend, &L->ps, MODE_SCORES);
     if (rc) return rc;
+    if (L->ps.k.tile != L->pv.k.tile) return fail(PAGER_ERR_CUDA, "scores and values passes disagree on the tile");
     const long long tiles = L->pv.gstride * L->pv.G / L->pv.k.tile;
     L->s_stride = tiles * L->pv.k.tile;
     L->mstride = tiles * kRefSlots;
@@ -1541,9 +1569,8 @@ int run_paged(const PagedArgs& a) {
     rp.gmax = lay.gmax;
     rp.mref = lay.mref;
     void* rargs[] = {&rp};
-    PAGER_CUDA(launch_serialized(reinterpret_cast<const void*>(&ref_max_kernel),
-                                 dim3((unsigned)((rows + kRefMaxWarps - 1) / kRefMaxWarps)), dim3(kRefMaxWarps * 32), 0,
-                                 st, rargs),
+    PAGER_CUDA(launch_serialized(reinterpret_cast<const void*>(&ref_max_kernel), dim3((unsigned)rows),
+                                 dim3(kRefMaxThreads), 0, st, rargs),
                "reference-max launch");
   }
   p.tiles_per_split = pp.plan.tiles_per_split;

@@ -168,7 +168,11 @@ template <typename T, int D, int MODE, int BACKEND>
 struct TileCfg {
   static constexpr int ELT = sizeof(T);
   static constexpr int ROW_BYTES = D * ELT;
-  static constexpr int TILE_RAW = 16384 / (2 * ROW_BYTES);
+  // 16 KiB of KV per stage: a K and a V tile, or one tile twice as long in the passes that read
+  // one of them (per-tile costs -- waits, table lookups, the online update -- then spread over as
+  // many bytes as in the one-pass kernel)
+  static constexpr bool SINGLE = MODE == MODE_STATS || MODE == MODE_SCORES || MODE == MODE_VALUES;
+  static constexpr int TILE_RAW = 16384 / ((SINGLE ? 1 : 2) * ROW_BYTES);
   static constexpr int TILE = TILE_RAW > 64 ? 64 : (TILE_RAW < 16 ? 16 : TILE_RAW);
   static constexpr int LOG2_TILE = TILE == 64 ? 6 : (TILE == 32 ? 5 : 4);
   static constexpr int PANEL_BYTES = ROW_BYTES < 128 ? ROW_BYTES : 128;
@@ -201,10 +205,11 @@ struct TileCfg {
   static constexpr int P_BYTES = BACKEND == BACKEND_FMA ? NCW * TILE * kMaxRep * 4 : 0;
   static constexpr int EXTRA = Q_BYTES + P_BYTES + kTableCache * 4 + 1536;
   // A deep ring: each consumer warp holds a stage while it computes, the rest stay in flight.
-  // Even, so that with two producer warps each stage is always filled by the same one.
-  static constexpr int STAGES_RAW = ((SMEM_BUDGET - EXTRA) / (STAGE_BYTES + AUX_BYTES)) & ~1;
+  // With two producer warps the count is even, so that each stage is always filled by the same one.
+  static constexpr int STAGES_FIT = (SMEM_BUDGET - EXTRA) / (STAGE_BYTES + AUX_BYTES);
+  static constexpr int STAGES_RAW = NPW == 2 ? (STAGES_FIT & ~1) : STAGES_FIT;
   static constexpr int STAGES = STAGES_RAW > 16 ? 16 : STAGES_RAW;
-  static_assert(STAGES >= NCW && STAGES % 2 == 0, "stage ring too shallow for the consumer warps");
+  static_assert(STAGES >= NCW && (NPW == 1 || STAGES % 2 == 0), "stage ring too shallow for the consumer warps");
   static constexpr int STAGE_AREA = STAGES * STAGE_BYTES;
   static constexpr int MERGE_BYTES = NCW * kMaxRep * (2 + (KONLY ? 0 : D)) * 4;
   static_assert(MERGE_BYTES <= STAGE_AREA, "merge region must fit in the stage ring");

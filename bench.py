@@ -783,6 +783,18 @@ def run_ours(args):
     ms_local = start.elapsed_time(end)
     per_launch = [ms_local / (args.steps * wl.L)]
     ms_total = max_over_ranks(ms_local, device)
+    # each rank's own view of the host side: its concurrently measured link and where the pages of its
+    # pinned host pool sit relative to its GPU's NUMA node
+    from pager_hf.host_pool import device_numa_node, numa_pages
+
+    mine_host = {"rank": rank, "host_link": link, "gpu_numa_node": device_numa_node(local),
+                 "host_pool_pages_by_numa_node": ({str(k): v for k, v in numa_pages(wl.host.data_ptr,
+                                                                                    wl.host.nbytes).items()}
+                                                  if wl.host is not None else {})}
+    per_rank_host = [mine_host]
+    if world > 1:
+        per_rank_host = [None] * world
+        dist.all_gather_object(per_rank_host, mine_host)
     ms_step = ms_total / args.steps
     value = world * wl.bytes_per_step / (ms_step / 1000) / 1e9
     tokens_per_s = world * wl.B / (ms_step / 1000)
@@ -850,6 +862,7 @@ def run_ours(args):
             "frac_of_overlapped_bound": achieved / (bytes_per_launch / max(t_hbm, t_link) / 1e9),
         },
         "host_link": link,
+        "host_per_rank": per_rank_host,
         "e2e": {"value": e2e_value, "unit": "GB/s", "ms_per_step": e2e_step,
                 "h2d_bytes_per_step": q_host.numel() * q_host.element_size(),
                 "d2h_bytes_per_step": out_host.numel() * out_host.element_size() + mass_host.numel() * 4},
@@ -865,6 +878,9 @@ def run_ours(args):
         if world == 1 and not args.no_extras:
             if args.workload != "hbm-32k":
                 line["kernel_hbm_32k"] = kernel_only_measurement("hbm-32k", device, args.rounding, hbm_peak, peak_src)
+                if args.rounding != "one_pass":
+                    line["kernel_hbm_32k_one_pass"] = kernel_only_measurement("hbm-32k", device, "one_pass", hbm_peak,
+                                                                              peak_src)
             line["model_decode"] = model_level_decode(device)
         if world == 1 and not args.no_cpu_baseline:
             arm = cpu_arm(args.workload, args.cpu_arm)

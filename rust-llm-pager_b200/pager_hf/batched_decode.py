@@ -103,10 +103,16 @@ class DecodeSession:
 
 
 class BatchedDecodeAttention:
-    """One decode step of attention for ``sessions``: ``layer()`` per layer, then ``finish()``."""
+    """One decode step of attention for ``sessions``: ``layer()`` per layer, then ``finish()``.
+
+    ``rounding`` (``paged_decode_attention``): "reference" rounds p as the reference's cross-session
+    path does -- its two-pass sequence when any session scores blocks, its one-pass sequence
+    otherwise (batched_decode.py:236-285), each session sitting as far into the reference's combined
+    block numbering as it has fewer blocks than the longest (``:185-234``), in groups of
+    ``group_size_blocks`` blocks; "one_pass" is the one-pass kernel."""
 
     def __init__(self, sessions: list[DecodeSession], num_query_heads: int, *, scale: float | None = None,
-                 softcap: float | None = None):
+                 softcap: float | None = None, rounding: str = "reference", group_size_blocks: int = 64):
         if not sessions:
             raise ValueError("batched decode needs at least one session")
         pools = sessions[0].pools
@@ -143,11 +149,18 @@ class BatchedDecodeAttention:
         self.positions = torch.tensor(pos, **i32)
         self.needs_attention = any(s.needs_attention for s in sessions)
         self.mass = torch.zeros(S, width, dtype=torch.float32, device=self.device) if self.needs_attention else None
+        from .paged_model import step_rounding
+
+        max_nb = width - 1
         self.plan = PagedDecodePlan(
             batch=S, num_query_heads=num_query_heads, dev_pool=pools.dev_pool, host_pool=pools.host_pool.tensor,
             num_layers=pools.num_layers, tokens_per_block=tpb, block_table=self.table, num_blocks=self.num_blocks,
             max_row_tokens=width * tpb, valid_lo=self.valid_lo, valid_hi=self.valid_hi, scale=scale,
-            softcap=softcap, mass_accum=self.mass, mass_mode="row_mean" if self.needs_attention else "none")
+            softcap=softcap, mass_accum=self.mass, mass_mode="row_mean" if self.needs_attention else "none",
+            rounding=step_rounding(rounding, self.needs_attention, pools.dtype, pools.head_dim, tpb),
+            ref_group_tokens=group_size_blocks * tpb,
+            ref_shift=torch.tensor([(max_nb - s.num_blocks) * tpb for s in sessions], **i32),
+            ref_tail_start=torch.tensor([s.num_blocks * tpb for s in sessions], **i32))
         self._layers_done = 0
         self._lib = L.lib()
 

@@ -50,6 +50,52 @@ def device_numa_cpus(device_index: int, sysfs: str | None = None) -> set[int] | 
         return None
 
 
+def device_numa_node(device_index: int, sysfs: str | None = None) -> int | None:
+    """The NUMA node of a GPU's PCIe link from sysfs, or None when the system does not say."""
+    sysfs = SYSFS if sysfs is None else sysfs
+    try:
+        p = torch.cuda.get_device_properties(device_index)
+        bdf = f"{p.pci_domain_id:04x}:{p.pci_bus_id:02x}:{p.pci_device_id:02x}.0"
+        with open(os.path.join(sysfs, "bus", "pci", "devices", bdf, "numa_node")) as f:
+            node = int(f.read().strip())
+        return node if node >= 0 else None
+    except (OSError, ValueError, RuntimeError, AssertionError):
+        return None
+
+
+def numa_pages(ptr: int, nbytes: int, proc: str = "/proc/self") -> dict[int, int]:
+    """Resident pages per NUMA node of the memory mappings overlapping ``[ptr, ptr + nbytes)``, from
+    the process's ``maps`` (address ranges) and ``numa_maps`` (``N<node>=<pages>`` per mapping);
+    {} when the kernel does not report them."""
+    try:
+        with open(os.path.join(proc, "maps")) as f:
+            ranges = []
+            for line in f:
+                lo, _, hi = line.split(" ", 1)[0].partition("-")
+                ranges.append((int(lo, 16), int(hi, 16)))
+        with open(os.path.join(proc, "numa_maps")) as f:
+            nodes_at = {}
+            for line in f:
+                parts = line.split()
+                if not parts:
+                    continue
+                counts = {}
+                for field in parts[2:]:
+                    if field.startswith("N") and "=" in field:
+                        node, _, pages = field[1:].partition("=")
+                        if node.isdigit():
+                            counts[int(node)] = int(pages)
+                nodes_at[int(parts[0], 16)] = counts
+    except (OSError, ValueError):
+        return {}
+    out: dict[int, int] = {}
+    for lo, hi in ranges:
+        if hi > ptr and lo < ptr + nbytes:
+            for node, pages in nodes_at.get(lo, {}).items():
+                out[node] = out.get(node, 0) + pages
+    return out
+
+
 @contextlib.contextmanager
 def on_cpus(cpus: set[int] | None):
     """Run the block with the calling thread restricted to ``cpus`` (those it may use at all), then

@@ -103,12 +103,14 @@ class ShardRunner:
 
     def __init__(self, device, *, geometry: dict = LLAMA3_8B, tokens_per_block: int = 64,
                  hbm_budget_bytes: float = 40e9, host_budget_bytes: float = 96e9, max_sessions: int = 16,
-                 policy: str = "recent_only", dtype: torch.dtype = torch.bfloat16, seed: int = 0):
+                 policy: str = "recent_only", dtype: torch.dtype = torch.bfloat16, seed: int = 0,
+                 rounding: str = "reference"):
         self.device = torch.device(device)
         self.g = dict(geometry)
         self.tpb = tokens_per_block
         self.max_sessions = max_sessions
         self.policy = policy
+        self.rounding = rounding  # of p before P.V: the reference's, or the one-pass kernel's
         L, hkv, d = self.g["layers"], self.g["hkv"], self.g["d"]
         elt = torch.tensor([], dtype=dtype).element_size()
         self.slot_bytes = 2 * L * hkv * tokens_per_block * d * elt
@@ -206,7 +208,7 @@ class ShardRunner:
             st.peak_sessions = max(st.peak_sessions, len(active))
             S = len(active)
             ts = time.perf_counter()
-            plan = BatchedDecodeAttention([a.session for a in active], self.g["hq"])
+            plan = BatchedDecodeAttention([a.session for a in active], self.g["hq"], rounding=self.rounding)
             for layer in range(self.g["layers"]):
                 plan.layer(layer, self.q[layer, :S], self.kn[layer, :S], self.vn[layer, :S])
             try:
@@ -275,6 +277,7 @@ def main(argv=None):
     ap.add_argument("--policy", default="recent_only")
     ap.add_argument("--tokens-per-block", type=int, default=64)
     ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--rounding", default="reference", choices=["reference", "one_pass"])
     a = ap.parse_args(argv)
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -289,7 +292,7 @@ def main(argv=None):
     mine = [reqs[i] for i in local_requests(route(reqs, world), rank)]
     runner = ShardRunner(f"cuda:{local}", tokens_per_block=a.tokens_per_block, hbm_budget_bytes=a.hbm_budget_gb * 1e9,
                          host_budget_bytes=a.host_budget_gb * 1e9, max_sessions=a.max_sessions, policy=a.policy,
-                         seed=a.seed + rank)
+                         seed=a.seed + rank, rounding=a.rounding)
     try:
         if world > 1:
             dist.barrier()

@@ -54,3 +54,19 @@ def test_affinity_is_restricted_inside_and_restored_after():
         with hp.on_cpus(one):
             raise RuntimeError("allocation failed")
     assert os.sched_getaffinity(0) == before
+
+
+def test_numa_pages_sums_the_mappings_over_a_range(tmp_path):
+    from pager_hf.host_pool import numa_pages
+
+    (tmp_path / "maps").write_text(
+        "7f0000000000-7f0000200000 rw-s 00000000 00:05 1 /dev/nvidia0\n"
+        "7f0000200000-7f0000400000 rw-s 00000000 00:05 1 /dev/nvidia0\n"
+        "7f1000000000-7f1000001000 r--p 00000000 00:05 2 /lib/x.so\n")
+    (tmp_path / "numa_maps").write_text(
+        "7f0000000000 default file=/dev/nvidia0 dirty=512 N0=300 N1=212 kernelpagesize_kB=4\n"
+        "7f0000200000 default file=/dev/nvidia0 dirty=512 N1=512 kernelpagesize_kB=4\n"
+        "7f1000000000 default file=/lib/x.so mapped=1 N0=1 kernelpagesize_kB=4\n")
+    assert numa_pages(0x7F0000000000, 0x400000, str(tmp_path)) == {0: 300, 1: 724}
+    assert numa_pages(0x7F0000300000, 0x1000, str(tmp_path)) == {1: 512}
+    assert numa_pages(0x7F0000000000, 16, str(tmp_path / "missing")) == {}

@@ -340,19 +340,76 @@ struct PagedMassParams {
 };
 
 // The combine/mass kernel of the paged op runs 256-thread CTAs: the first `rows` CTAs merge one
-// query row each, the rest compute the per-block mass of 32 blocks of one batch row (all rows in
-// batch-mean mode).  The mass CTAs derive each head's final (M, L) from the splits' statistics
-// themselves (a warp reduction; the merge's serial sum may differ in the last bit, far inside the
-// mass tolerance), so neither half waits for the other.
+// query row each, the rest compute the per-block mass of 32 blocks of one row (all rows in
+// batch-mean mode).  Both halves derive each head's final (M, L) from the splits' statistics the
+// same way -- lanes walk the splits with an online (max, sum), shuffles merge the lanes -- so
+// neither waits for the other and they agree on M and L bit for bit.
 constexpr int kFinishThreads = 256;
 constexpr int kFinishWarps = kFinishThreads / 32;
 constexpr int kHeadsPerWarp = 4;  // heads a warp handles at once: their loads are issued together
 constexpr int kMassHeadChunk = kFinishWarps * kHeadsPerWarp;
+constexpr int kPreload = 8;  // partial accumulators a combine thread loads before the statistics are known
 
+// Final (M, L) of one query row from its splits' (m, l), for every lane of the calling warp.
+__device__ __forceinline__ void warp_row_stats(const float* pm, const float* pl, int nsplit, float& M, float& L) {
+  const int lane = threadIdx.x & 31;
+  float mx = neg_inf(), sm = 0.f;
+  for (int s = lane; s < nsplit; s += 32) {
+    const float mv = pm[s], lv = pl[s];
+    const float nm = fmaxf(mx, mv);
+    sm = sm * split_weight(mx, nm) + lv * split_weight(mv, nm);
+    mx = nm;
+  }
+  M = warp_max(mx);
+  L = warp_sum(sm * split_weight(mx, M));
+}
+
+// One query row of the paged op: out = sum_s w_s acc_s / L.  Warp 0 reduces the statistics while the
+// other threads already load their columns' partial accumulators; one CTA barrier hands the split
+// weights over.
+__device__ __forceinline__ void paged_combine_row(const CombineParams& c, int row) {
+  __shared__ float w_s[kMaxSplits];
+  __shared__ float sh_L;
+  const int b = row / c.num_q_heads;
+  if (c.active && c.active[b] == 0) return;
+  int t_begin, t_end, nsplit;
+  geom_tiles(row_geom(c.geom, b), c.tile_shift, c.tiles_per_split, t_begin, t_end, nsplit);
+  const int D = c.head_dim;
+  const int tid = threadIdx.x;
+  const long long pbase = (long long)row * c.max_splits;
+  const int d = tid;  // this thread's column (head_dim <= kFinishThreads)
+  float pre[kPreload];
+  if (tid >= 32 && d < D) {
+#pragma unroll
+    for (int s = 0; s < kPreload; ++s) pre[s] = s < nsplit ? c.part_acc[(pbase + s) * D + d] : 0.f;
+  }
+  if (tid < 32) {
+    float M, L;
+    warp_row_stats(c.part_m + pbase, c.part_l + pbase, nsplit, M, L);
+    for (int s = tid; s < nsplit; s += 32) w_s[s] = split_weight(c.part_m[pbase + s], M);
+    if (tid == 0) sh_L = L;
+  }
+  __syncthreads();
+  if (d >= D) return;
+  if (tid < 32) {
+#pragma unroll
+    for (int s = 0; s < kPreload; ++s) pre[s] = s < nsplit ? c.part_acc[(pbase + s) * D + d] : 0.f;
+  }
+  float a = 0.f;
+#pragma unroll
+  for (int s = 0; s < kPreload; ++s)
+    if (s < nsplit) a += w_s[s] * pre[s];
+  for (int s = kPreload; s < nsplit; ++s) a += w_s[s] * c.part_acc[(pbase + s) * D + d];
+  store_any(c.out, (long long)row * D + d, c.out_dtype, a / sh_L);
+}
+
+// Per-block mass of 32 blocks (lane <-> block j) of one batch row, or of every row in batch-mean
+// mode.  Each warp owns kHeadsPerWarp heads of a chunk for both phases -- their final (M, L), then
+// their mass: sum over the block's groups of sum(p) * 2^((m_group - M) log2 e) / L (zero for a row
+// with nothing valid, streaming_attention.py:317 defaults l_final to 1 there) -- so no CTA barrier
+// separates the phases; one barrier at the end sums the warps' heads.
 __device__ __forceinline__ void paged_mass_cta(const PagedMassParams& p, int bx, int by) {
   __shared__ float red[kFinishWarps][32];
-  __shared__ float mf_s[kMassHeadChunk];
-  __shared__ float lf_s[kMassHeadChunk];
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
   const int j = bx * 32 + lane;
@@ -362,30 +419,29 @@ __device__ __forceinline__ void paged_mass_cta(const PagedMassParams& p, int bx,
   const int gpb = p.tpb >> p.group_shift;
   float tot = 0.f;
   for (int b = b_first; b < b_last; ++b) {
-    if (p.active && p.active[b] == 0) continue;  // uniform across the CTA
+    if (p.active && p.active[b] == 0) continue;
     const RowGeom g = row_geom(p.geom, b);
     int tb, te, ns;
     geom_tiles(g, p.tile_shift, p.tiles_per_split, tb, te, ns);
     const long long row0 = (long long)b * p.num_q_heads;
     for (int r0 = 0; r0 < p.num_q_heads; r0 += kMassHeadChunk) {
-      const int r_end = min(p.num_q_heads, r0 + kMassHeadChunk);
-      // Phase 1: warp w finalizes heads r0 + w + k * kFinishWarps (k < kHeadsPerWarp); lanes walk the
-      // splits keeping an online (max, sum), shuffles merge the lanes.
+      float M[kHeadsPerWarp], L[kHeadsPerWarp];
+      bool live[kHeadsPerWarp];
       {
         float mx[kHeadsPerWarp], sm[kHeadsPerWarp];
 #pragma unroll
         for (int k = 0; k < kHeadsPerWarp; ++k) {
           mx[k] = neg_inf();
           sm[k] = 0.f;
+          live[k] = r0 + warp + k * kFinishWarps < p.num_q_heads;
         }
         for (int s0 = 0; s0 < ns; s0 += 32) {
           const int s = s0 + lane;
           float mv[kHeadsPerWarp], lv[kHeadsPerWarp];
 #pragma unroll
           for (int k = 0; k < kHeadsPerWarp; ++k) {
-            const int r = r0 + warp + k * kFinishWarps;
-            const bool ok = r < r_end && s < ns;
-            const long long pi = (row0 + r) * p.max_splits + s;
+            const bool ok = live[k] && s < ns;
+            const long long pi = (row0 + r0 + warp + k * kFinishWarps) * p.max_splits + s;
             mv[k] = ok ? p.part_m[pi] : neg_inf();
             lv[k] = ok ? p.part_l[pi] : 0.f;
           }
@@ -398,19 +454,10 @@ __device__ __forceinline__ void paged_mass_cta(const PagedMassParams& p, int bx,
         }
 #pragma unroll
         for (int k = 0; k < kHeadsPerWarp; ++k) {
-          const float M = warp_max(mx[k]);
-          const float L = warp_sum(sm[k] * split_weight(mx[k], M));
-          const int r = r0 + warp + k * kFinishWarps;
-          if (lane == 0 && r < r_end) {
-            mf_s[r - r0] = M;
-            lf_s[r - r0] = L;
-          }
+          M[k] = warp_max(mx[k]);
+          L[k] = warp_sum(sm[k] * split_weight(mx[k], M[k]));
         }
       }
-      __syncthreads();
-      // Phase 2: lane <-> block j, the warp's heads at once: mass = sum over the block's groups of
-      // sum(p) * 2^((m_group - M) log2 e) / L (zero for a row with nothing valid,
-      // streaming_attention.py:317 defaults l_final to 1 there).
       if (j < g.nb && j < p.max_blocks) {
         float acc[kHeadsPerWarp];
 #pragma unroll
@@ -421,27 +468,20 @@ __device__ __forceinline__ void paged_mass_cta(const PagedMassParams& p, int bx,
           if (tile < tb || tile >= te) continue;  // never loaded: outside the attended range
           float2 v[kHeadsPerWarp];
 #pragma unroll
-          for (int k = 0; k < kHeadsPerWarp; ++k) {
-            const int r = r0 + warp + k * kFinishWarps;
-            v[k] = r < r_end ? p.mass_part[(row0 + r) * p.gstride + gi] : make_float2(0.f, 0.f);
-          }
+          for (int k = 0; k < kHeadsPerWarp; ++k)
+            v[k] = live[k] ? p.mass_part[(row0 + r0 + warp + k * kFinishWarps) * p.gstride + gi] : make_float2(0.f, 0.f);
 #pragma unroll
-          for (int k = 0; k < kHeadsPerWarp; ++k) {
-            const int r = r0 + warp + k * kFinishWarps;
-            if (v[k].x != 0.f) acc[k] += v[k].x * exp2f((v[k].y - mf_s[min(r, r_end - 1) - r0]) * kLog2e);
-          }
+          for (int k = 0; k < kHeadsPerWarp; ++k)
+            if (v[k].x != 0.f) acc[k] += v[k].x * exp2f((v[k].y - M[k]) * kLog2e);
         }
 #pragma unroll
         for (int k = 0; k < kHeadsPerWarp; ++k) {
-          const int r = r0 + warp + k * kFinishWarps;
-          if (r >= r_end) continue;
-          const float lf = lf_s[r - r0];
-          const float v = lf > 0.f ? acc[k] / lf : 0.f;
-          if (p.block_mass) p.block_mass[(row0 + r) * p.max_blocks + j] = v;
+          if (!live[k]) continue;
+          const float v = L[k] > 0.f ? acc[k] / L[k] : 0.f;
+          if (p.block_mass) p.block_mass[(row0 + r0 + warp + k * kFinishWarps) * p.max_blocks + j] = v;
           tot += v;
         }
       }
-      __syncthreads();
     }
   }
   red[warp][lane] = tot;
@@ -469,7 +509,7 @@ __global__ void __launch_bounds__(kFinishThreads) paged_finish_kernel(const Comb
   pdl_launch_dependents();
   const int cta = blockIdx.x;
   if (cta < rows) {
-    combine_row(c, cta);
+    paged_combine_row(c, cta);
   } else {
     const int m = cta - rows;
     paged_mass_cta(mp, m % mass_x, m / mass_x);

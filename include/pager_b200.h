@@ -87,7 +87,10 @@ size_t pager_attn_chunk_scratch_bytes(int op, int batch, int num_q_heads, int nu
                                       int head_dim, int kv_dtype, int tokens_per_block);
 
 /* ---- streaming_attention_step (pager_hf/streaming_attention.py:452-513):
- *      one-pass fold of a chunk into (m, l, acc), in place. */
+ *      fold a chunk into (m, l, acc), in place.  With fp16/bf16 KV, p is rounded exactly as the
+ *      reference's one-pass kernel rounds it (64-token tiles from the chunk's start, its running max
+ *      starting at the incoming m, :143-181): a K pass to scores, a scan seeded with m, a V pass;
+ *      pager_attn_chunk_scratch_bytes covers their scratch. */
 int pager_attn_step(const void* q, int q_dtype, const void* k, const void* v, int kv_dtype, const int32_t* valid,
                     const int32_t* active, float* m, float* l, float* acc, int batch, int num_q_heads,
                     int num_kv_heads, int tokens, int head_dim, float scale, float softcap, int backend,
@@ -211,10 +214,11 @@ int pager_paged_decode_attention_staged(const void* q, int q_dtype, const void* 
  *                              chunk: chunks of ref_group_tokens tokens (<= 0: one chunk) of a
  *                              numbering in which row b's token j sits at ref_shift[b] + j (NULL:
  *                              j), then the tail chunk from row-local token ref_tail_start[b]
- *                              (NULL: num_blocks[b] * tokens_per_block).  tokens_per_block >= 16.
+ *                              (NULL: num_blocks[b] * tokens_per_block).
  *        PAGER_ROUND_FINAL     the reference's two-pass path: m = the row's final max.
- *      fp16/bf16 KV at head_dim 64/128/256 (tensor-core kernels); fp32 KV rounds p to fp32, a
- *      no-op, so every mode runs the one pass there.  Other arguments as
+ *      fp16/bf16 KV, every head_dim (the tensor-core kernels need tokens_per_block >= 16 for
+ *      PAGER_ROUND_RUNNING); fp32 KV rounds p to fp32, a no-op, so every mode runs the one pass
+ *      there.  Other arguments as
  *      pager_paged_decode_attention_staged; scratch per pager_paged_decode_scratch_bytes_rounded. */
 enum { PAGER_ROUND_ONE_PASS = 0, PAGER_ROUND_RUNNING = 1, PAGER_ROUND_FINAL = 2 };
 size_t pager_paged_decode_scratch_bytes_rounded(int batch, int num_q_heads, int num_kv_heads, int head_dim,

@@ -1254,13 +1254,12 @@ struct ChunkExactLayout {
   size_t bytes;
 };
 
-bool chunk_exact(const ChunkArgs& a) {
-  return a.op == 0 && a.kv_dtype != PAGER_DTYPE_F32 && backend_for(a.backend, a.kv_dtype, a.head_dim) == BACKEND_MMA;
-}
+bool chunk_exact(const ChunkArgs& a) { return a.op == 0 && a.kv_dtype != PAGER_DTYPE_F32; }
 
 int chunk_exact_layout(const ChunkArgs& a, char* base, ChunkExactLayout* L) {
-  if (!lookup_split_kernel(a.kv_dtype, a.head_dim, MODE_SCORES, BACKEND_MMA, &L->ks) ||
-      !lookup_split_kernel(a.kv_dtype, a.head_dim, MODE_VALUES, BACKEND_MMA, &L->kv))
+  const int be = backend_for(a.backend, a.kv_dtype, a.head_dim);
+  if (!lookup_split_kernel(a.kv_dtype, a.head_dim, MODE_SCORES, be, &L->ks) ||
+      !lookup_split_kernel(a.kv_dtype, a.head_dim, MODE_VALUES, be, &L->kv))
     return fail(PAGER_ERR_UNSUPPORTED, "no exact-rounding kernels for dtype %d head_dim %d", a.kv_dtype, a.head_dim);
   if (L->ks.tile != L->kv.tile) return fail(PAGER_ERR_CUDA, "scores and values passes disagree on the tile");
   DevInfo* di;
@@ -1476,12 +1475,8 @@ int run_paged(const PagedArgs& a) {
     return fail(PAGER_ERR_INVALID, "unknown rounding mode %d", a.rounding);
   const bool exact = exact_rounding(a.rounding, a.kv_dtype);
   if (exact) {
-    if (backend_for(a.backend, a.kv_dtype, a.head_dim) != PAGER_BACKEND_MMA)
-      return fail(PAGER_ERR_UNSUPPORTED,
-                  "reference rounding runs on the tensor-core kernels (fp16/bf16 KV, head_dim 64, 128 or 256); got "
-                  "dtype %d head_dim %d backend %d",
-                  a.kv_dtype, a.head_dim, a.backend);
-    if (a.rounding == PAGER_ROUND_RUNNING && a.tokens_per_block < 16)
+    if (a.rounding == PAGER_ROUND_RUNNING && a.tokens_per_block < 16 &&
+        backend_for(a.backend, a.kv_dtype, a.head_dim) == PAGER_BACKEND_MMA)
       return fail(PAGER_ERR_UNSUPPORTED, "running-max reference rounding needs tokens_per_block >= 16, got %d",
                   a.tokens_per_block);
   }
@@ -1700,11 +1695,14 @@ size_t pager_paged_decode_scratch_bytes_rounded(int batch, int num_q_heads, int 
                                             0, max_row_tokens);
   if (check_geometry(batch, num_q_heads, num_kv_heads, head_dim, kv_dtype, kv_dtype)) return 0;
   if (batch <= 0 || max_row_tokens <= 0 || !is_pow2(tokens_per_block) || tokens_per_block < 8) return 0;
-  PagedLayout lay;
-  if (paged_layout(batch, num_q_heads, num_kv_heads, head_dim, kv_dtype, tokens_per_block, max_row_tokens,
-                   PAGER_BACKEND_MMA, rounding, nullptr, &lay))
-    return 0;
-  return lay.bytes;
+  size_t need = 0;  // the larger of the automatic backend's plan and the CUDA-core one's
+  for (int be : {PAGER_BACKEND_AUTO, PAGER_BACKEND_FMA}) {
+    PagedLayout lay;
+    if (!paged_layout(batch, num_q_heads, num_kv_heads, head_dim, kv_dtype, tokens_per_block, max_row_tokens, be,
+                      rounding, nullptr, &lay))
+      need = lay.bytes > need ? lay.bytes : need;
+  }
+  return need;
 }
 
 int pager_paged_decode_attention_rounded(const void* q, int q_dtype, const void* dev_pool, int dev_slots,

@@ -1196,6 +1196,33 @@ __device__ void run_consumer_fma(const SplitParams& p, const TableCache& tc, uin
         sc[u][r] = (t < TILE && bit_of(vlo, vhi, t)) ? x : neg_inf();
       }
     }
+    if constexpr (MODE == MODE_SCORES) {
+      // the masked scores of the tile (lane <-> token), and the max of each group_tokens group
+      float* const srow = p.scores + (long long)(b * num_q_heads + qh0) * p.s_stride + t0;
+#pragma unroll
+      for (int u = 0; u < TPL; ++u) {
+        const int t = lane + 32 * u;
+        if (t < TILE) {
+#pragma unroll
+          for (int r = 0; r < kMaxRep; ++r)
+            if (r < n_rep) srow[(long long)r * p.s_stride + t] = sc[u][r];
+        }
+      }
+      for (int gi = 0; gi < TILE / G; ++gi) {
+        for (int r = 0; r < n_rep; ++r) {
+          float v = neg_inf();
+#pragma unroll
+          for (int u = 0; u < TPL; ++u) {
+            const int t = lane + 32 * u;
+            if (t < TILE && t / G == gi) v = fmaxf(v, sc[u][r]);
+          }
+          v = warp_max(v);
+          if (lane == 0) p.gmax[((long long)b * num_q_heads + qh0 + r) * mass_gstride + (t0 >> log2_group) + gi] = v;
+        }
+      }
+      release_stage(&empty[s], (swm & 0xffu) != 0);
+      continue;
+    }
     float mref[kMaxRep];
 #pragma unroll
     for (int r = 0; r < kMaxRep; ++r) {
@@ -1297,6 +1324,7 @@ __device__ void run_consumer_fma(const SplitParams& p, const TableCache& tc, uin
     }
     release_stage(&empty[s], wrote);
   }
+  if constexpr (MODE == MODE_SCORES) return;
 
 #pragma unroll
   for (int r = 0; r < kMaxRep; ++r) l_r[r] = warp_sum(l_r[r]);
@@ -1323,6 +1351,165 @@ __device__ void run_consumer_fma(const SplitParams& p, const TableCache& tc, uin
   }
   named_bar_sync(1, Cfg::NCW * 32);
   merge_and_store<D, MODE, Cfg::NCW>(p, mw, b, h, split);
+}
+
+
+// ------------------------------------------------------------------ CUDA-core consumer, VALUES pass
+// As the tensor-core VALUES pass, lane <-> token: p = exp(s - M) against its group's reference max,
+// rounded to the KV dtype; the warp keeps O and l relative to the tile's last (largest) M, so a
+// token of an earlier group of the tile enters P.V as its rounded p times exp(M_group - M), the
+// scale applied after the rounding as the reference's later rescale of its accumulator is.
+template <typename T, int D>
+__device__ void run_consumer_fma_values(const SplitParams& p, const TableCache& tc, uint8_t* stages, uint8_t* aux,
+                                        uint64_t* full, uint64_t* empty, volatile int* infos, int b, int h,
+                                        int tile0, int ntiles, const RowGeom& g, volatile int* abort_flag,
+                                        int split, float* p_sm_all) {
+  using Cfg = TileCfg<T, D, MODE_VALUES, BACKEND_FMA>;
+  constexpr int TILE = Cfg::TILE;
+  constexpr int TPL = TILE > 32 ? TILE / 32 : 1;
+  constexpr int DPL = D >= 32 ? D / 32 : 1;
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const int n_rep = p.n_rep;
+  const int qh0 = h * n_rep;
+  float* p_sm = p_sm_all + warp * TILE * kMaxRep;
+  const int seg_rows = p.source == SRC_CONTIG ? TILE : min(TILE, p.tpb);
+  const uint64_t wait_limit = p.wait_limit_ns;
+  int* const status = p.status;
+  float2* const mass_part = p.mass_part;
+  const int num_q_heads = p.num_q_heads;
+  const int mass_gstride = p.mass_gstride;
+  const int log2_group = p.log2_group;
+  const int G = p.group_tokens;
+  const int ngroups = TILE / G;
+
+  float acc[kMaxRep][DPL];
+#pragma unroll
+  for (int r = 0; r < kMaxRep; ++r)
+#pragma unroll
+    for (int k = 0; k < DPL; ++k) acc[r][k] = 0.f;
+  float m_r[kMaxRep], l_r[kMaxRep];
+#pragma unroll
+  for (int r = 0; r < kMaxRep; ++r) {
+    m_r[r] = neg_inf();
+    l_r[r] = 0.f;
+  }
+
+  for (int i = warp; i < ntiles; i += Cfg::NCW) {
+    const int s = i % Cfg::STAGES;
+    if (*abort_flag) break;
+    uint32_t swm;
+    if (!consumer_wait(wait_limit, status, &full[s], &empty[s], &infos[s], i / Cfg::STAGES, abort_flag, &swm)) break;
+    const int t0 = (tile0 + i) * TILE;
+    uint8_t* vbuf = stages + s * Cfg::STAGE_BYTES;
+    const float* s_sm = reinterpret_cast<const float*>(aux + s * Cfg::AUX_BYTES);  // [n_rep][TILE]
+    const float* m_sm = s_sm + Cfg::AUX_S_BYTES / 4;                               // [n_rep][kRefSlots]
+    if (swm & 0xffu) copy_sw_segments<Cfg, false, true>(p, tc, g, b, h, t0, swm & 0xffu, vbuf, vbuf);
+    uint32_t vlo, vhi;
+    tile_bits_fast<TILE>(p.valid, p.valid_stride, b, t0, g, swm >> 8, seg_rows, vlo, vhi);
+    bool wrote = (swm & 0xffu) != 0;
+    wrote |= zero_masked_rows<Cfg>(vbuf, vlo, vhi);
+#pragma unroll
+    for (int r = 0; r < kMaxRep; ++r) {
+      if (r >= n_rep) continue;
+      const float mt = m_sm[r * kRefSlots + ngroups - 1];
+      if (mt > m_r[r]) {
+        const float alpha = m_r[r] == neg_inf() ? 0.f : fast_exp2((m_r[r] - mt) * kLog2e);
+        l_r[r] *= alpha;
+#pragma unroll
+        for (int k = 0; k < DPL; ++k) acc[r][k] *= alpha;
+        m_r[r] = mt;
+      }
+    }
+    float pe[TPL][kMaxRep];  // unrounded p against the token's group max
+#pragma unroll
+    for (int u = 0; u < TPL; ++u) {
+      const int t = lane + 32 * u;
+#pragma unroll
+      for (int r = 0; r < kMaxRep; ++r) {
+        float e = 0.f, pr = 0.f;
+        if (t < TILE && r < n_rep) {
+          const float mg = m_sm[r * kRefSlots + t / G];
+          if (mg != neg_inf()) {
+            e = fast_exp2(fmaf(s_sm[r * TILE + t], kLog2e, -mg * kLog2e));
+            const float w = fast_exp2((mg - m_r[r]) * kLog2e);
+            pr = to_f32(T(e)) * w;
+            l_r[r] += e * w;
+          }
+        }
+        pe[u][r] = e;
+        if (t < TILE) p_sm[t * kMaxRep + r] = pr;
+      }
+    }
+    for (int gi = 0; gi < ngroups; ++gi) {
+      for (int r = 0; r < n_rep; ++r) {
+        float v = 0.f;
+#pragma unroll
+        for (int u = 0; u < TPL; ++u) {
+          const int t = lane + 32 * u;
+          if (t < TILE && t / G == gi) v += pe[u][r];
+        }
+        v = warp_sum(v);
+        if (lane == 0)
+          mass_part[((long long)b * num_q_heads + qh0 + r) * mass_gstride + (t0 >> log2_group) + gi] =
+              make_float2(v, m_sm[r * kRefSlots + gi]);
+      }
+    }
+    __syncwarp();
+    const uint32_t vaddr = smem_u32(vbuf);
+    for (int t = 0; t < TILE; ++t) {
+      if (!bit_of(vlo, vhi, t)) continue;
+      float prr[kMaxRep];
+#pragma unroll
+      for (int r4 = 0; r4 < kMaxRep; r4 += 4) {
+        const float4 v4 = *reinterpret_cast<const float4*>(p_sm + t * kMaxRep + r4);
+        prr[r4] = v4.x;
+        prr[r4 + 1] = v4.y;
+        prr[r4 + 2] = v4.z;
+        prr[r4 + 3] = v4.w;
+      }
+#pragma unroll
+      for (int k = 0; k < DPL; ++k) {
+        const int d = lane + 32 * k;
+        if (d < D) {
+          const int byte = d * (int)sizeof(T);
+          const uint32_t a = chunk_addr<Cfg>(vaddr, t, byte >> 4) + (byte & 15);
+          unsigned short raw;
+          asm volatile("ld.shared.u16 %0, [%1];" : "=h"(raw) : "r"(a));
+          const float vv = std::is_same<T, __half>::value ? __half2float(__ushort_as_half(raw))
+                                                          : __uint_as_float(((uint32_t)raw) << 16);
+#pragma unroll
+          for (int r = 0; r < kMaxRep; ++r) acc[r][k] = fmaf(prr[r], vv, acc[r][k]);
+        }
+      }
+    }
+    __syncwarp();  // p_sm is rewritten by this warp's next tile
+    release_stage(&empty[s], wrote);
+  }
+
+#pragma unroll
+  for (int r = 0; r < kMaxRep; ++r) l_r[r] = warp_sum(l_r[r]);
+  named_bar_sync(1, Cfg::NCW * 32);
+  float* mw = reinterpret_cast<float*>(stages);
+  float* m_w = mw;
+  float* l_w = mw + Cfg::NCW * kMaxRep;
+  float* acc_w = mw + 2 * Cfg::NCW * kMaxRep;
+  if (lane == 0) {
+#pragma unroll
+    for (int r = 0; r < kMaxRep; ++r) {
+      m_w[warp * kMaxRep + r] = m_r[r];
+      l_w[warp * kMaxRep + r] = l_r[r];
+    }
+  }
+#pragma unroll
+  for (int r = 0; r < kMaxRep; ++r)
+#pragma unroll
+    for (int k = 0; k < DPL; ++k) {
+      const int d = lane + 32 * k;
+      if (d < D) acc_w[(warp * kMaxRep + r) * D + d] = acc[r][k];
+    }
+  named_bar_sync(1, Cfg::NCW * 32);
+  merge_and_store<D, MODE_ONLINE, Cfg::NCW>(p, mw, b, h, split);
 }
 
 // ------------------------------------------------------------------ kernel
@@ -1434,6 +1621,9 @@ __global__ void __launch_bounds__(TileCfg<T, D, MODE, BACKEND>::THREADS, TileCfg
     } else if constexpr (BACKEND == BACKEND_MMA) {
       run_consumer_mma<T, D, MODE>(p, tc, stages, full, empty, infos, b, h, tile0, ntiles, g, abort_flag, split,
                                    q_smem_t);
+    } else if constexpr (MODE == MODE_VALUES) {
+      run_consumer_fma_values<T, D>(p, tc, stages, aux, full, empty, infos, b, h, tile0, ntiles, g, abort_flag, split,
+                                    p_sm);
     } else {
       run_consumer_fma<T, D, MODE>(p, tc, stages, full, empty, infos, b, h, tile0, ntiles, g, abort_flag, split,
                                    q_sm, p_sm);

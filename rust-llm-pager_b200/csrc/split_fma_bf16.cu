@@ -4,12 +4,12 @@
 namespace pager {
 bool lookup_split_fma_bf16(int head_dim, int mode, SplitKernelInfo* out) {
   switch (head_dim) {
-    PAGER_MODE_CASES(__nv_bfloat16, 8, BACKEND_FMA)
-    PAGER_MODE_CASES(__nv_bfloat16, 16, BACKEND_FMA)
-    PAGER_MODE_CASES(__nv_bfloat16, 32, BACKEND_FMA)
-    PAGER_MODE_CASES(__nv_bfloat16, 64, BACKEND_FMA)
-    PAGER_MODE_CASES(__nv_bfloat16, 128, BACKEND_FMA)
-    PAGER_MODE_CASES(__nv_bfloat16, 256, BACKEND_FMA)
+    PAGER_FMA16_MODE_CASES(__nv_bfloat16, 8)
+    PAGER_FMA16_MODE_CASES(__nv_bfloat16, 16)
+    PAGER_FMA16_MODE_CASES(__nv_bfloat16, 32)
+    PAGER_FMA16_MODE_CASES(__nv_bfloat16, 64)
+    PAGER_FMA16_MODE_CASES(__nv_bfloat16, 128)
+    PAGER_FMA16_MODE_CASES(__nv_bfloat16, 256)
     default: return false;
   }
 }

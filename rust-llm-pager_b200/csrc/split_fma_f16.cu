@@ -4,12 +4,12 @@
 namespace pager {
 bool lookup_split_fma_f16(int head_dim, int mode, SplitKernelInfo* out) {
   switch (head_dim) {
-    PAGER_MODE_CASES(__half, 8, BACKEND_FMA)
-    PAGER_MODE_CASES(__half, 16, BACKEND_FMA)
-    PAGER_MODE_CASES(__half, 32, BACKEND_FMA)
-    PAGER_MODE_CASES(__half, 64, BACKEND_FMA)
-    PAGER_MODE_CASES(__half, 128, BACKEND_FMA)
-    PAGER_MODE_CASES(__half, 256, BACKEND_FMA)
+    PAGER_FMA16_MODE_CASES(__half, 8)
+    PAGER_FMA16_MODE_CASES(__half, 16)
+    PAGER_FMA16_MODE_CASES(__half, 32)
+    PAGER_FMA16_MODE_CASES(__half, 64)
+    PAGER_FMA16_MODE_CASES(__half, 128)
+    PAGER_FMA16_MODE_CASES(__half, 256)
     default: return false;
   }
 }

@@ -23,3 +23,16 @@
       case pager::MODE_VALUES: *out = pager::split_kernel_info<T, D, pager::MODE_VALUES, pager::BACKEND_MMA>(); return true; \
       default: return false;                                                         \
     }
+
+// Every mode of the CUDA-core kernels for 16-bit KV (fp32 KV rounds p to fp32, a no-op, so its
+// one-pass kernel already is the reference's arithmetic and it has no exact-rounding passes).
+#define PAGER_FMA16_MODE_CASES(T, D)                                                 \
+  case D:                                                                            \
+    switch (mode) {                                                                  \
+      case pager::MODE_ONLINE: *out = pager::split_kernel_info<T, D, pager::MODE_ONLINE, pager::BACKEND_FMA>(); return true; \
+      case pager::MODE_STATS: *out = pager::split_kernel_info<T, D, pager::MODE_STATS, pager::BACKEND_FMA>(); return true;   \
+      case pager::MODE_FIXED: *out = pager::split_kernel_info<T, D, pager::MODE_FIXED, pager::BACKEND_FMA>(); return true;   \
+      case pager::MODE_SCORES: *out = pager::split_kernel_info<T, D, pager::MODE_SCORES, pager::BACKEND_FMA>(); return true; \
+      case pager::MODE_VALUES: *out = pager::split_kernel_info<T, D, pager::MODE_VALUES, pager::BACKEND_FMA>(); return true; \
+      default: return false;                                                         \
+    }

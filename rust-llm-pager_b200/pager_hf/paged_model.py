@@ -148,23 +148,25 @@ def run_decoder_step(model, arch: dict, groups: list[AttentionGroup], input_ids,
     return logits
 
 
-_EXACT_HEAD_DIMS = frozenset({64, 128, 256})  # head_dims of the tensor-core kernels that round p exactly
+_TENSOR_CORE_HEAD_DIMS = frozenset({64, 128, 256})  # head_dims the tensor-core kernels serve
 
 
 def step_rounding(mode: str, needs_attention: bool, dtype, head_dim: int, tokens_per_block: int) -> str:
     """The fused op's ``rounding`` for a decode step.  ``mode="reference"``: p is rounded as the
     reference rounds it -- against its running max per 64-token tile ("running") in the one-pass
     path it runs for policies without an attention signal (paged_model.py:1055-1072), against the
-    row's final max ("final") in the two-pass path of the heavy-hitter policies (:993-1039).  The
-    fp32 path rounds nothing either way, and head_dims below 64 (CUDA-core kernels) keep the one
-    pass; ``mode="one_pass"`` always does."""
+    row's final max ("final") in the two-pass path of the heavy-hitter policies (:993-1039).  fp32
+    rounds nothing either way, so it keeps the one pass, as ``mode="one_pass"`` always does; so does
+    the running rule on the tensor-core kernels with blocks shorter than 16 tokens."""
     if mode not in ("reference", "one_pass"):
         raise ValueError(f"attention_rounding must be 'reference' or 'one_pass', got {mode!r}")
-    if mode == "one_pass" or dtype == torch.float32 or head_dim not in _EXACT_HEAD_DIMS:
+    if mode == "one_pass" or dtype == torch.float32:
         return "one_pass"
     if needs_attention:
         return "final"
-    return "running" if tokens_per_block >= 16 else "one_pass"
+    if tokens_per_block < 16 and head_dim in _TENSOR_CORE_HEAD_DIMS:
+        return "one_pass"
+    return "running"
 
 
 def window_lo(pad: int, total: int, window) -> int:

@@ -103,6 +103,9 @@ CASES = [
     (13, 2, 32, 4, 64, 32, 1, [17, 6], [3, 30], torch.bfloat16, set(), [100, 0], [500, 150], 3),
     (14, 2, 8, 4, 256, 16, 2, [13, 3], [5, 9], torch.bfloat16, set(), [10, 0], None, 2),
     (15, 2, 32, 8, 128, 16, 1, [40, 1], [15, 2], torch.float16, {(0, 0), (0, 11)}, None, None, 64),
+    # CUDA-core kernels (head_dim below 64), 8-token blocks included
+    (16, 2, 8, 2, 32, 16, 1, [12, 3], [5, 9], torch.float16, set(), None, None, 4),
+    (17, 2, 4, 1, 8, 8, 1, [20, 5], [3, 8], torch.bfloat16, set(), [7, 0], None, 64),
 ]
 
 
@@ -185,7 +188,8 @@ def _chunks(seed, B, Hq, Hkv, D, dtype, sizes):
 
 
 @pytest.mark.parametrize("dtype,D,Hq,Hkv", [(torch.bfloat16, 128, 32, 8), (torch.float16, 64, 14, 2),
-                                            (torch.bfloat16, 256, 8, 4)])
+                                            (torch.bfloat16, 256, 8, 4), (torch.float16, 32, 8, 2),
+                                            (torch.bfloat16, 16, 4, 4)])
 def test_drop_in_step_rounds_like_the_reference_step_kernel(dtype, D, Hq, Hkv):
     """``streaming_attention_step`` folds chunks into a running state as the reference's one-pass
     kernel does (64-token tiles from each chunk's start, its running max starting at the incoming m),

@@ -103,7 +103,20 @@ CASES = {
     # cross-session batched decode (batched_decode.py): block counts 6, 2, 0; tail 4 (+1 new token)
     "batched_sessions_f16": dict(kind="batched", seed=13, Hq=14, Hkv=2, D=64, tpb=16, nbs=[6, 2, 0], tail=4,
                                  group_blocks=4, dtype="f16"),
+    # native bf16 (fixtures from the reference's Triton kernels on a B200, make_golden.py --gpu): the
+    # reference's own rounding of p to bf16 is in these vectors
+    "bf16_steps_gqa4_d128": dict(kind="steps", seed=41, B=2, Hq=32, Hkv=8, D=128, T=1100, group=512, dtype="bf16",
+                                 pad_prefix=[0, 130], gpu_only=True),
+    "bf16_two_pass_gqa8_d64": dict(kind="two_pass", seed=42, B=2, Hq=32, Hkv=4, D=64, tpb=64, nb=9, tail=17,
+                                   group_blocks=4, dtype="bf16", pad_prefix=[0, 77], gpu_only=True),
+    "bf16_batched_gqa4_d128": dict(kind="batched", seed=43, Hq=32, Hkv=8, D=128, tpb=16, nbs=[9, 3, 6], tail=5,
+                                   group_blocks=4, dtype="bf16", gpu_only=True),
 }
+
+# cases whose reference outputs also exist as fixtures from the reference's kernels on a GPU, in the
+# cases' native dtype (``<case>__gpu.npz``)
+GPU_CASES = ("gqa4_d128_bf16_as_f32", "pin_d32_bf16_as_f32", "bf16_steps_gqa4_d128", "bf16_two_pass_gqa8_d64",
+             "bf16_batched_gqa4_d128")
 
 
 def build_contiguous(case):

@@ -1282,7 +1282,12 @@ __device__ void run_consumer_fma(const SplitParams& p, const TableCache& tc, uin
         const int t = lane + 32 * u;
         if (t < TILE) {
 #pragma unroll
-          for (int r = 0; r < kMaxRep; ++r) p_sm[t * kMaxRep + r] = sc[u][r];
+          for (int r = 0; r < kMaxRep; ++r) {
+            // against the fixed (final) max, p enters P.V rounded to the KV dtype, as the
+            // reference's accumulate and fold kernels round it (streaming_attention.py:346-347,
+            // :427-428); l and the mass partials above took the unrounded p
+            p_sm[t * kMaxRep + r] = MODE == MODE_FIXED ? to_f32(T(sc[u][r])) : sc[u][r];
+          }
         }
       }
       wrote |= zero_masked_rows<Cfg>(vbuf, vlo, vhi);

@@ -91,6 +91,8 @@ class ShardStats:
     wall_s: float = 0.0
     step_s: float = 0.0
     kv_bytes: int = 0
+    host_bytes: int = 0  # of kv_bytes, those read from the pinned host tier
+    link_gbs: float = 0.0  # this rank's measured host->device bandwidth (the faster of copy and zero-copy)
     latencies: list = field(default_factory=list)
     waits: list = field(default_factory=list)
     peak_sessions: int = 0
@@ -184,7 +186,11 @@ class ShardRunner:
 
     # ------------------------------------------------------------------ the serving loop
     def run(self, requests: list[Request], rank: int = 0) -> ShardStats:
+        from .host_staging import link_bandwidth
+
         st = ShardStats(rank=rank, requests=len(requests))
+        bw = link_bandwidth(self.device)
+        st.link_gbs = max(bw["copy_gbs"], bw["zero_copy_gbs"])
         for r in requests:
             if not self.fits_ever(r):
                 raise ValueError(f"request {r.rid} ({r.prompt_tokens} tokens) can never fit this rank's pools")
@@ -207,6 +213,7 @@ class ShardRunner:
                 continue
             st.peak_sessions = max(st.peak_sessions, len(active))
             S = len(active)
+            host_tokens = sum(len(a.session.store.cpu_block_ids()) for a in active) * self.tpb
             ts = time.perf_counter()
             plan = BatchedDecodeAttention([a.session for a in active], self.g["hq"], rounding=self.rounding)
             for layer in range(self.g["layers"]):
@@ -228,6 +235,7 @@ class ShardRunner:
             st.tokens += S
             st.kv_bytes += sum(a.session.num_tokens for a in active) * self.token_bytes  # after finish():
             # num_tokens now counts this step's token too, i.e. what the step attended
+            st.host_bytes += host_tokens * self.token_bytes
             st.host_blocks_peak = max(st.host_blocks_peak, self.pools.host_groups.used)
             done_at = time.perf_counter() - t0
             keep = []
@@ -248,7 +256,12 @@ class ShardRunner:
         self.pools.close()
 
 
-def summarize(stats: list[ShardStats]) -> dict:
+def summarize(stats: list[ShardStats], hbm_gbs: float = 6553.3) -> dict:
+    """The sweep's figures over all ranks.  ``roofline``: each rank's decode steps against the
+    combined floor of its attended bytes -- the HBM-resident ones at ``hbm_gbs`` (a measured B200
+    copy bandwidth by default) plus the host-resident ones at the rank's measured link bandwidth --
+    as the floor's share of the time spent in decode steps (``frac_steps``) and of the rank's wall
+    time, admission and prefill included (``frac_wall``); the slowest rank's figures."""
     wall = max(s.wall_s for s in stats) if stats else 0.0
     lat = sorted(x for s in stats for x in s.latencies)
     tokens = sum(s.tokens for s in stats)
@@ -259,9 +272,27 @@ def summarize(stats: list[ShardStats]) -> dict:
             "latency_s": {"mean": sum(lat) / len(lat) if lat else None, "p50": pct(0.5), "p90": pct(0.9)},
             "mean_step_ms": 1000 * sum(s.step_s for s in stats) / max(1, sum(s.steps for s in stats)),
             "errors": [e for s in stats for e in s.errors],
+            "roofline": _roofline(stats, hbm_gbs),
             "per_rank": [{"rank": s.rank, "requests": s.requests, "tokens": s.tokens, "wall_s": s.wall_s,
-                          "peak_sessions": s.peak_sessions, "host_blocks_peak": s.host_blocks_peak}
+                          "step_s": s.step_s, "kv_gb": s.kv_bytes / 1e9, "host_gb": s.host_bytes / 1e9,
+                          "link_gbs": s.link_gbs, "peak_sessions": s.peak_sessions,
+                          "host_blocks_peak": s.host_blocks_peak}
                          for s in stats]}
+
+
+def _roofline(stats: list[ShardStats], hbm_gbs: float) -> dict | None:
+    rows = []
+    for s in stats:
+        if not s.step_s or not s.link_gbs:
+            continue
+        t_hbm = (s.kv_bytes - s.host_bytes) / (hbm_gbs * 1e9)
+        t_host = s.host_bytes / (s.link_gbs * 1e9)
+        floor = t_hbm + t_host
+        rows.append({"rank": s.rank, "wall_s": s.wall_s, "floor_s": floor, "hbm_s": t_hbm, "host_link_s": t_host, "frac_steps": floor / s.step_s,
+                     "frac_wall": floor / s.wall_s, "bound": "host link" if t_host > t_hbm else "hbm"})
+    if not rows:
+        return None
+    return {"hbm_gbs": hbm_gbs, **max(rows, key=lambda r: r["wall_s"])}
 
 
 def main(argv=None):
@@ -278,6 +309,7 @@ def main(argv=None):
     ap.add_argument("--tokens-per-block", type=int, default=64)
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--rounding", default="reference", choices=["reference", "one_pass"])
+    ap.add_argument("--hbm-gbs", type=float, default=6553.3, help="HBM bandwidth of the roofline (GB/s)")
     a = ap.parse_args(argv)
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -306,7 +338,7 @@ def main(argv=None):
         stats = gathered
         dist.destroy_process_group()
     if rank == 0:
-        out = summarize(stats)
+        out = summarize(stats, a.hbm_gbs)
         out["config"] = vars(a) | {"world": world}
         print(json.dumps(out), flush=True)
 

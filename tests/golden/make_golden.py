@@ -54,9 +54,15 @@ DEV = "cuda" if GPU else "cpu"
 
 
 def _load_reference(ref_root):
+    import importlib.util
+
+    # the kernel module alone: the package's __init__ also imports the compiled pager core
+    spec = importlib.util.spec_from_file_location("reference_streaming_attention",
+                                                  os.path.join(ref_root, "pager_hf", "streaming_attention.py"))
+    sa = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(sa)
     sys.path.insert(0, ref_root)
     sys.path.insert(0, os.path.join(ref_root, "tests"))
-    from pager_hf import streaming_attention as sa  # noqa: E402
 
     try:
         import test_streaming_attention as ref_tests  # noqa: E402  (a checkout has the tests; an install may not)

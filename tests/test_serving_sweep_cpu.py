@@ -41,3 +41,18 @@ def test_summary_aggregates_over_ranks():
     assert out["decode_tokens_per_s"] == 4.0 and out["kv_gbs"] == 2.0
     assert out["latency_s"]["mean"] == 2.0 and out["latency_s"]["p50"] == 2.0
     assert abs(out["mean_step_ms"] - 1000 * 3.0 / 11) < 1e-9
+
+
+def test_roofline_is_the_slowest_ranks_combined_floor():
+    # rank 0: 3 GB from HBM at 6000 GB/s (0.5 ms) + 1 GB from the host at 50 GB/s (20 ms) in 25 ms of steps
+    s0 = ShardStats(rank=0, requests=1, tokens=4, steps=4, wall_s=0.05, step_s=0.025, kv_bytes=4 * 10**9,
+                    host_bytes=10**9, link_gbs=50.0)
+    # rank 1 (the faster one): HBM only, 6 GB (1 ms) in 4 ms of steps
+    s1 = ShardStats(rank=1, requests=1, tokens=4, steps=4, wall_s=0.004, step_s=0.004, kv_bytes=6 * 10**9,
+                    host_bytes=0, link_gbs=50.0)
+    r = summarize([s0, s1], hbm_gbs=6000.0)["roofline"]
+    assert r["bound"] == "host link"
+    assert abs(r["floor_s"] - 0.0205) < 1e-12
+    assert abs(r["frac_steps"] - 0.0205 / 0.025) < 1e-9 and abs(r["frac_wall"] - 0.0205 / 0.05) < 1e-9
+    assert summarize([s1], hbm_gbs=6000.0)["roofline"]["bound"] == "hbm"
+    assert summarize([ShardStats()])["roofline"] is None

@@ -398,6 +398,7 @@ __device__ void run_producer(const SplitParams& p, const TableCache& tc, const C
   const int nseg = Cfg::TILE / br;
   const int block_tokens = g.nb * k.tpb;
   const uint32_t seg_bytes = (uint32_t)br * Cfg::ROW_BYTES * ((kNeedK ? 1u : 0u) + (kNeedV ? 1u : 0u));
+  const uint64_t once = l2_policy_evict_first();  // every tile is read once per layer
   int last = -1;
   for (int i = producer; i < ntiles; i += Cfg::NPW) {
     const int s = i % Cfg::STAGES;
@@ -415,16 +416,18 @@ __device__ void run_producer(const SplitParams& p, const TableCache& tc, const C
     if (Cfg::VONLY) {
       uint8_t* a = aux + s * Cfg::AUX_BYTES;
       mbar_expect_tx(&full[s], aux_tx);
-      tma_load_2d(a, maps, t0, aux_row0, &full[s]);
-      tma_load_2d(a + Cfg::AUX_S_BYTES, mapm, (tile0 + i) * kRefSlots, aux_row0, &full[s]);
+      tma_load_2d_hint(a, maps, t0, aux_row0, &full[s], once);
+      tma_load_2d_hint(a + Cfg::AUX_S_BYTES, mapm, (tile0 + i) * kRefSlots, aux_row0, &full[s], once);
     }
     if (k.source == SRC_CONTIG) {
       present = 1u;  // one segment: the whole tile
       mbar_expect_tx(&full[s], (uint32_t)Cfg::STAGE_BYTES);
 #pragma unroll
       for (int pn = 0; pn < Cfg::NPANEL; ++pn) {
-        if (kNeedK) tma_load_3d(kbuf + pn * Cfg::PANEL_TILE_BYTES, mapk, pn * Cfg::PANEL_ELTS, t0, zc, &full[s]);
-        if (kNeedV) tma_load_3d(vbuf + pn * Cfg::PANEL_TILE_BYTES, mapv, pn * Cfg::PANEL_ELTS, t0, zc, &full[s]);
+        if (kNeedK)
+          tma_load_3d_hint(kbuf + pn * Cfg::PANEL_TILE_BYTES, mapk, pn * Cfg::PANEL_ELTS, t0, zc, &full[s], once);
+        if (kNeedV)
+          tma_load_3d_hint(vbuf + pn * Cfg::PANEL_TILE_BYTES, mapv, pn * Cfg::PANEL_ELTS, t0, zc, &full[s], once);
       }
     } else {
       for (int sg = 0; sg < nseg; ++sg) {
@@ -455,8 +458,8 @@ __device__ void run_producer(const SplitParams& p, const TableCache& tc, const C
 #pragma unroll
         for (int pn = 0; pn < Cfg::NPANEL; ++pn) {
           const int off = pn * Cfg::PANEL_TILE_BYTES + sg * br * Cfg::PANEL_BYTES;
-          if (kNeedK) tma_load_3d(kbuf + off, map, pn * Cfg::PANEL_ELTS, y, zk, &full[s]);
-          if (kNeedV) tma_load_3d(vbuf + off, map, pn * Cfg::PANEL_ELTS, y, zk + k.hkv, &full[s]);
+          if (kNeedK) tma_load_3d_hint(kbuf + off, map, pn * Cfg::PANEL_ELTS, y, zk, &full[s], once);
+          if (kNeedV) tma_load_3d_hint(vbuf + off, map, pn * Cfg::PANEL_ELTS, y, zk + k.hkv, &full[s], once);
         }
       }
     }
@@ -738,14 +741,14 @@ __device__ void run_consumer_mma(const SplitParams& p, const TableCache& tc, uin
     if constexpr (MODE == MODE_SCORES) {
       // the masked scores of the tile, and the max of each group_tokens group, per query head
       float* const srow = p.scores + (long long)(b * num_q_heads + qh0) * p.s_stride + t0 + 2 * tq;
+      const uint64_t keep = l2_policy_evict_last();  // read back by the values pass of this layer
 #pragma unroll
       for (int rr = 0; rr < 2; ++rr) {
         const int row = gr + 8 * rr;
         if (row < n_rep) {
 #pragma unroll
           for (int j = 0; j < NT_S; ++j)
-            *reinterpret_cast<float2*>(srow + (long long)row * p.s_stride + 8 * j) =
-                make_float2(sc[j][2 * rr], sc[j][2 * rr + 1]);
+            st_global_f2_hint(srow + (long long)row * p.s_stride + 8 * j, sc[j][2 * rr], sc[j][2 * rr + 1], keep);
         }
       }
       const int ntg = G >> 3;  // S n-tiles per group
@@ -1199,13 +1202,14 @@ __device__ void run_consumer_fma(const SplitParams& p, const TableCache& tc, uin
     if constexpr (MODE == MODE_SCORES) {
       // the masked scores of the tile (lane <-> token), and the max of each group_tokens group
       float* const srow = p.scores + (long long)(b * num_q_heads + qh0) * p.s_stride + t0;
+      const uint64_t keep = l2_policy_evict_last();  // read back by the values pass of this layer
 #pragma unroll
       for (int u = 0; u < TPL; ++u) {
         const int t = lane + 32 * u;
         if (t < TILE) {
 #pragma unroll
           for (int r = 0; r < kMaxRep; ++r)
-            if (r < n_rep) srow[(long long)r * p.s_stride + t] = sc[u][r];
+            if (r < n_rep) st_global_f1_hint(srow + (long long)r * p.s_stride + t, sc[u][r], keep);
         }
       }
       for (int gi = 0; gi < TILE / G; ++gi) {

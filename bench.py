@@ -62,6 +62,10 @@ WORKLOADS = {
     # small HBM-only case for ncu captures (two requests, four layers: 1 GB of KV, 268 MB per launch > L2)
     "prof-hbm": dict(model="Llama-3-8B attention (L4 slice, Hq32, Hkv8, D128)", layers=4, hq=32, hkv=8, d=128,
                      dtype="bf16", tpb=64, batch=2, context=32768, hbm_budget_gb=40.0, window=None),
+    # one layer of hbm-32k for ncu captures: the same launch (8 rows x 32k, 256 CTAs of 128 tiles each),
+    # 1.07 GB of KV on the device
+    "prof-b8": dict(model="Llama-3-8B attention (L1 slice, Hq32, Hkv8, D128)", layers=1, hq=32, hkv=8, d=128,
+                    dtype="bf16", tpb=64, batch=8, context=32768, hbm_budget_gb=40.0, window=None),
     # small tiered case for ncu captures: two requests, four layers, 20% of each row's blocks in HBM, the
     # rest in the host pool (staged per layer by the copy engines when the link favours it)
     "prof-tiered": dict(model="Llama-3-8B attention (L4 slice, Hq32, Hkv8, D128)", layers=4, hq=32, hkv=8, d=128,

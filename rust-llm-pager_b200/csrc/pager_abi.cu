@@ -615,6 +615,11 @@ int backend_for(int requested, int kv_dtype, int head_dim) {
   return PAGER_BACKEND_FMA;
 }
 
+// The values pass of reference-exact rounding for a geometry: on the tensor-core kernels with at
+// most 4 query heads per KV head (Llama, Mistral), the variant whose 4-row score ring leaves room for
+// a sixth stage of V tiles in the same shared memory; otherwise the general one.
+int values_mode(int n_rep, int be) { return be == BACKEND_MMA && n_rep <= 4 ? MODE_VALUES_R4 : MODE_VALUES; }
+
 int check_geometry(int batch, int hq, int hkv, int head_dim, int kv_dtype, int q_dtype) {
   if (batch < 0 || hq <= 0 || hkv <= 0) return fail(PAGER_ERR_INVALID, "bad shape: batch=%d heads=%d kv_heads=%d", batch, hq, hkv);
   if (hq % hkv) return fail(PAGER_ERR_INVALID, "num_query_heads (%d) is not a multiple of num_kv_heads (%d)", hq, hkv);
@@ -810,6 +815,7 @@ struct PagedPlan {
 int paged_plan(int batch, int hq, int hkv, int head_dim, int kv_dtype, int tpb, int max_row_tokens, int backend,
                PagedPlan* out, int mode = MODE_ONLINE) {
   const int be = backend_for(backend, kv_dtype, head_dim);
+  if (mode == MODE_VALUES) mode = values_mode(hq / hkv, be);
   if (!lookup_split_kernel(kv_dtype, head_dim, mode, be, &out->k))
     return fail(PAGER_ERR_UNSUPPORTED, "no split kernel for dtype %d head_dim %d backend %d", kv_dtype, head_dim, be);
   DevInfo* di;
@@ -1204,7 +1210,7 @@ void preload_kernels() {
   const int dims[] = {8, 16, 32, 64, 128, 256};
   for (int dt = 0; dt < 3; ++dt)
     for (int d : dims)
-      for (int mode = 0; mode <= MODE_VALUES; ++mode)
+      for (int mode = 0; mode <= MODE_VALUES_R4; ++mode)
         for (int be : {BACKEND_MMA, BACKEND_FMA}) {
           SplitKernelInfo k;
           if (lookup_split_kernel(dt, d, mode, be, &k)) cudaFuncGetAttributes(&fa, k.fn);
@@ -1259,7 +1265,7 @@ bool chunk_exact(const ChunkArgs& a) { return a.op == 0 && a.kv_dtype != PAGER_D
 int chunk_exact_layout(const ChunkArgs& a, char* base, ChunkExactLayout* L) {
   const int be = backend_for(a.backend, a.kv_dtype, a.head_dim);
   if (!lookup_split_kernel(a.kv_dtype, a.head_dim, MODE_SCORES, be, &L->ks) ||
-      !lookup_split_kernel(a.kv_dtype, a.head_dim, MODE_VALUES, be, &L->kv))
+      !lookup_split_kernel(a.kv_dtype, a.head_dim, values_mode(a.hq / a.hkv, be), be, &L->kv))
     return fail(PAGER_ERR_UNSUPPORTED, "no exact-rounding kernels for dtype %d head_dim %d", a.kv_dtype, a.head_dim);
   if (L->ks.tile != L->kv.tile) return fail(PAGER_ERR_CUDA, "scores and values passes disagree on the tile");
   DevInfo* di;

@@ -40,7 +40,9 @@
 
 namespace pager {
 
-enum Mode { MODE_ONLINE = 0, MODE_STATS = 1, MODE_FIXED = 2, MODE_SCORES = 3, MODE_VALUES = 4 };
+// MODE_VALUES_R4: MODE_VALUES for at most 4 query heads per KV head, whose smaller score ring
+// leaves room for one more stage of V in the same shared memory.
+enum Mode { MODE_ONLINE = 0, MODE_STATS = 1, MODE_FIXED = 2, MODE_SCORES = 3, MODE_VALUES = 4, MODE_VALUES_R4 = 5 };
 enum Source { SRC_CONTIG = 0, SRC_PAGED = 1 };
 enum Backend { BACKEND_MMA = 1, BACKEND_FMA = 2 };
 
@@ -171,7 +173,7 @@ struct TileCfg {
   // 16 KiB of KV per stage: a K and a V tile, or one tile twice as long in the passes that read
   // one of them (per-tile costs -- waits, table lookups, the online update -- then spread over as
   // many bytes as in the one-pass kernel)
-  static constexpr bool SINGLE = MODE == MODE_STATS || MODE == MODE_SCORES || MODE == MODE_VALUES;
+  static constexpr bool SINGLE = MODE == MODE_STATS || MODE == MODE_SCORES || MODE == MODE_VALUES || MODE == MODE_VALUES_R4;
   static constexpr int TILE_RAW = 16384 / ((SINGLE ? 1 : 2) * ROW_BYTES);
   static constexpr int TILE = TILE_RAW > 64 ? 64 : (TILE_RAW < 16 ? 16 : TILE_RAW);
   static constexpr int LOG2_TILE = TILE == 64 ? 6 : (TILE == 32 ? 5 : 4);
@@ -184,12 +186,13 @@ struct TileCfg {
   static constexpr int PANEL_TILE_BYTES = TILE * PANEL_BYTES;
   static constexpr int TENSOR_BYTES = TILE * ROW_BYTES;
   static constexpr bool KONLY = MODE == MODE_STATS || MODE == MODE_SCORES;  // K tiles only
-  static constexpr bool VONLY = MODE == MODE_VALUES;                         // V tiles only
+  static constexpr bool VONLY = MODE == MODE_VALUES || MODE == MODE_VALUES_R4;  // V tiles only
+  static constexpr int AUX_REP = MODE == MODE_VALUES_R4 ? 4 : kMaxRep;        // score rows per stage
   static constexpr int STAGE_BYTES = (KONLY || VONLY ? 1 : 2) * TENSOR_BYTES;
   // VALUES: a second ring beside the tensor ring holds each stage's score tile [n_rep][TILE] and
   // reference maxima [n_rep][kRefSlots] (fp32, no swizzle), filled by the same full barrier.
-  static constexpr int AUX_S_BYTES = VONLY ? kMaxRep * TILE * 4 : 0;
-  static constexpr int AUX_BYTES = VONLY ? (AUX_S_BYTES + kMaxRep * kRefSlots * 4 + 127) / 128 * 128 : 0;
+  static constexpr int AUX_S_BYTES = VONLY ? AUX_REP * TILE * 4 : 0;
+  static constexpr int AUX_BYTES = VONLY ? (AUX_S_BYTES + AUX_REP * kRefSlots * 4 + 127) / 128 * 128 : 0;
   // Shared memory outside the stage ring: Q (bf16/fp16 for mma, fp32 for fma), the fma
   // path's P buffer, the block-table cache, barriers.
   // CTA shape.  Tensor-core configs: 3 consumer warps + 1 producer warp in 128 threads, two CTAs
@@ -924,12 +927,12 @@ __device__ void run_consumer_mma(const SplitParams& p, const TableCache& tc, uin
 // its tiles in order, so the warp keeps O and l relative to the latest M and rescales them when M
 // grows (at most once per group; G >= 16 puts every 16-token k-step in one group, and under the
 // final-max rule all groups share M).  The split's (m, l, acc) then merge like ONLINE partials.
-template <typename T, int D>
+template <typename T, int D, int MODE>
 __device__ void run_consumer_mma_values(const SplitParams& p, const TableCache& tc, uint8_t* stages, uint8_t* aux,
                                         uint64_t* full, uint64_t* empty, volatile int* infos, int b, int h,
                                         int tile0, int ntiles, const RowGeom& g, volatile int* abort_flag,
                                         int split) {
-  using Cfg = TileCfg<T, D, MODE_VALUES, BACKEND_MMA>;
+  using Cfg = TileCfg<T, D, MODE, BACKEND_MMA>;
   using Op = MmaOp<T>;
   static_assert(Cfg::PANEL_BYTES == 128, "mma path expects 128-byte panels");
   constexpr int NT_O = D / 8;
@@ -1368,12 +1371,12 @@ __device__ void run_consumer_fma(const SplitParams& p, const TableCache& tc, uin
 // rounded to the KV dtype; the warp keeps O and l relative to the tile's last (largest) M, so a
 // token of an earlier group of the tile enters P.V as its rounded p times exp(M_group - M), the
 // scale applied after the rounding as the reference's later rescale of its accumulator is.
-template <typename T, int D>
+template <typename T, int D, int MODE>
 __device__ void run_consumer_fma_values(const SplitParams& p, const TableCache& tc, uint8_t* stages, uint8_t* aux,
                                         uint64_t* full, uint64_t* empty, volatile int* infos, int b, int h,
                                         int tile0, int ntiles, const RowGeom& g, volatile int* abort_flag,
                                         int split, float* p_sm_all) {
-  using Cfg = TileCfg<T, D, MODE_VALUES, BACKEND_FMA>;
+  using Cfg = TileCfg<T, D, MODE, BACKEND_FMA>;
   constexpr int TILE = Cfg::TILE;
   constexpr int TPL = TILE > 32 ? TILE / 32 : 1;
   constexpr int DPL = D >= 32 ? D / 32 : 1;
@@ -1552,6 +1555,10 @@ __global__ void __launch_bounds__(TileCfg<T, D, MODE, BACKEND>::THREADS, TileCfg
   pdl_wait();
   pdl_launch_dependents();
   if (p.active && p.active[b] == 0) return;
+  if (Cfg::VONLY && p.n_rep > Cfg::AUX_REP) {  // the host picks the variant; never overrun its score ring
+    if (blockIdx.x == 0 && h == 0 && threadIdx.x == 0) atomicExch(p.status, kStatusBadBlock);
+    return;
+  }
   bool clamped = false;
   const RowGeom g = row_geom(p.geom, b, &clamped);
   if (clamped && split == 0 && h == 0 && threadIdx.x == 0) atomicExch(p.status, kStatusBadBlock);
@@ -1624,14 +1631,14 @@ __global__ void __launch_bounds__(TileCfg<T, D, MODE, BACKEND>::THREADS, TileCfg
     run_producer<Cfg, MODE>(p, tc, &mapk, &mapv, &maps, &mapm, stages, aux, full, empty, infos, b, h, tile0, ntiles,
                             g, abort_flag, warp - Cfg::NCW);
   } else {
-    if constexpr (BACKEND == BACKEND_MMA && MODE == MODE_VALUES) {
-      run_consumer_mma_values<T, D>(p, tc, stages, aux, full, empty, infos, b, h, tile0, ntiles, g, abort_flag,
+    if constexpr (BACKEND == BACKEND_MMA && Cfg::VONLY) {
+      run_consumer_mma_values<T, D, MODE>(p, tc, stages, aux, full, empty, infos, b, h, tile0, ntiles, g, abort_flag,
                                     split);
     } else if constexpr (BACKEND == BACKEND_MMA) {
       run_consumer_mma<T, D, MODE>(p, tc, stages, full, empty, infos, b, h, tile0, ntiles, g, abort_flag, split,
                                    q_smem_t);
-    } else if constexpr (MODE == MODE_VALUES) {
-      run_consumer_fma_values<T, D>(p, tc, stages, aux, full, empty, infos, b, h, tile0, ntiles, g, abort_flag, split,
+    } else if constexpr (Cfg::VONLY) {
+      run_consumer_fma_values<T, D, MODE>(p, tc, stages, aux, full, empty, infos, b, h, tile0, ntiles, g, abort_flag, split,
                                     p_sm);
     } else {
       run_consumer_fma<T, D, MODE>(p, tc, stages, full, empty, infos, b, h, tile0, ntiles, g, abort_flag, split,

@@ -21,6 +21,7 @@
       case pager::MODE_FIXED: *out = pager::split_kernel_info<T, D, pager::MODE_FIXED, pager::BACKEND_MMA>(); return true;   \
       case pager::MODE_SCORES: *out = pager::split_kernel_info<T, D, pager::MODE_SCORES, pager::BACKEND_MMA>(); return true; \
       case pager::MODE_VALUES: *out = pager::split_kernel_info<T, D, pager::MODE_VALUES, pager::BACKEND_MMA>(); return true; \
+      case pager::MODE_VALUES_R4: *out = pager::split_kernel_info<T, D, pager::MODE_VALUES_R4, pager::BACKEND_MMA>(); return true; \
       default: return false;                                                         \
     }
 

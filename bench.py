@@ -48,9 +48,13 @@ for _p in (ROOT, os.path.join(ROOT, "rust-llm-pager_b200")):
         sys.path.insert(0, _p)
 
 METRIC = "decode-attn effective KV GB/s (HBM + host tiers) at 32k ctx"
-# (268.83 MB read + 4.59 MB written) / 268.75 MB of K/V per launch, from one ncu capture of the
-# split kernel on the prof-hbm workload (profiles/split_kernel_paged_hbm_prof-hbm.md).
-NCU_DRAM_PER_HBM_BYTE = (268.83 + 4.59) / 268.75
+# DRAM bytes (read + written) per algorithmic K/V byte of one layer's kernels, from ncu captures
+# with caches left warm between kernels (--cache-control none) on prof-b8, one layer of hbm-32k
+# (the prof-b8 traffic summary under profiles/): the one-pass kernel + combine/mass, 1051.87 MB read +
+# 4.94 MB written; the reference-rounding passes (scores, reference-max scan, values,
+# combine/mass), 1070.60 MB + 14.74 MB, the scores mostly staying in L2 between the passes.
+# Algorithmic bytes per layer: 1073.74 MB.
+NCU_DRAM_PER_HBM_BYTE = {"one_pass": (1051.87 + 4.94) / 1073.74, "exact": (1070.60 + 14.74) / 1073.74}
 
 WORKLOADS = {
     # the serving config's Llama-3-8B geometry at 32k: 40 GB HBM budget, overflow in the pinned host pool
@@ -836,7 +840,8 @@ def run_ours(args):
     # host tier is staged (zero-copy host reads cross the link, not DRAM) -- and to those copies
     # themselves: the copy engines write every staged host byte into device memory first.
     staged = wl.plan.host_read == "staged"
-    kernel_dram_bytes = (wl.hbm_bytes + (wl.host_bytes if staged else 0)) / wl.L * NCU_DRAM_PER_HBM_BYTE
+    dram_ratio = NCU_DRAM_PER_HBM_BYTE["one_pass" if wl.plan.rounding == 0 else "exact"]
+    kernel_dram_bytes = (wl.hbm_bytes + (wl.host_bytes if staged else 0)) / wl.L * dram_ratio
     copy_engine_writes = wl.host_bytes / wl.L if staged else 0.0
     traffic = kernel_dram_bytes + copy_engine_writes
     clocks = clk.summary()
@@ -850,8 +855,9 @@ def run_ours(args):
         "roofline": {
             "bound": "hbm", "achieved": achieved, "peak": combined_peak, "unit": "GB/s",
             "frac": achieved / combined_peak, "traffic": traffic,
-            "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of split_kernel on prof-hbm "
-                              f"({NCU_DRAM_PER_HBM_BYTE:.4f} B per algorithmic HBM byte) scaled to the bytes this "
+            "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one layer's kernels on prof-b8 "
+                              f"(caches warm between kernels; {dram_ratio:.4f} B per algorithmic HBM byte) scaled to "
+                              "the bytes this "
                               "launch reads from DRAM (HBM tier + staged copies), plus the copy engines' writes of "
                               f"the staged host blocks ({copy_engine_writes:.0f} B per launch)",
             "traffic_per_algorithmic_byte": traffic / (wl.bytes_per_step / wl.L),

@@ -739,6 +739,9 @@ def run_ours(args):
 
     world, rank, local = _dist_env()
     out = _json_stdout(world)
+    from pager_hf.request_shard import device_for_local_rank
+
+    local = device_for_local_rank(local, int(os.environ.get("LOCAL_WORLD_SIZE", world)), torch.cuda.device_count())
     if world > 1:
         torch.cuda.set_device(local)
         from datetime import timedelta

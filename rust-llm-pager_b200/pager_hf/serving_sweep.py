@@ -45,7 +45,7 @@ import torch
 from ._lib import DeviceStatusError
 from .batched_decode import BatchedDecodeAttention, DecodeSession
 from .kv_block_store import KVPools
-from .request_shard import local_requests, shard_requests
+from .request_shard import device_for_local_rank, local_requests, shard_requests
 
 LLAMA3_8B = dict(layers=32, hq=32, hkv=8, d=128)  # attention geometry of the reference's serving config
 PAGER_BLOCK_BYTES = 16 * 1024 * 1024  # the pager's budget unit (pager/src/core.rs:6)
@@ -313,7 +313,8 @@ def main(argv=None):
     a = ap.parse_args(argv)
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
+    local = device_for_local_rank(int(os.environ.get("LOCAL_RANK", "0")),
+                                  int(os.environ.get("LOCAL_WORLD_SIZE", str(world))), torch.cuda.device_count())
     torch.cuda.set_device(local)
     if world > 1:
         import torch.distributed as dist

@@ -110,3 +110,14 @@ def test_two_gloo_ranks_shard_requests_and_reduce_time(tmp_path):
 def test_max_over_ranks_without_process_group_is_identity():
     assert max_over_ranks(3.5) == 3.5
     assert torch.distributed.is_available()
+
+
+def test_ranks_spread_over_the_visible_gpus():
+    from pager_hf.request_shard import device_for_local_rank
+
+    assert [device_for_local_rank(r, 4, 8) for r in range(4)] == [0, 2, 4, 6]
+    assert [device_for_local_rank(r, 2, 8) for r in range(2)] == [0, 4]
+    assert [device_for_local_rank(r, 8, 8) for r in range(8)] == list(range(8))
+    assert [device_for_local_rank(r, 3, 8) for r in range(3)] == [0, 2, 4]
+    assert device_for_local_rank(0, 1, 8) == 0
+    assert [device_for_local_rank(r, 4, 4) for r in range(4)] == [0, 1, 2, 3]  # one GPU per rank: identity

@@ -1113,6 +1113,172 @@ __device__ void run_consumer_mma_values(const SplitParams& p, const TableCache& 
   merge_and_store<D, MODE_ONLINE, Cfg::NCW>(p, mw, b, h, split);
 }
 
+// The values pass with the mma operands' roles swapped, for at most 8 query heads per KV head:
+// O^T[d][h] += V^T[d][t] . P^T[t][h].  V is the m16 operand (ldmatrix.trans of the token-major
+// tile) and the heads fill the n8 side, so a k-step of 16 tokens takes D/16 mma instead of D/8, each
+// lane forms p for one head (row gr) instead of two, and the accumulator is D/4 floats per lane.
+// The arithmetic is that of run_consumer_mma_values: p against its group's reference max, rounded
+// to the KV dtype, O and l rescaled when the reference max grows.  A lane keeps two views of the
+// running max: m_p for head gr (its p and l) and m_c for heads 2tq, 2tq+1 (its accumulator
+// columns); both follow the same reference maxima, so they agree head by head.
+template <typename T, int D, int MODE>
+__device__ void run_consumer_mma_values_t(const SplitParams& p, const TableCache& tc, uint8_t* stages, uint8_t* aux,
+                                          uint64_t* full, uint64_t* empty, volatile int* infos, int b, int h,
+                                          int tile0, int ntiles, const RowGeom& g, volatile int* abort_flag,
+                                          int split) {
+  using Cfg = TileCfg<T, D, MODE, BACKEND_MMA>;
+  using Op = MmaOp<T>;
+  static_assert(Cfg::PANEL_BYTES == 128, "mma path expects 128-byte panels");
+  static_assert(Cfg::AUX_REP <= 8, "one n8 tile holds the heads");
+  constexpr int MT = D / 16;  // m16 tiles over head_dim
+  constexpr int NT_S = Cfg::TILE / 8;
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const int gr = lane >> 2;
+  const int tq = lane & 3;
+  const int n_rep = p.n_rep;
+  const int qh0 = h * n_rep;
+  const int l7 = lane & 7;
+  const int db = (lane >> 3) & 1;  // ldmatrix: which 8 head_dim columns this lane's row address covers
+  const int tb = (lane >> 4) & 1;  // ... and which 8 tokens
+  const bool row_ok = gr < n_rep;  // head gr exists
+  const int seg_rows = p.source == SRC_CONTIG ? Cfg::TILE : min(Cfg::TILE, p.tpb);
+  const int* const valid = p.valid;
+  const long long valid_stride = p.valid_stride;
+  const uint64_t wait_limit = p.wait_limit_ns;
+  int* const status = p.status;
+  float2* const mass_part = p.mass_part;
+  const int num_q_heads = p.num_q_heads;
+  const int mass_gstride = p.mass_gstride;
+  const int log2_group = p.log2_group;
+  const int G = p.group_tokens;
+  const uint64_t full_mask = Cfg::TILE == 64 ? ~0ull : ((1ull << Cfg::TILE) - 1ull);
+
+  float o[MT][4];
+#pragma unroll
+  for (int m = 0; m < MT; ++m) o[m][0] = o[m][1] = o[m][2] = o[m][3] = 0.f;
+  float m_p = neg_inf(), l_p = 0.f;
+  float m_c[2] = {neg_inf(), neg_inf()};
+
+  for (int i = warp; i < ntiles; i += Cfg::NCW) {
+    const int s = i % Cfg::STAGES;
+    if (*abort_flag) break;
+    uint32_t swm;
+    if (!consumer_wait(wait_limit, status, &full[s], &empty[s], &infos[s], i / Cfg::STAGES, abort_flag, &swm)) break;
+    const int t0 = (tile0 + i) * Cfg::TILE;
+    uint8_t* vbuf = stages + s * Cfg::STAGE_BYTES;
+    const float* s_sm = reinterpret_cast<const float*>(aux + s * Cfg::AUX_BYTES);  // [n_rep][TILE]
+    const float* m_sm = s_sm + Cfg::AUX_S_BYTES / 4;                               // [n_rep][kRefSlots]
+    if (swm & 0xffu) copy_sw_segments<Cfg, false, true>(p, tc, g, b, h, t0, swm & 0xffu, vbuf, vbuf);
+    uint32_t vlo, vhi;
+    tile_bits_fast<Cfg::TILE>(valid, valid_stride, b, t0, g, swm >> 8, seg_rows, vlo, vhi);
+    bool wrote = (swm & 0xffu) != 0;
+    if ((((uint64_t)vhi << 32) | vlo) != full_mask) wrote |= zero_masked_rows<Cfg>(vbuf, vlo, vhi);
+
+    // scores of head gr (masked tokens hold -inf), tokens 8j + 2tq + {0, 1}
+    float sc[NT_S][2];
+#pragma unroll
+    for (int j = 0; j < NT_S; ++j) {
+      float2 v = make_float2(neg_inf(), neg_inf());
+      if (row_ok) v = *reinterpret_cast<const float2*>(s_sm + gr * Cfg::TILE + 8 * j + 2 * tq);
+      sc[j][0] = v.x;
+      sc[j][1] = v.y;
+    }
+    float gsum = 0.f;  // this lane's sum of p over the current mass group
+    const uint32_t vaddr = smem_u32(vbuf);
+#pragma unroll
+    for (int kt = 0; kt < Cfg::TILE / 16; ++kt) {
+      const int gi = (16 * kt) / G;  // the k-step's group within the tile
+      const float mn = row_ok ? m_sm[gr * kRefSlots + gi] : neg_inf();
+      if (mn > m_p) {
+        l_p *= m_p == neg_inf() ? 0.f : fast_exp2((m_p - mn) * kLog2e);
+        m_p = mn;
+      }
+      float alpha[2];
+      bool changed = false;
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        const int head = 2 * tq + c;
+        const float mc = head < n_rep ? m_sm[head * kRefSlots + gi] : neg_inf();
+        alpha[c] = 1.f;
+        if (mc > m_c[c]) {
+          alpha[c] = m_c[c] == neg_inf() ? 0.f : fast_exp2((m_c[c] - mc) * kLog2e);
+          m_c[c] = mc;
+          changed = true;
+        }
+      }
+      if (__any_sync(0xffffffffu, changed)) {
+#pragma unroll
+        for (int m = 0; m < MT; ++m) {
+          o[m][0] *= alpha[0];
+          o[m][1] *= alpha[1];
+          o[m][2] *= alpha[0];
+          o[m][3] *= alpha[1];
+        }
+      }
+      const float mref = m_p == neg_inf() ? 0.f : m_p * kLog2e;
+#pragma unroll
+      for (int jj = 2 * kt; jj < 2 * kt + 2; ++jj) {
+        sc[jj][0] = fast_exp2(fmaf(sc[jj][0], kLog2e, -mref));
+        sc[jj][1] = fast_exp2(fmaf(sc[jj][1], kLog2e, -mref));
+        l_p += sc[jj][0] + sc[jj][1];
+        gsum += sc[jj][0] + sc[jj][1];
+      }
+      // P^T as the col-major B operand: tokens 2tq + {0, 1} and 2tq + 8 + {0, 1} of head gr
+      const uint32_t b0 = Op::pack(sc[2 * kt][0], sc[2 * kt][1]);
+      const uint32_t b1 = Op::pack(sc[2 * kt + 1][0], sc[2 * kt + 1][1]);
+#pragma unroll
+      for (int m = 0; m < MT; ++m) {
+        uint32_t a[4];
+        const int c = 2 * m + db;  // 16-byte chunk of the token row: head_dim 8c .. 8c + 7
+        const uint32_t voff = (c >> 3) * Cfg::PANEL_TILE_BYTES + (tb * 8 + l7) * 128 + (((c & 7) ^ l7) << 4);
+        ldmatrix_x4_trans(vaddr + voff + kt * 16 * 128, a[0], a[1], a[2], a[3]);
+        Op::run(o[m], a, b0, b1);
+      }
+      // a mass group ends after this k-step: (sum p, the group's reference max)
+      if (G > 0 && ((16 * (kt + 1)) % G == 0 || G < 16)) {
+        // G == 8 (final-max rule only): this k-step holds two groups; split the sum by token half
+        const int ngs = G < 16 ? 2 : 1;
+#pragma unroll
+        for (int q2 = 0; q2 < 2; ++q2) {
+          if (q2 >= ngs) break;
+          float gs = ngs == 2 ? sc[2 * kt + q2][0] + sc[2 * kt + q2][1] : gsum;
+          gs += __shfl_xor_sync(0xffffffffu, gs, 1);
+          gs += __shfl_xor_sync(0xffffffffu, gs, 2);
+          const int gl = ngs == 2 ? 2 * kt + q2 : gi;  // group index within the tile
+          if (tq == 0 && row_ok)
+            mass_part[((long long)b * num_q_heads + qh0 + gr) * mass_gstride + (t0 >> log2_group) + gl] =
+                make_float2(gs, m_sm[gr * kRefSlots + gl]);
+        }
+        gsum = 0.f;
+      }
+    }
+    release_stage(&empty[s], wrote);
+  }
+
+  l_p += __shfl_xor_sync(0xffffffffu, l_p, 1);
+  l_p += __shfl_xor_sync(0xffffffffu, l_p, 2);
+  named_bar_sync(1, Cfg::NCW * 32);
+  float* mw = reinterpret_cast<float*>(stages);
+  float* m_w = mw;
+  float* l_w = mw + Cfg::NCW * kMaxRep;
+  float* acc_w = mw + 2 * Cfg::NCW * kMaxRep;
+  if (tq == 0) {
+    m_w[warp * kMaxRep + gr] = m_p;
+    l_w[warp * kMaxRep + gr] = l_p;
+  }
+#pragma unroll
+  for (int m = 0; m < MT; ++m) {
+    const int d = 16 * m + gr;
+    acc_w[(warp * kMaxRep + 2 * tq) * D + d] = o[m][0];
+    acc_w[(warp * kMaxRep + 2 * tq + 1) * D + d] = o[m][1];
+    acc_w[(warp * kMaxRep + 2 * tq) * D + d + 8] = o[m][2];
+    acc_w[(warp * kMaxRep + 2 * tq + 1) * D + d + 8] = o[m][3];
+  }
+  named_bar_sync(1, Cfg::NCW * 32);
+  merge_and_store<D, MODE_ONLINE, Cfg::NCW>(p, mw, b, h, split);
+}
+
 // ------------------------------------------------------------------ CUDA-core consumer
 // Lane <-> token for Q.K (q broadcast from shared memory), lane <-> head_dim
 // column for P.V (p broadcast from shared memory); fp32 throughout.
@@ -1631,7 +1797,10 @@ __global__ void __launch_bounds__(TileCfg<T, D, MODE, BACKEND>::THREADS, TileCfg
     run_producer<Cfg, MODE>(p, tc, &mapk, &mapv, &maps, &mapm, stages, aux, full, empty, infos, b, h, tile0, ntiles,
                             g, abort_flag, warp - Cfg::NCW);
   } else {
-    if constexpr (BACKEND == BACKEND_MMA && Cfg::VONLY) {
+    if constexpr (BACKEND == BACKEND_MMA && MODE == MODE_VALUES_R4) {
+      run_consumer_mma_values_t<T, D, MODE>(p, tc, stages, aux, full, empty, infos, b, h, tile0, ntiles, g, abort_flag,
+                                            split);
+    } else if constexpr (BACKEND == BACKEND_MMA && Cfg::VONLY) {
       run_consumer_mma_values<T, D, MODE>(p, tc, stages, aux, full, empty, infos, b, h, tile0, ntiles, g, abort_flag,
                                     split);
     } else if constexpr (BACKEND == BACKEND_MMA) {

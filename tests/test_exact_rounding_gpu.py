@@ -103,6 +103,9 @@ CASES = [
     (13, 2, 32, 4, 64, 32, 1, [17, 6], [3, 30], torch.bfloat16, set(), [100, 0], [500, 150], 3),
     (14, 2, 8, 4, 256, 16, 2, [13, 3], [5, 9], torch.bfloat16, set(), [10, 0], None, 2),
     (15, 2, 32, 8, 128, 16, 1, [40, 1], [15, 2], torch.float16, {(0, 0), (0, 11)}, None, None, 64),
+    # the swapped-operand values pass (n_rep <= 4) at n_rep 1 (MHA) and 3, head_dim 64 and 128
+    (18, 2, 8, 8, 64, 64, 1, [7, 4], [30, 1], torch.bfloat16, set(), [0, 33], None, 64),
+    (19, 2, 12, 4, 128, 32, 1, [11, 6], [9, 32], torch.float16, {(1, 2)}, None, [600, 180], 2),
     # CUDA-core kernels (head_dim below 64), 8-token blocks included
     (16, 2, 8, 2, 32, 16, 1, [12, 3], [5, 9], torch.float16, set(), None, None, 4),
     (17, 2, 4, 1, 8, 8, 1, [20, 5], [3, 8], torch.bfloat16, set(), [7, 0], None, 64),

@@ -1,14 +1,16 @@
 // Split-KV decode-attention kernel for sm_100a.
 //
 // One CTA = one work unit (batch row b, KV head h, split s): a contiguous run
-// of TILE-token tiles of row b.  Warp 4 is the producer: it streams K/V tiles
-// into a ring of shared-memory stages -- TMA tensor loads (128B-swizzled) for
-// HBM-resident data, 16-byte zero-copy loads for blocks in the pinned host
-// pool and for the tail -- signalling per-stage mbarriers.  Warps 0-3 are
-// consumers: tile i goes to warp i % 4, which folds it into its own online
-// softmax state (m, l, acc) for the n_rep query heads sharing KV head h.  At
-// the end the four warp states are merged and the split's partial state is
-// written to scratch; a combine kernel merges splits.
+// of TILE-token tiles of row b.  Warps 0 .. NCW-1 are consumers, the warps after
+// them producers (TileCfg: NCW 3 or 4 and one producer on the tensor-core path, 6
+// and 2 on the CUDA-core path).  A producer streams K/V tiles into a ring of
+// shared-memory stages -- TMA tensor loads (128B-swizzled) for HBM-resident
+// data, 16-byte zero-copy loads for blocks in the pinned host pool and for the
+// tail -- signalling per-stage mbarriers.  Tile i goes to consumer warp
+// i % NCW, which folds it into its own online softmax state (m, l, acc) for the
+// n_rep query heads sharing KV head h.  At the end the warp states are merged
+// and the split's partial state is written to scratch; a combine kernel merges
+// splits.
 //
 // Modes (the reference's four kernels, pager_hf/streaming_attention.py):
 //   ONLINE  one-pass (m, l, acc) fold            (_decode_attention_step_kernel :77-185)
@@ -195,11 +197,14 @@ struct TileCfg {
   static constexpr int AUX_BYTES = VONLY ? (AUX_S_BYTES + AUX_REP * kRefSlots * 4 + 127) / 128 * 128 : 0;
   // Shared memory outside the stage ring: Q (bf16/fp16 for mma, fp32 for fma), the fma
   // path's P buffer, the block-table cache, barriers.
-  // CTA shape.  Tensor-core configs: 3 consumer warps + 1 producer warp in 128 threads, two CTAs
+  // CTA shape.  Tensor-core configs: 3 consumer warps (4 for MODE_VALUES_R4) + 1 producer warp, two CTAs
   // per SM (half the shared memory each), so that one CTA's prologue, pipeline fill and merge
   // overlap the other's streaming and the grid has twice the slots to balance splits over.
   // CUDA-core configs (compute-bound): 6 consumer + 2 producer warps, one CTA per SM.
-  static constexpr int NCW = BACKEND == BACKEND_MMA ? 3 : 6;  // consumer warps
+  // consumer warps: the swapped-operand values pass (184 registers a thread) fits a fourth warp at
+  // two CTAs per SM, which hides more of its per-tile latency (measured: 206.0 -> 199.4 us per
+  // hbm-32k layer; a fourth scores warp, or a fifth values warp, measured slower)
+  static constexpr int NCW = BACKEND == BACKEND_MMA ? (MODE == MODE_VALUES_R4 ? 4 : 3) : 6;
   static constexpr int NPW = BACKEND == BACKEND_MMA ? 1 : 2;  // producer warps (one thread each)
   static constexpr int THREADS = (NCW + NPW) * 32;
   static constexpr int MIN_BLOCKS = BACKEND == BACKEND_MMA ? 2 : 1;

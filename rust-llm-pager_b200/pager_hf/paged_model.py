@@ -553,7 +553,7 @@ class PagedModel:
                           torch.full((B,), self._tail_len, dtype=torch.int32),
                           torch.full((B,), nb * self.tokens_per_block, dtype=torch.int32)] + los)
         g.load(ints, input_ids, self._position_ids_from_mask(attention_mask)[:, -1:])
-        logits = g.step()
+        logits = g.step().clone()  # the graph's logits buffer is overwritten by the next replay
         self.last_host_read = "zero_copy"
         L.watch_for(input_ids.device).sync_and_check("PagedModel decode step")
         return logits, self._finish_token(None if g.mass is None else g.mass[:nb])

@@ -340,3 +340,31 @@ def test_beam_search_matches_hf_beam_search_in_fp32():
     three = pm.generate_beam_search(ids[:1], mask[:1], num_beams=3, max_new_tokens=12, length_penalty=0.0,
                                     num_return_sequences=3)
     assert len(three) == 3 and three[0] == got[0]
+
+
+def test_captured_step_logits_are_not_overwritten_by_the_next_step():
+    """The logits a captured decode step returns are the caller's: the next replay writes the
+    graph's own buffer, not the tensor handed out (as an eager step's logits are fresh tensors)."""
+    from pager_hf.paged_model import PagedModel
+
+    model = _model("qwen2")
+    g = torch.Generator().manual_seed(6)
+    ids = torch.randint(0, 2000, (2, 120), generator=g).cuda()
+    mask = torch.ones_like(ids)
+    pm = PagedModel(model, vram_budget=3 * BLOCK, ram_budget=64 * BLOCK, recent_window=1, policy="recent_only",
+                    tokens_per_block=16, decode_graphs=True)
+    kept, copies = [], []
+    orig = pm._forward_step
+
+    def step(input_ids, attention_mask):
+        logits, info = orig(input_ids, attention_mask)
+        kept.append(logits)  # no copy: must stay this step's values
+        copies.append(logits.clone())
+        return logits, info
+
+    pm._forward_step = step
+    pm.generate(ids, mask, 6)
+    assert len(kept) >= 5
+    for a, b in zip(kept, copies):
+        assert torch.equal(a, b)
+    assert not torch.equal(kept[-2], kept[-1])

@@ -1194,31 +1194,35 @@ __device__ void run_consumer_mma_values_t(const SplitParams& p, const TableCache
 #pragma unroll
     for (int kt = 0; kt < Cfg::TILE / 16; ++kt) {
       const int gi = (16 * kt) / G;  // the k-step's group within the tile
-      const float mn = row_ok ? m_sm[gr * kRefSlots + gi] : neg_inf();
-      if (mn > m_p) {
-        l_p *= m_p == neg_inf() ? 0.f : fast_exp2((m_p - mn) * kLog2e);
-        m_p = mn;
-      }
-      float alpha[2];
-      bool changed = false;
-#pragma unroll
-      for (int c = 0; c < 2; ++c) {
-        const int head = 2 * tq + c;
-        const float mc = head < n_rep ? m_sm[head * kRefSlots + gi] : neg_inf();
-        alpha[c] = 1.f;
-        if (mc > m_c[c]) {
-          alpha[c] = m_c[c] == neg_inf() ? 0.f : fast_exp2((m_c[c] - mc) * kLog2e);
-          m_c[c] = mc;
-          changed = true;
+      // the reference max changes only where a group starts: once a tile when groups are tiles
+      // (blocks of at least 64 tokens), so the check runs at the first k-step only
+      if (kt == 0 || G < Cfg::TILE) {
+        const float mn = row_ok ? m_sm[gr * kRefSlots + gi] : neg_inf();
+        if (mn > m_p) {
+          l_p *= m_p == neg_inf() ? 0.f : fast_exp2((m_p - mn) * kLog2e);
+          m_p = mn;
         }
-      }
-      if (__any_sync(0xffffffffu, changed)) {
+        float alpha[2];
+        bool changed = false;
 #pragma unroll
-        for (int m = 0; m < MT; ++m) {
-          o[m][0] *= alpha[0];
-          o[m][1] *= alpha[1];
-          o[m][2] *= alpha[0];
-          o[m][3] *= alpha[1];
+        for (int c = 0; c < 2; ++c) {
+          const int head = 2 * tq + c;
+          const float mc = head < n_rep ? m_sm[head * kRefSlots + gi] : neg_inf();
+          alpha[c] = 1.f;
+          if (mc > m_c[c]) {
+            alpha[c] = m_c[c] == neg_inf() ? 0.f : fast_exp2((m_c[c] - mc) * kLog2e);
+            m_c[c] = mc;
+            changed = true;
+          }
+        }
+        if (__any_sync(0xffffffffu, changed)) {
+#pragma unroll
+          for (int m = 0; m < MT; ++m) {
+            o[m][0] *= alpha[0];
+            o[m][1] *= alpha[1];
+            o[m][2] *= alpha[0];
+            o[m][3] *= alpha[1];
+          }
         }
       }
       const float mref = m_p == neg_inf() ? 0.f : m_p * kLog2e;

@@ -1000,27 +1000,30 @@ __device__ void run_consumer_mma_values(const SplitParams& p, const TableCache& 
 #pragma unroll
     for (int kt = 0; kt < Cfg::TILE / 16; ++kt) {
       const int gi = (16 * kt) / G;  // the k-step's group within the tile
-      float alpha[2];
-      bool changed = false;
-#pragma unroll
-      for (int rr = 0; rr < 2; ++rr) {
-        const int row = gr + 8 * rr;
-        const float mn = row < n_rep ? m_sm[row * kRefSlots + gi] : neg_inf();
-        alpha[rr] = 1.f;
-        if (mn > m_r[rr]) {
-          alpha[rr] = m_r[rr] == neg_inf() ? 0.f : fast_exp2((m_r[rr] - mn) * kLog2e);
-          m_r[rr] = mn;
-          changed = true;
-        }
-      }
-      if (__any_sync(0xffffffffu, changed)) {
+      // the reference max changes only where a group starts: once a tile when groups are tiles
+      if (kt == 0 || G < Cfg::TILE) {
+        float alpha[2];
+        bool changed = false;
 #pragma unroll
         for (int rr = 0; rr < 2; ++rr) {
-          l_r[rr] *= alpha[rr];
+          const int row = gr + 8 * rr;
+          const float mn = row < n_rep ? m_sm[row * kRefSlots + gi] : neg_inf();
+          alpha[rr] = 1.f;
+          if (mn > m_r[rr]) {
+            alpha[rr] = m_r[rr] == neg_inf() ? 0.f : fast_exp2((m_r[rr] - mn) * kLog2e);
+            m_r[rr] = mn;
+            changed = true;
+          }
+        }
+        if (__any_sync(0xffffffffu, changed)) {
 #pragma unroll
-          for (int n = 0; n < NT_O; ++n) {
-            o[n][2 * rr] *= alpha[rr];
-            o[n][2 * rr + 1] *= alpha[rr];
+          for (int rr = 0; rr < 2; ++rr) {
+            l_r[rr] *= alpha[rr];
+#pragma unroll
+            for (int n = 0; n < NT_O; ++n) {
+              o[n][2 * rr] *= alpha[rr];
+              o[n][2 * rr + 1] *= alpha[rr];
+            }
           }
         }
       }

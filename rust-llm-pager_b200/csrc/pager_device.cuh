@@ -35,6 +35,18 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
       "{\n\t.reg .b64 st;\n\tmbarrier.arrive.shared::cta.b64 st, [%0];\n\t}" ::"r"(smem_u32(bar))
       : "memory");
 }
+// try_wait with a suspend-time hint: a warp whose phase is not complete sleeps in hardware (up to
+// the hint, 1 ms) and wakes when the phase completes, instead of re-issuing the test; waiting
+// consumer and producer warps then take fewer issue slots from the warps doing the work.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(done)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(1000000u)
+      : "memory");
+  return done != 0;
+}
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t done;
   asm volatile(
@@ -61,16 +73,14 @@ __device__ __forceinline__ uint64_t global_timer_ns() {
   return t;
 }
 
-// Bounded wait: spins on try_wait (which itself suspends for a hardware time
-// slice) until the phase completes or `limit_ns` of wall time passes.
-// Returns false on timeout; the caller records the error and aborts.
+// Bounded wait: repeats a sleeping try_wait until the phase completes or `limit_ns` of wall time
+// passes (overshooting it by at most two suspends, 2 ms).  Returns false on timeout; the caller
+// records the error and aborts.
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, uint64_t limit_ns) {
-#pragma unroll 1
-  for (int i = 0; i < 64; ++i)
-    if (mbar_try_wait(bar, parity)) return true;
+  if (mbar_try_wait_sleep(bar, parity)) return true;
   const uint64_t start = global_timer_ns();
   while (true) {
-    if (mbar_try_wait(bar, parity)) return true;
+    if (mbar_try_wait_sleep(bar, parity)) return true;
     if (global_timer_ns() - start > limit_ns) return false;
   }
 }

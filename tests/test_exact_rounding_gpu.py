@@ -106,6 +106,8 @@ CASES = [
     # the swapped-operand values pass (n_rep <= 4) at n_rep 1 (MHA) and 3, head_dim 64 and 128
     (18, 2, 8, 8, 64, 64, 1, [7, 4], [30, 1], torch.bfloat16, set(), [0, 33], None, 64),
     (19, 2, 12, 4, 128, 32, 1, [11, 6], [9, 32], torch.float16, {(1, 2)}, None, [600, 180], 2),
+    # a row of 300 16-token groups: the reference-max scan runs over more than one 256-group chunk
+    (20, 2, 8, 2, 64, 16, 1, [300, 17], [7, 3], torch.bfloat16, {(0, 100)}, [40, 0], None, 4),
     # CUDA-core kernels (head_dim below 64), 8-token blocks included
     (16, 2, 8, 2, 32, 16, 1, [12, 3], [5, 9], torch.float16, set(), None, None, 4),
     (17, 2, 4, 1, 8, 8, 1, [20, 5], [3, 8], torch.bfloat16, set(), [7, 0], None, 64),

@@ -70,6 +70,10 @@ WORKLOADS = {
     # 1.07 GB of KV on the device
     "prof-b8": dict(model="Llama-3-8B attention (L1 slice, Hq32, Hkv8, D128)", layers=1, hq=32, hkv=8, d=128,
                     dtype="bf16", tpb=64, batch=8, context=32768, hbm_budget_gb=40.0, window=None),
+    # BASELINE config 3's attention geometry (TinyLlama: 8 query heads per KV head, head_dim 64, fp16),
+    # 16 rows x 16k, all in HBM: the kernel-bound case of the n_rep-8 values pass
+    "cfg3-hbm-16k": dict(model="TinyLlama-1.1B attention (L22, Hq32, Hkv4, D64)", layers=22, hq=32, hkv=4, d=64,
+                         dtype="f16", tpb=64, batch=16, context=16384, hbm_budget_gb=40.0, window=None),
     # small tiered case for ncu captures: two requests, four layers, 20% of each row's blocks in HBM, the
     # rest in the host pool (staged per layer by the copy engines when the link favours it)
     "prof-tiered": dict(model="Llama-3-8B attention (L4 slice, Hq32, Hkv8, D128)", layers=4, hq=32, hkv=8, d=128,

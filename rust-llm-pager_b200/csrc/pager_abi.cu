@@ -617,8 +617,12 @@ int backend_for(int requested, int kv_dtype, int head_dim) {
 
 // The values pass of reference-exact rounding for a geometry: on the tensor-core kernels with at
 // most 4 query heads per KV head (Llama, Mistral), the variant whose 4-row score ring leaves room for
-// a sixth stage of V tiles in the same shared memory; otherwise the general one.
-int values_mode(int n_rep, int be) { return be == BACKEND_MMA && n_rep <= 4 ? MODE_VALUES_R4 : MODE_VALUES; }
+// a sixth stage of V tiles in the same shared memory; with at most 8 (TinyLlama), the 8-row one;
+// both with the swapped-operand consumers.  Otherwise the general one.
+int values_mode(int n_rep, int be) {
+  if (be != BACKEND_MMA) return MODE_VALUES;
+  return n_rep <= 4 ? MODE_VALUES_R4 : (n_rep <= 8 ? MODE_VALUES_R8 : MODE_VALUES);
+}
 
 int check_geometry(int batch, int hq, int hkv, int head_dim, int kv_dtype, int q_dtype) {
   if (batch < 0 || hq <= 0 || hkv <= 0) return fail(PAGER_ERR_INVALID, "bad shape: batch=%d heads=%d kv_heads=%d", batch, hq, hkv);
@@ -1210,7 +1214,7 @@ void preload_kernels() {
   const int dims[] = {8, 16, 32, 64, 128, 256};
   for (int dt = 0; dt < 3; ++dt)
     for (int d : dims)
-      for (int mode = 0; mode <= MODE_VALUES_R4; ++mode)
+      for (int mode = 0; mode <= MODE_VALUES_R8; ++mode)
         for (int be : {BACKEND_MMA, BACKEND_FMA}) {
           SplitKernelInfo k;
           if (lookup_split_kernel(dt, d, mode, be, &k)) cudaFuncGetAttributes(&fa, k.fn);

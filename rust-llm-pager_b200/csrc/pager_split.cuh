@@ -42,9 +42,13 @@
 
 namespace pager {
 
-// MODE_VALUES_R4: MODE_VALUES for at most 4 query heads per KV head, whose smaller score ring
-// leaves room for one more stage of V in the same shared memory.
-enum Mode { MODE_ONLINE = 0, MODE_STATS = 1, MODE_FIXED = 2, MODE_SCORES = 3, MODE_VALUES = 4, MODE_VALUES_R4 = 5 };
+// MODE_VALUES_R4 / MODE_VALUES_R8: MODE_VALUES for at most 4 / 8 query heads per KV head, with a
+// score ring of that many rows (R4: room for one more stage of V in the same shared memory) and the
+// swapped-operand consumers.
+enum Mode {
+  MODE_ONLINE = 0, MODE_STATS = 1, MODE_FIXED = 2, MODE_SCORES = 3, MODE_VALUES = 4, MODE_VALUES_R4 = 5,
+  MODE_VALUES_R8 = 6
+};
 enum Source { SRC_CONTIG = 0, SRC_PAGED = 1 };
 enum Backend { BACKEND_MMA = 1, BACKEND_FMA = 2 };
 
@@ -175,7 +179,8 @@ struct TileCfg {
   // 16 KiB of KV per stage: a K and a V tile, or one tile twice as long in the passes that read
   // one of them (per-tile costs -- waits, table lookups, the online update -- then spread over as
   // many bytes as in the one-pass kernel)
-  static constexpr bool SINGLE = MODE == MODE_STATS || MODE == MODE_SCORES || MODE == MODE_VALUES || MODE == MODE_VALUES_R4;
+  static constexpr bool SINGLE =
+      MODE == MODE_STATS || MODE == MODE_SCORES || MODE == MODE_VALUES || MODE == MODE_VALUES_R4 || MODE == MODE_VALUES_R8;
   static constexpr int TILE_RAW = 16384 / ((SINGLE ? 1 : 2) * ROW_BYTES);
   static constexpr int TILE = TILE_RAW > 64 ? 64 : (TILE_RAW < 16 ? 16 : TILE_RAW);
   static constexpr int LOG2_TILE = TILE == 64 ? 6 : (TILE == 32 ? 5 : 4);
@@ -188,8 +193,9 @@ struct TileCfg {
   static constexpr int PANEL_TILE_BYTES = TILE * PANEL_BYTES;
   static constexpr int TENSOR_BYTES = TILE * ROW_BYTES;
   static constexpr bool KONLY = MODE == MODE_STATS || MODE == MODE_SCORES;  // K tiles only
-  static constexpr bool VONLY = MODE == MODE_VALUES || MODE == MODE_VALUES_R4;  // V tiles only
-  static constexpr int AUX_REP = MODE == MODE_VALUES_R4 ? 4 : kMaxRep;        // score rows per stage
+  static constexpr bool VONLY = MODE == MODE_VALUES || MODE == MODE_VALUES_R4 || MODE == MODE_VALUES_R8;  // V only
+  static constexpr bool SWAPPED = MODE == MODE_VALUES_R4 || MODE == MODE_VALUES_R8;  // swapped-operand consumers
+  static constexpr int AUX_REP = MODE == MODE_VALUES_R4 ? 4 : (MODE == MODE_VALUES_R8 ? 8 : kMaxRep);  // score rows
   static constexpr int STAGE_BYTES = (KONLY || VONLY ? 1 : 2) * TENSOR_BYTES;
   // VALUES: a second ring beside the tensor ring holds each stage's score tile [n_rep][TILE] and
   // reference maxima [n_rep][kRefSlots] (fp32, no swizzle), filled by the same full barrier.
@@ -197,14 +203,14 @@ struct TileCfg {
   static constexpr int AUX_BYTES = VONLY ? (AUX_S_BYTES + AUX_REP * kRefSlots * 4 + 127) / 128 * 128 : 0;
   // Shared memory outside the stage ring: Q (bf16/fp16 for mma, fp32 for fma), the fma
   // path's P buffer, the block-table cache, barriers.
-  // CTA shape.  Tensor-core configs: 3 consumer warps (4 for MODE_VALUES_R4) + 1 producer warp, two CTAs
+  // CTA shape.  Tensor-core configs: 3 consumer warps (4 for MODE_VALUES_R4/R8) + 1 producer warp, two CTAs
   // per SM (half the shared memory each), so that one CTA's prologue, pipeline fill and merge
   // overlap the other's streaming and the grid has twice the slots to balance splits over.
   // CUDA-core configs (compute-bound): 6 consumer + 2 producer warps, one CTA per SM.
   // consumer warps: the swapped-operand values pass (184 registers a thread) fits a fourth warp at
   // two CTAs per SM, which hides more of its per-tile latency (measured: 206.0 -> 199.4 us per
   // hbm-32k layer; a fourth scores warp, or a fifth values warp, measured slower)
-  static constexpr int NCW = BACKEND == BACKEND_MMA ? (MODE == MODE_VALUES_R4 ? 4 : 3) : 6;
+  static constexpr int NCW = BACKEND == BACKEND_MMA ? (SWAPPED ? 4 : 3) : 6;
   static constexpr int NPW = BACKEND == BACKEND_MMA ? 1 : 2;  // producer warps (one thread each)
   static constexpr int THREADS = (NCW + NPW) * 32;
   static constexpr int MIN_BLOCKS = BACKEND == BACKEND_MMA ? 2 : 1;
@@ -1809,7 +1815,7 @@ __global__ void __launch_bounds__(TileCfg<T, D, MODE, BACKEND>::THREADS, TileCfg
     run_producer<Cfg, MODE>(p, tc, &mapk, &mapv, &maps, &mapm, stages, aux, full, empty, infos, b, h, tile0, ntiles,
                             g, abort_flag, warp - Cfg::NCW);
   } else {
-    if constexpr (BACKEND == BACKEND_MMA && MODE == MODE_VALUES_R4) {
+    if constexpr (BACKEND == BACKEND_MMA && Cfg::SWAPPED) {
       run_consumer_mma_values_t<T, D, MODE>(p, tc, stages, aux, full, empty, infos, b, h, tile0, ntiles, g, abort_flag,
                                             split);
     } else if constexpr (BACKEND == BACKEND_MMA && Cfg::VONLY) {

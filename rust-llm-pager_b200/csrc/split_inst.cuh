@@ -22,6 +22,7 @@
       case pager::MODE_SCORES: *out = pager::split_kernel_info<T, D, pager::MODE_SCORES, pager::BACKEND_MMA>(); return true; \
       case pager::MODE_VALUES: *out = pager::split_kernel_info<T, D, pager::MODE_VALUES, pager::BACKEND_MMA>(); return true; \
       case pager::MODE_VALUES_R4: *out = pager::split_kernel_info<T, D, pager::MODE_VALUES_R4, pager::BACKEND_MMA>(); return true; \
+      case pager::MODE_VALUES_R8: *out = pager::split_kernel_info<T, D, pager::MODE_VALUES_R8, pager::BACKEND_MMA>(); return true; \
       default: return false;                                                         \
     }
 

@@ -207,7 +207,7 @@ struct TileCfg {
   // per SM (half the shared memory each), so that one CTA's prologue, pipeline fill and merge
   // overlap the other's streaming and the grid has twice the slots to balance splits over.
   // CUDA-core configs (compute-bound): 6 consumer + 2 producer warps, one CTA per SM.
-  // consumer warps: the swapped-operand values pass (184 registers a thread) fits a fourth warp at
+  // consumer warps: the swapped-operand values pass (at most 184 registers a thread) fits a fourth warp at
   // two CTAs per SM, which hides more of its per-tile latency (measured: 206.0 -> 199.4 us per
   // hbm-32k layer; a fourth scores warp, or a fifth values warp, measured slower)
   static constexpr int NCW = BACKEND == BACKEND_MMA ? (SWAPPED ? 4 : 3) : 6;
